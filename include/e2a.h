@@ -1,0 +1,180 @@
+/*
+ * e2a.h -- C ABI of the B200 (sm_100a) E2Former-V2 sparse equivariant attention library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*; NULL = legacy
+ * default stream), returns an int status (E2A_OK = 0) and never allocates device memory: the caller
+ * owns all outputs and passes scratch as a workspace whose size it queries first.  Device code never
+ * traps; bad arguments return E2A_ERR_ARG and CUDA failures E2A_ERR_CUDA (the cudaError_t is kept in
+ * e2a_last_cuda_error()).  All reductions are CSR-ordered (no float atomics): results are bitwise
+ * reproducible run to run.
+ *
+ * Reference interfaces replaced (paths inside IQuestLab/UBio-MolFM, e2f = src/molfm/models/e2former):
+ *   e2a_csr_*            prepare_sparse_qk_edge_index_metadata   e2f/triton_dr/triton_sparse_qk_autograd.py:635-652
+ *   e2a_pbc_expand       CellExpander.expand_includeself         e2f/module_utils.py:1065-1275
+ *   e2a_radius_graph_*   construct_radius_neighbor               e2f/module_utils.py:3119-3242
+ *   e2a_sparse_qk_fwd    sparse_qk_edge_index_triton (forward)   e2f/triton_dr/triton_sparse_qk_autograd.py:839-871, 52-98
+ *   e2a_grouped_reduce   _edge_grouped_reduce_triton (dQ, dK)    e2f/triton_dr/triton_sparse_qk_autograd.py:654-673, 388-435
+ *   e2a_alpha_sum_*      sparse_alpha_sum_edge_index_triton      e2f/triton_dr/sparse_alpha_sum_edge_index_autograd.py:207-213
+ *   e2a_v_agg_*          sparse_v_agg_edge_index_triton_cblocked e2f/triton_dr/sparse_v_agg_edge_index_cblocked_bench.py:428-449
+ *   e2a_edge_outer_*     edge_degree_outer_triton                e2f/triton_dr/edge_degree_outer_autograd.py:348-375
+ *   e2a_attn_fwd         E2AttentionArbOrder_sparse.forward, QK logits -> segmented softmax ->
+ *                        alpha/r -> value aggregation            e2f/e2former.py:311-364, 393-422;
+ *                                                                e2f/wigner6j/so2_tensor_product.py:370-377
+ *   e2a_attn_bwd_query / e2a_attn_bwd_key
+ *                        the first-order backward of the same span (what autograd runs for forces)
+ */
+#ifndef E2A_H
+#define E2A_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define E2A_OK 0
+#define E2A_ERR_ARG 1
+#define E2A_ERR_CUDA 2
+#define E2A_ERR_WORKSPACE 3
+#define E2A_ERR_UNSUPPORTED 4
+
+/* Library version (major*10000 + minor*100 + patch). */
+int e2a_version(void);
+/* Human-readable name of a status code. */
+const char* e2a_status_string(int status);
+/* cudaError_t of the most recent E2A_ERR_CUDA on this host thread (0 if none). */
+int e2a_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* CSR metadata: prepare_sparse_qk_edge_index_metadata (triton_sparse_qk_autograd.py:635-652). */
+/* query-CSR: q_row_ptr[N+1], q_col[E] (neighbour of each CSR slot), q_perm[E] (edge id of each  */
+/* slot; identity when query_idx is already sorted).  key-CSR: the stable grouping by neighbour: */
+/* k_row_ptr[M+1], k_col[E] (query of each slot), k_perm[E] (edge id).  int32 everywhere.        */
+/* ------------------------------------------------------------------------------------------ */
+size_t e2a_csr_workspace_bytes(int64_t num_edges, int64_t num_queries, int64_t num_keys);
+int e2a_csr_build(const int32_t* query_idx, const int32_t* neighbor_idx, int64_t num_edges,
+                  int64_t num_queries, int64_t num_keys,
+                  int32_t* q_row_ptr, int32_t* q_col, int32_t* q_perm,
+                  int32_t* k_row_ptr, int32_t* k_col, int32_t* k_perm,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* PBC image expansion: CellExpander.expand_includeself (module_utils.py:1065-1275).            */
+/* offsets[n_img,3] are the fp32 lattice translations in the reference's cell order with image 0 */
+/* = (0,0,0).  Image (c, a) = pos[a] + offsets[c] is kept iff some atom lies strictly within     */
+/* `cutoff` of it; kept images are written cell-major, atom-ascending: exp_pos[k] its position,  */
+/* image_atom[k] = c * n_atoms + a.  Both must hold n_img*n_atoms entries; *n_expanded (host)    */
+/* receives the kept count (synchronises).                                                       */
+/* ------------------------------------------------------------------------------------------ */
+size_t e2a_pbc_expand_workspace_bytes(int64_t n_atoms, int n_img);
+int e2a_pbc_expand(const float* pos, int64_t n_atoms, const float* offsets, int n_img, float cutoff,
+                   float* exp_pos, int64_t* image_atom, int64_t* n_expanded,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Radius graph: construct_radius_neighbor (module_utils.py:3119-3242), cell-list build.        */
+/* Systems b = 0..B-1 own queries [q_ptr[b], q_ptr[b+1]) and expanded points                     */
+/* [p_ptr[b], p_ptr[b+1]) (q_ptr/p_ptr are DEVICE int64 arrays).  Row i keeps the candidates j   */
+/* of its system with min_dist <= |pos_i - pts_j| <= max_dist, ordered by (distance, j)          */
+/* ascending and truncated to max_neighbors (<= 0: no cap).  Distances use the fp32 operation    */
+/* sequence of torch.linalg.norm on CPU, so edge sets and distances are bit-exact.               */
+/* Two phases sharing one workspace: _plan counts (synchronises; returns E and the candidate     */
+/* total on the host), _fill writes E edges.                                                     */
+/* ------------------------------------------------------------------------------------------ */
+size_t e2a_radius_graph_workspace_bytes(int64_t n_queries, int64_t n_points, int64_t n_systems);
+int e2a_radius_graph_plan(const float* pos, const float* pts, const int64_t* q_ptr, const int64_t* p_ptr,
+                          int64_t n_queries, int64_t n_points, int64_t n_systems,
+                          float max_dist, float min_dist, int64_t max_neighbors,
+                          int64_t* num_edges, int64_t* num_candidates,
+                          void* workspace, size_t workspace_bytes, void* stream);
+size_t e2a_radius_graph_fill_workspace_bytes(int64_t num_candidates);
+int e2a_radius_graph_fill(const float* pos, const float* pts, const int64_t* q_ptr, const int64_t* p_ptr,
+                          int64_t n_queries, int64_t n_points, int64_t n_systems,
+                          float max_dist, float min_dist, int64_t max_neighbors,
+                          int64_t num_edges, int64_t num_candidates,
+                          int64_t* query_idx, int64_t* neighbor_idx, int32_t* row_ptr, int32_t* col,
+                          float* edge_vec, float* dist, float* poly,
+                          void* workspace, size_t workspace_bytes,
+                          void* fill_workspace, size_t fill_workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Kernel-level sparse ops (same arithmetic as the reference's Triton kernels).                  */
+/* ------------------------------------------------------------------------------------------ */
+/* out[perm[p], h] = <q[i,h,:], k[col[p],h,:]> for p in row i of the query-CSR.  q:[N,H,D] k:[M,H,D] */
+int e2a_sparse_qk_fwd(const float* q, const float* k, const int32_t* row_ptr, const int32_t* col,
+                      const int32_t* perm, int64_t n_rows, int64_t n_edges, int H, int D,
+                      float* out, void* stream);
+/* out[r,h,:] = sum_{p in row r} alpha[perm[p],h] * x[col[p],h,:]   (dQ with the query-CSR and x=k, */
+/* dK with the key-CSR and x=q).  alpha:[E,H]  x:[*,H,D]  out:[n_rows,H,D]                         */
+int e2a_grouped_reduce(const float* alpha, const float* x, const int32_t* row_ptr, const int32_t* col,
+                       const int32_t* perm, int64_t n_rows, int H, int D, float* out, void* stream);
+/* out[i,h] = sum_{p in row i} alpha[perm[p],h] */
+int e2a_alpha_sum_fwd(const float* alpha, const int32_t* row_ptr, const int32_t* perm, int64_t n_rows,
+                      int H, float* out, void* stream);
+/* grad_alpha[e,h] = grad_out[query_idx[e],h] */
+int e2a_alpha_sum_bwd(const float* grad_out, const int32_t* query_idx, int64_t n_edges, int H,
+                      float* grad_alpha, void* stream);
+/* out[i,c,h] = sum_{p in row i} alpha[perm[p],h] * value[col[p],c,h].  value:[M,C,H] out:[N,C,H] */
+int e2a_v_agg_fwd(const float* value, const float* alpha, const int32_t* row_ptr, const int32_t* col,
+                  const int32_t* perm, int64_t n_rows, int C, int H, float* out, void* stream);
+/* d_alpha[perm[p],h] = sum_c dout[i,c,h] * value[col[p],c,h]  (query-CSR) */
+int e2a_v_agg_bwd_alpha(const float* dout, const float* value, const int32_t* row_ptr, const int32_t* col,
+                        const int32_t* perm, int64_t n_rows, int C, int H, float* d_alpha, void* stream);
+/* d_value[m,c,h] = sum_{p in key row m} alpha[perm[p],h] * dout[col[p],c,h]  (key-CSR) */
+int e2a_v_agg_bwd_value(const float* alpha, const float* dout, const int32_t* k_row_ptr,
+                        const int32_t* k_col, const int32_t* k_perm, int64_t n_keys, int C, int H,
+                        float* d_value, void* stream);
+/* out[i,l,h] = sum_{p in row i} sh[perm[p],l] * fea[perm[p],h].  sh:[E,L] fea:[E,F] out:[N,L,F] */
+int e2a_edge_outer_fwd(const float* sh, const float* fea, const int32_t* row_ptr, const int32_t* perm,
+                       int64_t n_rows, int L, int F, float* out, void* stream);
+/* d_sh[e,l] = sum_h go[q_e,l,h] fea[e,h];  d_fea[e,h] = sum_l go[q_e,l,h] sh[e,l] (either may be NULL) */
+int e2a_edge_outer_bwd(const float* grad_out, const float* sh, const float* fea, const int32_t* query_idx,
+                       int64_t n_edges, int L, int F, float* d_sh, float* d_fea, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Fused attention span of E2AttentionArbOrder_sparse (e2former.py:311-364, 393-422, and the    */
+/* sparse aggregation inside E2TensorProductSO2_FirstOrder, so2_tensor_product.py:370-377):      */
+/*   s  = <q_i, k_j>          (q already scaled by 1/sqrt(D))                                    */
+/*   a  = gate * s;  m_i = max_e a;  x = exp(a - m_i) * poly;  S_i = sum_e x                      */
+/*   beta = x * inputhead / (S_i + 1e-3) / max(dist, 1e-6)                                       */
+/*   out[i,c,h] = sum_e beta[e,h] * value[j,c,h]                                                 */
+/* Edges are in query-CSR order (row_ptr/col; edge id = CSR slot).  gate / inputhead point at    */
+/* [E,H] views with row stride ld_gi (the two halves of the radial-MLP output).  row_order (may  */
+/* be NULL) is a processing order of the rows (a spatially coherent order improves L2 reuse of   */
+/* the gathered value rows); results do not depend on it.  Saves beta [E,H], row_max and row_sum */
+/* [N,H] for the backward.  Requires D % 4 == 0, D/4 a power of two <= 32, H dividing 256,      */
+/* H % 4 == 0 and (C*H) % 4 == 0.                                                                */
+/* ------------------------------------------------------------------------------------------ */
+int e2a_attn_fwd(const float* q, const float* k, const float* value,
+                 const float* gate, const float* inputhead, int64_t ld_gi,
+                 const float* poly, const float* dist,
+                 const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
+                 int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                 float* out, float* beta, float* row_max, float* row_sum, void* stream);
+/* Query-side backward: given dout [N,C,H] produces d_q [N,H,D] (w.r.t. the scaled q), d_gate and */
+/* d_inputhead ([E,H] views with row stride ld_dgi), d_poly [E], d_dist [E] and d_logit [E,H]     */
+/* (= dL/ds, consumed by e2a_attn_bwd_key).  The gradient of the row max follows PyTorch's        */
+/* scatter_reduce(amax) rule: shared equally by the tied maxima.  Scratch: a workspace of        */
+/* e2a_attn_bwd_workspace_bytes(n_edges, H) bytes.                                               */
+size_t e2a_attn_bwd_workspace_bytes(int64_t n_edges, int H);
+int e2a_attn_bwd_query(const float* q, const float* k, const float* value,
+                       const float* gate, const float* inputhead, int64_t ld_gi,
+                       const float* poly, const float* dist,
+                       const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
+                       int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                       const float* beta, const float* row_max, const float* row_sum, const float* dout,
+                       float* d_q, float* d_gate, float* d_inputhead, int64_t ld_dgi,
+                       float* d_poly, float* d_dist, float* d_logit,
+                       void* workspace, size_t workspace_bytes, void* stream);
+/* Key-side backward over the key-CSR (k_row_ptr, k_col = query of each slot, k_perm = edge id):  */
+/* d_value[j,c,h] = sum_e beta[e,h] dout[i_e,c,h];  d_k[j,h,:] = sum_e d_logit[e,h] q[i_e,h,:].    */
+int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const float* d_logit,
+                     const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm,
+                     int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                     float* d_k, float* d_value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* E2A_H */

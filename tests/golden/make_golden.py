@@ -1,0 +1,266 @@
+"""Generate the golden fixtures under ``tests/golden/`` by running the REFERENCE code on CPU.
+
+TEST INFRASTRUCTURE ONLY.  Run in a container where the reference sources are mounted
+(default ``/root/reference``; override with ``E2A_REFERENCE_ROOT``)::
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own modules through ``refshim`` (stand-ins for the missing third-party
+packages) and records, as compressed ``.npz`` files:
+
+* ``graph_*.npz`` -- ``CellExpander.expand_includeself`` (module_utils.py:1065-1275) and
+  ``construct_radius_neighbor`` (module_utils.py:3119-3242) outputs: expanded positions, image
+  -> atom map, edge lists, distances, edge vectors, envelope values and the CSR metadata of
+  ``prepare_sparse_qk_edge_index_metadata`` (triton_sparse_qk_autograd.py:635-652).
+* ``layer_*.npz`` -- ``E2AttentionArbOrder_sparse.forward`` (e2former.py:223-436) with
+  ``tp_type="QK_alpha"`` / ``attn_type="so2-first-order"`` on seeded inputs and seeded weights
+  (:func:`ubio_molfm_b200.synthetic.seeded_params_`), plus the gradients of ``<out, dOut>`` with
+  respect to every floating-point input, for a seeded ``dOut``.
+* ``so2_pin.json`` -- the reference's own identity check ``test_so2_o1`` (so2_tensor_product.py:
+  392-478), restated with the current ``eulers_to_wigner`` return convention: the node-decomposed
+  first-order TP equals the per-edge rotated TP.
+
+Weights are not stored: tests regenerate them with the same seeded function.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+import refshim  # noqa: E402
+from ubio_molfm_b200 import synthetic  # noqa: E402
+
+torch.set_default_dtype(torch.float32)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def reference_graph(mods, pos, Z, cell, pbc, cutoff, max_neighbors, batch_sizes=None):
+    """Run the reference PBC expansion + dense radius graph. ``pos`` is [B,L,3] padded."""
+    mu = mods["mu"]
+    qkmod = mods["qk"]
+    pos = torch.as_tensor(pos, dtype=torch.float32)
+    B, L = pos.shape[:2]
+    Z = torch.as_tensor(Z, dtype=torch.long)
+    node_mask = Z != 0
+    padding_mask = ~node_mask
+    pos = torch.where(padding_mask.unsqueeze(-1).repeat(1, 1, 3), 999.0, pos)
+    cell = torch.as_tensor(cell, dtype=torch.float32)
+    pbc_t = torch.as_tensor(pbc, dtype=torch.bool)
+    if bool(pbc_t.any()):
+        ce = mu.CellExpander(cutoff, 512, 4)
+        ex = ce.expand_includeself(pos, pbc_t, Z, cell, neighbors_radius=(None, cutoff),
+                                   use_grad=False, padding_mask=padding_mask)
+    else:
+        ex = {"expand_node_pos": pos, "outcell_index": torch.arange(L).unsqueeze(0).repeat(B, 1),
+              "expand_node_mask": node_mask}
+    exp_pos = ex["expand_node_pos"].masked_fill(~ex["expand_node_mask"].unsqueeze(-1), 999)
+    ptr = torch.nn.functional.pad(node_mask.sum(-1).to(torch.int32).cumsum(0), (1, 0))
+    f_exp_node_pos = exp_pos[ex["expand_node_mask"]]
+    f_outcell_index = (ex["outcell_index"] + ptr[:B, None])[ex["expand_node_mask"]]
+    nb = mu.construct_radius_neighbor(pos, node_mask, exp_pos, ex["expand_node_mask"],
+                                      max_dist=cutoff, min_dist=1e-4, max_neighbors=max_neighbors)
+    md = nb["metadata"]
+    return {
+        "pos": _np(pos[node_mask]),
+        "Z": _np(Z[node_mask]),
+        "batch_ptr": _np(ptr),
+        "exp_ptr": _np(torch.nn.functional.pad(ex["expand_node_mask"].sum(-1).cumsum(0), (1, 0))),
+        "f_exp_node_pos": _np(f_exp_node_pos),
+        "f_outcell_index": _np(f_outcell_index),
+        "query_idx": _np(nb["query_idx"]).astype(np.int64),
+        "neighbor_idx": _np(nb["neighbor_idx"]).astype(np.int64),
+        "f_edge_vec": _np(nb["f_edge_vec"]),
+        "f_dist": _np(nb["f_dist"]),
+        "f_poly_dist": _np(nb["f_poly_dist"]),
+        **{f"md{i}": _np(m) for i, m in enumerate(md)},
+    }
+
+
+def pad_systems(systems):
+    """List of (pos, Z) -> padded [B,L,3], [B,L] with Z=0 padding."""
+    B = len(systems)
+    L = max(len(z) for _, z in systems)
+    P = np.zeros((B, L, 3), np.float32)
+    ZZ = np.zeros((B, L), np.int64)
+    for b, (p, z) in enumerate(systems):
+        P[b, : len(z)] = p
+        ZZ[b, : len(z)] = z
+    return P, ZZ
+
+
+def graph_cases(mods):
+    cases = {}
+    # 648-atom water box (the CPU plumbing workload), cutoff 5.0, no neighbour cap.
+    pos, Z, cell = synthetic.water_box(seed=0)
+    cases["graph_water648"] = reference_graph(mods, pos[None], Z[None], cell[None],
+                                              [[True, True, True]], 5.0, None)
+    # 1,500-atom biomolecular box, cutoff 4.5, max_neighbors 32 (the full-backbone workload).
+    pos, Z, cell = synthetic.bio_box(1500, seed=1)
+    cases["graph_bio1500"] = reference_graph(mods, pos[None], Z[None], cell[None],
+                                             [[True, True, True]], 4.5, 32)
+    # Small periodic box where cutoff > half the box (many images per atom, exact ties possible).
+    rng = np.random.default_rng(2)
+    pos = rng.uniform(0, 7.0, size=(40, 3))
+    Z = rng.choice([1, 6, 8], size=40)
+    cases["graph_smallpbc40"] = reference_graph(mods, pos[None], Z[None], (np.eye(3) * 7.0)[None],
+                                                [[True, True, True]], 5.0, None)
+    # Triclinic cell, mixed pbc (periodic in x,y only).
+    cellt = np.array([[9.0, 0.0, 0.0], [2.5, 8.0, 0.0], [1.0, 1.5, 10.0]])
+    frac = rng.uniform(0, 1, size=(60, 3))
+    pos = frac @ cellt
+    Z = rng.choice([1, 6, 7, 8], size=60)
+    cases["graph_triclinic60"] = reference_graph(mods, pos[None], Z[None], cellt[None],
+                                                 [[True, True, False]], 5.0, 24)
+    # Batch of three non-periodic molecules with a neighbour cap (top-K truncation).
+    mols = synthetic.molecule_batch(3, 10, 30, seed=3)
+    P, ZZ = pad_systems([(m[0], m[1]) for m in mols])
+    cases["graph_mol3"] = reference_graph(mods, P, ZZ, np.zeros((3, 3, 3)), [[False] * 3] * 3, 4.0, 8)
+    # Lattice with exact distance ties (simple cubic, spacing 2.0, cutoff 4.1, cap 10).
+    g = np.arange(4) * 2.0
+    pos = np.stack(np.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3)
+    Z = np.full(len(pos), 6)
+    cases["graph_lattice64"] = reference_graph(mods, pos[None], Z[None], (np.eye(3) * 8.0)[None],
+                                               [[True, True, True]], 4.1, 10)
+    return cases
+
+
+def layer_case(mods, name, C, H, D, head_irreps, nb, cutoff, pos, Z, cell, pbc, max_neighbors, seed):
+    mu, e2f = mods["mu"], mods["e2f"]
+    g = reference_graph(mods, pos[None], Z[None], cell[None], [pbc], cutoff, max_neighbors)
+    irreps = f"{C}x0e+{C}x1e+{C}x2e"
+    layer = e2f.E2AttentionArbOrder_sparse(
+        irreps, nb, num_attn_heads=H, attn_scalar_head=D, irreps_head=head_irreps,
+        alpha_drop=0.0, tp_type="QK_alpha", attn_type="so2-first-order", atom_type_cnt=256)
+    layer.eval()
+    synthetic.seeded_params_(layer, seed)
+    l3_seq = layer.first_order_tp.so2_tp.l3_sequential
+    Jd = [j.double() for j in torch.load(os.path.join(refshim.E2F_DIR, "Jd.pt"))]
+
+    pos_t = torch.tensor(g["pos"])
+    exp_t = torch.tensor(g["f_exp_node_pos"])
+    W, Wi = mu.eulers_to_wigner(mu.init_edge_rot_euler_angles(pos_t.double(), training=False), 0, 2, Jd, l3_seq)
+    if any(pbc):
+        We, Wie = mu.eulers_to_wigner(mu.init_edge_rot_euler_angles(exp_t.double(), training=False), 0, 2, Jd, l3_seq)
+    else:
+        We, Wie = W, Wi
+    rbf = mu.GaussianSmearing(nb, cutoff=cutoff, basis_width_scalar=2)
+
+    gen = torch.Generator().manual_seed(seed + 17)
+    N = pos_t.shape[0]
+    x = torch.randn((N, 9, C), generator=gen)
+    leaves = {
+        "node_pos": pos_t.clone(),
+        "node_irreps_input": x,
+        "edge_dis": torch.tensor(g["f_dist"]),
+        "poly_dist": torch.tensor(g["f_poly_dist"]),
+        "f_exp_node_pos": exp_t.clone(),
+        "wigner": W.float(), "wigner_inv": Wi.float(),
+        "wigner_exp": We.float(), "wigner_inv_exp": Wie.float(),
+    }
+    leaves["attn_weight"] = rbf(leaves["edge_dis"]).detach()
+    for v in leaves.values():
+        v.requires_grad_(True)
+    qi = torch.tensor(g["query_idx"])
+    ni = torch.tensor(g["neighbor_idx"])
+    md = tuple(torch.tensor(g[f"md{i}"]) for i in range(6))
+    bd = {"query_idx": qi, "neighbor_idx": ni, "metadata": md,
+          "f_outcell_index": torch.tensor(g["f_outcell_index"]),
+          "f_exp_node_pos": leaves["f_exp_node_pos"],
+          "wigner": leaves["wigner"], "wigner_inv": leaves["wigner_inv"],
+          "wigner_exp": leaves["wigner_exp"], "wigner_inv_exp": leaves["wigner_inv_exp"]}
+    out, _ = layer(node_pos=leaves["node_pos"], node_irreps_input=leaves["node_irreps_input"],
+                   edge_dis=leaves["edge_dis"], edge_vec=torch.tensor(g["f_edge_vec"]),
+                   attn_weight=leaves["attn_weight"], atomic_numbers=torch.tensor(g["Z"]),
+                   poly_dist=leaves["poly_dist"], batched_data=bd)
+    dout = torch.randn(out.shape, generator=gen)
+    grads = torch.autograd.grad(out, list(leaves.values()), dout, allow_unused=True)
+    rec = dict(g)
+    rec.update({
+        "cfg": np.array(json.dumps(dict(C=C, H=H, D=D, head_irreps=head_irreps, nb=nb, cutoff=cutoff,
+                                        seed=seed, pbc=list(pbc), max_neighbors=max_neighbors))),
+        "out": _np(out), "dout": _np(dout),
+    })
+    for (k, v), gr in zip(leaves.items(), grads):
+        rec[f"in_{k}"] = _np(v)
+        rec[f"grad_{k}"] = np.zeros(v.shape, np.float32) if gr is None else _np(gr)
+    return rec
+
+
+def layer_cases(mods):
+    cases = {}
+    rng = np.random.default_rng(5)
+    pos = rng.uniform(0, 7.5, size=(36, 3))
+    Z = rng.choice([1, 6, 7, 8], size=36)
+    cases["layer_small_pbc"] = layer_case(mods, "small", 32, 8, 8, "4x0e+4x1e+4x2e", 32, 5.0,
+                                          pos, Z, np.eye(3) * 7.5, [True, True, True], None, seed=11)
+    mols = synthetic.molecule_batch(1, 24, 24, seed=6)
+    cases["layer_full_mol24"] = layer_case(mods, "full", 256, 128, 8, "2x0e+2x1e+2x2e", 256, 6.0,
+                                           mols[0][0], mols[0][1], np.zeros((3, 3)), [False] * 3, None,
+                                           seed=12)
+    return cases
+
+
+def so2_pin(mods):
+    mu, so2tp = mods["mu"], mods["so2tp"]
+    torch.manual_seed(0)
+    C = 16
+    tp = so2tp.SO2_TP_givenl2(l1_list=range(3), l2=1, l3_legal=range(3), in_c=C, out_c=C,
+                              with_linear=True).double()
+    Jd = [j.double() for j in torch.load(os.path.join(refshim.E2F_DIR, "Jd.pt"))]
+    N = 10
+    pos = torch.randn(N, 3, dtype=torch.float64)
+    h = torch.randn(N, 9, C, dtype=torch.float64)
+    alpha = torch.randn(N, N, C, dtype=torch.float64)
+    eye = torch.eye(N).bool()
+    alpha[eye] = 0
+    r = torch.norm(pos[:, None] - pos[None], dim=-1, keepdim=True)
+    r[eye] = 1
+    adr = alpha / r
+    W, Wi = mu.eulers_to_wigner(mu.init_edge_rot_euler_angles(pos, training=False), 0, 2, Jd, tp.l3_sequential)
+    nrm = pos.norm(dim=-1).reshape(-1, 1, 1)
+    hb = torch.bmm(Wi, tp(torch.bmm(W, h), with_linear=False) * nrm)
+    hb = (hb[None] * adr.reshape(N, N, 1, C)).sum(1)
+    ha = (h[None] * adr.reshape(N, N, 1, C)).sum(1)
+    ha = torch.bmm(Wi, tp(torch.bmm(W, ha), with_linear=False) * nrm)
+    out1 = tp.forward_linear(ha - hb)
+    ev = pos[:, None] - pos[None]
+    ev[eye] = torch.tensor([0.0, 1e-3, 0.0], dtype=torch.float64)
+    ev = (ev / ev.norm(dim=-1, keepdim=True)).reshape(-1, 3)
+    We, Wie = mu.eulers_to_wigner(mu.init_edge_rot_euler_angles(ev, training=False), 0, 2, Jd, tp.l3_sequential)
+    hij = h[None].repeat(N, 1, 1, 1).reshape(N * N, 9, C)
+    hij = torch.bmm(Wie, tp(torch.bmm(We, hij), with_linear=False)).reshape(N, N, -1, C)
+    out2 = tp.forward_linear((hij * alpha.reshape(N, N, 1, C)).sum(1))
+    return {
+        "max_abs_diff": float((out1 - out2).abs().max()),
+        "selected_idx": tp.selected_idx.tolist(),
+        "CG_weight": [float(v) for v in tp.CG_weight.double()],
+        "l3_sequential": [list(x) for x in tp.l3_sequential],
+    }
+
+
+def main():
+    mods = refshim.load_reference()
+    pin = so2_pin(mods)
+    assert pin["max_abs_diff"] < 1e-5, pin
+    with open(os.path.join(HERE, "so2_pin.json"), "w") as f:
+        json.dump(pin, f, indent=1)
+    print("so2 pin", pin["max_abs_diff"])
+    for name, rec in {**graph_cases(mods), **layer_cases(mods)}.items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
+        print(name, "E=", len(rec["query_idx"]), "N=", len(rec["pos"]), "N2=", len(rec["f_exp_node_pos"]))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,330 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle and the reference's golden vectors."""
+import numpy as np
+import pytest
+import torch
+
+from golden_io import LEAVES, build_product_layer, layer_cfg, layer_inputs, load
+from oracle import attention_ref as R
+from oracle import graph_ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+GRAPH_CASES = {
+    "graph_water648": (5.0, None, [True, True, True], np.eye(3) * 18.64),
+    "graph_bio1500": (4.5, 32, [True, True, True], None),
+    "graph_smallpbc40": (5.0, None, [True, True, True], np.eye(3) * 7.0),
+    "graph_triclinic60": (5.0, 24, [True, True, False],
+                          np.array([[9.0, 0.0, 0.0], [2.5, 8.0, 0.0], [1.0, 1.5, 10.0]])),
+    "graph_mol3": (4.0, 8, [False, False, False], None),
+    "graph_lattice64": (4.1, 10, [True, True, True], np.eye(3) * 8.0),
+}
+
+
+def _t(a, dtype=None):
+    return torch.as_tensor(np.asarray(a), device=DEV, dtype=dtype)
+
+
+# ------------------------------------------------------------------------------------------------
+# graph
+# ------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", sorted(GRAPH_CASES))
+def test_csr_metadata_bit_exact(name):
+    from ubio_molfm_b200.ops import prepare_sparse_qk_edge_index_metadata
+
+    g = load(name)
+    md = prepare_sparse_qk_edge_index_metadata(_t(g["query_idx"]), _t(g["neighbor_idx"]), len(g["pos"]),
+                                               len(g["f_exp_node_pos"]))
+    for i in range(6):
+        assert np.array_equal(md[i].cpu().numpy(), g[f"md{i}"].astype(np.int32)), i
+
+
+def test_csr_metadata_unsorted_queries():
+    from ubio_molfm_b200.ops import prepare_sparse_qk_edge_index_metadata
+
+    rng = np.random.default_rng(0)
+    q = rng.integers(0, 50, 3000)
+    n = rng.integers(0, 70, 3000)
+    md = [m.cpu().numpy() for m in prepare_sparse_qk_edge_index_metadata(_t(q), _t(n), 50, 70)]
+    perm = np.argsort(q, kind="stable")
+    assert np.array_equal(md[2], perm)
+    assert np.array_equal(md[1], n[perm])
+    assert np.array_equal(md[0], np.concatenate([[0], np.cumsum(np.bincount(q, minlength=50))]))
+    kp = np.argsort(n, kind="stable")
+    assert np.array_equal(md[5], kp)
+    assert np.array_equal(md[4], q[kp])
+
+
+def test_csr_rejects_out_of_range():
+    from ubio_molfm_b200._lib import E2AError
+    from ubio_molfm_b200.ops import prepare_sparse_qk_edge_index_metadata
+
+    with pytest.raises(E2AError):
+        prepare_sparse_qk_edge_index_metadata(_t([0, 1, 5]), _t([0, 0, 0]), 3, 1)
+
+
+@pytest.mark.parametrize("name", ["graph_water648", "graph_smallpbc40", "graph_triclinic60", "graph_lattice64"])
+def test_pbc_expand_bit_exact(name):
+    from ubio_molfm_b200.graph import expand_pbc
+
+    g = load(name)
+    cutoff, _, pbc, cell = GRAPH_CASES[name]
+    exp_pos, outcell, _ = expand_pbc(_t(g["pos"]), cell, pbc, cutoff)
+    assert np.array_equal(outcell.cpu().numpy(), g["f_outcell_index"])
+    assert np.array_equal(exp_pos.cpu().numpy(), g["f_exp_node_pos"])
+
+
+def _check_graph(q, n, d, qr, nr, dr, allow_tie_subset=False):
+    assert np.array_equal(q, qr)
+    assert np.array_equal(d, dr)
+    if allow_tie_subset:
+        return
+    k1, k2 = np.lexsort((n, d, q)), np.lexsort((nr, dr, qr))
+    assert np.array_equal(n[k1], nr[k2])
+    ties = np.zeros(len(q), bool)
+    same = (q[1:] == q[:-1]) & (d[1:] == d[:-1])
+    ties[1:] |= same
+    ties[:-1] |= same
+    assert np.array_equal(n[~ties], nr[~ties])
+
+
+@pytest.mark.parametrize("name", sorted(GRAPH_CASES))
+def test_radius_graph_matches_reference(name):
+    from ubio_molfm_b200.graph import radius_graph
+
+    g = load(name)
+    cutoff, maxnb, _, _ = GRAPH_CASES[name]
+    out = radius_graph(_t(g["pos"]), _t(g["f_exp_node_pos"]), g["batch_ptr"], g["exp_ptr"], cutoff, 1e-4, maxnb)
+    q, n = out["query_idx"].cpu().numpy(), out["neighbor_idx"].cpu().numpy()
+    d = out["f_dist"].detach().cpu().numpy()
+    _check_graph(q, n, d, g["query_idx"], g["neighbor_idx"], g["f_dist"], allow_tie_subset=name == "graph_lattice64")
+    # the GPU itself is a (distance, index) order: identical to the oracle's sequence everywhere
+    qo, no, do = graph_ref.radius_graph(g["pos"], g["f_exp_node_pos"], g["batch_ptr"], g["exp_ptr"], cutoff, 1e-4,
+                                        maxnb)
+    assert np.array_equal(q, qo) and np.array_equal(n, no) and np.array_equal(d, do)
+    assert np.array_equal(out["f_edge_vec"].detach().cpu().numpy(), g["f_edge_vec"]) or name == "graph_lattice64"
+    np.testing.assert_allclose(out["f_poly_dist"].detach().cpu().numpy(), g["f_poly_dist"], atol=2e-6)
+
+
+@pytest.mark.parametrize("n_atoms,k", [(10000, 32), (100000, 32)])
+def test_radius_graph_large_vs_c_oracle(n_atoms, k):
+    from ubio_molfm_b200.graph import expand_pbc, radius_graph, pbc_image_offsets
+    from ubio_molfm_b200.synthetic import uniform_box
+
+    pos, Z, cell = uniform_box(n_atoms, k, 6.0, seed=3)
+    pos32 = pos.astype(np.float32)
+    exp_pos, outcell, image = expand_pbc(_t(pos32), cell, [True] * 3, 6.0)
+    off = pbc_image_offsets(cell, [True] * 3, 6.0).numpy()
+    ia = graph_ref.pbc_expand(pos32, off, 6.0) if n_atoms <= 10000 else None
+    if ia is not None:
+        assert np.array_equal((image * n_atoms + outcell).cpu().numpy(), ia)
+    ep = exp_pos.cpu().numpy()
+    out = radius_graph(_t(pos32), exp_pos, [0, n_atoms], [0, len(ep)], 6.0, 1e-4, None)
+    qo, no, do = graph_ref.radius_graph(pos32, ep, [0, n_atoms], [0, len(ep)], 6.0, 1e-4, None)
+    assert np.array_equal(out["query_idx"].cpu().numpy(), qo)
+    assert np.array_equal(out["neighbor_idx"].cpu().numpy(), no)
+    assert np.array_equal(out["f_dist"].detach().cpu().numpy(), do)
+    assert abs(len(qo) / n_atoms - k) < 0.1 * k
+
+
+def test_radius_graph_max_neighbors_and_self_distance():
+    from ubio_molfm_b200.graph import radius_graph
+
+    rng = np.random.default_rng(1)
+    pos = rng.uniform(0, 6, (300, 3)).astype(np.float32)
+    for maxnb in (1, 5, 17):
+        out = radius_graph(_t(pos), _t(pos), [0, 300], [0, 300], 3.0, -1.0, maxnb)
+        qo, no, do = graph_ref.radius_graph(pos, pos, [0, 300], [0, 300], 3.0, -1.0, maxnb)
+        assert np.array_equal(out["neighbor_idx"].cpu().numpy(), no)
+        # min_dist=-1 keeps the self edge (distance 0) first in every row
+        first = np.searchsorted(qo, np.arange(300))
+        assert np.all(no[first] == np.arange(300))
+
+
+def test_radius_graph_empty_and_isolated():
+    from ubio_molfm_b200.graph import radius_graph
+
+    pos = np.array([[0, 0, 0], [100, 0, 0], [0.5, 0, 0]], np.float32)
+    out = radius_graph(_t(pos), _t(pos), [0, 3], [0, 3], 1.0, 1e-4, None)
+    assert out["query_idx"].cpu().tolist() == [0, 2]
+    assert out["neighbor_idx"].cpu().tolist() == [2, 0]
+    out = radius_graph(_t(pos), _t(pos), [0, 3], [0, 3], 0.1, 1e-4, None)
+    assert out["query_idx"].numel() == 0
+
+
+# ------------------------------------------------------------------------------------------------
+# kernel-level ops
+# ------------------------------------------------------------------------------------------------
+def _random_graph(N, M, E, seed, sort=True):
+    rng = np.random.default_rng(seed)
+    q = rng.integers(0, N, E)
+    if sort:
+        q = np.sort(q)
+    n = rng.integers(0, M, E)
+    return q, n
+
+
+@pytest.mark.parametrize("sort", [True, False])
+def test_kernel_ops_match_torch_fallbacks(sort):
+    from ubio_molfm_b200 import ops
+
+    N, M, E, H, D, C = 40, 55, 900, 8, 8, 12
+    q, n = _random_graph(N, M, E, 2, sort)
+    g = torch.Generator().manual_seed(0)
+    Q = torch.randn(N, H, D, generator=g, dtype=torch.float32)
+    K = torch.randn(M, H, D, generator=g)
+    V = torch.randn(M, C, H, generator=g)
+    A = torch.randn(E, H, generator=g)
+    SH = torch.randn(E, 5, generator=g)
+    FE = torch.randn(E, 16, generator=g)
+    qt, nt = _t(q), _t(n)
+    md = ops.prepare_sparse_qk_edge_index_metadata(qt, nt, N, M)
+    cases = [
+        (lambda a, b: ops.sparse_qk_edge_index_triton(a, b, qt, nt, md),
+         lambda a, b: R.sparse_qk(a, b, torch.tensor(q), torch.tensor(n)), (Q, K)),
+        (lambda v, a: ops.sparse_v_agg_edge_index_triton_cblocked(v, a, qt, nt, N, md),
+         lambda v, a: R.v_agg(v, a, torch.tensor(q), torch.tensor(n), N), (V, A)),
+        (lambda a: ops.sparse_alpha_sum_edge_index_triton(a, qt, N, (md[0], md[2])),
+         lambda a: R.alpha_sum(a, torch.tensor(q), N), (A,)),
+        (lambda s, f: ops.edge_degree_outer_triton(s, f, qt, N, None),
+         lambda s, f: R.edge_outer(s, f, torch.tensor(q), N), (SH, FE)),
+    ]
+    for fg, fr, args in cases:
+        ag = [a.to(DEV).requires_grad_(True) for a in args]
+        ar = [a.clone().requires_grad_(True) for a in args]
+        og, orf = fg(*ag), fr(*ar)
+        torch.testing.assert_close(og.cpu(), orf, atol=1e-5, rtol=1e-5)
+        w = torch.randn(orf.shape, generator=g)
+        gg = torch.autograd.grad(og, ag, w.to(DEV))
+        gr = torch.autograd.grad(orf, ar, w)
+        for a, b in zip(gg, gr):
+            torch.testing.assert_close(a.cpu(), b, atol=1e-4, rtol=1e-5)
+
+
+def test_kernel_ops_errors():
+    from ubio_molfm_b200 import ops
+
+    with pytest.raises(ValueError):
+        ops.sparse_v_agg_edge_index_triton_cblocked(torch.zeros(3, 4, device=DEV), torch.zeros(2, 4, device=DEV),
+                                                    _t([0, 1]), _t([0, 1]), 2, None)
+    with pytest.raises(ValueError):
+        ops.sparse_qk_edge_index_triton(torch.zeros(3, 4, 8, device=DEV), torch.zeros(3, 4, 8, device=DEV),
+                                        _t([0]), _t([0]), metadata=(1, 2, 3))
+    with pytest.raises(ValueError):
+        ops.sparse_qk_edge_index_triton(torch.zeros(3, 4, 8), torch.zeros(3, 4, 8), _t([0]), _t([0]))
+
+
+# ------------------------------------------------------------------------------------------------
+# fused attention span
+# ------------------------------------------------------------------------------------------------
+def _span_inputs(N, M, q, n, H, D, C, seed, gate_zero=False):
+    g = torch.Generator().manual_seed(seed)
+    E = len(q)
+    Q = torch.randn(N, H, D, generator=g) / D ** 0.5
+    K = torch.randn(M, H, D, generator=g)
+    V = torch.randn(M, C, H, generator=g)
+    G = torch.randn(E, 2 * H, generator=g)
+    if gate_zero:
+        G[:, :H] = 0.0
+    P = torch.rand(E, generator=g)
+    Dd = 1.0 + 4 * torch.rand(E, generator=g)
+    return [Q, K, V, G, P, Dd]
+
+
+def _span_parity(N, M, q, n, H, D, C, seed, gate_zero=False, row_order=None):
+    from ubio_molfm_b200 import ops
+
+    ins = _span_inputs(N, M, q, n, H, D, C, seed, gate_zero)
+    qt, nt = _t(q), _t(n)
+    md = ops.prepare_sparse_qk_edge_index_metadata(qt, nt, N, M)
+    ag = [a.to(DEV).requires_grad_(True) for a in ins]
+    ar = [a.clone().double().requires_grad_(True) for a in ins]
+    og = ops.attention_span(*ag, md, row_order)
+    orf = R.attention_span(*ar, torch.tensor(q), torch.tensor(n), N)
+    scale = orf.abs().max().item()
+    assert (og.cpu().double() - orf).abs().max().item() <= 2e-5 * max(scale, 1.0)
+    w = torch.randn(orf.shape, generator=torch.Generator().manual_seed(seed + 1))
+    gg = torch.autograd.grad(og, ag, w.to(DEV))
+    gr = torch.autograd.grad(orf, ar, w.double())
+    for name, a, b in zip(["q", "k", "v", "gate", "poly", "dist"], gg, gr):
+        tol = 5e-5 * max(b.abs().max().item(), 1.0)
+        assert (a.cpu().double() - b).abs().max().item() <= tol, name
+    return og
+
+
+@pytest.mark.parametrize("H,D,C", [(8, 8, 116), (128, 8, 58), (16, 4, 20), (32, 16, 7)])
+def test_attention_span_random_graphs(H, D, C):
+    N, M, E = 60, 90, 1500
+    q, n = _random_graph(N, M, E, H + C)
+    _span_parity(N, M, q, n, H, D, C, seed=H)
+
+
+def test_attention_span_ties_and_empty_rows():
+    # gate = 0 makes every logit of a row equal: the max gradient is shared among all of them
+    N, M = 30, 40
+    q = np.sort(np.random.default_rng(4).integers(0, N - 5, 400))  # the last 5 rows have no edges
+    n = np.random.default_rng(5).integers(0, M, 400)
+    out = _span_parity(N, M, q, n, 8, 8, 16, seed=9, gate_zero=True)
+    assert torch.all(out[N - 5:] == 0)
+
+
+def test_attention_span_row_order_and_determinism():
+    from ubio_molfm_b200 import ops
+
+    N, M, E, H, D, C = 200, 260, 6000, 128, 8, 58
+    q, n = _random_graph(N, M, E, 11)
+    order = _t(np.random.default_rng(3).permutation(N).astype(np.int32))
+    ins = [a.to(DEV) for a in _span_inputs(N, M, q, n, H, D, C, 12)]
+    md = ops.prepare_sparse_qk_edge_index_metadata(_t(q), _t(n), N, M)
+    outs = []
+    for ro in (None, order, order):
+        a = [x.clone().requires_grad_(True) for x in ins]
+        o = ops.attention_span(*a, md, ro)
+        gr = torch.autograd.grad(o, a, torch.ones_like(o))
+        outs.append([o] + list(gr))
+    for x, y in zip(outs[1], outs[2]):
+        assert torch.equal(x, y)  # bitwise reproducible
+    for x, y in zip(outs[0], outs[1]):
+        assert torch.equal(x, y)  # independent of the processing order
+
+
+# ------------------------------------------------------------------------------------------------
+# full layer against the reference's golden vectors
+# ------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["layer_small_pbc", "layer_full_mol24"])
+def test_layer_matches_reference_golden(name):
+    rec = load(name)
+    cfg = layer_cfg(rec)
+    layer = build_product_layer(cfg, DEV)
+    leaves, bd, Z = layer_inputs(rec, DEV)
+    out, _ = layer(node_pos=leaves["node_pos"], node_irreps_input=leaves["node_irreps_input"],
+                   edge_dis=leaves["edge_dis"], edge_vec=None, attn_weight=leaves["attn_weight"], atomic_numbers=Z,
+                   poly_dist=leaves["poly_dist"], batched_data=bd)
+    ref = torch.tensor(rec["out"])
+    assert (out.detach().cpu() - ref).abs().max().item() <= 1e-4 * max(ref.abs().max().item(), 1.0)
+    grads = torch.autograd.grad(out, [leaves[k] for k in LEAVES], torch.tensor(rec["dout"], device=DEV),
+                                allow_unused=True)
+    for k, gd in zip(LEAVES, grads):
+        gref = torch.tensor(rec[f"grad_{k}"])
+        gd = torch.zeros_like(gref) if gd is None else gd.cpu()
+        assert (gd - gref).abs().max().item() <= 1e-4 * max(gref.abs().max().item(), 1.0), k
+
+
+def test_layer_unsorted_edges_equal_sorted():
+    rec = load("layer_small_pbc")
+    cfg = layer_cfg(rec)
+    layer = build_product_layer(cfg, DEV)
+    leaves, bd, Z = layer_inputs(rec, DEV, requires_grad=False)
+    kw = dict(node_pos=leaves["node_pos"], node_irreps_input=leaves["node_irreps_input"], edge_vec=None,
+              atomic_numbers=Z)
+    out1, _ = layer(edge_dis=leaves["edge_dis"], attn_weight=leaves["attn_weight"], poly_dist=leaves["poly_dist"],
+                    batched_data=dict(bd), **kw)
+    perm = torch.randperm(len(rec["query_idx"]), generator=torch.Generator().manual_seed(0)).to(DEV)
+    from ubio_molfm_b200.ops import prepare_sparse_qk_edge_index_metadata
+    bd2 = dict(bd)
+    bd2["query_idx"], bd2["neighbor_idx"] = bd["query_idx"][perm], bd["neighbor_idx"][perm]
+    bd2["metadata"] = prepare_sparse_qk_edge_index_metadata(bd2["query_idx"], bd2["neighbor_idx"], len(rec["pos"]),
+                                                            len(rec["f_exp_node_pos"]))
+    out2, _ = layer(edge_dis=leaves["edge_dis"][perm], attn_weight=leaves["attn_weight"][perm],
+                    poly_dist=leaves["poly_dist"][perm], batched_data=bd2, **kw)
+    torch.testing.assert_close(out1, out2, atol=1e-5, rtol=1e-5)

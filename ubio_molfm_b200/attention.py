@@ -1,0 +1,126 @@
+"""``E2AttentionArbOrder_sparse`` -- drop-in for the reference attention layer (e2former.py:80-436).
+
+Same constructor arguments, parameter names (``state_dict`` keys) and ``forward`` signature as the
+reference with ``tp_type="QK_alpha"`` (``"+triton"`` accepted and ignored) and
+``attn_type="so2-first-order"`` / ``"first-order"``.  Per layer:
+
+* node side (dense, cuBLAS): Q/K ``SO3_Linear2Scalar``, ``proj_value``, the two node-local halves
+  of the first-order SO(2) tensor product with the per-node Wigner matrices, ``forward_linear``,
+  ``proj_first``;
+* edge side: the radial MLP ``fc_easy`` with its first layer decomposed exactly into an RBF part
+  and per-element tables (no ``[E, nb+256]`` concatenation), then ONE fused CUDA kernel for
+  QK logits -> gated segmented softmax -> alpha/r -> value aggregation (and two for its backward),
+  which never materialises per-edge value tensors.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+
+from .nn import (E2TensorProductSO2_FirstOrder, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
+                 irreps_channels_lmax, parse_irreps)
+from .ops import attention_span
+
+
+class E2AttentionArbOrder_sparse(nn.Module):
+    def __init__(self, irreps_node_input="256x0e+256x1e+256x2e", attn_weight_input_dim: int = 32,
+                 num_attn_heads: int = 8, attn_scalar_head: int = 32, irreps_head="32x0e+32x1e+32x2e",
+                 alpha_drop=0.1, tp_type="QK_alpha", attn_type="first-order", atom_type_cnt=256,
+                 norm_layer="identity", **kwargs):
+        super().__init__()
+        base_tp = tp_type.split("+")[0]
+        if base_tp != "QK_alpha" or "softplus" in tp_type or "sigmoid" in tp_type:
+            raise NotImplementedError(f"tp_type={tp_type!r}: only the default QK_alpha attention is built")
+        if attn_type not in ("first-order", "so2-first-order"):
+            raise NotImplementedError(f"attn_type={attn_type!r}: only the first-order SO(2) attention is built")
+        self.tp_type = base_tp
+        self.attn_type = attn_type
+        self.atom_type_cnt = atom_type_cnt
+        C, lmax = irreps_channels_lmax(irreps_node_input)
+        if lmax != 2 or any(m != C for m, _, _ in parse_irreps(irreps_node_input)):
+            raise NotImplementedError("node irreps must be Cx0e+Cx1e+Cx2e")
+        self.scalar_dim = C
+        self.lmax = lmax
+        self.num_attn_heads = num_attn_heads
+        self.attn_scalar_head = attn_scalar_head
+        self.attn_weight_input_dim = attn_weight_input_dim
+        head_mul = parse_irreps(irreps_head)[0][0]
+        self.node_embed_dim = 128
+        self.alpha_drop = alpha_drop
+        self.source_embedding = nn.Embedding(atom_type_cnt, self.node_embed_dim)
+        self.target_embedding = nn.Embedding(atom_type_cnt, self.node_embed_dim)
+        nn.init.uniform_(self.source_embedding.weight.data, -0.001, 0.001)
+        nn.init.uniform_(self.target_embedding.weight.data, -0.001, 0.001)
+        self.edge_channel_list = [attn_weight_input_dim + self.node_embed_dim * 2,
+                                  min(128, attn_weight_input_dim // 2), min(128, attn_weight_input_dim // 2)]
+        self.fc_easy = RadialProfile(self.edge_channel_list + [2 * num_attn_heads])
+        self.query_linear = SO3_Linear2Scalar_e2former(C, num_attn_heads * attn_scalar_head, lmax=lmax)
+        self.key_linear = SO3_Linear2Scalar_e2former(C, num_attn_heads * attn_scalar_head, lmax=lmax)
+        self.proj_value = SO3_Linear_e2former(C, C, lmax=lmax)
+        self.first_order_tp = E2TensorProductSO2_FirstOrder(C, head_mul * num_attn_heads, lmax, num_attn_heads)
+        self.proj_first = SO3_Linear_e2former(num_attn_heads * head_mul, C, lmax=lmax)
+        if (29 * C) % num_attn_heads:
+            raise NotImplementedError("29*C must be divisible by the number of heads")
+
+    # -- edge radial MLP with the first layer split as W_r rbf + (W_t T)[Z_i] + (W_s S)[Z_j] + b --
+    def edge_gate(self, attn_weight, atomic_numbers, f_outcell_index, query_idx, neighbor_idx):
+        net = self.fc_easy.net
+        lin0 = net[0]
+        nb = self.attn_weight_input_dim
+        e = self.node_embed_dim
+        w = lin0.weight
+        t_tab = self.target_embedding.weight @ w[:, nb:nb + e].t()          # [types, h]
+        s_tab = self.source_embedding.weight @ w[:, nb + e:].t()            # [types, h]
+        z_q = atomic_numbers[query_idx]
+        z_k = atomic_numbers[f_outcell_index][neighbor_idx]
+        h = torch.addmm(lin0.bias, attn_weight, w[:, :nb].t()) + t_tab[z_q] + s_tab[z_k]
+        for layer in list(net)[1:]:
+            h = layer(h)
+        return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
+
+    def forward(self, node_pos, node_irreps_input, edge_dis, edge_vec, attn_weight, atomic_numbers,
+                poly_dist=None, attn_mask=None, batch=None, batched_data=None, **kwargs):
+        if self.training and self.alpha_drop > 0:
+            raise NotImplementedError("attention dropout (training) is not part of the inference path")
+        N1 = node_irreps_input.shape[0]
+        H = self.num_attn_heads
+        C = self.scalar_dim
+        bd = batched_data
+        outcell = bd["f_outcell_index"]
+        N2 = outcell.shape[0]
+        query_idx = bd["query_idx"].to(torch.long)
+        neighbor_idx = bd["neighbor_idx"].to(torch.long)
+        metadata = bd["metadata"]
+        x = node_irreps_input
+
+        query = self.query_linear(x).reshape(N1, H, -1)
+        key = self.key_linear(x)[outcell].reshape(N2, H, -1)
+        q_scaled = query / math.sqrt(query.shape[-1])
+        gate = self.edge_gate(attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx)
+
+        value = self.proj_value(x)[outcell]                                          # [N2, 9, C]
+        tp = self.first_order_tp
+        h_b = tp.node_half(bd["wigner_exp"], bd["wigner_inv_exp"], value, bd["f_exp_node_pos"])  # [N2, 20, C]
+        n_b = h_b.shape[1]
+        merged = torch.cat([h_b, value], dim=1).reshape(N2, -1, H)                   # [N2, 29*C/H, H]
+
+        poly = poly_dist if poly_dist is not None else torch.ones_like(edge_dis)
+        if bd.get("query_sorted", None) is None:
+            qi = bd["query_idx"]
+            bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
+        if bd["query_sorted"]:
+            agg = attention_span(q_scaled, key, merged, gate, poly, edge_dis, metadata, bd.get("row_order"))
+        else:
+            # permute the edges into query-CSR order (q_perm) so that edge id == CSR slot
+            perm = metadata[2].to(torch.long)
+            md = (metadata[0], metadata[1], torch.arange(perm.numel(), device=perm.device, dtype=torch.int32),
+                  metadata[3], metadata[4], torch.argsort(perm)[metadata[5].to(torch.long)].to(torch.int32))
+            agg = attention_span(q_scaled, key, merged, gate[perm], poly[perm], edge_dis[perm], md,
+                                 bd.get("row_order"))
+        agg = agg.reshape(N1, -1, C)
+        h_b_agg, h_a = agg[:, :n_b], agg[:, n_b:]
+        h_a = tp.node_half(bd["wigner"], bd["wigner_inv"], h_a, node_pos)
+        out = tp.so2_tp.forward_linear(h_a - h_b_agg)
+        return self.proj_first(out), attn_weight

@@ -1,0 +1,68 @@
+// Shared helpers for the E2Former-V2 attention kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "../../include/e2a.h"
+
+#define E2A_CHECK_LAUNCH()                                   \
+  do {                                                       \
+    cudaError_t _e = cudaGetLastError();                     \
+    if (_e != cudaSuccess) { e2a_set_cuda_error(_e); return E2A_ERR_CUDA; } \
+  } while (0)
+
+#define E2A_CUDA(call)                                       \
+  do {                                                       \
+    cudaError_t _e = (call);                                 \
+    if (_e != cudaSuccess) { e2a_set_cuda_error(_e); return E2A_ERR_CUDA; } \
+  } while (0)
+
+void e2a_set_cuda_error(cudaError_t e);
+
+static inline size_t e2a_align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Bump allocator over a caller-provided workspace.  Every sub-buffer is 256-byte aligned.
+struct E2aArena {
+  char* base;
+  size_t cap;
+  size_t used;
+  __host__ void* take(size_t bytes) {
+    size_t off = e2a_align_up(used, 256);
+    used = off + e2a_align_up(bytes, 256);
+    if (base == nullptr || used > cap) return nullptr;
+    return base + off;
+  }
+};
+
+__device__ __forceinline__ float e2a_warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float4 f4_fma(float s, float4 v, float4 acc) {
+  acc.x = fmaf(s, v.x, acc.x);
+  acc.y = fmaf(s, v.y, acc.y);
+  acc.z = fmaf(s, v.z, acc.z);
+  acc.w = fmaf(s, v.w, acc.w);
+  return acc;
+}
+
+__device__ __forceinline__ float4 f4_fma4(float4 s, float4 v, float4 acc) {
+  acc.x = fmaf(s.x, v.x, acc.x);
+  acc.y = fmaf(s.y, v.y, acc.y);
+  acc.z = fmaf(s.z, v.z, acc.z);
+  acc.w = fmaf(s.w, v.w, acc.w);
+  return acc;
+}
+
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Euclidean norm of a 3-vector, evaluated as fma(z,z,fma(y,y,x*x)) then a correctly rounded
+// sqrt: the exact fp32 operation sequence of PyTorch's CPU vector-norm kernel for a length-3
+// reduction (torch.linalg.norm / torch.norm, p=2), which the reference uses for every distance
+// (module_utils.py:3164, 1205).  Bit-equal distances are what makes the edge lists bit-exact.
+__device__ __forceinline__ float e2a_norm3(float x, float y, float z) {
+  return __fsqrt_rn(__fmaf_rn(z, z, __fmaf_rn(y, y, __fmul_rn(x, x))));
+}

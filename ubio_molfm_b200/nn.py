@@ -1,0 +1,207 @@
+"""Node-side building blocks of the E2Former-V2 attention layer, with the reference's parameter
+names and shapes so that reference ``state_dict``s load unchanged.
+
+These are dense per-node contractions ([N, (lmax+1)^2, C] x [C, C']); they run as batched GEMMs
+(cuBLAS through ``torch.matmul``) on the GPU.  The sparse edge work lives in :mod:`.ops`.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+
+from .cg import so2_first_order_tables
+
+
+def parse_irreps(irreps):
+    """Parse ``"256x0e+256x1e+256x2e"`` into ``[(mul, l, parity), ...]``."""
+    if not isinstance(irreps, str):
+        return [(int(m), int(ir[0]), int(ir[1]) if len(ir) > 1 else 1) for m, ir in irreps]
+    out = []
+    for part in irreps.split("+"):
+        part = part.strip()
+        if not part:
+            continue
+        mul, ir = part.split("x") if "x" in part else ("1", part)
+        out.append((int(mul), int(ir[:-1]), 1 if ir[-1] == "e" else -1))
+    return out
+
+
+def irreps_channels_lmax(irreps):
+    """(channels of the l=0 block, lmax) of an irreps spec with one block per l."""
+    ir = parse_irreps(irreps)
+    return ir[0][0], ir[-1][1]
+
+
+class SO3_Linear_e2former(nn.Module):
+    """Per-degree linear map ``out[:, m, :] = x[:, m, :] @ W[l(m)].T`` (+ bias on the l=0 row).
+
+    Follows module_utils.py:2010-2055 (weight [(lmax+1), out, in], bias [out])."""
+
+    def __init__(self, in_features, out_features, lmax, bias=True):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.lmax = lmax
+        self.weight = nn.Parameter(torch.empty(lmax + 1, out_features, in_features))
+        bound = 1 / math.sqrt(in_features)
+        nn.init.uniform_(self.weight, -bound, bound)
+        self.bias = nn.Parameter(torch.zeros(out_features))
+        expand_index = torch.zeros((lmax + 1) ** 2, dtype=torch.long)
+        for l in range(lmax + 1):
+            expand_index[l * l:(l + 1) ** 2] = l
+        self.register_buffer("expand_index", expand_index, persistent=False)
+
+    def forward(self, x):
+        shape = x.shape[:-2]
+        x = x.reshape(-1, x.shape[-2], x.shape[-1])
+        outs = []
+        for l in range(self.lmax + 1):
+            blk = x[:, l * l:(l + 1) ** 2, :]
+            o = torch.matmul(blk, self.weight[l].t())
+            if l == 0:
+                o = o + self.bias
+            outs.append(o)
+        out = torch.cat(outs, dim=1)
+        return out.reshape(*shape, out.shape[-2], self.out_features)
+
+
+class SO3_Linear2Scalar_e2former(nn.Module):
+    """Two per-degree linears, per-degree inner product over m, then an MLP (module_utils.py:2198-2274)."""
+
+    def __init__(self, in_features, out_features, lmax, hidden_features=None, bias=True):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.lmax = lmax
+        hidden = out_features // 2 if hidden_features is None else hidden_features
+        self.hidden = hidden
+        bound = 1 / math.sqrt(in_features)
+        self.weight = nn.Parameter(torch.empty(lmax + 1, hidden, in_features).uniform_(-bound, bound))
+        self.bias = nn.Parameter(torch.zeros(1, 1, hidden))
+        self.weight2 = nn.Parameter(torch.empty(lmax + 1, hidden, in_features).uniform_(-bound, bound))
+        expand_index = torch.zeros((lmax + 1) ** 2, dtype=torch.long)
+        for l in range(lmax + 1):
+            expand_index[l * l:(l + 1) ** 2] = l
+        self.register_buffer("expand_index", expand_index)
+        self.final_linear = nn.Sequential(
+            nn.Linear(hidden * (lmax + 1), hidden), nn.LayerNorm(hidden), nn.SiLU(), nn.Linear(hidden, out_features))
+
+    def forward(self, x):
+        shape = x.shape[:-2]
+        x = x.reshape(-1, x.shape[-2], x.shape[-1])
+        # both projections in one GEMM per degree: [*, 2l+1, in] @ [in, 2*hidden]
+        parts = []
+        for l in range(self.lmax + 1):
+            blk = x[:, l * l:(l + 1) ** 2, :]
+            w = torch.cat([self.weight[l], self.weight2[l]], dim=0)
+            o = torch.matmul(blk, w.t())
+            o1, o2 = o[..., :self.hidden], o[..., self.hidden:]
+            if l == 0:
+                o1 = o1 + self.bias.reshape(1, 1, -1)
+            parts.append((o1 * o2).sum(dim=1))
+        out = self.final_linear(torch.cat(parts, dim=-1))
+        return out.reshape(*shape, self.out_features)
+
+
+class RadialProfile(nn.Module):
+    """Linear -> (LayerNorm) -> SiLU ... -> Linear, parameter names as module_utils.py:2151-2178."""
+
+    def __init__(self, ch_list, use_layer_norm=True, use_offset=True):
+        super().__init__()
+        mods = []
+        cin = ch_list[0]
+        for i in range(1, len(ch_list)):
+            mods.append(nn.Linear(cin, ch_list[i], bias=use_offset))
+            cin = ch_list[i]
+            if i == len(ch_list) - 1:
+                break
+            if use_layer_norm:
+                mods.append(nn.LayerNorm(ch_list[i]))
+            mods.append(nn.SiLU())
+        self.net = nn.Sequential(*mods)
+
+    def forward(self, f_in):
+        return self.net(f_in)
+
+
+class GaussianSmearing(nn.Module):
+    """``exp(coeff (d - mu_k)^2)``, mu = linspace(0, cutoff, n), coeff = -0.5 / (width*dmu)^2
+    (module_utils.py:1853-1870)."""
+
+    def __init__(self, num_basis, cutoff=5.0, basis_width_scalar=2.0):
+        super().__init__()
+        offset = torch.linspace(0, cutoff, num_basis)
+        self.coeff = -0.5 / (basis_width_scalar * (offset[1] - offset[0])).item() ** 2
+        self.register_buffer("offset", offset)
+
+    def forward(self, dist):
+        shape = dist.shape
+        d = dist.view(-1, 1) - self.offset.view(1, -1)
+        return torch.exp(self.coeff * torch.pow(d, 2)).reshape(*shape, -1)
+
+
+def polynomial(dist, cutoff, exponent=5):
+    """Smooth envelope 1 + r^p (a + r (b + c r)), zero for r >= 1 (module_utils.py:1946-1954)."""
+    a = -(exponent + 1) * (exponent + 2) / 2
+    b = exponent * (exponent + 2)
+    c = -exponent * (exponent + 1) / 2
+    ratio = dist / cutoff
+    env = 1 + ratio ** exponent * (a + ratio * (b + c * ratio))
+    return torch.where(ratio < 1, env, 0)
+
+
+class SO2_TP_givenl2(nn.Module):
+    """First-order (l2 = 1) SO(2) tensor product in the node frame + per-l3 output linear.
+
+    ``forward`` selects one input row per output row and scales it by its CG coefficient
+    (so2_tensor_product.py:263-271); ``forward_linear`` mixes the ``count`` paths of each l3 with
+    one Linear(count*C -> C') and multiplies by 1/sqrt(count) (so2_tensor_product.py:273-290)."""
+
+    def __init__(self, lmax=2, in_c=None, out_c=None, with_linear=True):
+        super().__init__()
+        _, seq, sel, w, norm = so2_first_order_tables(lmax, 1)
+        self.l3_sequential = seq
+        self.with_linear = with_linear
+        self.in_c, self.out_c = in_c, out_c
+        self.out_linear = nn.ModuleList()
+        if with_linear:
+            for l3, cnt in seq:
+                self.out_linear.append(nn.Linear(cnt * in_c, out_c, bias=False))
+        self.path_norm = nn.Parameter(torch.tensor(norm, dtype=torch.float32).reshape(1, -1, 1), requires_grad=False)
+        self.selected_idx = nn.Parameter(torch.tensor(sel, dtype=torch.long), requires_grad=False)
+        self.CG_weight = nn.Parameter(torch.tensor(w, dtype=torch.float32), requires_grad=False)
+
+    def forward(self, x, with_linear=True):
+        y = x[:, self.selected_idx] * self.CG_weight.reshape(1, -1, 1)
+        if with_linear and self.with_linear:
+            return self.forward_linear(y)
+        return y
+
+    def forward_linear(self, y):
+        bs = y.shape[0]
+        start = 0
+        outs = []
+        for idx, (l3, cnt) in enumerate(self.l3_sequential):
+            end = start + (2 * l3 + 1) * cnt
+            blk = y[:, start:end].reshape(bs, cnt, 2 * l3 + 1, -1).permute(0, 2, 1, 3).reshape(bs, 2 * l3 + 1, -1)
+            outs.append(self.out_linear[idx](blk))
+            start = end
+        return torch.cat(outs, dim=1) * self.path_norm
+
+
+class E2TensorProductSO2_FirstOrder(nn.Module):
+    """Holds the SO(2) product of the node-decomposed first-order TP (so2_tensor_product.py:293-389).
+    The sparse aggregation between the two node-local halves is done by the fused attention kernel
+    (see :class:`ubio_molfm_b200.attention.E2AttentionArbOrder_sparse`)."""
+
+    def __init__(self, in_c, out_c, lmax, head):
+        super().__init__()
+        self.in_c, self.out_c, self.lmax, self.head = in_c, out_c, lmax, head
+        self.so2_tp = SO2_TP_givenl2(lmax, in_c, out_c, with_linear=True)
+
+    def node_half(self, wigner, wigner_inv, h, pos):
+        """W_inv @ (CG-select(W @ h) * |pos|): the per-node half of h (x) r."""
+        y = self.so2_tp(torch.bmm(wigner, h), with_linear=False) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
+        return torch.bmm(wigner_inv, y)

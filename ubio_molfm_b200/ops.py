@@ -1,0 +1,323 @@
+"""PyTorch-facing wrappers of the C ABI: CSR metadata, the reference's kernel-level sparse ops
+(same names, arguments and error behaviour as its ``triton_dr`` functions) and the fused attention
+span used by :class:`ubio_molfm_b200.attention.E2AttentionArbOrder_sparse`.
+
+Outputs are allocated through the PyTorch caching allocator and the kernels run on the current
+CUDA stream.  Every op raises on non-CUDA inputs: there is no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, require_cuda, stream_of
+
+
+def _i32(t):
+    return t.contiguous().to(torch.int32)
+
+
+def _f32(t):
+    return t.contiguous().to(torch.float32)
+
+
+def _workspace(nbytes, device):
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+# ------------------------------------------------------------------------------------------------
+# CSR metadata  (triton_sparse_qk_autograd.py:635-652)
+# ------------------------------------------------------------------------------------------------
+def prepare_sparse_qk_edge_index_metadata(query_index, neighbor_index, num_queries, num_keys):
+    """Query-CSR and key-CSR of an edge list: ``(q_row_ptr, q_col, q_perm, k_row_ptr, k_col, k_perm)``,
+    int32; the key-CSR orders the edges of a key by edge id (a stable grouping)."""
+    require_cuda(query_index, neighbor_index)
+    lib = _lib.load()
+    dev = query_index.device
+    q = _i32(query_index)
+    n = _i32(neighbor_index)
+    E = q.numel()
+    N, M = int(num_queries), int(num_keys)
+    out = [torch.empty(N + 1, dtype=torch.int32, device=dev), torch.empty(E, dtype=torch.int32, device=dev),
+           torch.empty(E, dtype=torch.int32, device=dev), torch.empty(M + 1, dtype=torch.int32, device=dev),
+           torch.empty(E, dtype=torch.int32, device=dev), torch.empty(E, dtype=torch.int32, device=dev)]
+    ws = _workspace(lib.e2a_csr_workspace_bytes(E, N, M), dev)
+    check(lib.e2a_csr_build(ptr(q), ptr(n), E, N, M, *[ptr(t) for t in out], ptr(ws), ws.numel(), stream_of(dev)),
+          "e2a_csr_build (an index is out of range)")
+    return tuple(out)
+
+
+def _check_md(metadata):
+    if metadata is None or len(metadata) != 6:
+        raise ValueError("metadata must be a 6-tuple from prepare_sparse_qk_edge_index_metadata")
+    return tuple(_i32(m) for m in metadata)
+
+
+# ------------------------------------------------------------------------------------------------
+# sparse_qk_edge_index  (triton_sparse_qk_autograd.py:839-871)
+# ------------------------------------------------------------------------------------------------
+def _qk_forward(query, key, md, E):
+    lib = _lib.load()
+    N, H, D = query.shape
+    out = torch.empty((E, H), device=query.device, dtype=torch.float32)
+    check(lib.e2a_sparse_qk_fwd(ptr(query), ptr(key), ptr(md[0]), ptr(md[1]), ptr(md[2]), N, E, H, D, ptr(out),
+                                stream_of(query.device)), "e2a_sparse_qk_fwd")
+    return out
+
+
+def _grouped_reduce(alpha, x, row_ptr, col, perm, rows):
+    lib = _lib.load()
+    _, H, D = x.shape
+    out = torch.empty((rows, H, D), device=x.device, dtype=torch.float32)
+    check(lib.e2a_grouped_reduce(ptr(alpha), ptr(x), ptr(row_ptr), ptr(col), ptr(perm), rows, H, D, ptr(out),
+                                 stream_of(x.device)), "e2a_grouped_reduce")
+    return out
+
+
+class SparseQKEdgeIndexFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, query, key, md):
+        q, k = _f32(query), _f32(key)
+        E = md[1].numel()
+        out = _qk_forward(q, k, md, E)
+        ctx.save_for_backward(q, k, *md)
+        ctx.dtypes = (query.dtype, key.dtype)
+        return out.to(query.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        q, k, *md = ctx.saved_tensors
+        g = _f32(g)
+        dq = dk = None
+        if ctx.needs_input_grad[0]:
+            dq = _grouped_reduce(g, k, md[0], md[1], md[2], q.shape[0]).to(ctx.dtypes[0])
+        if ctx.needs_input_grad[1]:
+            dk = _grouped_reduce(g, q, md[3], md[4], md[5], k.shape[0]).to(ctx.dtypes[1])
+        return dq, dk, None
+
+
+def sparse_qk_edge_index(query, key, query_index, neighbor_index, metadata=None):
+    """``out[e, h] = <query[query_index[e], h], key[neighbor_index[e], h]>`` -> [E, H]."""
+    require_cuda(query, key, query_index, neighbor_index)
+    if query.ndim != 3 or key.ndim != 3 or query.shape[1:] != key.shape[1:]:
+        raise ValueError("query must be [N,H,D] and key [M,H,D]")
+    if metadata is None:
+        metadata = prepare_sparse_qk_edge_index_metadata(query_index, neighbor_index, query.shape[0], key.shape[0])
+    md = _check_md(metadata)
+    return SparseQKEdgeIndexFn.apply(query, key, md)
+
+
+# ------------------------------------------------------------------------------------------------
+# sparse_alpha_sum_edge_index  (sparse_alpha_sum_edge_index_autograd.py:207-213)
+# ------------------------------------------------------------------------------------------------
+def prepare_sparse_alpha_sum_edge_index_metadata(query_index, num_queries):
+    md = prepare_sparse_qk_edge_index_metadata(query_index, query_index, num_queries, num_queries)
+    return md[0], md[2]
+
+
+class SparseAlphaSumFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, alpha, query_index, row_ptr, perm, num_queries):
+        lib = _lib.load()
+        a = _f32(alpha)
+        H = a.shape[1]
+        out = torch.empty((num_queries, H), device=a.device, dtype=torch.float32)
+        check(lib.e2a_alpha_sum_fwd(ptr(a), ptr(row_ptr), ptr(perm), num_queries, H, ptr(out), stream_of(a.device)),
+              "e2a_alpha_sum_fwd")
+        ctx.save_for_backward(_i32(query_index))
+        ctx.shape = a.shape
+        ctx.dtype = alpha.dtype
+        return out.to(alpha.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        (qi,) = ctx.saved_tensors
+        lib = _lib.load()
+        g = _f32(g)
+        E, H = ctx.shape
+        ga = torch.empty((E, H), device=g.device, dtype=torch.float32)
+        check(lib.e2a_alpha_sum_bwd(ptr(g), ptr(qi), E, H, ptr(ga), stream_of(g.device)), "e2a_alpha_sum_bwd")
+        return ga.to(ctx.dtype), None, None, None, None
+
+
+def sparse_alpha_sum_edge_index(alpha, query_index, num_queries, metadata=None):
+    """``out[n, h] = sum_{e: query_index[e] = n} alpha[e, h]`` -> [N, H]; metadata = (row_ptr, perm)."""
+    require_cuda(alpha, query_index)
+    if metadata is None:
+        metadata = prepare_sparse_alpha_sum_edge_index_metadata(query_index, num_queries)
+    row_ptr, perm = (_i32(m) for m in metadata)
+    return SparseAlphaSumFn.apply(alpha, query_index, row_ptr, perm, int(num_queries))
+
+
+# ------------------------------------------------------------------------------------------------
+# sparse_v_agg_edge_index_cblocked  (sparse_v_agg_edge_index_cblocked_bench.py:428-449)
+# ------------------------------------------------------------------------------------------------
+class SparseVAggFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, value, alpha, md, num_queries):
+        lib = _lib.load()
+        v, a = _f32(value), _f32(alpha)
+        M, C, H = v.shape
+        out = torch.empty((num_queries, C, H), device=v.device, dtype=torch.float32)
+        check(lib.e2a_v_agg_fwd(ptr(v), ptr(a), ptr(md[0]), ptr(md[1]), ptr(md[2]), num_queries, C, H, ptr(out),
+                                stream_of(v.device)), "e2a_v_agg_fwd")
+        ctx.save_for_backward(v, a, *md)
+        ctx.dtypes = (value.dtype, alpha.dtype)
+        return out.to(value.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        v, a, *md = ctx.saved_tensors
+        lib = _lib.load()
+        g = _f32(g)
+        M, C, H = v.shape
+        N = g.shape[0]
+        dv = da = None
+        if ctx.needs_input_grad[0]:
+            dv = torch.empty_like(v)
+            check(lib.e2a_v_agg_bwd_value(ptr(a), ptr(g), ptr(md[3]), ptr(md[4]), ptr(md[5]), M, C, H, ptr(dv),
+                                          stream_of(g.device)), "e2a_v_agg_bwd_value")
+            dv = dv.to(ctx.dtypes[0])
+        if ctx.needs_input_grad[1]:
+            da = torch.empty_like(a)
+            check(lib.e2a_v_agg_bwd_alpha(ptr(g), ptr(v), ptr(md[0]), ptr(md[1]), ptr(md[2]), N, C, H, ptr(da),
+                                          stream_of(g.device)), "e2a_v_agg_bwd_alpha")
+            da = da.to(ctx.dtypes[1])
+        return dv, da, None, None
+
+
+def sparse_v_agg_edge_index_cblocked(value, alpha, query_index, value_index, num_queries, metadata=None):
+    """``out[query_index[e], c, h] += alpha[e, h] * value[value_index[e], c, h]`` -> [N, C, H]."""
+    require_cuda(value, alpha, query_index, value_index)
+    if value.ndim != 3:
+        raise ValueError("value must be [M, C, H]")
+    if alpha.ndim != 2:
+        raise ValueError("alpha must be [E, H]")
+    if metadata is None:
+        metadata = prepare_sparse_qk_edge_index_metadata(query_index, value_index, num_queries, value.shape[0])
+    md = _check_md(metadata)
+    return SparseVAggFn.apply(value, alpha, md, int(num_queries))
+
+
+# ------------------------------------------------------------------------------------------------
+# edge_degree_outer  (edge_degree_outer_autograd.py:348-375)
+# ------------------------------------------------------------------------------------------------
+class EdgeDegreeOuterFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, edge_sh, edge_fea, query_index, row_ptr, perm, num_queries):
+        lib = _lib.load()
+        sh, fea = _f32(edge_sh), _f32(edge_fea)
+        E, L = sh.shape
+        F = fea.shape[1]
+        out = torch.empty((num_queries, L, F), device=sh.device, dtype=torch.float32)
+        check(lib.e2a_edge_outer_fwd(ptr(sh), ptr(fea), ptr(row_ptr), ptr(perm), num_queries, L, F, ptr(out),
+                                     stream_of(sh.device)), "e2a_edge_outer_fwd")
+        ctx.save_for_backward(sh, fea, _i32(query_index))
+        ctx.dtypes = (edge_sh.dtype, edge_fea.dtype)
+        return out.to(edge_fea.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        sh, fea, qi = ctx.saved_tensors
+        lib = _lib.load()
+        g = _f32(g)
+        E, L = sh.shape
+        F = fea.shape[1]
+        dsh = torch.empty_like(sh) if ctx.needs_input_grad[0] else None
+        dfea = torch.empty_like(fea) if ctx.needs_input_grad[1] else None
+        if dsh is not None or dfea is not None:
+            check(lib.e2a_edge_outer_bwd(ptr(g), ptr(sh), ptr(fea), ptr(qi), E, L, F, ptr(dsh), ptr(dfea),
+                                         stream_of(g.device)), "e2a_edge_outer_bwd")
+        return (None if dsh is None else dsh.to(ctx.dtypes[0]), None if dfea is None else dfea.to(ctx.dtypes[1]),
+                None, None, None, None)
+
+
+def edge_degree_outer(edge_sh, edge_fea, query_index, num_queries, metadata=None):
+    """``out[n, l, h] = sum_{e: query_index[e] = n} edge_sh[e, l] * edge_fea[e, h]`` -> [N, L, H]."""
+    require_cuda(edge_sh, edge_fea, query_index)
+    if metadata is None:
+        md = prepare_sparse_qk_edge_index_metadata(query_index, torch.arange(query_index.numel(),
+                                                                             device=query_index.device),
+                                                   num_queries, query_index.numel())
+    elif isinstance(metadata, (tuple, list)):
+        if len(metadata) != 6:
+            raise ValueError("metadata must be a 6-tuple")
+        md = metadata
+    else:
+        raise ValueError("metadata must be a tuple/list")
+    return EdgeDegreeOuterFn.apply(edge_sh, edge_fea, query_index, _i32(md[0]), _i32(md[2]), int(num_queries))
+
+
+# Names of the reference's kernel API (the "triton" suffix is kept so callers need no edit).
+sparse_qk_edge_index_triton = sparse_qk_edge_index
+sparse_alpha_sum_edge_index_triton = sparse_alpha_sum_edge_index
+sparse_v_agg_edge_index_triton_cblocked = sparse_v_agg_edge_index_cblocked
+edge_degree_outer_triton = edge_degree_outer
+
+
+# ------------------------------------------------------------------------------------------------
+# Fused attention span
+# ------------------------------------------------------------------------------------------------
+class AttnSpanFn(torch.autograd.Function):
+    """QK logits -> gated segmented softmax -> alpha/r -> value aggregation, and its backward.
+
+    Inputs (fp32, CUDA): q_scaled [N,H,D], key [M,H,D], value [M,C,H], edge_gate [E,2H] (gate =
+    [:, :H], inputhead = [:, H:]), poly [E], dist [E], and the CSR of the (query-sorted) edge list.
+    """
+
+    @staticmethod
+    def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order):
+        lib = _lib.load()
+        q, key, value = _f32(q), _f32(key), _f32(value)
+        edge_gate, poly, dist = _f32(edge_gate), _f32(poly), _f32(dist)
+        N, H, D = q.shape
+        M, C, H2 = value.shape
+        E = edge_gate.shape[0]
+        if H2 != H or edge_gate.shape[1] != 2 * H or key.shape != (M, H, D):
+            raise ValueError("inconsistent attention span shapes")
+        dev = q.device
+        out = torch.empty((N, C, H), device=dev, dtype=torch.float32)
+        beta = torch.empty((E, H), device=dev, dtype=torch.float32)
+        rmax = torch.empty((N, H), device=dev, dtype=torch.float32)
+        rsum = torch.empty((N, H), device=dev, dtype=torch.float32)
+        check(lib.e2a_attn_fwd(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
+                               ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
+                               ptr(out), ptr(beta), ptr(rmax), ptr(rsum), stream_of(dev)), "e2a_attn_fwd")
+        ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, *md)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, *md = ctx.saved_tensors
+        lib = _lib.load()
+        dout = _f32(dout)
+        N, H, D = q.shape
+        M, C, _ = value.shape
+        E = edge_gate.shape[0]
+        dev = q.device
+        st = stream_of(dev)
+        d_q = torch.empty_like(q)
+        d_gate = torch.empty((E, 2 * H), device=dev, dtype=torch.float32)
+        d_poly = torch.empty(E, device=dev, dtype=torch.float32)
+        d_dist = torch.empty(E, device=dev, dtype=torch.float32)
+        d_logit = torch.empty((E, H), device=dev, dtype=torch.float32)
+        ws = _workspace(lib.e2a_attn_bwd_workspace_bytes(E, H), dev)
+        check(lib.e2a_attn_bwd_query(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
+                                     ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
+                                     ptr(beta), ptr(rmax), ptr(rsum), ptr(dout), ptr(d_q), ptr(d_gate),
+                                     ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit), ptr(ws),
+                                     ws.numel(), st), "e2a_attn_bwd_query")
+        d_k = torch.empty_like(key)
+        d_v = torch.empty_like(value)
+        check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]),
+                                   N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
+        return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None
+
+
+def attention_span(q_scaled, key, value, edge_gate, poly, dist, metadata, row_order=None):
+    """Fused attention span (see :class:`AttnSpanFn`); ``metadata`` is the 6-tuple CSR of a
+    query-sorted edge list (identity query permutation)."""
+    require_cuda(q_scaled, key, value, edge_gate, poly, dist)
+    md = _check_md(metadata)
+    ro = None if row_order is None else _i32(row_order)
+    return AttnSpanFn.apply(q_scaled, key, value, edge_gate, poly, dist, md, ro)
