@@ -1,0 +1,425 @@
+"""Benchmark of the E2Former-V2 sparse equivariant attention layer on B200.
+
+Workload (the attention-layer microbenchmark): one ``E2AttentionArbOrder_sparse`` forward + the
+first-order backward autograd runs for forces, at the full layer size (node irreps
+256x0e+256x1e+256x2e, 128 heads, 8 scalar dims, head irreps 2x0e+2x1e+2x2e, 256 RBF), fp32, on a
+periodic box of seeded uniform positions (default 1e5 atoms, ~32 neighbours within 6 A).  Weights are
+seeded random (no checkpoint).  Metric: atom-steps/s = atoms x steps / device seconds.
+
+* ``value``: inputs resident in HBM (graph, Wigner matrices, RBF built once), CUDA events around
+  exactly K steps, barrier + synchronize on both sides, max over ranks.  All inputs are larger than L2.
+* ``e2e``: the same step through the public API from pinned HOST buffers each step: copy positions,
+  atomic numbers, node features and the output cotangent to the device, build the periodic images,
+  radius graph, CSR metadata, Wigner matrices and RBF, run the layer forward + backward, and copy the
+  output, d(features) and d(positions) back.
+* ``roofline``: the dominant kernel of this package, timed with CUDA events on its launch stream
+  inside the timed region, against its compulsory (algorithmic) bytes.
+* ``cpu_baseline``: the CPU oracle (the reference algorithm restated) on a bounded sample.
+
+Multi-GPU: ``--gpus N`` under torchrun runs one independent replica per rank (the layer has no
+exchange step), ``scaling: weak``.  ``--impl reference`` times the CPU restatement of the reference
+path (the reference itself is pure Python and is not installed on the GPU box).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+C_CH, HEADS, DHEAD, NB, CUTOFF = 256, 128, 8, 256, 6.0
+HEAD_IRREPS = "2x0e+2x1e+2x2e"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--atoms", type=int, default=100_000)
+    ap.add_argument("--k", type=int, default=32)
+    ap.add_argument("--cpu-atoms", type=int, default=1500, help="CPU baseline sample size")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------
+def dist_init(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend=backend)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, ws, dev):
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def config_dict(args, E=None, N2=None, extra=None):
+    d = {"workload": f"E2AttentionArbOrder_sparse forward+backward, periodic uniform box {args.atoms} atoms, "
+                     f"~{args.k} neighbours within {CUTOFF} A",
+         "atoms_per_rank": args.atoms, "k_avg": args.k, "irreps": f"{C_CH}x0e+{C_CH}x1e+{C_CH}x2e",
+         "heads": HEADS, "attn_scalar_head": DHEAD, "irreps_head": HEAD_IRREPS, "rbf": NB, "cutoff": CUTOFF,
+         "l2": "inputs larger than L2 (value rows alone are GBs)", "parallelism": f"replicas x{args.gpus}"}
+    if E is not None:
+        d["edges_per_rank"] = E
+        d["expanded_nodes_per_rank"] = N2
+    if extra:
+        d.update(extra)
+    return d
+
+
+# ------------------------------------------------------------------------------------------------
+def make_layer(dev, seed=0):
+    from ubio_molfm_b200.attention import E2AttentionArbOrder_sparse
+    from ubio_molfm_b200.synthetic import seeded_params_
+
+    layer = E2AttentionArbOrder_sparse(f"{C_CH}x0e+{C_CH}x1e+{C_CH}x2e", NB, num_attn_heads=HEADS,
+                                       attn_scalar_head=DHEAD, irreps_head=HEAD_IRREPS, alpha_drop=0.0,
+                                       tp_type="QK_alpha+triton", attn_type="so2-first-order")
+    seeded_params_(layer, seed)
+    return layer.to(dev).eval()
+
+
+def build_inputs(pos, Z, cell, dev, layer):
+    """Graph + per-node geometry for one periodic system (all on ``dev``)."""
+    from ubio_molfm_b200.graph import expand_pbc, radius_graph
+    from ubio_molfm_b200.nn import GaussianSmearing
+    from ubio_molfm_b200.wigner import node_wigner
+
+    N = pos.shape[0]
+    exp_pos, outcell, _ = expand_pbc(pos, cell, [True, True, True], CUTOFF)
+    g = radius_graph(pos, exp_pos, torch.tensor([0, N]), torch.tensor([0, exp_pos.shape[0]]), CUTOFF, 1e-4, None)
+    W, Wi = node_wigner(pos)
+    We, Wie = node_wigner(exp_pos)
+    rbf = GaussianSmearing(NB, cutoff=CUTOFF).to(dev)(g["f_dist"])
+    bd = dict(g)
+    bd.update({"f_outcell_index": outcell, "f_exp_node_pos": exp_pos, "wigner": W, "wigner_inv": Wi,
+               "wigner_exp": We, "wigner_inv_exp": Wie})
+    return bd, rbf
+
+
+def layer_step(layer, pos, x, Z, bd, rbf, dout, leaves):
+    out, _ = layer(node_pos=pos, node_irreps_input=x, edge_dis=bd["f_dist"], edge_vec=bd["f_edge_vec"],
+                   attn_weight=rbf, atomic_numbers=Z, poly_dist=bd["f_poly_dist"], batched_data=bd)
+    grads = torch.autograd.grad(out, leaves, dout, allow_unused=True)
+    return out, grads
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    def __init__(self, index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) >= 9:
+                for nme, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nme)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def fwd_algorithmic_bytes(N, N2, E):
+    """Compulsory bytes of one e2a_attn_fwd launch (fp32): q, k, value rows, gate+inputhead, poly, dist,
+    col, row_ptr read once; out, beta, row stats written once."""
+    HD, CH = HEADS * DHEAD, 58 * HEADS
+    return 4 * (N * HD + N2 * HD + N2 * CH + E * 2 * HEADS + E * 3 + (N + 1) + N * CH + E * HEADS + 2 * N * HEADS)
+
+
+def bwdq_algorithmic_bytes(N, N2, E):
+    HD, CH = HEADS * DHEAD, 58 * HEADS
+    reads = N * HD + N2 * HD + N2 * CH + E * 2 * HEADS + E * 3 + (N + 1) + E * HEADS + 2 * N * HEADS + N * CH
+    writes = N * HD + E * 2 * HEADS + 2 * E + E * HEADS
+    return 4 * (reads + writes)
+
+
+def bwdk_algorithmic_bytes(N, N2, E):
+    HD, CH = HEADS * DHEAD, 58 * HEADS
+    reads = N * HD + N * CH + E * HEADS * 2 + 2 * E + (N2 + 1)
+    writes = N2 * HD + N2 * CH
+    return 4 * (reads + writes)
+
+
+# ------------------------------------------------------------------------------------------------
+def cpu_baseline_setup(n_atoms, k):
+    """Build the CPU oracle of the layer (reference algorithm restated) on a bounded sample and
+    return a closure running one forward + backward on all host threads."""
+    from oracle import attention_ref as R
+    from oracle import graph_ref
+    from ubio_molfm_b200.graph import pbc_image_offsets
+    from ubio_molfm_b200.nn import GaussianSmearing, polynomial
+    from ubio_molfm_b200.synthetic import uniform_box
+    from ubio_molfm_b200.wigner import node_wigner
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    pos, Z, cell = uniform_box(n_atoms, k, CUTOFF, seed=7)
+    pos = pos.astype(np.float32)
+    off = pbc_image_offsets(cell, [True] * 3, CUTOFF).numpy()
+    ia = graph_ref.pbc_expand(pos, off, CUTOFF)
+    outcell = ia % n_atoms
+    exp_pos = (pos[outcell] + off[ia // n_atoms]).astype(np.float32)
+    qi, ni, d = graph_ref.radius_graph(pos, exp_pos, [0, n_atoms], [0, len(exp_pos)], CUTOFF, 1e-4, None)
+    layer = make_layer("cpu")
+    p = {kk: v.detach() for kk, v in layer.state_dict().items()}
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(n_atoms, 9, C_CH, generator=g, requires_grad=True)
+    dout = torch.randn(n_atoms, 9, C_CH, generator=g)
+    Zt = torch.tensor(Z)
+
+    def run():
+        pos_t = torch.tensor(pos, requires_grad=True)
+        exp_t = torch.tensor(exp_pos, requires_grad=True)
+        dist = torch.tensor(d, requires_grad=True)
+        W, Wi = node_wigner(pos_t)
+        We, Wie = node_wigner(exp_t)
+        poly = polynomial(dist, CUTOFF)
+        rbf = GaussianSmearing(NB, cutoff=CUTOFF)(dist)
+        bd = {"query_idx": torch.tensor(qi), "neighbor_idx": torch.tensor(ni),
+              "f_outcell_index": torch.tensor(outcell), "f_exp_node_pos": exp_t, "wigner": W, "wigner_inv": Wi,
+              "wigner_exp": We, "wigner_inv_exp": Wie}
+        out = R.attention_layer(p, HEADS, DHEAD, pos_t, x, dist, rbf, Zt, poly, bd)
+        torch.autograd.grad(out, [x, pos_t, exp_t, dist], dout)
+
+    desc = (f"{n_atoms} atoms, {len(qi)} edges: 1 layer fwd+bwd of the CPU oracle (the reference's "
+            f"pure-PyTorch attention path restated), fp32")
+    return run, desc
+
+
+def run_cpu_baseline(n_atoms, k, steps=1, warmup=0):
+    run, desc = cpu_baseline_setup(n_atoms, k)
+    for _ in range(warmup):
+        run()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{desc}; median of {steps} steps, {t:.2f} s/step", "cpu_model": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------------------------------------
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    cb = run_cpu_baseline(args.cpu_atoms, args.k, args.steps, min(args.warmup, 1))
+    v = cb["value"]
+    line = {"impl": "reference", "metric": "atom-steps/s", "value": v, "unit": "atom-steps/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.cpu_atoms / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform periodic box, seeded random weights)",
+            "config": config_dict(args, extra={"reference_sample_atoms": args.cpu_atoms}),
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args, ws, rank, local):
+    from ubio_molfm_b200 import ops
+    from ubio_molfm_b200.synthetic import uniform_box
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    layer = make_layer(dev)
+    pos_np, Z_np, cell = uniform_box(args.atoms, args.k, CUTOFF, seed=100 + rank)
+    pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
+    Z = torch.tensor(Z_np, device=dev)
+    bd, rbf = build_inputs(pos, Z, cell, dev, layer)
+    N, N2, E = args.atoms, bd["f_outcell_index"].shape[0], bd["query_idx"].numel()
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(N, 9, C_CH, device=dev, generator=g)
+    dout = torch.randn(N, 9, C_CH, device=dev, generator=g)
+    # leaves: everything the forces chain differentiates through
+    leaf = {k: v.detach().requires_grad_(True) for k, v in
+            {"x": x, "pos": pos, "f_dist": bd["f_dist"], "poly": bd["f_poly_dist"], "rbf": rbf,
+             "exp": bd["f_exp_node_pos"], "W": bd["wigner"], "Wi": bd["wigner_inv"], "We": bd["wigner_exp"],
+             "Wie": bd["wigner_inv_exp"]}.items()}
+    bdl = dict(bd)
+    bdl.update({"f_dist": leaf["f_dist"], "f_poly_dist": leaf["poly"], "f_exp_node_pos": leaf["exp"],
+                "wigner": leaf["W"], "wigner_inv": leaf["Wi"], "wigner_exp": leaf["We"], "wigner_inv_exp": leaf["Wie"]})
+    leaves = list(leaf.values())
+
+    def step():
+        return layer_step(layer, leaf["pos"], leaf["x"], Z, bdl, leaf["rbf"], dout, leaves)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    ops.TIMER.enabled = True
+    ops.TIMER.events = {}
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    ops.TIMER.enabled = False
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms, ws, dev)
+    kern = ops.TIMER.summary()
+    launches = sum(v[0] for v in kern.values())
+    # dominant kernel of this package
+    top = max(kern.items(), key=lambda kv: kv[1][1])
+    name, (nl, tot) = top
+    alg = {"e2a_attn_fwd": fwd_algorithmic_bytes, "e2a_attn_bwd_query": bwdq_algorithmic_bytes,
+           "e2a_attn_bwd_key": bwdk_algorithmic_bytes}[name](N, N2, E)
+    per_launch_ms = tot / nl
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (per_launch_ms * 1e-3) / 1e9
+    roof = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+            "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
+            "kernels_ms_per_step": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
+            "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
+    value = ws * N * 1e3 / ms
+
+    # ---------------- e2e through the public API from pinned host buffers ----------------
+    e2e = None
+    if not args.no_e2e:
+        del leaf, bdl, leaves, bd, rbf
+        torch.cuda.empty_cache()
+        h_pos = torch.tensor(pos_np, dtype=torch.float32).pin_memory()
+        h_Z = torch.tensor(Z_np).pin_memory()
+        h_x = x.cpu().pin_memory()
+        h_dout = dout.cpu().pin_memory()
+        h_out = torch.empty((N, 9, C_CH), dtype=torch.float32).pin_memory()
+        h_dx = torch.empty_like(h_out).pin_memory()
+        h_dpos = torch.empty((N, 3), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            p = h_pos.to(dev, non_blocking=True).requires_grad_(True)
+            z = h_Z.to(dev, non_blocking=True)
+            xx = h_x.to(dev, non_blocking=True).requires_grad_(True)
+            do = h_dout.to(dev, non_blocking=True)
+            b, r = build_inputs(p, z, cell, dev, layer)
+            out, (gx, gp) = layer_step(layer, p, xx, z, b, r, do, [xx, p])
+            h_out.copy_(out.detach(), non_blocking=True)
+            h_dx.copy_(gx, non_blocking=True)
+            h_dpos.copy_(gp, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        ems = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
+        h2d = h_pos.numel() * 4 + h_Z.numel() * 8 + h_x.numel() * 4 + h_dout.numel() * 4
+        d2h = h_out.numel() * 4 + h_dx.numel() * 4 + h_dpos.numel() * 4
+        e2e = {"value": ws * N * 1e3 / ems, "unit": "atom-steps/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 3),
+               "includes": "H2D, PBC images, radius graph + CSR, Wigner, RBF, layer fwd+bwd, D2H"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = run_cpu_baseline(args.cpu_atoms, args.k, 1, 0)
+
+    if rank == 0:
+        line = {"metric": "atom-steps/s", "value": round(value, 1), "unit": "atom-steps/s", "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded uniform periodic box, seeded random weights)",
+                "config": config_dict(args, E, N2), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clk}
+        print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_init(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+    else:
+        run_ours(args, ws, rank, local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -13,6 +13,38 @@ from . import _lib
 from ._lib import check, ptr, require_cuda, stream_of
 
 
+class KernelTimer:
+    """Optional CUDA-event bracketing of the fused-attention launches (used by the benchmark).
+
+    Events are recorded on the current stream, the stream every kernel of this package runs on."""
+
+    def __init__(self):
+        self.enabled = False
+        self.events = {}
+
+    def start(self, name):
+        if not self.enabled:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return (name, ev)
+
+    def stop(self, tok):
+        if tok is None:
+            return
+        name, s = tok
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events.setdefault(name, []).append((s, e))
+
+    def summary(self):
+        """name -> (launches, total ms); call after synchronising."""
+        return {k: (len(v), sum(s.elapsed_time(e) for s, e in v)) for k, v in self.events.items()}
+
+
+TIMER = KernelTimer()
+
+
 def _i32(t):
     return t.contiguous().to(torch.int32)
 
@@ -280,9 +312,11 @@ class AttnSpanFn(torch.autograd.Function):
         beta = torch.empty((E, H), device=dev, dtype=torch.float32)
         rmax = torch.empty((N, H), device=dev, dtype=torch.float32)
         rsum = torch.empty((N, H), device=dev, dtype=torch.float32)
+        tok = TIMER.start("e2a_attn_fwd")
         check(lib.e2a_attn_fwd(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
                                ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
                                ptr(out), ptr(beta), ptr(rmax), ptr(rsum), stream_of(dev)), "e2a_attn_fwd")
+        TIMER.stop(tok)
         ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, *md)
         return out
 
@@ -302,15 +336,19 @@ class AttnSpanFn(torch.autograd.Function):
         d_dist = torch.empty(E, device=dev, dtype=torch.float32)
         d_logit = torch.empty((E, H), device=dev, dtype=torch.float32)
         ws = _workspace(lib.e2a_attn_bwd_workspace_bytes(E, H), dev)
+        tok = TIMER.start("e2a_attn_bwd_query")
         check(lib.e2a_attn_bwd_query(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
                                      ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
                                      ptr(beta), ptr(rmax), ptr(rsum), ptr(dout), ptr(d_q), ptr(d_gate),
                                      ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit), ptr(ws),
                                      ws.numel(), st), "e2a_attn_bwd_query")
+        TIMER.stop(tok)
         d_k = torch.empty_like(key)
         d_v = torch.empty_like(value)
+        tok = TIMER.start("e2a_attn_bwd_key")
         check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]),
                                    N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
+        TIMER.stop(tok)
         return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None
 
 
