@@ -174,6 +174,23 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
                      int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
                      float* d_k, float* d_value, void* stream);
 
+/* Same as e2a_attn_bwd_query, but allocates nothing and takes no workspace.  No counterpart in  */
+/* the reference: it serves callers that cannot allocate device memory when they run the        */
+/* backward (an operator plugin handed only its tensors, code that must not call cudaMalloc).    */
+/* Its scratch is a fixed 8 MiB array in the library's device memory, held by every GPU that     */
+/* loads the library until exit; n_edges * H above 2^20 returns E2A_ERR_WORKSPACE.  The first    */
+/* call on a device looks up that array's address, so make it before any stream capture.  All   */
+/* calls share the array: calls that overlap on the GPU race.                                    */
+int e2a_attn_bwd_query_noalloc(const float* q, const float* k, const float* value,
+                               const float* gate, const float* inputhead, int64_t ld_gi,
+                               const float* poly, const float* dist,
+                               const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
+                               int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                               const float* beta, const float* row_max, const float* row_sum,
+                               const float* dout, float* d_q, float* d_gate, float* d_inputhead,
+                               int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,8 @@ SIGNATURES = {
     "e2a_attn_bwd_workspace_bytes": (SZ, [I64, I32]),
     "e2a_attn_bwd_query": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                  P, P, P, P, P, P, P, I64, P, P, P, P, SZ, P]),
+    "e2a_attn_bwd_query_noalloc": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
+                                         P, P, P, P, P, P, P, I64, P, P, P, P]),
     "e2a_attn_bwd_key": (I32, [P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
 }
 

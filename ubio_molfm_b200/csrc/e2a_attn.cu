@@ -583,3 +583,69 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Query-side backward without any allocation (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory at the moment they call the backward: code running
+// inside a host framework whose allocator they do not own, plugins that are handed only the tensors
+// of one operator, or code paths that must not call cudaMalloc (which synchronises the device).
+// For them this variant keeps its scratch (two [E, H] fp32 buffers) in a fixed array in the
+// library's device memory instead of a caller workspace.
+//
+// Limits and behaviour:
+//  * the scratch holds kNoAllocScratchFloats floats (2 x 2^20 floats = 8 MiB); calls with
+//    n_edges * H > 2^20 are rejected with E2A_ERR_WORKSPACE;
+//  * every GPU that loads the library holds the 8 MiB array until the process exits;
+//  * the first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+//    that device current; make that first call before any stream capture;
+//  * all calls share the one array: calls whose execution overlaps on the GPU (different streams,
+//    or different host threads on one device) race and corrupt each other's results.  Nothing in the
+//    array needs to start at zero: every scratch element is written before it is read in a call.
+// ------------------------------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchFloats = (size_t)2 << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+}  // namespace
+
+extern "C" int e2a_attn_bwd_query_noalloc(
+    const float* q, const float* k, const float* value, const float* gate, const float* inputhead, int64_t ld_gi,
+    const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
+    int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C, const float* beta, const float* row_max,
+    const float* row_sum, const float* dout, float* d_q, float* d_gate, float* d_inputhead, int64_t ld_dgi,
+    float* d_poly, float* d_dist, float* d_logit, void* stream) {
+  Dims dm;
+  int ks;
+  int rc = check_dims(H, D, C, dm, ks);
+  if (rc) return rc;
+  if (n_rows < 0 || n_keys < 0 || n_edges < 0 || ld_gi < H || ld_dgi < H || n_edges > INT32_MAX) return E2A_ERR_ARG;
+  if ((size_t)n_edges * (size_t)H > kNoAllocScratchFloats / 2) return E2A_ERR_WORKSPACE;  // beyond the fixed scratch
+  if (n_rows == 0) return E2A_OK;
+  if (!q || !row_ptr || !d_q) return E2A_ERR_ARG;
+  if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta || !dout ||
+                      !d_gate || !d_inputhead || !d_poly || !d_dist || !d_logit))
+    return E2A_ERR_ARG;
+  int dev = 0;
+  E2A_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return E2A_ERR_UNSUPPORTED;
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    E2A_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  float* bufA = g_noalloc_ptr[dev];
+  float* bufB = bufA + kNoAllocScratchFloats / 2;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t smem = (size_t)kEB * kThreads * 16 + (size_t)dm.HD4 * 16 + (kThreads + 3 * H) * 4;
+  if ((size_t)kEB * kThreads < (size_t)kWarps * dm.HD4) return E2A_ERR_UNSUPPORTED;
+  E2A_DISPATCH_KS(ks, k_attn_bwd_query, {
+    E2A_CUDA(prep_smem(kf, smem));
+    kf<<<grid_for(n_rows), kThreads, smem, st>>>(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                 row_order, n_rows, dm, beta, row_max, row_sum, dout, d_q, d_gate,
+                                                 d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
+  });
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
