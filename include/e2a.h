@@ -144,7 +144,7 @@ int e2a_edge_outer_bwd(const float* grad_out, const float* sh, const float* fea,
 /* be NULL) is a processing order of the rows (a spatially coherent order improves L2 reuse of   */
 /* the gathered value rows); results do not depend on it.  Saves beta [E,H], row_max and row_sum */
 /* [N,H] for the backward.  Requires D % 4 == 0, D/4 a power of two <= 32, H dividing 256,      */
-/* H % 4 == 0 and (C*H) % 4 == 0.                                                                */
+/* H % 4 == 0, H*D <= 1024 and (C*H) % 4 == 0.                                                                */
 /* ------------------------------------------------------------------------------------------ */
 int e2a_attn_fwd(const float* q, const float* k, const float* value,
                  const float* gate, const float* inputhead, int64_t ld_gi,
@@ -169,10 +169,11 @@ int e2a_attn_bwd_query(const float* q, const float* k, const float* value,
                        void* workspace, size_t workspace_bytes, void* stream);
 /* Key-side backward over the key-CSR (k_row_ptr, k_col = query of each slot, k_perm = edge id):  */
 /* d_value[j,c,h] = sum_e beta[e,h] dout[i_e,c,h];  d_k[j,h,:] = sum_e d_logit[e,h] q[i_e,h,:].    */
+/* key_order (may be NULL) is a processing order of the key rows, like row_order above.          */
 int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const float* d_logit,
                      const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm,
-                     int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
-                     float* d_k, float* d_value, void* stream);
+                     const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,
+                     int H, int D, int C, float* d_k, float* d_value, void* stream);
 
 /* Same as e2a_attn_bwd_query, but allocates nothing and takes no workspace.  No counterpart in  */
 /* the reference: it serves callers that cannot allocate device memory when they run the        */

@@ -278,12 +278,13 @@ def test_attention_span_row_order_and_determinism():
     N, M, E, H, D, C = 200, 260, 6000, 128, 8, 58
     q, n = _random_graph(N, M, E, 11)
     order = _t(np.random.default_rng(3).permutation(N).astype(np.int32))
+    korder = _t(np.random.default_rng(4).permutation(M).astype(np.int32))
     ins = [a.to(DEV) for a in _span_inputs(N, M, q, n, H, D, C, 12)]
     md = ops.prepare_sparse_qk_edge_index_metadata(_t(q), _t(n), N, M)
     outs = []
-    for ro in (None, order, order):
+    for ro, ko in ((None, None), (order, korder), (order, korder)):
         a = [x.clone().requires_grad_(True) for x in ins]
-        o = ops.attention_span(*a, md, ro)
+        o = ops.attention_span(*a, md, ro, ko)
         gr = torch.autograd.grad(o, a, torch.ones_like(o))
         outs.append([o] + list(gr))
     for x, y in zip(outs[1], outs[2]):

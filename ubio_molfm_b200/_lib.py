@@ -49,7 +49,7 @@ SIGNATURES = {
                                  P, P, P, P, P, P, P, I64, P, P, P, P, SZ, P]),
     "e2a_attn_bwd_query_noalloc": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                          P, P, P, P, P, P, P, I64, P, P, P, P]),
-    "e2a_attn_bwd_key": (I32, [P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
+    "e2a_attn_bwd_key": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
 }
 
 _lib = None

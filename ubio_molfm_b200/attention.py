@@ -111,14 +111,15 @@ class E2AttentionArbOrder_sparse(nn.Module):
             qi = bd["query_idx"]
             bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
         if bd["query_sorted"]:
-            agg = attention_span(q_scaled, key, merged, gate, poly, edge_dis, metadata, bd.get("row_order"))
+            agg = attention_span(q_scaled, key, merged, gate, poly, edge_dis, metadata, bd.get("row_order"),
+                                 bd.get("key_order"))
         else:
             # permute the edges into query-CSR order (q_perm) so that edge id == CSR slot
             perm = metadata[2].to(torch.long)
             md = (metadata[0], metadata[1], torch.arange(perm.numel(), device=perm.device, dtype=torch.int32),
                   metadata[3], metadata[4], torch.argsort(perm)[metadata[5].to(torch.long)].to(torch.int32))
             agg = attention_span(q_scaled, key, merged, gate[perm], poly[perm], edge_dis[perm], md,
-                                 bd.get("row_order"))
+                                 bd.get("row_order"), bd.get("key_order"))
         agg = agg.reshape(N1, -1, C)
         h_b_agg, h_a = agg[:, :n_b], agg[:, n_b:]
         h_a = tp.node_half(bd["wigner"], bd["wigner_inv"], h_a, node_pos)

@@ -1,15 +1,21 @@
-// Fused sparse attention span of E2AttentionArbOrder_sparse (QK logits, segmented softmax with the
+// Sparse attention span of E2AttentionArbOrder_sparse (QK logits, segmented softmax with the
 // reference's non-standard eps/envelope, alpha/r, value aggregation) and its first-order backward.
 //
 // Layout (fp32, row-major): q [N,H,D] (already scaled by 1/sqrt(D)), k [M,H,D], value [M,C,H] (the
 // merged SO(2)+irreps message, head innermost), gate / inputhead [E,H] views (row stride ld_gi),
 // poly/dist [E].  Edges are in query-CSR order; edge id == CSR slot.
 //
-// One CTA (256 threads) owns one destination row.  The dominant cost is the gather of the value row
-// of every neighbour (C*H*4 bytes, 29.7 KB at the full config): each thread owns fixed float4 slots
-// of the [C,H] output tile, so every gathered row is read with fully coalesced 16-byte loads and
-// accumulated in registers; per-edge softmax weights are shared by the whole CTA.  All sums over
-// edges run in CSR order inside one CTA: results are deterministic and need no atomics.
+// Each C-ABI entry point launches a short pipeline of kernels of two kinds:
+//  * softmax kernels (one CTA per destination row): q.k logits with one warp per edge, then row
+//    reductions with one thread per head.  Few registers, so many CTAs stay resident and the latency
+//    of the row-sequential phases is hidden by occupancy.
+//  * row-aggregation kernels (one CTA per output row): out[r] = sum_p w[p] * X[col[p]] where every
+//    X row is a contiguous row (29.7 KB value / cotangent rows, 4 KB q / k rows).  Each thread owns
+//    fixed float4 slots of the row, so every gathered row is read with fully coalesced 16-byte loads
+//    and accumulated in registers; register use is bounded so that enough CTAs are resident to keep
+//    the gathers in flight.  Rows run in a spatially coherent (Morton) order so that concurrently
+//    running CTAs share their gathered rows in L2.
+// Every sum over edges runs in CSR order inside one CTA: deterministic, no atomics.
 #include "e2a_common.cuh"
 
 namespace {
@@ -18,6 +24,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr float kSoftmaxEps = 1e-3f;   // e2former.py:364
 constexpr float kMinDist = 1e-6f;      // e2former.py:422 clamp_min
+constexpr int kEB = 8;                 // edges per cross-thread reduction batch in the d(beta) kernel
 
 struct Dims {
   int H, D, C;
@@ -53,8 +60,7 @@ __device__ __forceinline__ void edge_scores(const float* __restrict__ q_s, const
 }
 
 __device__ __forceinline__ void stage_row(float* __restrict__ dst, const float* __restrict__ src, int n4) {
-  for (int f = threadIdx.x; f < n4; f += kThreads)
-    reinterpret_cast<float4*>(dst)[f] = ldg4(src + 4 * f);
+  for (int f = threadIdx.x; f < n4; f += kThreads) reinterpret_cast<float4*>(dst)[f] = ldg4(src + 4 * f);
 }
 
 // Combine per-stripe partials red[stripe*H + h] (fixed order) -> out_s[h].
@@ -69,17 +75,59 @@ __device__ __forceinline__ void combine_stripes(float* red, float* out_s, int H,
 }
 
 // ------------------------------------------------------------------------------------------------
-// Forward
+// CSR row aggregation: out[r, :] = sum_{p in row r} w[e_p, head(f)] * X[col[p], f]
+//   HEAD_INNER = true : rows are [C, H] (head = f % H, four heads per float4)
+//   HEAD_INNER = false: rows are [H, D] (head = f / D, one head per float4, D % 4 == 0)
+// e_p = perm[p] (or p).  One CTA per output row, launched over the rows in `order`.
 // ------------------------------------------------------------------------------------------------
-template <int KS>
+template <int KS, bool HEAD_INNER>
+__global__ void __launch_bounds__(kThreads, 3)
+k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D, int row_f4,
+          const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const int32_t* __restrict__ perm,
+          const int32_t* __restrict__ order, int64_t n_rows, float* __restrict__ out) {
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const int i = row_of(order, r);
+    const int rs = row_ptr[i], re = row_ptr[i + 1];
+    float4 acc[KS];
+#pragma unroll
+    for (int s = 0; s < KS; ++s) acc[s] = f4_zero();
+    const int h0 = HEAD_INNER ? (4 * threadIdx.x) % H : 0;
+    for (int p = rs; p < re; ++p) {
+      const int64_t e = perm ? perm[p] : p;
+      const float* xr = X + (int64_t)col[p] * row_f4 * 4;
+      if (HEAD_INNER) {
+        const float4 b = ldg4(w + e * H + h0);
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const int f = threadIdx.x + s * kThreads;
+          if (f < row_f4) acc[s] = f4_fma4(b, ldg4(xr + 4 * f), acc[s]);
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const int f = threadIdx.x + s * kThreads;
+          if (f < row_f4) acc[s] = f4_fma(__ldg(w + e * H + (4 * f) / D), ldg4(xr + 4 * f), acc[s]);
+        }
+      }
+    }
+    float* orow = out + (int64_t)i * row_f4 * 4;
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int f = threadIdx.x + s * kThreads;
+      if (f < row_f4) reinterpret_cast<float4*>(orow)[f] = acc[s];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Forward softmax: beta[e,h] = exp(g s - m) poly ih / (S + eps) / max(d, 1e-6), plus row stats
+// ------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
-k_attn_fwd(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ value,
-           const float* __restrict__ gate, const float* __restrict__ inputhead, int64_t ld_gi,
-           const float* __restrict__ poly, const float* __restrict__ dist,
-           const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
-           const int32_t* __restrict__ order, int64_t n_rows, Dims dm,
-           float* __restrict__ out, float* __restrict__ beta, float* __restrict__ row_max,
-           float* __restrict__ row_sum) {
+k_softmax_fwd(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
+              const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
+              const float* __restrict__ dist, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
+              const int32_t* __restrict__ order, int64_t n_rows, Dims dm, float* __restrict__ beta,
+              float* __restrict__ row_max, float* __restrict__ row_sum) {
   extern __shared__ float4 smem4[];
   float* q_s = reinterpret_cast<float*>(smem4);      // H*D
   float* red = q_s + dm.HD4 * 4;                     // kThreads
@@ -88,7 +136,6 @@ k_attn_fwd(const float* __restrict__ q, const float* __restrict__ k, const float
   const int H = dm.H;
   const int stripes = kThreads / H;
   const int hh = threadIdx.x % H, stripe = threadIdx.x / H;
-
   for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
     const int i = row_of(order, r);
     const int rs = row_ptr[i], re = row_ptr[i + 1];
@@ -127,131 +174,93 @@ k_attn_fwd(const float* __restrict__ q, const float* __restrict__ k, const float
       row_sum[(int64_t)i * H + hh] = sum_s[hh];
     }
     __syncthreads();
-    // 5. out[i,c,h] = sum_e beta[e,h] value[j,c,h]
-    const int h0 = (4 * threadIdx.x) % H;
-    float4 acc[KS];
-#pragma unroll
-    for (int s = 0; s < KS; ++s) acc[s] = f4_zero();
-    int e = rs;
-    for (; e + 1 < re; e += 2) {
-      const float* v0 = value + (int64_t)col[e] * dm.CH4 * 4;
-      const float* v1 = value + (int64_t)col[e + 1] * dm.CH4 * 4;
-      const float4 b0 = *reinterpret_cast<const float4*>(beta + (int64_t)e * H + h0);
-      const float4 b1 = *reinterpret_cast<const float4*>(beta + (int64_t)(e + 1) * H + h0);
-      float4 x0[KS], x1[KS];
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) { x0[s] = ldg4(v0 + 4 * f); x1[s] = ldg4(v1 + 4 * f); }
-      }
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) acc[s] = f4_fma4(b1, x1[s], f4_fma4(b0, x0[s], acc[s]));
-      }
-    }
-    if (e < re) {
-      const float* v0 = value + (int64_t)col[e] * dm.CH4 * 4;
-      const float4 b0 = *reinterpret_cast<const float4*>(beta + (int64_t)e * H + h0);
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) acc[s] = f4_fma4(b0, ldg4(v0 + 4 * f), acc[s]);
-      }
-    }
-    float* orow = out + (int64_t)i * dm.CH4 * 4;
-#pragma unroll
-    for (int s = 0; s < KS; ++s) {
-      const int f = threadIdx.x + s * kThreads;
-      if (f < dm.CH4) reinterpret_cast<float4*>(orow)[f] = acc[s];
-    }
-    __syncthreads();
   }
 }
 
 // ------------------------------------------------------------------------------------------------
-// Backward, query side
+// Backward: d(beta)[e,h] = sum_c dout[i,c,h] value[j,c,h]  (gather kernel, one CTA per row)
 // ------------------------------------------------------------------------------------------------
-constexpr int kEB = 8;  // edges per reduction batch in the d(beta) pass
-
 template <int KS>
-__global__ void __launch_bounds__(kThreads)
-k_attn_bwd_query(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ value,
-                 const float* __restrict__ gate, const float* __restrict__ inputhead, int64_t ld_gi,
-                 const float* __restrict__ poly, const float* __restrict__ dist,
-                 const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
-                 const int32_t* __restrict__ order, int64_t n_rows, Dims dm,
-                 const float* __restrict__ beta, const float* __restrict__ row_max,
-                 const float* __restrict__ row_sum, const float* __restrict__ dout,
-                 float* __restrict__ d_q, float* __restrict__ d_gate, float* __restrict__ d_inputhead,
-                 int64_t ld_dgi, float* __restrict__ d_poly, float* __restrict__ d_dist,
-                 float* __restrict__ d_logit, float* __restrict__ bufA, float* __restrict__ bufB) {
+__global__ void __launch_bounds__(kThreads, 2)
+k_dbeta(const float* __restrict__ value, const float* __restrict__ dout, const int32_t* __restrict__ row_ptr,
+        const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows, Dims dm,
+        float* __restrict__ dbeta) {
   extern __shared__ float4 smem4[];
-  float4* red4 = smem4;                                         // kEB * kThreads float4
-  float* q_s = reinterpret_cast<float*>(red4 + kEB * kThreads); // H*D
-  float* red = q_s + dm.HD4 * 4;                                // kThreads
-  float* T_s = red + kThreads;                                  // H
-  float* dm_s = T_s + dm.H;                                     // H
-  float* nt_s = dm_s + dm.H;                                    // H
-  const int H = dm.H;
-  const int H4 = H / 4;
-  const int stripes = kThreads / H;
-  const int hh = threadIdx.x % H, stripe = threadIdx.x / H;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
+  float4* red4 = smem4;  // kEB * kThreads
+  const int H = dm.H, H4 = H / 4;
   for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
     const int i = row_of(order, r);
     const int rs = row_ptr[i], re = row_ptr[i + 1];
-    if (rs == re) {  // isolated query: only d_q (zero) to write
-      for (int f = threadIdx.x; f < dm.HD4 * 4; f += kThreads) d_q[(int64_t)i * dm.HD4 * 4 + f] = 0.f;
-      continue;
+    float4 go[KS];
+    const float* gr = dout + (int64_t)i * dm.CH4 * 4;
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int f = threadIdx.x + s * kThreads;
+      go[s] = f < dm.CH4 ? ldg4(gr + 4 * f) : f4_zero();
     }
+    for (int e0 = rs; e0 < re; e0 += kEB) {
+      const int ne = min(kEB, re - e0);
+      for (int b = 0; b < ne; ++b) {
+        float4 p = f4_zero();
+        const float* vr = value + (int64_t)col[e0 + b] * dm.CH4 * 4;
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const int f = threadIdx.x + s * kThreads;
+          if (f < dm.CH4) p = f4_fma4(go[s], ldg4(vr + 4 * f), p);
+        }
+        red4[b * kThreads + threadIdx.x] = p;
+      }
+      __syncthreads();
+      // threads sharing head group t % H4 hold partial sums of the same four heads
+      for (int o = threadIdx.x; o < ne * H4; o += kThreads) {
+        const int b = o / H4, hg = o % H4;
+        float4 a = f4_zero();
+        for (int t = hg; t < kThreads; t += H4) {
+          const float4 v = red4[b * kThreads + t];
+          a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+        }
+        *reinterpret_cast<float4*>(dbeta + (int64_t)(e0 + b) * H + 4 * hg) = a;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Backward softmax: from d(beta) (bufA) to d_gate, d_inputhead, d_poly, d_dist and ds = d_logit
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads)
+k_softmax_bwd(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
+              const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
+              const float* __restrict__ dist, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
+              const int32_t* __restrict__ order, int64_t n_rows, Dims dm, const float* __restrict__ beta,
+              const float* __restrict__ row_max, const float* __restrict__ row_sum, float* __restrict__ d_gate,
+              float* __restrict__ d_inputhead, int64_t ld_dgi, float* __restrict__ d_poly,
+              float* __restrict__ d_dist, float* __restrict__ d_logit, const float* __restrict__ bufA,
+              float* __restrict__ bufB) {
+  extern __shared__ float4 smem4[];
+  float* q_s = reinterpret_cast<float*>(smem4);  // H*D
+  float* red = q_s + dm.HD4 * 4;                 // kThreads
+  float* T_s = red + kThreads;                   // H
+  float* dm_s = T_s + dm.H;                      // H
+  float* nt_s = dm_s + dm.H;                     // H
+  const int H = dm.H;
+  const int stripes = kThreads / H;
+  const int hh = threadIdx.x % H, stripe = threadIdx.x / H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const int i = row_of(order, r);
+    const int rs = row_ptr[i], re = row_ptr[i + 1];
+    if (rs == re) continue;
     stage_row(q_s, q + (int64_t)i * dm.HD4 * 4, dm.HD4);
-    // 1. d(beta)[e,h] = sum_c dout[i,c,h] value[j,c,h]  -> bufA
-    {
-      float4 go[KS];
-      const float* gr = dout + (int64_t)i * dm.CH4 * 4;
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        go[s] = f < dm.CH4 ? ldg4(gr + 4 * f) : f4_zero();
-      }
-      for (int e0 = rs; e0 < re; e0 += kEB) {
-        const int ne = min(kEB, re - e0);
-#pragma unroll
-        for (int b = 0; b < kEB; ++b) {
-          float4 p = f4_zero();
-          if (b < ne) {
-            const float* vr = value + (int64_t)col[e0 + b] * dm.CH4 * 4;
-#pragma unroll
-            for (int s = 0; s < KS; ++s) {
-              const int f = threadIdx.x + s * kThreads;
-              if (f < dm.CH4) p = f4_fma4(go[s], ldg4(vr + 4 * f), p);
-            }
-          }
-          red4[b * kThreads + threadIdx.x] = p;
-        }
-        __syncthreads();
-        // thread t reduces edge b = t / H4... over all threads sharing head group t % H4
-        for (int o = threadIdx.x; o < ne * H4; o += kThreads) {
-          const int b = o / H4, hg = o % H4;
-          float4 a = f4_zero();
-          for (int t = hg; t < kThreads; t += H4) {
-            const float4 v = red4[b * kThreads + t];
-            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-          }
-          *reinterpret_cast<float4*>(bufA + (int64_t)(e0 + b) * H + 4 * hg) = a;
-        }
-        __syncthreads();
-      }
-    }
-    // 2. s = q.k -> bufB
+    __syncthreads();
+    // s = q.k -> bufB
     edge_scores(q_s, k, col, rs, re, dm, [&](int e, int h, float s) { bufB[(int64_t)e * H + h] = s; });
     __syncthreads();
     const float m = row_max[(int64_t)i * H + hh];
     const float S = row_sum[(int64_t)i * H + hh];
     const float den = S + kSoftmaxEps;
-    // 3. T_h = sum_e d_alpha * alpha
+    // T_h = sum_e d_alpha * alpha
     {
       float T = 0.f;
       for (int e = rs + stripe; e < re; e += stripes) {
@@ -266,7 +275,7 @@ k_attn_bwd_query(const float* __restrict__ q, const float* __restrict__ k, const
       combine_stripes(red, T_s, H, stripes, false);
     }
     const float dS = -T_s[hh] / den;
-    // 4. dz = dx * x; d_inputhead; accumulate dm and tie counts
+    // dz = dx * x; d_inputhead; accumulate dm and tie counts
     {
       float dmacc = 0.f, nt = 0.f;
       for (int e = rs + stripe; e < re; e += stripes) {
@@ -288,7 +297,7 @@ k_attn_bwd_query(const float* __restrict__ q, const float* __restrict__ k, const
       red[threadIdx.x] = nt;
       combine_stripes(red, nt_s, H, stripes, false);
     }
-    // 5. da = dz + [a == m] dm / n_ties;  d_gate = da * s;  d_logit = ds = da * gate
+    // da = dz + [a == m] dm / n_ties (PyTorch's amax rule); d_gate = da * s; d_logit = ds = da * gate
     {
       const float share = nt_s[hh] > 0.f ? dm_s[hh] / nt_s[hh] : 0.f;
       for (int e = rs + stripe; e < re; e += stripes) {
@@ -301,12 +310,10 @@ k_attn_bwd_query(const float* __restrict__ q, const float* __restrict__ k, const
         d_logit[o] = da * g;
       }
     }
-    // 6. per-edge sums over heads: d_dist = -sum_h dbeta * beta / r ; d_poly = sum_h dx * exp(a-m)
-    //    (T_s and the row stats are complete; one warp per edge, fixed shuffle order)
+    // per-edge sums over heads: d_dist = -sum_h dbeta * beta / r ; d_poly = sum_h dx * exp(a-m)
     for (int e = rs + warp; e < re; e += kWarps) {
       const float d = dist[e];
       const float rr = fmaxf(d, kMinDist);
-      const float p = poly[e];
       float sd = 0.f, sp = 0.f;
       for (int h = lane; h < H; h += 32) {
         const int64_t o = (int64_t)e * H + h;
@@ -325,128 +332,7 @@ k_attn_bwd_query(const float* __restrict__ q, const float* __restrict__ k, const
       if (lane == 0) {
         d_dist[e] = d >= kMinDist ? -sd / rr : 0.f;
         d_poly[e] = sp;
-        (void)p;
       }
-    }
-    __syncthreads();
-    // 7. d_q[i,h,:] = sum_e ds[e,h] k[j,h,:]   (warps take edges, fixed-order cross-warp sum)
-    {
-      constexpr int kMaxSlots = 8;  // H*D/4 <= 32 * 8 float4 per lane
-      float4 acc[kMaxSlots];
-#pragma unroll
-      for (int s = 0; s < kMaxSlots; ++s) acc[s] = f4_zero();
-      for (int e = rs + warp; e < re; e += kWarps) {
-        const float* kr = k + (int64_t)col[e] * dm.HD4 * 4;
-#pragma unroll
-        for (int s = 0; s < kMaxSlots; ++s) {
-          const int f = lane + 32 * s;
-          if (f < dm.HD4) {
-            const float w = d_logit[(int64_t)e * H + (4 * f) / dm.D];
-            acc[s] = f4_fma(w, ldg4(kr + 4 * f), acc[s]);
-          }
-        }
-      }
-      // cross-warp reduction through red4 (kEB*kThreads float4 >= kWarps * HD4)
-#pragma unroll
-      for (int s = 0; s < kMaxSlots; ++s) {
-        const int f = lane + 32 * s;
-        if (f < dm.HD4) red4[warp * dm.HD4 + f] = acc[s];
-      }
-      __syncthreads();
-      for (int f = threadIdx.x; f < dm.HD4; f += kThreads) {
-        float4 a = red4[f];
-        for (int w = 1; w < kWarps; ++w) {
-          const float4 v = red4[w * dm.HD4 + f];
-          a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-        }
-        reinterpret_cast<float4*>(d_q + (int64_t)i * dm.HD4 * 4)[f] = a;
-      }
-      __syncthreads();
-    }
-  }
-}
-
-// ------------------------------------------------------------------------------------------------
-// Backward, key side (key-CSR)
-// ------------------------------------------------------------------------------------------------
-template <int KS>
-__global__ void __launch_bounds__(kThreads)
-k_attn_bwd_key(const float* __restrict__ q, const float* __restrict__ dout, const float* __restrict__ beta,
-               const float* __restrict__ d_logit, const int32_t* __restrict__ k_row_ptr,
-               const int32_t* __restrict__ k_col, const int32_t* __restrict__ k_perm, int64_t n_keys, Dims dm,
-               float* __restrict__ d_k, float* __restrict__ d_value) {
-  extern __shared__ float4 smem4[];
-  const int H = dm.H;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t j = blockIdx.x; j < n_keys; j += gridDim.x) {
-    const int rs = k_row_ptr[j], re = k_row_ptr[j + 1];
-    // d_value[j] = sum_p beta[e_p] * dout[i_p]
-    const int h0 = (4 * threadIdx.x) % H;
-    float4 acc[KS];
-#pragma unroll
-    for (int s = 0; s < KS; ++s) acc[s] = f4_zero();
-    int p = rs;
-    for (; p + 1 < re; p += 2) {
-      const int e0 = k_perm[p], e1 = k_perm[p + 1];
-      const float* g0 = dout + (int64_t)k_col[p] * dm.CH4 * 4;
-      const float* g1 = dout + (int64_t)k_col[p + 1] * dm.CH4 * 4;
-      const float4 b0 = ldg4(beta + (int64_t)e0 * H + h0);
-      const float4 b1 = ldg4(beta + (int64_t)e1 * H + h0);
-      float4 x0[KS], x1[KS];
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) { x0[s] = ldg4(g0 + 4 * f); x1[s] = ldg4(g1 + 4 * f); }
-      }
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) acc[s] = f4_fma4(b1, x1[s], f4_fma4(b0, x0[s], acc[s]));
-      }
-    }
-    if (p < re) {
-      const int e0 = k_perm[p];
-      const float* g0 = dout + (int64_t)k_col[p] * dm.CH4 * 4;
-      const float4 b0 = ldg4(beta + (int64_t)e0 * H + h0);
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        const int f = threadIdx.x + s * kThreads;
-        if (f < dm.CH4) acc[s] = f4_fma4(b0, ldg4(g0 + 4 * f), acc[s]);
-      }
-    }
-    float* vrow = d_value + (int64_t)j * dm.CH4 * 4;
-#pragma unroll
-    for (int s = 0; s < KS; ++s) {
-      const int f = threadIdx.x + s * kThreads;
-      if (f < dm.CH4) reinterpret_cast<float4*>(vrow)[f] = acc[s];
-    }
-    // d_k[j,h,:] = sum_p ds[e_p,h] q[i_p,h,:]
-    constexpr int kMaxSlots = 8;
-    float4 kacc[kMaxSlots];
-#pragma unroll
-    for (int s = 0; s < kMaxSlots; ++s) kacc[s] = f4_zero();
-    for (int pp = rs + warp; pp < re; pp += kWarps) {
-      const int e = k_perm[pp];
-      const float* qr = q + (int64_t)k_col[pp] * dm.HD4 * 4;
-#pragma unroll
-      for (int s = 0; s < kMaxSlots; ++s) {
-        const int f = lane + 32 * s;
-        if (f < dm.HD4) kacc[s] = f4_fma(__ldg(d_logit + (int64_t)e * H + (4 * f) / dm.D), ldg4(qr + 4 * f), kacc[s]);
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < kMaxSlots; ++s) {
-      const int f = lane + 32 * s;
-      if (f < dm.HD4) smem4[warp * dm.HD4 + f] = kacc[s];
-    }
-    __syncthreads();
-    for (int f = threadIdx.x; f < dm.HD4; f += kThreads) {
-      float4 a = smem4[f];
-      for (int w = 1; w < kWarps; ++w) {
-        const float4 v = smem4[w * dm.HD4 + f];
-        a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-      }
-      reinterpret_cast<float4*>(d_k + (int64_t)j * dm.HD4 * 4)[f] = a;
     }
     __syncthreads();
   }
@@ -459,7 +345,7 @@ int check_dims(int H, int D, int C, Dims& dm, int& ks) {
   const int g = D / 4;
   if (g > 32 || (g & (g - 1))) return E2A_ERR_UNSUPPORTED;
   if ((C * H) % 4) return E2A_ERR_UNSUPPORTED;
-  if (H * D / 4 > 32 * 8) return E2A_ERR_UNSUPPORTED;
+  if (H * D / 4 > kThreads) return E2A_ERR_UNSUPPORTED;
   dm.H = H; dm.D = D; dm.C = C; dm.HD4 = H * D / 4; dm.CH4 = C * H / 4; dm.g = g;
   const int need = (dm.CH4 + kThreads - 1) / kThreads;
   if (need <= 1) ks = 1;
@@ -483,8 +369,6 @@ cudaError_t prep_smem(Kern kern, size_t smem) {
   return cudaSuccess;
 }
 
-}  // namespace
-
 #define E2A_DISPATCH_KS(ks, KERN, ...)                               \
   switch (ks) {                                                      \
     case 1: { auto kf = KERN<1>; __VA_ARGS__; break; }               \
@@ -493,6 +377,63 @@ cudaError_t prep_smem(Kern kern, size_t smem) {
     case 8: { auto kf = KERN<8>; __VA_ARGS__; break; }               \
     default: { auto kf = KERN<16>; __VA_ARGS__; break; }             \
   }
+
+template <int KS>
+void agg_ch(const float* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
+            const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
+  k_row_agg<KS, true><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
+                                                             n_rows, out);
+}
+
+// out rows = CSR aggregation of [C,H] rows (value / cotangent), weights w[E,H]
+int launch_agg_ch(const float* X, const float* w, const Dims& dm, int ks, const int32_t* row_ptr, const int32_t* col,
+                  const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
+  switch (ks) {
+    case 1: agg_ch<1>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 2: agg_ch<2>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 4: agg_ch<4>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 8: agg_ch<8>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    default: agg_ch<16>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+// out rows = CSR aggregation of [H,D] rows (q / k), weights w[E,H]; H*D/4 <= kThreads
+int launch_agg_hd(const float* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
+                  const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
+  k_row_agg<1, false><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.HD4, row_ptr, col, perm, order,
+                                                             n_rows, out);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+size_t softmax_smem(const Dims& dm, int extra_h) { return (size_t)dm.HD4 * 16 + (kThreads + extra_h * dm.H) * 4; }
+
+// Query-side backward with caller-provided scratch bufA/bufB ([E,H] each).
+int bwd_query_launch(const float* q, const float* k, const float* value, const float* gate, const float* inputhead,
+                     int64_t ld_gi, const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                     const int32_t* row_order, int64_t n_rows, const Dims& dm, int ks, const float* beta,
+                     const float* row_max, const float* row_sum, const float* dout, float* d_q, float* d_gate,
+                     float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit, float* bufA,
+                     float* bufB, cudaStream_t st) {
+  const size_t dsm = (size_t)kEB * kThreads * 16;
+  E2A_DISPATCH_KS(ks, k_dbeta, {
+    E2A_CUDA(prep_smem(kf, dsm));
+    kf<<<grid_for(n_rows), kThreads, dsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA);
+  });
+  E2A_CHECK_LAUNCH();
+  const size_t ssm = softmax_smem(dm, 3);
+  E2A_CUDA(prep_smem(k_softmax_bwd, ssm));
+  k_softmax_bwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                         row_order, n_rows, dm, beta, row_max, row_sum, d_gate,
+                                                         d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
+  E2A_CHECK_LAUNCH();
+  // d_q[i] = sum_e ds[e] k[j]  (isolated rows get zeros from the empty sum)
+  return launch_agg_hd(k, d_logit, dm, row_ptr, col, nullptr, row_order, n_rows, d_q, st);
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -509,14 +450,12 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value, const float
   if (!q || !row_ptr || !out || !row_max || !row_sum) return E2A_ERR_ARG;
   if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t smem = (size_t)dm.HD4 * 16 + (kThreads + 2 * H) * 4;
-  E2A_DISPATCH_KS(ks, k_attn_fwd, {
-    E2A_CUDA(prep_smem(kf, smem));
-    kf<<<grid_for(n_rows), kThreads, smem, st>>>(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                                 row_order, n_rows, dm, out, beta, row_max, row_sum);
-  });
+  const size_t ssm = softmax_smem(dm, 2);
+  E2A_CUDA(prep_smem(k_softmax_fwd, ssm));
+  k_softmax_fwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                         row_order, n_rows, dm, beta, row_max, row_sum);
   E2A_CHECK_LAUNCH();
-  return E2A_OK;
+  return launch_agg_ch(value, beta, dm, ks, row_ptr, col, nullptr, row_order, n_rows, out, st);
 }
 
 size_t e2a_attn_bwd_workspace_bytes(int64_t n_edges, int H) {
@@ -541,27 +480,19 @@ int e2a_attn_bwd_query(const float* q, const float* k, const float* value, const
                       !d_gate || !d_inputhead || !d_poly || !d_dist || !d_logit))
     return E2A_ERR_ARG;
   if (workspace_bytes < e2a_attn_bwd_workspace_bytes(n_edges, H)) return E2A_ERR_WORKSPACE;
-  cudaStream_t st = (cudaStream_t)stream;
   E2aArena ar{(char*)workspace, workspace_bytes, 0};
   const size_t half = (size_t)(n_edges > 0 ? n_edges : 1) * H * 4;
   float* bufA = (float*)ar.take(half);
   float* bufB = (float*)ar.take(half);
   if (!bufA || !bufB) return E2A_ERR_WORKSPACE;
-  const size_t smem = (size_t)kEB * kThreads * 16 + (size_t)dm.HD4 * 16 + (kThreads + 3 * H) * 4;
-  if ((size_t)kEB * kThreads < (size_t)kWarps * dm.HD4) return E2A_ERR_UNSUPPORTED;
-  E2A_DISPATCH_KS(ks, k_attn_bwd_query, {
-    E2A_CUDA(prep_smem(kf, smem));
-    kf<<<grid_for(n_rows), kThreads, smem, st>>>(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                                 row_order, n_rows, dm, beta, row_max, row_sum, dout, d_q, d_gate,
-                                                 d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
-  });
-  E2A_CHECK_LAUNCH();
-  return E2A_OK;
+  return bwd_query_launch(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm, ks,
+                          beta, row_max, row_sum, dout, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,
+                          bufA, bufB, (cudaStream_t)stream);
 }
 
 int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const float* d_logit,
-                     const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm, int64_t n_rows,
-                     int64_t n_keys, int64_t n_edges, int H, int D, int C, float* d_k, float* d_value,
+                     const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm, const int32_t* key_order,
+                     int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C, float* d_k, float* d_value,
                      void* stream) {
   Dims dm;
   int ks;
@@ -572,14 +503,9 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
   if (!k_row_ptr || !d_k || !d_value) return E2A_ERR_ARG;
   if (n_edges > 0 && (!q || !dout || !beta || !d_logit || !k_col || !k_perm)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t smem = (size_t)kWarps * dm.HD4 * 16;
-  E2A_DISPATCH_KS(ks, k_attn_bwd_key, {
-    E2A_CUDA(prep_smem(kf, smem));
-    kf<<<grid_for(n_keys), kThreads, smem, st>>>(q, dout, beta, d_logit, k_row_ptr, k_col, k_perm, n_keys, dm, d_k,
-                                                 d_value);
-  });
-  E2A_CHECK_LAUNCH();
-  return E2A_OK;
+  rc = launch_agg_ch(dout, beta, dm, ks, k_row_ptr, k_col, k_perm, key_order, n_keys, d_value, st);
+  if (rc) return rc;
+  return launch_agg_hd(q, d_logit, dm, k_row_ptr, k_col, k_perm, key_order, n_keys, d_k, st);
 }
 
 }  // extern "C"
@@ -637,15 +563,7 @@ extern "C" int e2a_attn_bwd_query_noalloc(
   }
   float* bufA = g_noalloc_ptr[dev];
   float* bufB = bufA + kNoAllocScratchFloats / 2;
-  cudaStream_t st = (cudaStream_t)stream;
-  const size_t smem = (size_t)kEB * kThreads * 16 + (size_t)dm.HD4 * 16 + (kThreads + 3 * H) * 4;
-  if ((size_t)kEB * kThreads < (size_t)kWarps * dm.HD4) return E2A_ERR_UNSUPPORTED;
-  E2A_DISPATCH_KS(ks, k_attn_bwd_query, {
-    E2A_CUDA(prep_smem(kf, smem));
-    kf<<<grid_for(n_rows), kThreads, smem, st>>>(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                                 row_order, n_rows, dm, beta, row_max, row_sum, dout, d_q, d_gate,
-                                                 d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
-  });
-  E2A_CHECK_LAUNCH();
-  return E2A_OK;
+  return bwd_query_launch(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm, ks,
+                          beta, row_max, row_sum, dout, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,
+                          bufA, bufB, (cudaStream_t)stream);
 }

@@ -186,6 +186,7 @@ def radius_graph(pos, pts, q_ptr, p_ptr, max_dist, min_dist=-1.0, max_neighbors=
         "f_dist": dist,
         "f_poly_dist": poly,
         "row_order": morton_row_order(pos, max(float(max_dist), 1e-3)),
+        "key_order": morton_row_order(pts, max(float(max_dist), 1e-3)),
         "query_sorted": True,
     }
 

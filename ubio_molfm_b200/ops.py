@@ -298,7 +298,7 @@ class AttnSpanFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order):
+    def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order, key_order):
         lib = _lib.load()
         q, key, value = _f32(q), _f32(key), _f32(value)
         edge_gate, poly, dist = _f32(edge_gate), _f32(poly), _f32(dist)
@@ -317,12 +317,12 @@ class AttnSpanFn(torch.autograd.Function):
                                ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
                                ptr(out), ptr(beta), ptr(rmax), ptr(rsum), stream_of(dev)), "e2a_attn_fwd")
         TIMER.stop(tok)
-        ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, *md)
+        ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, key_order, *md)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, *md = ctx.saved_tensors
+        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, key_order, *md = ctx.saved_tensors
         lib = _lib.load()
         dout = _f32(dout)
         N, H, D = q.shape
@@ -347,15 +347,16 @@ class AttnSpanFn(torch.autograd.Function):
         d_v = torch.empty_like(value)
         tok = TIMER.start("e2a_attn_bwd_key")
         check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]),
-                                   N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
+                                   ptr(key_order), N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
         TIMER.stop(tok)
-        return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None
+        return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None
 
 
-def attention_span(q_scaled, key, value, edge_gate, poly, dist, metadata, row_order=None):
+def attention_span(q_scaled, key, value, edge_gate, poly, dist, metadata, row_order=None, key_order=None):
     """Fused attention span (see :class:`AttnSpanFn`); ``metadata`` is the 6-tuple CSR of a
     query-sorted edge list (identity query permutation)."""
     require_cuda(q_scaled, key, value, edge_gate, poly, dist)
     md = _check_md(metadata)
     ro = None if row_order is None else _i32(row_order)
-    return AttnSpanFn.apply(q_scaled, key, value, edge_gate, poly, dist, md, ro)
+    ko = None if key_order is None else _i32(key_order)
+    return AttnSpanFn.apply(q_scaled, key, value, edge_gate, poly, dist, md, ro, ko)
