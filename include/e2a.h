@@ -175,6 +175,21 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
                      const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,
                      int H, int D, int C, float* d_k, float* d_value, void* stream);
 
+/* ------------------------------------------------------------------------------------------ */
+/* Dense fp32 projection on tcgen05 tensor cores: C[M,N] = A[M,K] B[N,K]^T (+bias[N]) (+C when  */
+/* accumulate != 0); A, B row-major (K contiguous, leading dims lda/ldb >= K), C leading dim     */
+/* ldc >= N.  passes = 3 splits every operand into tf32 hi + lo parts and accumulates           */
+/* hi*hi + hi*lo + lo*hi (fp32-level accuracy); passes = 1 is plain TF32.  Replaces the         */
+/* nn.Linear / einsum products of SO3_Linear_e2former (module_utils.py:2035-2052),              */
+/* SO3_Linear2Scalar_e2former (2240-2274), RadialProfile (2151-2178) and forward_linear          */
+/* (so2_tensor_product.py:273-290).                                                             */
+/* ------------------------------------------------------------------------------------------ */
+int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                    const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes,
+                    void* stream);
+/* Status bits of the GEMM's bounded waits (1 = a wait timed out); copies and optionally clears. */
+int e2a_gemm_status(unsigned int* status, int reset, void* stream);
+
 /* Same as e2a_attn_bwd_query, but allocates nothing and takes no workspace.  No counterpart in  */
 /* the reference: it serves callers that cannot allocate device memory when they run the        */
 /* backward (an operator plugin handed only its tensors, code that must not call cudaMalloc).    */

@@ -1,0 +1,50 @@
+"""tcgen05 3xTF32 GEMM through the C ABI against a float64 product."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 200, 70), (1000, 512, 256), (4099, 1024, 1536),
+                                   (7, 3, 5), (129, 130, 0), (256, 128, 1)])
+def test_gemm_tf32x3_matches_fp64(M, N, K):
+    from ubio_molfm_b200._lib import device_status_gemm
+    from ubio_molfm_b200.linear import gemm
+
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = torch.randn(M, K, device="cuda", generator=g)
+    b = torch.randn(N, K, device="cuda", generator=g)
+    bias = torch.randn(N, device="cuda", generator=g)
+    ref = a.double() @ b.double().t() + bias.double()
+    out = gemm(a, b, bias)
+    scale = max(1.0, (K ** 0.5))
+    err = (out.double() - ref).abs().max().item() / scale
+    # fp32-level: within 4x the error of torch's fp32 SIMT product (plus an absolute floor)
+    err32 = ((a @ b.t() + bias).double() - ref).abs().max().item() / scale
+    assert err < 4 * err32 + 2e-6, (err, err32)
+    out1 = gemm(a, b, bias, passes=1)
+    assert (out1.double() - ref).abs().max().item() <= 2e-3 * max(1.0, ref.abs().max().item())  # plain TF32
+    acc = out.clone()
+    gemm(a, b, None, out=acc, accumulate=True)
+    assert (acc.double() - (2 * ref - bias.double())).abs().max().item() / scale < 8 * err32 + 4e-6
+    assert device_status_gemm() == 0
+
+
+def test_gemm_strided_operands_and_linear_grad():
+    from ubio_molfm_b200.linear import gemm, linear
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    big = torch.randn(500, 96, device="cuda", generator=g)
+    a = big[:, 10:74]            # lda = 96, not 16-byte aligned start -> scalar load path
+    w = torch.randn(40, 64, device="cuda", generator=g)
+    ref = a.double() @ w.double().t()
+    assert (gemm(a, w).double() - ref).abs().max().item() < 2e-5
+    x = torch.randn(3, 70, 64, device="cuda", generator=g, requires_grad=True)
+    b = torch.randn(40, device="cuda", generator=g)
+    y = linear(x, w, b)
+    yr = torch.nn.functional.linear(x.double(), w.double(), b.double())
+    assert (y.double() - yr).abs().max().item() < 2e-5
+    gy = torch.randn_like(y)
+    (gx,) = torch.autograd.grad(y, x, gy)
+    (gxr,) = torch.autograd.grad(yr, x, gy.double())
+    assert (gx.double() - gxr).abs().max().item() < 2e-5

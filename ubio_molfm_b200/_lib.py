@@ -47,6 +47,8 @@ SIGNATURES = {
     "e2a_attn_bwd_workspace_bytes": (SZ, [I64, I32]),
     "e2a_attn_bwd_query": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                  P, P, P, P, P, P, P, I64, P, P, P, P, SZ, P]),
+    "e2a_gemm_tf32x3": (I32, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, I32, P]),
+    "e2a_gemm_status": (I32, [P, I32, P]),
     "e2a_attn_bwd_query_noalloc": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                          P, P, P, P, P, P, P, I64, P, P, P, P]),
     "e2a_attn_bwd_key": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
@@ -82,6 +84,14 @@ def check(status: int, what: str):
         msg = lib.e2a_status_string(status).decode()
         cuda = lib.e2a_last_cuda_error()
         raise E2AError(f"{what} failed: {msg} (status {status}, cudaError {cuda})")
+
+
+def device_status_gemm(device=None, reset=True):
+    """Status bits of the GEMM kernel's bounded waits (0 = nothing happened)."""
+    lib = load()
+    v = ctypes.c_uint(0)
+    check(lib.e2a_gemm_status(ctypes.byref(v), 1 if reset else 0, stream_of(device)), "e2a_gemm_status")
+    return int(v.value)
 
 
 def ptr(t):

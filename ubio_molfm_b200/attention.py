@@ -20,7 +20,7 @@ import torch
 from torch import nn
 
 from .nn import (E2TensorProductSO2_FirstOrder, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
-                 irreps_channels_lmax, parse_irreps)
+                 irreps_channels_lmax, lin, parse_irreps)
 from .ops import attention_span
 
 
@@ -75,9 +75,10 @@ class E2AttentionArbOrder_sparse(nn.Module):
         s_tab = self.source_embedding.weight @ w[:, nb + e:].t()            # [types, h]
         z_q = atomic_numbers[query_idx]
         z_k = atomic_numbers[f_outcell_index][neighbor_idx]
-        h = torch.addmm(lin0.bias, attn_weight, w[:, :nb].t()) + t_tab[z_q] + s_tab[z_k]
+        cw = not self.training
+        h = lin(attn_weight, w[:, :nb], lin0.bias, cw) + t_tab[z_q] + s_tab[z_k]
         for layer in list(net)[1:]:
-            h = layer(h)
+            h = lin(h, layer.weight, layer.bias, cw) if isinstance(layer, nn.Linear) else layer(h)
         return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
 
     def forward(self, node_pos, node_irreps_input, edge_dis, edge_vec, attn_weight, atomic_numbers,

@@ -226,6 +226,47 @@ k_dbeta(const float* __restrict__ value, const float* __restrict__ dout, const i
   }
 }
 
+// Same d(beta), one warp per edge: the destination cotangent row is staged once in shared memory and
+// lane l owns head group l % (H/4) of rows c = l / (H/4) (mod 32 / (H/4)): no cross-warp reduction.
+// Requires H/4 to divide 32.
+__global__ void __launch_bounds__(kThreads)
+k_dbeta_warp(const float* __restrict__ value, const float* __restrict__ dout, const int32_t* __restrict__ row_ptr,
+             const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows, Dims dm,
+             float* __restrict__ dbeta) {
+  extern __shared__ float4 smem4[];
+  float4* go_s = smem4;  // CH4
+  const int H4 = dm.H / 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int hg = lane % H4, csub = lane / H4, cstep = 32 / H4;
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const int i = row_of(order, r);
+    const int rs = row_ptr[i], re = row_ptr[i + 1];
+    stage_row(reinterpret_cast<float*>(go_s), dout + (int64_t)i * dm.CH4 * 4, dm.CH4);
+    __syncthreads();
+    for (int e = rs + warp; e < re; e += kWarps) {
+      const float4* vr = reinterpret_cast<const float4*>(value + (int64_t)col[e] * dm.CH4 * 4);
+      float4 a0 = f4_zero(), a1 = f4_zero();
+      int c = csub;
+#pragma unroll 4
+      for (; c + cstep < dm.C; c += 2 * cstep) {
+        const int f0 = c * H4 + hg, f1 = (c + cstep) * H4 + hg;
+        a0 = f4_fma4(go_s[f0], __ldg(vr + f0), a0);
+        a1 = f4_fma4(go_s[f1], __ldg(vr + f1), a1);
+      }
+      if (c < dm.C) a0 = f4_fma4(go_s[c * H4 + hg], __ldg(vr + c * H4 + hg), a0);
+      a0.x += a1.x; a0.y += a1.y; a0.z += a1.z; a0.w += a1.w;
+      for (int o = H4; o < 32; o <<= 1) {
+        a0.x += __shfl_xor_sync(0xffffffffu, a0.x, o);
+        a0.y += __shfl_xor_sync(0xffffffffu, a0.y, o);
+        a0.z += __shfl_xor_sync(0xffffffffu, a0.z, o);
+        a0.w += __shfl_xor_sync(0xffffffffu, a0.w, o);
+      }
+      if (csub == 0) *reinterpret_cast<float4*>(dbeta + (int64_t)e * dm.H + 4 * hg) = a0;
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // Backward softmax: from d(beta) (bufA) to d_gate, d_inputhead, d_poly, d_dist and ds = d_logit
 // ------------------------------------------------------------------------------------------------
@@ -417,11 +458,17 @@ int bwd_query_launch(const float* q, const float* k, const float* value, const f
                      const float* row_max, const float* row_sum, const float* dout, float* d_q, float* d_gate,
                      float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit, float* bufA,
                      float* bufB, cudaStream_t st) {
-  const size_t dsm = (size_t)kEB * kThreads * 16;
-  E2A_DISPATCH_KS(ks, k_dbeta, {
-    E2A_CUDA(prep_smem(kf, dsm));
-    kf<<<grid_for(n_rows), kThreads, dsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA);
-  });
+  if (32 % (dm.H / 4) == 0) {
+    const size_t wsm = (size_t)dm.CH4 * 16;
+    E2A_CUDA(prep_smem(k_dbeta_warp, wsm));
+    k_dbeta_warp<<<grid_for(n_rows), kThreads, wsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA);
+  } else {
+    const size_t dsm = (size_t)kEB * kThreads * 16;
+    E2A_DISPATCH_KS(ks, k_dbeta, {
+      E2A_CUDA(prep_smem(kf, dsm));
+      kf<<<grid_for(n_rows), kThreads, dsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA);
+    });
+  }
   E2A_CHECK_LAUNCH();
   const size_t ssm = softmax_smem(dm, 3);
   E2A_CUDA(prep_smem(k_softmax_bwd, ssm));

@@ -66,3 +66,57 @@ __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpre
 __device__ __forceinline__ float e2a_norm3(float x, float y, float z) {
   return __fsqrt_rn(__fmaf_rn(z, z, __fmaf_rn(y, y, __fmul_rn(x, x))));
 }
+
+// ------------------------------------------------------------------------------------------------
+// mbarrier / async-proxy primitives.  Every wait is bounded in time.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e2a_smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void e2a_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(e2a_smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void e2a_fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// orders this thread's (and, after a barrier, the block's) generic shared-memory accesses before
+// later async-proxy accesses (tensor-core operand reads, bulk copies)
+__device__ __forceinline__ void e2a_fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ bool e2a_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(e2a_smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t e2a_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+#define E2A_DEV_WAIT_TIMEOUT 1u
+
+// Wait for phase `parity` of `bar`, giving up after ~2 s (then sets E2A_DEV_WAIT_TIMEOUT in
+// *status); returns false on timeout.
+__device__ __forceinline__ bool e2a_mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* status) {
+  if (e2a_mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = e2a_globaltimer();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    if (e2a_mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u && e2a_globaltimer() - t0 > 2000000000ull) break;
+  }
+  atomicOr(status, E2A_DEV_WAIT_TIMEOUT);
+  return false;
+}

@@ -1,0 +1,502 @@
+// Dense fp32 GEMM on the 5th-generation tensor cores with fp32-level accuracy (3xTF32 split).
+//
+//   C[M,N] = A[M,K] * B[N,K]^T (+ bias[N]) (+ C if accumulate)       (both operands K-major)
+//
+// This is the node-side projection workhorse of the attention layer (the per-degree SO(3) linears,
+// the Q/K scalar MLPs, the edge radial MLP): nn.Linear-shaped products y = x W^T.
+//
+// Design (one CTA = one 128 x 128 output tile, 256 threads):
+//  * all threads stream a 128 x 32 fp32 k-slab of A and of B from global memory (coalesced 16-byte
+//    loads), split every value into a tf32 "hi" part (round to nearest, low 13 bits zero) and the
+//    fp32 remainder "lo", and store hi and lo into shared memory in the 128-byte-swizzled K-major
+//    layout the tensor core reads (8-row atoms of 1 KB, 16-byte chunk c of row r at c ^ (r % 8));
+//  * one thread issues, per 8-wide k step, tcgen05.mma kind::tf32 for hi*hi + hi*lo + lo*hi into a
+//    fp32 accumulator in tensor memory (128 lanes x 128 columns), then tcgen05.commit to the stage's
+//    mbarrier; the loads of slab k+1 overlap the MMAs of slab k;
+//  * the tensor core's fp32 accumulation truncates, so long accumulation chains drift (measured ~7x
+//    the error of an fp32 SIMT GEMM at K = 1536).  Each 32-wide k-slab therefore accumulates into a
+//    fresh tensor-memory buffer (12 MMA steps per chain; two buffers alternate) and every thread adds
+//    its 64 values of that buffer into fp32 registers with round-to-nearest adds;
+//  * the epilogue adds bias / the previous C to the register accumulators and stores.
+// The dropped lo*lo term is below fp32 resolution (|error| ~ 2^-22 relative per product).
+// Every mbarrier wait is bounded in time; on a timeout the kernel records E2A_DEV_WAIT_TIMEOUT,
+// still waits (bounded) for its MMAs, frees its tensor memory and returns.
+#include "e2a_common.cuh"
+
+__device__ unsigned int g_e2a_gemm_status = 0;
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 2, kThreads = 256;
+constexpr int kTileBytes = BM * BK * 4;            // 16 KB per operand part
+constexpr int kStageBytes = 4 * kTileBytes;        // A_hi, A_lo, B_hi, B_lo
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kTmemCols = 256;  // two 128-column accumulators
+
+// instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = 128
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  // K-major, 128-byte swizzle: LBO unused (1), SBO = 1024 B between 8-row atoms, version 1
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(e2a_smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_hi(float a) {
+  return __uint_as_float((__float_as_uint(a) + 0x1000u) & 0xFFFFE000u);
+}
+
+// A 128 x 32 slab (rows r0.., cols k0..) of a row-major fp32 matrix: each thread loads 4 float4
+// (zero outside the matrix) into registers ...
+constexpr int kF4PerThread = (BM * BK / 4) / kThreads;
+
+template <bool VEC>
+__device__ __forceinline__ void load_slab(const float* __restrict__ X, int64_t ld, int rows, int K, int r0, int k0,
+                                          float4 (&v)[kF4PerThread]) {
+#pragma unroll
+  for (int j = 0; j < kF4PerThread; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    const int r = c >> 3, ch = c & 7;
+    const int gr = r0 + r, gk = k0 + ch * 4;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (gr < rows) {
+      const float* p = X + (int64_t)gr * ld + gk;
+      if (VEC && gk + 3 < K) {
+        x = __ldg(reinterpret_cast<const float4*>(p));
+      } else {
+        if (gk < K) x.x = __ldg(p);
+        if (gk + 1 < K) x.y = __ldg(p + 1);
+        if (gk + 2 < K) x.z = __ldg(p + 2);
+        if (gk + 3 < K) x.w = __ldg(p + 3);
+      }
+    }
+    v[j] = x;
+  }
+}
+
+// ... then splits them into hi / lo and stores both in the swizzled K-major layout.
+__device__ __forceinline__ void split_store(const float4 (&v)[kF4PerThread], uint8_t* hi, uint8_t* lo) {
+#pragma unroll
+  for (int j = 0; j < kF4PerThread; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    const int r = c >> 3, ch = c & 7;
+    float4 h, l;
+    h.x = tf32_hi(v[j].x); h.y = tf32_hi(v[j].y); h.z = tf32_hi(v[j].z); h.w = tf32_hi(v[j].w);
+    l.x = v[j].x - h.x; l.y = v[j].y - h.y; l.z = v[j].z - h.z; l.w = v[j].w - h.w;
+    const int off = r * 128 + ((ch ^ (r & 7)) << 4);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads, 1)
+k_gemm_tf32x3(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
+              int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = e2a_smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);  // STAGES barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(e2a_smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) e2a_mbar_init(&bars[s], 1);
+    e2a_fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int nk = (K + BK - 1) / BK;
+  const int q = warp & 3, half = warp >> 2;        // TMEM lane quadrant and column half of this warp
+  const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+  float acc[BN / 2];
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) acc[i] = 0.f;
+  bool ok = true;
+  float4 ra[kF4PerThread], rb[kF4PerThread];  // slab kb, loaded one iteration ahead
+  if (nk > 0) {
+    load_slab<VEC>(A, lda, M, K, m0, 0, ra);
+    load_slab<VEC>(B, ldb, N, K, n0, 0, rb);
+  }
+  for (int kb = 0; kb < nk; ++kb) {
+    const int s = kb % STAGES;
+    uint8_t* st = smem + s * kStageBytes;
+    // issue the loads of slab kb+1 now; they are in flight during the stores, the MMAs and the drain
+    float4 na[kF4PerThread], nb[kF4PerThread];
+    if (kb + 1 < nk) {
+      load_slab<VEC>(A, lda, M, K, m0, (kb + 1) * BK, na);
+      load_slab<VEC>(B, ldb, N, K, n0, (kb + 1) * BK, nb);
+    }
+    // stage s was last read by the MMAs of slab kb-2, which finished before slab kb-1 was drained
+    split_store(ra, st, st + kTileBytes);
+    split_store(rb, st + 2 * kTileBytes, st + 3 * kTileBytes);
+    e2a_fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)((kb & 1) * BN);
+      const uint32_t a_hi = e2a_smem_u32(st), a_lo = a_hi + kTileBytes;
+      const uint32_t b_hi = a_hi + 2 * kTileBytes, b_lo = a_hi + 3 * kTileBytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t koff = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+        mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_hi + koff), kk > 0 ? 1u : 0u);
+        if (passes == 3) {
+          mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_lo + koff), 1u);
+          mma_tf32(d, smem_desc_sw128(a_lo + koff), smem_desc_sw128(b_hi + koff), 1u);
+        }
+      }
+      mma_commit(&bars[s]);
+    }
+    // drain the previous slab's buffer into registers while slab kb runs on the tensor core
+    if (kb >= 1) {
+      const int pk = kb - 1;
+      ok = e2a_mbar_wait_bounded(&bars[pk % STAGES], (pk / STAGES) & 1, &g_e2a_gemm_status);
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
+      }
+    }
+    if (kb + 1 < nk) {
+#pragma unroll
+      for (int j = 0; j < kF4PerThread; ++j) { ra[j] = na[j]; rb[j] = nb[j]; }
+    }
+  }
+  if (ok && nk > 0) {
+    const int pk = nk - 1;
+    ok = e2a_mbar_wait_bounded(&bars[pk % STAGES], (pk / STAGES) & 1, &g_e2a_gemm_status);
+    if (!__syncthreads_or(!ok)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
+      }
+    } else {
+      ok = false;
+    }
+  }
+  const bool all_ok = !__syncthreads_or(!ok);
+  if (all_ok) {
+    const int row = m0 + 32 * q + lane;
+    if (row < M) {
+      float* crow = C + (int64_t)row * ldc + n0 + 64 * half;
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) {
+        const int gc = n0 + 64 * half + i;
+        if (gc < N) {
+          float x = acc[i];
+          if (bias) x += bias[gc];
+          if (accumulate) x += crow[i];
+          crow[i] = x;
+        }
+      }
+    }
+  } else if (threadIdx.x == 0 && nk > 0) {
+    // a wait gave up: give the issued MMAs a bounded chance to finish before the memory is freed
+    for (int pk = (nk >= 2 ? nk - 2 : 0); pk < nk; ++pk)
+      e2a_mbar_wait_bounded(&bars[pk % STAGES], (pk / STAGES) & 1, &g_e2a_gemm_status);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------------
+// Pipelined variant for 16-byte-aligned operands: raw fp32 slabs arrive by cp.async (16-byte
+// copies, zero-filled past the matrix edge, destination already in the swizzled layout) RAW_STAGES
+// slabs ahead; each slab is split shared -> shared into one of two hi/lo operand buffers while the
+// tensor core works on the other.  Global-memory latency is off the critical path.
+// ------------------------------------------------------------------------------------------------
+constexpr int RAW_STAGES = 3;
+constexpr int kRawBytes = 2 * kTileBytes;                    // A and B raw slab
+constexpr int kOpBytes = 4 * kTileBytes;                     // A_hi, A_lo, B_hi, B_lo
+constexpr int kSmemAsync = RAW_STAGES * kRawBytes + 2 * kOpBytes + 1024 + 256;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void issue_slab(const float* __restrict__ X, int64_t ld, int rows, int K, int r0, int k0,
+                                           uint32_t dst) {
+#pragma unroll
+  for (int j = 0; j < kF4PerThread; ++j) {
+    const int c = threadIdx.x + j * kThreads;
+    const int r = c >> 3, ch = c & 7;
+    const int gr = r0 + r, gk = k0 + ch * 4;
+    const int valid = (gr < rows && gk < K) ? min(4, K - gk) : 0;
+    const float* src = valid ? X + (int64_t)gr * ld + gk : X;
+    cp_async16(dst + (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)), src, (uint32_t)valid * 4u);
+  }
+}
+
+__device__ __forceinline__ void split_smem(const uint8_t* raw, uint8_t* hi, uint8_t* lo) {
+#pragma unroll
+  for (int j = 0; j < kF4PerThread; ++j) {
+    const int off = (threadIdx.x + j * kThreads) * 16;  // same swizzled offset in and out
+    const float4 v = *reinterpret_cast<const float4*>(raw + off);
+    float4 h, l;
+    h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
+    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
+                    int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = e2a_smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* raw = smem;                                        // RAW_STAGES x (A, B)
+  uint8_t* ops = smem + RAW_STAGES * kRawBytes;               // 2 x (A_hi, A_lo, B_hi, B_lo)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ops + 2 * kOpBytes);  // one per operand buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(e2a_smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    e2a_mbar_init(&bars[0], 1);
+    e2a_mbar_init(&bars[1], 1);
+    e2a_fence_mbar_init();
+  }
+  const int nk = (K + BK - 1) / BK;
+  // prologue: raw slabs 0 .. RAW_STAGES-2 in flight (one commit group each, possibly empty)
+#pragma unroll
+  for (int p = 0; p < RAW_STAGES - 1; ++p) {
+    if (p < nk) {
+      const uint32_t d = e2a_smem_u32(raw + p * kRawBytes);
+      issue_slab(A, lda, M, K, m0, p * BK, d);
+      issue_slab(B, ldb, N, K, n0, p * BK, d + kTileBytes);
+    }
+    cp_async_commit();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int q = warp & 3, half = warp >> 2;
+  const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+  float acc[BN / 2];
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) acc[i] = 0.f;
+  bool ok = true;
+  for (int kb = 0; kb < nk; ++kb) {
+    // keep RAW_STAGES-1 slabs in flight: slab kb + RAW_STAGES - 1 into the stage freed last iteration
+    {
+      const int p = kb + RAW_STAGES - 1;
+      if (p < nk) {
+        const uint32_t d = e2a_smem_u32(raw + (p % RAW_STAGES) * kRawBytes);
+        issue_slab(A, lda, M, K, m0, p * BK, d);
+        issue_slab(B, ldb, N, K, n0, p * BK, d + kTileBytes);
+      }
+      cp_async_commit();
+    }
+    cp_async_wait<RAW_STAGES - 1>();  // this thread's copies of slab kb have landed
+    __syncthreads();                  // ... and everybody's
+    // operand buffer kb & 1 was last read by the MMAs of slab kb-2, drained in iteration kb-1
+    const uint8_t* rs = raw + (kb % RAW_STAGES) * kRawBytes;
+    uint8_t* op = ops + (kb & 1) * kOpBytes;
+    split_smem(rs, op, op + kTileBytes);
+    split_smem(rs + kTileBytes, op + 2 * kTileBytes, op + 3 * kTileBytes);
+    e2a_fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)((kb & 1) * BN);
+      const uint32_t a_hi = e2a_smem_u32(op), a_lo = a_hi + kTileBytes;
+      const uint32_t b_hi = a_hi + 2 * kTileBytes, b_lo = a_hi + 3 * kTileBytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t koff = kk * 32;
+        mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_hi + koff), kk > 0 ? 1u : 0u);
+        if (passes == 3) {
+          mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_lo + koff), 1u);
+          mma_tf32(d, smem_desc_sw128(a_lo + koff), smem_desc_sw128(b_hi + koff), 1u);
+        }
+      }
+      mma_commit(&bars[kb & 1]);
+    }
+    if (kb >= 1) {
+      const int pk = kb - 1;
+      ok = e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (ok && nk > 0) {
+    const int pk = nk - 1;
+    ok = e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
+    if (!__syncthreads_or(!ok)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
+      }
+    } else {
+      ok = false;
+    }
+  }
+  const bool all_ok = !__syncthreads_or(!ok);
+  if (all_ok) {
+    // stage the tile through shared memory (row stride 132 floats: conflict-free 16-byte stores)
+    // so that every warp then writes whole 512-byte rows of C
+    constexpr int kLd = BN + 4;
+    float* tile = reinterpret_cast<float*>(ops);
+    {
+      float* trow = tile + (32 * q + lane) * kLd + 64 * half;
+#pragma unroll
+      for (int i = 0; i < BN / 2; i += 4)
+        *reinterpret_cast<float4*>(trow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+    }
+    __syncthreads();
+    const int gc = n0 + 4 * lane;
+    float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (bias) {
+      if (gc < N) bv.x = bias[gc];
+      if (gc + 1 < N) bv.y = bias[gc + 1];
+      if (gc + 2 < N) bv.z = bias[gc + 2];
+      if (gc + 3 < N) bv.w = bias[gc + 3];
+    }
+    const bool cvec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
+    for (int r = warp; r < BM; r += kThreads / 32) {
+      const int row = m0 + r;
+      if (row >= M) break;
+      float4 x = *reinterpret_cast<const float4*>(tile + r * kLd + 4 * lane);
+      x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
+      float* cp = C + (int64_t)row * ldc + gc;
+      if (cvec) {
+        if (accumulate) {
+          const float4 o = *reinterpret_cast<const float4*>(cp);
+          x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+        }
+        *reinterpret_cast<float4*>(cp) = x;
+      } else {
+        const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (gc + t < N) cp[t] = accumulate ? cp[t] + xv[t] : xv[t];
+      }
+    }
+  } else if (threadIdx.x == 0 && nk > 0) {
+    for (int pk = (nk >= 2 ? nk - 2 : 0); pk < nk; ++pk)
+      e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                    const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!C || (K > 0 && (!A || !B)) || lda < K || ldb < K || ldc < N) return E2A_ERR_ARG;
+  if ((M + BM - 1) / BM > INT32_MAX || (N + BN - 1) / BN > 65535 || K > INT32_MAX) return E2A_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  if (vec) {
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_async, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAsync));
+    k_gemm_tf32x3_async<<<grid, kThreads, kSmemAsync, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                            accumulate, passes);
+  } else {
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    k_gemm_tf32x3<false><<<grid, kThreads, kSmemBytes, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                             accumulate, passes);
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_gemm_status(unsigned int* status, int reset, void* stream) {
+  if (!status) return E2A_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  E2A_CUDA(cudaMemcpyFromSymbolAsync(status, g_e2a_gemm_status, sizeof(unsigned int), 0, cudaMemcpyDeviceToHost, st));
+  E2A_CUDA(cudaStreamSynchronize(st));
+  if (reset) {
+    const unsigned int zero = 0;
+    E2A_CUDA(cudaMemcpyToSymbolAsync(g_e2a_gemm_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st));
+    E2A_CUDA(cudaStreamSynchronize(st));
+  }
+  return E2A_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,116 @@
+"""Tensor-core fp32 projections: ``y = x W^T (+ b)`` on tcgen05 through ``e2a_gemm_tf32x3``.
+
+The 3xTF32 split keeps fp32-level accuracy (parity mode); ``passes=1`` is plain TF32.  Only the
+input gradient is produced by the CUDA path (what force evaluation needs); a weight gradient, when a
+caller asks for one, is formed with ``torch.matmul``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_of
+
+PASSES = 3
+
+
+def gemm(a, b, bias=None, out=None, accumulate=False, passes=None):
+    """``a [M,K] @ b[N,K]^T (+ bias)`` -> [M,N] (fp32, CUDA, row-major with unit inner stride)."""
+    lib = _lib.load()
+    if a.dtype != torch.float32 or b.dtype != torch.float32:
+        raise TypeError("gemm expects float32 operands")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f"gemm shape mismatch {tuple(a.shape)} x {tuple(b.shape)}^T")
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if b.stride(1) != 1:
+        b = b.contiguous()
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=torch.float32)
+    if bias is not None:
+        bias = bias.contiguous()
+    check(lib.e2a_gemm_tf32x3(ptr(a), max(a.stride(0), K), ptr(b), max(b.stride(0), K), ptr(out), out.stride(0),
+                              ptr(bias), M, N, K, 1 if accumulate else 0, PASSES if passes is None else passes,
+                              stream_of(a.device)), "e2a_gemm_tf32x3")
+    return out
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        y = gemm(x2, w, b)
+        ctx.save_for_backward(x2 if w.requires_grad else None, w)
+        ctx.shape = shape
+        ctx.has_b = b is not None
+        return y.reshape(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, w = ctx.saved_tensors
+        g2 = gy.reshape(-1, gy.shape[-1]).contiguous()
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(g2, w.t().contiguous()).reshape(ctx.shape)
+        if ctx.needs_input_grad[1]:
+            dw = g2.t() @ x2
+        if ctx.has_b and ctx.needs_input_grad[2]:
+            db = g2.sum(0)
+        return dx, dw, db
+
+
+def linear(x, w, b=None):
+    """``torch.nn.functional.linear`` on the tensor cores (CUDA fp32 inputs)."""
+    if not x.is_cuda:
+        raise ValueError("ubio_molfm_b200 kernels need CUDA tensors (there is no CPU path)")
+    return _LinearFn.apply(x.float(), w, b)
+
+
+class _SO3LinearFn(torch.autograd.Function):
+    """``out[:, m, :] = x[:, m, :] @ W[l(m)]^T`` (+ bias on row 0) as one strided GEMM per row m.
+
+    ``x`` is [N, R, C] contiguous; every row m is read in place as an [N, C] matrix with leading
+    dimension R*C and written in place into ``out`` [N, R, C_out] -- no copies."""
+
+    @staticmethod
+    def forward(ctx, x, w, bias, lidx):
+        N, R, C = x.shape
+        Co = w.shape[1]
+        x = x.contiguous()
+        out = torch.empty((N, R, Co), device=x.device, dtype=torch.float32)
+        for m in range(R):
+            gemm(x[:, m, :], w[lidx[m]], bias if (m == 0 and bias is not None) else None, out=out[:, m, :])
+        ctx.save_for_backward(x if w.requires_grad else None, w)
+        ctx.lidx = lidx
+        ctx.has_bias = bias is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        g = g.contiguous()
+        N, R, Co = g.shape
+        C = w.shape[2]
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            wt = w.transpose(1, 2).contiguous()  # [L, C, Co]
+            dx = torch.empty((N, R, C), device=g.device, dtype=torch.float32)
+            for m in range(R):
+                gemm(g[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :])
+        if ctx.needs_input_grad[1]:
+            dw = torch.zeros_like(w)
+            for m in range(R):
+                dw[ctx.lidx[m]] += g[:, m, :].t() @ x[:, m, :]
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = g[:, 0, :].sum(0)
+        return dx, dw, db, None
+
+
+def so3_linear(x, w, bias, lidx):
+    """Per-degree linear of [N, R, C] irreps features with weights [L+1, C_out, C] (CUDA)."""
+    if not x.is_cuda:
+        raise ValueError("ubio_molfm_b200 kernels need CUDA tensors (there is no CPU path)")
+    return _SO3LinearFn.apply(x.float(), w, bias, tuple(int(v) for v in lidx))

@@ -1,8 +1,9 @@
 """Node-side building blocks of the E2Former-V2 attention layer, with the reference's parameter
 names and shapes so that reference ``state_dict``s load unchanged.
 
-These are dense per-node contractions ([N, (lmax+1)^2, C] x [C, C']); they run as batched GEMMs
-(cuBLAS through ``torch.matmul``) on the GPU.  The sparse edge work lives in :mod:`.ops`.
+These are dense per-node contractions ([N, (lmax+1)^2, C] x [C, C']); on the GPU they run on the
+tcgen05 tensor cores with the 3xTF32 split (:mod:`.linear`).  The sparse edge work lives in :mod:`.ops`.
+On the CPU (used only to build / inspect modules) they fall back to plain torch arithmetic.
 """
 from __future__ import annotations
 
@@ -11,7 +12,27 @@ import math
 import torch
 from torch import nn
 
+from . import linear as tc
 from .cg import so2_first_order_tables
+
+
+def _degree_of_rows(lmax):
+    return [l for l in range(lmax + 1) for _ in range(2 * l + 1)]
+
+
+def lin(x, w, b=None, const_weights=False):
+    """``F.linear`` on the tensor cores for CUDA inputs.  ``const_weights`` (eval mode) treats the
+    parameters as constants, so the backward forms only the input gradient -- the one force
+    evaluation needs -- instead of weight gradients nobody asked for."""
+    if const_weights:
+        w = w.detach()
+        b = None if b is None else b.detach()
+    return tc.linear(x, w, b) if x.is_cuda else nn.functional.linear(x, w, b)
+
+
+def _cw(module, t):
+    """Parameter as seen by the forward: a constant in eval mode."""
+    return t if module.training else t.detach()
 
 
 def parse_irreps(irreps):
@@ -56,6 +77,9 @@ class SO3_Linear_e2former(nn.Module):
     def forward(self, x):
         shape = x.shape[:-2]
         x = x.reshape(-1, x.shape[-2], x.shape[-1])
+        if x.is_cuda:
+            out = tc.so3_linear(x, _cw(self, self.weight), _cw(self, self.bias), _degree_of_rows(self.lmax)[: x.shape[1]])
+            return out.reshape(*shape, out.shape[-2], self.out_features)
         outs = []
         for l in range(self.lmax + 1):
             blk = x[:, l * l:(l + 1) ** 2, :]
@@ -91,6 +115,22 @@ class SO3_Linear2Scalar_e2former(nn.Module):
     def forward(self, x):
         shape = x.shape[:-2]
         x = x.reshape(-1, x.shape[-2], x.shape[-1])
+        if x.is_cuda:
+            # both projections in one tensor-core GEMM per row: [N, in] @ [in, 2*hidden]
+            w12 = torch.cat([_cw(self, self.weight), _cw(self, self.weight2)], dim=1)   # [L+1, 2h, in]
+            bb = _cw(self, self.bias).reshape(-1)
+            b12 = torch.cat([bb, torch.zeros_like(bb)])
+            o = tc.so3_linear(x, w12, b12, _degree_of_rows(self.lmax)[: x.shape[1]])  # [N, R, 2h]
+            o1, o2 = o[..., :self.hidden], o[..., self.hidden:]
+            prod = o1 * o2
+            parts = [prod[:, l * l:(l + 1) ** 2].sum(dim=1) for l in range(self.lmax + 1)]
+            h = torch.cat(parts, dim=-1)
+            fl = self.final_linear
+            cwt = not self.training
+            h = lin(h, fl[0].weight, fl[0].bias, cwt)
+            h = fl[2](fl[1](h))
+            h = lin(h, fl[3].weight, fl[3].bias, cwt)
+            return h.reshape(*shape, self.out_features)
         # both projections in one GEMM per degree: [*, 2l+1, in] @ [in, 2*hidden]
         parts = []
         for l in range(self.lmax + 1):
@@ -123,7 +163,10 @@ class RadialProfile(nn.Module):
         self.net = nn.Sequential(*mods)
 
     def forward(self, f_in):
-        return self.net(f_in)
+        h = f_in
+        for layer in self.net:
+            h = lin(h, layer.weight, layer.bias, not self.training) if isinstance(layer, nn.Linear) else layer(h)
+        return h
 
 
 class GaussianSmearing(nn.Module):
@@ -186,7 +229,7 @@ class SO2_TP_givenl2(nn.Module):
         for idx, (l3, cnt) in enumerate(self.l3_sequential):
             end = start + (2 * l3 + 1) * cnt
             blk = y[:, start:end].reshape(bs, cnt, 2 * l3 + 1, -1).permute(0, 2, 1, 3).reshape(bs, 2 * l3 + 1, -1)
-            outs.append(self.out_linear[idx](blk))
+            outs.append(lin(blk, self.out_linear[idx].weight, None, not self.training))
             start = end
         return torch.cat(outs, dim=1) * self.path_norm
 
