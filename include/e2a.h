@@ -190,6 +190,20 @@ int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, fl
 /* Status bits of the GEMM's bounded waits (1 = a wait timed out); copies and optionally clears. */
 int e2a_gemm_status(unsigned int* status, int reset, void* stream);
 
+/* ------------------------------------------------------------------------------------------ */
+/* Fused row-wise LayerNorm + SiLU of the radial MLP (RadialProfile, module_utils.py:2151-2178), */
+/* one warp per row of width W (W % 128 == 0, W <= 1024):                                       */
+/*   x = h (+ T[zt[r]] + S[zs[r]] when T != NULL; written to x_out if x_out != NULL),            */
+/*   y = SiLU((x - mean) * rstd * gamma + beta), mean / rstd saved per row.                      */
+/* The optional tables are the per-element embedding part of fc_easy's first Linear             */
+/* (e2former.py:258-266) gathered per edge.  Backward: input gradient only.                      */
+/* ------------------------------------------------------------------------------------------ */
+int e2a_ln_silu_fwd(const float* h, const float* T, const int64_t* zt, const float* S, const int64_t* zs,
+                    const float* gamma, const float* beta, int64_t rows, int W, float eps, float* x_out,
+                    float* y, float* mean, float* rstd, void* stream);
+int e2a_ln_silu_bwd(const float* x, const float* dy, const float* gamma, const float* beta,
+                    const float* mean, const float* rstd, int64_t rows, int W, float* dx, void* stream);
+
 /* Same as e2a_attn_bwd_query, but allocates nothing and takes no workspace.  No counterpart in  */
 /* the reference: it serves callers that cannot allocate device memory when they run the        */
 /* backward (an operator plugin handed only its tensors, code that must not call cudaMalloc).    */

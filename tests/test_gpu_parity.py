@@ -333,3 +333,29 @@ def test_layer_unsorted_edges_equal_sorted():
     out2, _ = layer(edge_dis=leaves["edge_dis"][perm], attn_weight=leaves["attn_weight"][perm],
                     poly_dist=leaves["poly_dist"][perm], batched_data=bd2, **kw)
     torch.testing.assert_close(out1, out2, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("W,tables", [(128, True), (128, False), (512, False), (256, True)])
+def test_fused_ln_silu_matches_torch(W, tables):
+    from ubio_molfm_b200.linear import ln_silu
+
+    g = torch.Generator().manual_seed(W)
+    rows = 3001
+    ln = torch.nn.LayerNorm(W)
+    with torch.no_grad():
+        ln.weight.copy_(1 + 0.1 * torch.randn(W, generator=g))
+        ln.bias.copy_(0.1 * torch.randn(W, generator=g))
+    h = torch.randn(rows, W, generator=g, dtype=torch.float64)
+    T, S = torch.randn(7, W, generator=g, dtype=torch.float64), torch.randn(5, W, generator=g, dtype=torch.float64)
+    zt, zs = torch.randint(0, 7, (rows,), generator=g), torch.randint(0, 5, (rows,), generator=g)
+    hr = h.clone().requires_grad_(True)
+    x = hr + (T[zt] + S[zs] if tables else 0)
+    ref = torch.nn.functional.silu(torch.nn.functional.layer_norm(x, (W,), ln.weight.double(), ln.bias.double()))
+    hg = h.float().to(DEV).requires_grad_(True)
+    tb = (T.float().to(DEV), zt.to(DEV), S.float().to(DEV), zs.to(DEV)) if tables else None
+    out = ln_silu(hg, ln.to(DEV), tb)
+    assert (out.double().cpu() - ref).abs().max().item() < 2e-5
+    w = torch.randn(rows, W, generator=g, dtype=torch.float64)
+    (gr,) = torch.autograd.grad(ref, hr, w)
+    (gg,) = torch.autograd.grad(out, hg, w.float().to(DEV))
+    assert (gg.double().cpu() - gr).abs().max().item() < 5e-5

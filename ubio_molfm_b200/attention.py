@@ -20,7 +20,7 @@ import torch
 from torch import nn
 
 from .nn import (E2TensorProductSO2_FirstOrder, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
-                 irreps_channels_lmax, lin, parse_irreps)
+                 irreps_channels_lmax, lin, parse_irreps, run_mlp)
 from .ops import attention_span
 
 
@@ -70,15 +70,15 @@ class E2AttentionArbOrder_sparse(nn.Module):
         lin0 = net[0]
         nb = self.attn_weight_input_dim
         e = self.node_embed_dim
-        w = lin0.weight
-        t_tab = self.target_embedding.weight @ w[:, nb:nb + e].t()          # [types, h]
-        s_tab = self.source_embedding.weight @ w[:, nb + e:].t()            # [types, h]
+        cw = not self.training
+        w = lin0.weight.detach() if cw else lin0.weight
+        with torch.set_grad_enabled(torch.is_grad_enabled() and not cw):
+            t_tab = (self.target_embedding.weight @ w[:, nb:nb + e].t()).contiguous()   # [types, h]
+            s_tab = (self.source_embedding.weight @ w[:, nb + e:].t()).contiguous()     # [types, h]
         z_q = atomic_numbers[query_idx]
         z_k = atomic_numbers[f_outcell_index][neighbor_idx]
-        cw = not self.training
-        h = lin(attn_weight, w[:, :nb], lin0.bias, cw) + t_tab[z_q] + s_tab[z_k]
-        for layer in list(net)[1:]:
-            h = lin(h, layer.weight, layer.bias, cw) if isinstance(layer, nn.Linear) else layer(h)
+        h = lin(attn_weight, w[:, :nb], lin0.bias, cw)
+        h = run_mlp(list(net)[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
         return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
 
     def forward(self, node_pos, node_irreps_input, edge_dis, edge_vec, attn_weight, atomic_numbers,

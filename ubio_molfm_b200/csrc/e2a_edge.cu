@@ -1,0 +1,173 @@
+// Fused row-wise pieces of the edge radial MLP (RadialProfile, module_utils.py:2151-2178, used by
+// fc_easy in e2former.py:134-138, 301-306):
+//
+//   forward   y = SiLU(LayerNorm(x)),  x = h (+ T[zt[e]] + S[zs[e]])     one warp per row
+//   backward  dx = d/dx of the same map (input gradient; gamma / beta / tables treated as constants)
+//
+// The optional table terms are the exact decomposition of the first Linear over the concatenated
+// [rbf, target_embedding(Z_i), source_embedding(Z_j)] input: the embedding parts are per-element
+// tables gathered per edge instead of an [E, nb + 256] concatenation.  Each row (width W, W % 128
+// == 0 and W <= 1024) is held in registers (W/32 floats per lane); mean / rstd are saved for the
+// backward, which recomputes the normalised row.  LayerNorm eps and the two-pass variance match
+// torch.nn.LayerNorm (biased variance, eps = 1e-5).
+#include "e2a_common.cuh"
+
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+__device__ __forceinline__ float silu(float z) { return z / (1.f + expf(-z)); }
+
+template <int V>  // V = W / 128 float4 per lane
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+k_ln_silu_fwd(const float* __restrict__ h, const float* __restrict__ T, const int64_t* __restrict__ zt,
+              const float* __restrict__ S, const int64_t* __restrict__ zs, const float* __restrict__ gamma,
+              const float* __restrict__ beta, int64_t rows, int W, float eps, float* __restrict__ x_out,
+              float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out) {
+  const int lane = threadIdx.x & 31;
+  int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (; r < rows; r += nw) {
+    float4 v[V];
+    const float* hr = h + r * W;
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = ldg4(hr + 4 * (lane + 32 * i));
+    if (T) {
+      const float* tr = T + zt[r] * W;
+      const float* sr = S + zs[r] * W;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float4 a = ldg4(tr + 4 * (lane + 32 * i)), b = ldg4(sr + 4 * (lane + 32 * i));
+        v[i].x += a.x + b.x; v[i].y += a.y + b.y; v[i].z += a.z + b.z; v[i].w += a.w + b.w;
+      }
+      if (x_out) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) reinterpret_cast<float4*>(x_out + r * W)[lane + 32 * i] = v[i];
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = e2a_warp_sum(s) / W;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+    const float rstd = rsqrtf(e2a_warp_sum(q) / W + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      const float4 g = ldg4(gamma + c), b = ldg4(beta + c);
+      float4 o;
+      o.x = silu((v[i].x - mean) * rstd * g.x + b.x);
+      o.y = silu((v[i].y - mean) * rstd * g.y + b.y);
+      o.z = silu((v[i].z - mean) * rstd * g.z + b.z);
+      o.w = silu((v[i].w - mean) * rstd * g.w + b.w);
+      reinterpret_cast<float4*>(y + r * W)[lane + 32 * i] = o;
+    }
+    if (lane == 0) {
+      mean_out[r] = mean;
+      rstd_out[r] = rstd;
+    }
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+k_ln_silu_bwd(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ gamma,
+              const float* __restrict__ beta, const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+              int64_t rows, int W, float* __restrict__ dx) {
+  const int lane = threadIdx.x & 31;
+  int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (; r < rows; r += nw) {
+    const float mean = mean_in[r], rstd = rstd_in[r];
+    float4 xh[V], g[V];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      const float4 xv = ldg4(x + r * W + c), d = ldg4(dy + r * W + c);
+      const float4 ga = ldg4(gamma + c), be = ldg4(beta + c);
+      const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ds[4] = {d.x, d.y, d.z, d.w};
+      const float gs[4] = {ga.x, ga.y, ga.z, ga.w}, bs[4] = {be.x, be.y, be.z, be.w};
+      float hs[4], gg[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float xn = (xs[t] - mean) * rstd;
+        const float z = xn * gs[t] + bs[t];
+        const float sg = 1.f / (1.f + expf(-z));
+        const float dz = ds[t] * sg * (1.f + z * (1.f - sg));  // d SiLU
+        const float dxn = dz * gs[t];
+        hs[t] = xn;
+        gg[t] = dxn;
+        s1 += dxn;
+        s2 += dxn * xn;
+      }
+      xh[i] = make_float4(hs[0], hs[1], hs[2], hs[3]);
+      g[i] = make_float4(gg[0], gg[1], gg[2], gg[3]);
+    }
+    s1 = e2a_warp_sum(s1) / W;
+    s2 = e2a_warp_sum(s2) / W;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float4 o;
+      o.x = rstd * (g[i].x - s1 - xh[i].x * s2);
+      o.y = rstd * (g[i].y - s1 - xh[i].y * s2);
+      o.z = rstd * (g[i].z - s1 - xh[i].z * s2);
+      o.w = rstd * (g[i].w - s1 - xh[i].w * s2);
+      reinterpret_cast<float4*>(dx + r * W)[lane + 32 * i] = o;
+    }
+  }
+}
+
+int grid_rows(int64_t rows) {
+  int64_t b = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  if (b > 148 * 64) b = 148 * 64;
+  return (int)(b > 0 ? b : 1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int e2a_ln_silu_fwd(const float* h, const float* T, const int64_t* zt, const float* S, const int64_t* zs,
+                    const float* gamma, const float* beta, int64_t rows, int W, float eps, float* x_out, float* y,
+                    float* mean, float* rstd, void* stream) {
+  if (rows < 0 || W <= 0 || W % 128 || W > 1024) return rows < 0 || W <= 0 ? E2A_ERR_ARG : E2A_ERR_UNSUPPORTED;
+  if (rows == 0) return E2A_OK;
+  if (!h || !gamma || !beta || !y || !mean || !rstd || (T && (!zt || !S || !zs))) return E2A_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int g = grid_rows(rows), b = kWarpsPerBlock * 32;
+  switch (W / 128) {
+    case 1: k_ln_silu_fwd<1><<<g, b, 0, st>>>(h, T, zt, S, zs, gamma, beta, rows, W, eps, x_out, y, mean, rstd); break;
+    case 2: k_ln_silu_fwd<2><<<g, b, 0, st>>>(h, T, zt, S, zs, gamma, beta, rows, W, eps, x_out, y, mean, rstd); break;
+    case 4: k_ln_silu_fwd<4><<<g, b, 0, st>>>(h, T, zt, S, zs, gamma, beta, rows, W, eps, x_out, y, mean, rstd); break;
+    case 8: k_ln_silu_fwd<8><<<g, b, 0, st>>>(h, T, zt, S, zs, gamma, beta, rows, W, eps, x_out, y, mean, rstd); break;
+    default: return E2A_ERR_UNSUPPORTED;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_ln_silu_bwd(const float* x, const float* dy, const float* gamma, const float* beta, const float* mean,
+                    const float* rstd, int64_t rows, int W, float* dx, void* stream) {
+  if (rows < 0 || W <= 0 || W % 128 || W > 1024) return rows < 0 || W <= 0 ? E2A_ERR_ARG : E2A_ERR_UNSUPPORTED;
+  if (rows == 0) return E2A_OK;
+  if (!x || !dy || !gamma || !beta || !mean || !rstd || !dx) return E2A_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int g = grid_rows(rows), b = kWarpsPerBlock * 32;
+  switch (W / 128) {
+    case 1: k_ln_silu_bwd<1><<<g, b, 0, st>>>(x, dy, gamma, beta, mean, rstd, rows, W, dx); break;
+    case 2: k_ln_silu_bwd<2><<<g, b, 0, st>>>(x, dy, gamma, beta, mean, rstd, rows, W, dx); break;
+    case 4: k_ln_silu_bwd<4><<<g, b, 0, st>>>(x, dy, gamma, beta, mean, rstd, rows, W, dx); break;
+    case 8: k_ln_silu_bwd<8><<<g, b, 0, st>>>(x, dy, gamma, beta, mean, rstd, rows, W, dx); break;
+    default: return E2A_ERR_UNSUPPORTED;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // extern "C"

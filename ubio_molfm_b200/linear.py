@@ -114,3 +114,48 @@ def so3_linear(x, w, bias, lidx):
     if not x.is_cuda:
         raise ValueError("ubio_molfm_b200 kernels need CUDA tensors (there is no CPU path)")
     return _SO3LinearFn.apply(x.float(), w, bias, tuple(int(v) for v in lidx))
+
+
+class _LnSiluFn(torch.autograd.Function):
+    """y = SiLU(LayerNorm(h [+ T[zt] + S[zs]])) with constant gamma / beta / tables (eval mode)."""
+
+    @staticmethod
+    def forward(ctx, h, gamma, beta, eps, T, zt, S, zs):
+        lib = _lib.load()
+        h = h.contiguous()
+        rows, W = h.shape
+        y = torch.empty_like(h)
+        mean = torch.empty(rows, device=h.device, dtype=torch.float32)
+        rstd = torch.empty_like(mean)
+        x = torch.empty_like(h) if T is not None else h
+        check(lib.e2a_ln_silu_fwd(ptr(h), ptr(T), ptr(zt), ptr(S), ptr(zs), ptr(gamma), ptr(beta), rows, W, float(eps),
+                                  ptr(x) if T is not None else None, ptr(y), ptr(mean), ptr(rstd),
+                                  stream_of(h.device)), "e2a_ln_silu_fwd")
+        ctx.save_for_backward(x, gamma, beta, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _lib.load()
+        x, gamma, beta, mean, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = torch.empty_like(dy)
+        rows, W = dy.shape
+        check(lib.e2a_ln_silu_bwd(ptr(x), ptr(dy), ptr(gamma), ptr(beta), ptr(mean), ptr(rstd), rows, W, ptr(dx),
+                                  stream_of(dy.device)), "e2a_ln_silu_bwd")
+        return dx, None, None, None, None, None, None, None
+
+
+def ln_silu_supported(W):
+    return W % 128 == 0 and W <= 1024
+
+
+def ln_silu(h, ln, tables=None):
+    """Fused SiLU(LayerNorm(h + tables)) for a 2-D CUDA tensor, LayerNorm module ``ln`` (constants).
+
+    ``tables`` = (T, zt, S, zs): per-row gathered table rows T[zt] + S[zs] added before the norm."""
+    T = zt = S = zs = None
+    if tables is not None:
+        T, zt, S, zs = (t.contiguous() for t in tables)
+    return _LnSiluFn.apply(h.float(), ln.weight.detach().contiguous(), ln.bias.detach().contiguous(), ln.eps,
+                           T, zt, S, zs)

@@ -128,7 +128,7 @@ class SO3_Linear2Scalar_e2former(nn.Module):
             fl = self.final_linear
             cwt = not self.training
             h = lin(h, fl[0].weight, fl[0].bias, cwt)
-            h = fl[2](fl[1](h))
+            h = tc.ln_silu(h, fl[1]) if (cwt and tc.ln_silu_supported(h.shape[-1])) else fl[2](fl[1](h))
             h = lin(h, fl[3].weight, fl[3].bias, cwt)
             return h.reshape(*shape, self.out_features)
         # both projections in one GEMM per degree: [*, 2l+1, in] @ [in, 2*hidden]
@@ -163,10 +163,33 @@ class RadialProfile(nn.Module):
         self.net = nn.Sequential(*mods)
 
     def forward(self, f_in):
-        h = f_in
-        for layer in self.net:
-            h = lin(h, layer.weight, layer.bias, not self.training) if isinstance(layer, nn.Linear) else layer(h)
-        return h
+        return run_mlp(list(self.net), f_in, not self.training)
+
+
+def run_mlp(layers, h, const_weights, first_tables=None):
+    """Linear / LayerNorm / SiLU stack; on CUDA in eval mode each LayerNorm+SiLU pair is one fused kernel
+    (``first_tables`` are added to the first Linear's output inside that fused kernel)."""
+    i = 0
+    pending = first_tables
+    while i < len(layers):
+        layer = layers[i]
+        if isinstance(layer, nn.Linear):
+            h = lin(h, layer.weight, layer.bias, const_weights)
+            i += 1
+        elif (isinstance(layer, nn.LayerNorm) and i + 1 < len(layers) and isinstance(layers[i + 1], nn.SiLU)
+              and h.is_cuda and const_weights and h.dim() == 2 and tc.ln_silu_supported(h.shape[-1])):
+            h = tc.ln_silu(h, layer, pending)
+            pending = None
+            i += 2
+            continue
+        else:
+            if pending is not None:
+                T, zt, S, zs = pending
+                h = h + T[zt] + S[zs]
+                pending = None
+            h = layer(h)
+            i += 1
+    return h
 
 
 class GaussianSmearing(nn.Module):
