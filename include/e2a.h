@@ -187,6 +187,15 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
 int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
                     const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes,
                     void* stream);
+/* Pair-product epilogue for SO3_Linear2Scalar_e2former (module_utils.py:2240-2274): B's rows come */
+/* interleaved (o1_j, o2_j); P[r, j] = (P[r, j] if accumulate) + o1_j * o2_j with leading dim ldp, */
+/* C (may be NULL) receives the raw [M, N] values.  N even; 16-byte-aligned A / B rows required.  */
+int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                             const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
+                             int accumulate, int passes, void* stream);
+/* Backward of the pair product: D[n,m,2j] = G[n,l(m),j] O[n,m,2j+1], D[n,m,2j+1] = G[n,l(m),j] O[n,m,2j] */
+/* for O, D [n_nodes, R, 2h], G [n_nodes, L1, h], l(m) the degree of row m.                      */
+int e2a_pair_grad(const float* O, const float* G, int64_t n_nodes, int R, int L1, int h, float* D, void* stream);
 /* Status bits of the GEMM's bounded waits (1 = a wait timed out); copies and optionally clears. */
 int e2a_gemm_status(unsigned int* status, int reset, void* stream);
 

@@ -48,3 +48,31 @@ def test_gemm_strided_operands_and_linear_grad():
     (gx,) = torch.autograd.grad(y, x, gy)
     (gxr,) = torch.autograd.grad(yr, x, gy.double())
     assert (gx.double() - gxr).abs().max().item() < 2e-5
+
+
+def test_so3_pair_product_matches_torch():
+    from ubio_molfm_b200.linear import so3_pair_product
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    N, C, h = 777, 256, 192
+    x = torch.randn(N, 9, C, device="cuda", generator=g, requires_grad=True)
+    w1 = torch.randn(3, h, C, device="cuda", generator=g) / 16
+    w2 = torch.randn(3, h, C, device="cuda", generator=g) / 16
+    b = torch.randn(h, device="cuda", generator=g)
+    lidx = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+    P = so3_pair_product(x, w1, w2, b, lidx)
+    xd = x.detach().double().requires_grad_(True)
+    parts = []
+    for l in range(3):
+        blk = xd[:, l * l:(l + 1) ** 2]
+        o1 = blk @ w1[l].double().t()
+        if l == 0:
+            o1 = o1 + b.double()
+        o2 = blk @ w2[l].double().t()
+        parts.append((o1 * o2).sum(1))
+    ref = torch.stack(parts, 1)
+    assert (P.double() - ref).abs().max().item() <= 2e-5 * max(1.0, ref.abs().max().item())
+    G = torch.randn(N, 3, h, device="cuda", generator=g)
+    (dx,) = torch.autograd.grad(P, x, G)
+    (dxr,) = torch.autograd.grad(ref, xd, G.double())
+    assert (dx.double() - dxr).abs().max().item() <= 2e-5 * max(1.0, dxr.abs().max().item())

@@ -129,9 +129,38 @@ int grid_rows(int64_t rows) {
   return (int)(b > 0 ? b : 1);
 }
 
+// D[n, m, 2j] = G[n, l(m), j] * O[n, m, 2j+1];  D[n, m, 2j+1] = G[n, l(m), j] * O[n, m, 2j]
+__global__ void k_pair_grad(const float* __restrict__ O, const float* __restrict__ G, int64_t n_nodes, int R,
+                            int L1, int h, float* __restrict__ D) {
+  const int64_t total = n_nodes * R * (int64_t)(h / 2);  // float4 units of O / D
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j2 = t % (h / 2);           // pair of pairs: j = 2*j2, 2*j2+1
+    const int64_t nm = t / (h / 2);
+    const int m = (int)(nm % R);
+    const int64_t n = nm / R;
+    int l = 0;
+    while ((l + 1) * (l + 1) <= m) ++l;
+    const float4 o = ldg4(O + nm * (2 * h) + 4 * j2);
+    const float2 g = __ldg(reinterpret_cast<const float2*>(G + (n * L1 + l) * h + 2 * j2));
+    reinterpret_cast<float4*>(D + nm * (2 * h))[j2] = make_float4(g.x * o.y, g.x * o.x, g.y * o.w, g.y * o.z);
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int e2a_pair_grad(const float* O, const float* G, int64_t n_nodes, int R, int L1, int h, float* D, void* stream) {
+  if (n_nodes < 0 || R <= 0 || L1 <= 0 || h <= 0 || (h & 1) || R > L1 * L1) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!O || !G || !D) return E2A_ERR_ARG;
+  const int64_t total = n_nodes * R * (int64_t)(h / 2);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_pair_grad<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(O, G, n_nodes, R, L1, h, D);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
 
 int e2a_ln_silu_fwd(const float* h, const float* T, const int64_t* zt, const float* S, const int64_t* zs,
                     const float* gamma, const float* beta, int64_t rows, int W, float eps, float* x_out, float* y,

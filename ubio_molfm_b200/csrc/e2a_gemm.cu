@@ -296,7 +296,8 @@ __device__ __forceinline__ void split_smem(const uint8_t* raw, uint8_t* hi, uint
 
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
-                    int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes) {
+                    int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes,
+                    float* P, int64_t ldp) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = e2a_smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -427,12 +428,29 @@ k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __res
       if (gc + 2 < N) bv.z = bias[gc + 2];
       if (gc + 3 < N) bv.w = bias[gc + 3];
     }
-    const bool cvec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
+    const bool cvec = C && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
     for (int r = warp; r < BM; r += kThreads / 32) {
       const int row = m0 + r;
       if (row >= M) break;
       float4 x = *reinterpret_cast<const float4*>(tile + r * kLd + 4 * lane);
       x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
+      if (P) {
+        // pair-product mode: columns (2j, 2j+1) hold (o1_j, o2_j); P[row, j] (+)= o1_j * o2_j, and C
+        // (optional) receives the raw values for the backward
+        float* pp = P + (int64_t)row * ldp + (gc >> 1);
+        if (gc + 1 < N) pp[0] = (accumulate ? pp[0] : 0.f) + x.x * x.y;
+        if (gc + 3 < N) pp[1] = (accumulate ? pp[1] : 0.f) + x.z * x.w;
+        if (!C) continue;
+        float* cp = C + (int64_t)row * ldc + gc;
+        if (cvec) {
+          *reinterpret_cast<float4*>(cp) = x;
+        } else {
+          const float xv[4] = {x.x, x.y, x.z, x.w};
+          for (int t = 0; t < 4; ++t)
+            if (gc + t < N) cp[t] = xv[t];
+        }
+        continue;
+      }
       float* cp = C + (int64_t)row * ldc + gc;
       if (cvec) {
         if (accumulate) {
@@ -476,12 +494,31 @@ int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, fl
   if (vec) {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_async, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAsync));
     k_gemm_tf32x3_async<<<grid, kThreads, kSmemAsync, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                            accumulate, passes);
+                                                            accumulate, passes, nullptr, 0);
   } else {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     k_gemm_tf32x3<false><<<grid, kThreads, kSmemBytes, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
                                                              accumulate, passes);
   }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                             const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
+                             int accumulate, int passes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3) || (N & 1)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!P || (K > 0 && (!A || !B)) || lda < K || ldb < K || (C && ldc < N) || ldp < N / 2) return E2A_ERR_ARG;
+  if ((M + BM - 1) / BM > INT32_MAX || (N + BN - 1) / BN > 65535 || K > INT32_MAX) return E2A_ERR_ARG;
+  const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
+  if (!vec) return E2A_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_async, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAsync));
+  k_gemm_tf32x3_async<<<grid, kThreads, kSmemAsync, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                          accumulate, passes, P, ldp);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }

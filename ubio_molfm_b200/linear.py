@@ -159,3 +159,57 @@ def ln_silu(h, ln, tables=None):
         T, zt, S, zs = (t.contiguous() for t in tables)
     return _LnSiluFn.apply(h.float(), ln.weight.detach().contiguous(), ln.bias.detach().contiguous(), ln.eps,
                            T, zt, S, zs)
+
+
+class _SO3PairProdFn(torch.autograd.Function):
+    """``P[n, l, j] = sum_{m in degree l} o1[n,m,j] * o2[n,m,j]`` with ``o1 = x W1[l]^T (+b on m=0)``,
+    ``o2 = x W2[l]^T`` (the inner product of SO3_Linear2Scalar_e2former), fused into the GEMM
+    epilogue.  ``w12`` [L+1, 2h, C] holds W1 / W2 rows interleaved; ``b12`` [2h] the bias (0 on odd)."""
+
+    @staticmethod
+    def forward(ctx, x, w12, b12, lidx):
+        lib = _lib.load()
+        x = x.contiguous()
+        N, R, C = x.shape
+        L1, h2, _ = w12.shape
+        h = h2 // 2
+        dev = x.device
+        O = torch.empty((N, R, h2), device=dev, dtype=torch.float32)
+        P = torch.empty((N, L1, h), device=dev, dtype=torch.float32)
+        st = stream_of(dev)
+        for m in range(R):
+            l = lidx[m]
+            first = m == l * l
+            xm = x[:, m, :]
+            check(lib.e2a_gemm_tf32x3_pairprod(ptr(xm), R * C, ptr(w12[l]), C, ptr(O[:, m, :]), R * h2,
+                                               ptr(b12) if m == 0 else None, ptr(P[:, l, :]), L1 * h, N, h2, C,
+                                               0 if first else 1, PASSES, st), "e2a_gemm_tf32x3_pairprod")
+        ctx.save_for_backward(O, w12)
+        ctx.lidx = lidx
+        return P
+
+    @staticmethod
+    def backward(ctx, G):
+        lib = _lib.load()
+        O, w12 = ctx.saved_tensors
+        G = G.contiguous()
+        N, R, h2 = O.shape
+        L1 = w12.shape[0]
+        C = w12.shape[2]
+        D = torch.empty_like(O)
+        check(lib.e2a_pair_grad(ptr(O), ptr(G), N, R, L1, h2 // 2, ptr(D), stream_of(O.device)), "e2a_pair_grad")
+        wt = w12.transpose(1, 2).contiguous()  # [L+1, C, 2h]
+        dx = torch.empty((N, R, C), device=O.device, dtype=torch.float32)
+        for m in range(R):
+            gemm(D[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :])
+        return dx, None, None, None
+
+
+def so3_pair_product(x, w1, w2, bias, lidx):
+    """Fused per-degree inner product of two per-degree linears (constant weights)."""
+    if not x.is_cuda:
+        raise ValueError("ubio_molfm_b200 kernels need CUDA tensors (there is no CPU path)")
+    L1, h, C = w1.shape
+    w12 = torch.stack([w1, w2], dim=2).reshape(L1, 2 * h, C).contiguous()
+    b12 = torch.stack([bias.reshape(-1), torch.zeros_like(bias.reshape(-1))], dim=1).reshape(2 * h).contiguous()
+    return _SO3PairProdFn.apply(x.float(), w12, b12, tuple(int(v) for v in lidx))

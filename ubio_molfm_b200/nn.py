@@ -115,16 +115,11 @@ class SO3_Linear2Scalar_e2former(nn.Module):
     def forward(self, x):
         shape = x.shape[:-2]
         x = x.reshape(-1, x.shape[-2], x.shape[-1])
-        if x.is_cuda:
-            # both projections in one tensor-core GEMM per row: [N, in] @ [in, 2*hidden]
-            w12 = torch.cat([_cw(self, self.weight), _cw(self, self.weight2)], dim=1)   # [L+1, 2h, in]
-            bb = _cw(self, self.bias).reshape(-1)
-            b12 = torch.cat([bb, torch.zeros_like(bb)])
-            o = tc.so3_linear(x, w12, b12, _degree_of_rows(self.lmax)[: x.shape[1]])  # [N, R, 2h]
-            o1, o2 = o[..., :self.hidden], o[..., self.hidden:]
-            prod = o1 * o2
-            parts = [prod[:, l * l:(l + 1) ** 2].sum(dim=1) for l in range(self.lmax + 1)]
-            h = torch.cat(parts, dim=-1)
+        if x.is_cuda and not self.training:
+            # both projections and the inner product over m in one tensor-core GEMM per row
+            h = tc.so3_pair_product(x, self.weight.detach(), self.weight2.detach(), self.bias.detach(),
+                                    _degree_of_rows(self.lmax)[: x.shape[1]])
+            h = h.reshape(x.shape[0], -1)
             fl = self.final_linear
             cwt = not self.training
             h = lin(h, fl[0].weight, fl[0].bias, cwt)
