@@ -359,3 +359,26 @@ def test_fused_ln_silu_matches_torch(W, tables):
     (gr,) = torch.autograd.grad(ref, hr, w)
     (gg,) = torch.autograd.grad(out, hg, w.float().to(DEV))
     assert (gg.double().cpu() - gr).abs().max().item() < 5e-5
+
+
+def test_node_half_fused_matches_torch():
+    from ubio_molfm_b200.nn import E2TensorProductSO2_FirstOrder
+    from ubio_molfm_b200.wigner import node_wigner
+
+    g = torch.Generator().manual_seed(5)
+    n, C = 300, 64
+    tp = E2TensorProductSO2_FirstOrder(C, C, 2, 8)
+    pos = torch.randn(n, 3, generator=g, dtype=torch.float64) * 3
+    h = torch.randn(n, 29, C, generator=g, dtype=torch.float64)[:, 20:]  # strided view like the layer's
+    W, Wi = node_wigner(pos, dtype=torch.float64)
+    ins = [W, Wi, h, pos]
+    ar = [t.clone().requires_grad_(True) for t in ins]
+    ref = tp.double().node_half(*ar)
+    ag = [t.float().to(DEV).requires_grad_(True) for t in ins]
+    out = tp.float().to(DEV).node_half(*ag)
+    assert (out.double().cpu() - ref).abs().max().item() < 1e-5 * max(1.0, ref.abs().max().item())
+    w = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    gr = torch.autograd.grad(ref, ar, w)
+    gg = torch.autograd.grad(out, ag, w.float().to(DEV))
+    for a, b in zip(gg, gr):
+        assert (a.double().cpu() - b).abs().max().item() < 2e-5 * max(1.0, b.abs().max().item())

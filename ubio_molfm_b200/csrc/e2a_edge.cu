@@ -200,3 +200,118 @@ int e2a_ln_silu_bwd(const float* x, const float* dy, const float* gamma, const f
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Node-local linear map of irreps rows: out[n, k, c] = sum_s A[n, k, s] h[n, s, c]  (A: [n, KO, KI]),
+// used for both halves of the first-order SO(2) tensor product (so2_tensor_product.py:363-385) with
+// A = W_inv diag(CG |pos|) S W.  One CTA per node, one thread per channel (coalesced rows).
+// Backward: dh = A^T dout, dA[n,k,s] = sum_c dout[n,k,c] h[n,s,c].
+// ------------------------------------------------------------------------------------------------
+namespace {
+// fixed shape of the first-order SO(2) product: 20 output rows from 9 input rows
+constexpr int KO = 20, KI = 9;
+
+__global__ void __launch_bounds__(256)
+k_node_apply_fwd(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
+                 int64_t n_nodes, int C, float* __restrict__ out, int64_t out_node_stride) {
+  __shared__ float As[KO * KI];
+  for (int64_t n = blockIdx.x; n < n_nodes; n += gridDim.x) {
+    __syncthreads();
+    for (int t = threadIdx.x; t < KO * KI; t += blockDim.x) As[t] = A[n * KO * KI + t];
+    __syncthreads();
+    const float* hn = h + n * h_node_stride;
+    float* on = out + n * out_node_stride;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float hv[KI];
+#pragma unroll
+      for (int s = 0; s < KI; ++s) hv[s] = __ldg(hn + (int64_t)s * C + c);
+#pragma unroll
+      for (int k = 0; k < KO; ++k) {
+        float acc = 0.f;
+#pragma unroll
+        for (int s = 0; s < KI; ++s) acc = fmaf(As[k * KI + s], hv[s], acc);
+        on[(int64_t)k * C + c] = acc;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
+                 const float* __restrict__ dout, int64_t dout_node_stride, int64_t n_nodes, int C,
+                 float* __restrict__ dh, float* __restrict__ dA) {
+  __shared__ float As[KO * KI];
+  __shared__ float red[KO * KI][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t n = blockIdx.x; n < n_nodes; n += gridDim.x) {
+    __syncthreads();
+    for (int t = threadIdx.x; t < KO * KI; t += blockDim.x) As[t] = A[n * KO * KI + t];
+    __syncthreads();
+    const float* hn = h + n * h_node_stride;
+    const float* gn = dout + n * dout_node_stride;
+    float pa[KO * KI];
+#pragma unroll
+    for (int t = 0; t < KO * KI; ++t) pa[t] = 0.f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float hv[KI], dv[KI];
+#pragma unroll
+      for (int s = 0; s < KI; ++s) { hv[s] = __ldg(hn + (int64_t)s * C + c); dv[s] = 0.f; }
+#pragma unroll
+      for (int k = 0; k < KO; ++k) {
+        const float g = __ldg(gn + (int64_t)k * C + c);
+#pragma unroll
+        for (int s = 0; s < KI; ++s) {
+          dv[s] = fmaf(As[k * KI + s], g, dv[s]);
+          pa[k * KI + s] = fmaf(g, hv[s], pa[k * KI + s]);
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < KI; ++s) dh[n * (int64_t)KI * C + (int64_t)s * C + c] = dv[s];
+    }
+    if (dA) {
+      // fixed-order reduction: warp shuffle, then the warp partials in order
+#pragma unroll
+      for (int t = 0; t < KO * KI; ++t) {
+        const float v = e2a_warp_sum(pa[t]);
+        if (lane == 0) red[t][warp] = v;
+      }
+      __syncthreads();
+      for (int t = threadIdx.x; t < KO * KI; t += blockDim.x) {
+        float v = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[t][w];
+        dA[n * KO * KI + t] = v;
+      }
+    }
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int e2a_node_apply_fwd(const float* A, const float* h, int64_t h_node_stride, int64_t n_nodes, int ko, int ki, int C,
+                       float* out, int64_t out_node_stride, void* stream) {
+  if (n_nodes < 0 || C <= 0) return E2A_ERR_ARG;
+  if (ko != KO || ki != KI) return E2A_ERR_UNSUPPORTED;
+  if (n_nodes == 0) return E2A_OK;
+  if (!A || !h || !out || h_node_stride < (int64_t)KI * C || out_node_stride < (int64_t)KO * C) return E2A_ERR_ARG;
+  const int64_t g = n_nodes < (1 << 30) ? n_nodes : (1 << 30);
+  k_node_apply_fwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, n_nodes, C, out, out_node_stride);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_node_apply_bwd(const float* A, const float* h, int64_t h_node_stride, const float* dout,
+                       int64_t dout_node_stride, int64_t n_nodes, int ko, int ki, int C, float* dh, float* dA,
+                       void* stream) {
+  if (n_nodes < 0 || C <= 0) return E2A_ERR_ARG;
+  if (ko != KO || ki != KI) return E2A_ERR_UNSUPPORTED;
+  if (n_nodes == 0) return E2A_OK;
+  if (!A || !h || !dout || !dh) return E2A_ERR_ARG;
+  const int64_t g = n_nodes < (1 << 30) ? n_nodes : (1 << 30);
+  k_node_apply_bwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, dout, dout_node_stride, n_nodes, C,
+                                                             dh, dA);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // extern "C"

@@ -213,3 +213,39 @@ def so3_pair_product(x, w1, w2, bias, lidx):
     w12 = torch.stack([w1, w2], dim=2).reshape(L1, 2 * h, C).contiguous()
     b12 = torch.stack([bias.reshape(-1), torch.zeros_like(bias.reshape(-1))], dim=1).reshape(2 * h).contiguous()
     return _SO3PairProdFn.apply(x.float(), w12, b12, tuple(int(v) for v in lidx))
+
+
+class _NodeApplyFn(torch.autograd.Function):
+    """out[n] = A[n] @ h[n] for A [n, 20, 9] and h [n, 9, C] (h may be a row-strided view)."""
+
+    @staticmethod
+    def forward(ctx, A, h):
+        lib = _lib.load()
+        A = A.contiguous()
+        n, KO, KI = A.shape
+        C = h.shape[2]
+        if h.stride(2) != 1 or h.stride(1) != C:
+            h = h.contiguous()
+        out = torch.empty((n, KO, C), device=h.device, dtype=torch.float32)
+        check(lib.e2a_node_apply_fwd(ptr(A), ptr(h), h.stride(0), n, KO, KI, C, ptr(out), out.stride(0),
+                                     stream_of(h.device)), "e2a_node_apply_fwd")
+        ctx.save_for_backward(A, h)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        A, h = ctx.saved_tensors
+        g = g.contiguous()
+        n, KO, KI = A.shape
+        C = h.shape[2]
+        dh = torch.empty((n, KI, C), device=h.device, dtype=torch.float32)
+        dA = torch.empty_like(A) if ctx.needs_input_grad[0] else None
+        check(lib.e2a_node_apply_bwd(ptr(A), ptr(h), h.stride(0), ptr(g), g.stride(0), n, KO, KI, C, ptr(dh), ptr(dA),
+                                     stream_of(h.device)), "e2a_node_apply_bwd")
+        return dA, dh
+
+
+def node_apply(A, h):
+    """Per-node [20 x 9] map of irreps rows (CUDA)."""
+    return _NodeApplyFn.apply(A.float(), h.float())

@@ -263,6 +263,15 @@ class E2TensorProductSO2_FirstOrder(nn.Module):
         self.so2_tp = SO2_TP_givenl2(lmax, in_c, out_c, with_linear=True)
 
     def node_half(self, wigner, wigner_inv, h, pos):
-        """W_inv @ (CG-select(W @ h) * |pos|): the per-node half of h (x) r."""
-        y = self.so2_tp(torch.bmm(wigner, h), with_linear=False) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
+        """W_inv @ (CG-select(W @ h) * |pos|): the per-node half of h (x) r.
+
+        On CUDA the whole map is one per-node [20 x 9] matrix A = W_inv diag(CG |pos|) S W, built with
+        small batched products (autograd carries the Wigner / position gradients) and applied to the
+        [9, C] rows by one kernel."""
+        tp = self.so2_tp
+        if h.is_cuda:
+            scale = tp.CG_weight.reshape(1, -1, 1) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
+            A = torch.bmm(wigner_inv, wigner[:, tp.selected_idx, :] * scale)          # [n, 20, 9]
+            return tc.node_apply(A, h)
+        y = tp(torch.bmm(wigner, h), with_linear=False) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
         return torch.bmm(wigner_inv, y)
