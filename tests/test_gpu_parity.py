@@ -263,12 +263,13 @@ def test_attention_span_random_graphs(H, D, C):
     _span_parity(N, M, q, n, H, D, C, seed=H)
 
 
-def test_attention_span_ties_and_empty_rows():
+@pytest.mark.parametrize("H", [8, 128])
+def test_attention_span_ties_and_empty_rows(H):
     # gate = 0 makes every logit of a row equal: the max gradient is shared among all of them
     N, M = 30, 40
     q = np.sort(np.random.default_rng(4).integers(0, N - 5, 400))  # the last 5 rows have no edges
     n = np.random.default_rng(5).integers(0, M, 400)
-    out = _span_parity(N, M, q, n, 8, 8, 16, seed=9, gate_zero=True)
+    out = _span_parity(N, M, q, n, H, 8, 16, seed=9, gate_zero=True)
     assert torch.all(out[N - 5:] == 0)
 
 

@@ -379,6 +379,190 @@ k_softmax_bwd(const float* __restrict__ q, const float* __restrict__ k, const fl
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Warp-per-row softmax kernels for H = 32 * HPL heads of width D (full config: HPL = 4, D = 8):
+// lane l owns heads [l*HPL, (l+1)*HPL), so every per-head row statistic is lane-local and the q.k
+// dot needs only the lane's own HPL*D-float slice of each k row (coalesced across the warp).
+// ------------------------------------------------------------------------------------------------
+template <int HPL, int D>
+__global__ void __launch_bounds__(kThreads)
+k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
+                   const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
+                   const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
+                   const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows,
+                   float* __restrict__ beta, float* __restrict__ row_max, float* __restrict__ row_sum) {
+  static_assert(HPL == 4, "float4 head groups");
+  constexpr int H = 32 * HPL, F4 = HPL * D / 4;  // float4 per lane slice
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (r >= n_rows) return;
+  const int i = row_of(order, r);
+  const int rs = row_ptr[i], re = row_ptr[i + 1];
+  float4 qv[F4];
+  const float* qr = q + (int64_t)i * H * D + lane * HPL * D;
+#pragma unroll
+  for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
+  float m[HPL];
+#pragma unroll
+  for (int u = 0; u < HPL; ++u) m[u] = -INFINITY;
+  for (int e = rs; e < re; ++e) {
+    const float* kr = k + (int64_t)col[e] * H * D + lane * HPL * D;
+    float sv[HPL];
+#pragma unroll
+    for (int u = 0; u < HPL; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < D / 4; ++t) {
+        const float4 kv = ldg4(kr + 4 * (u * (D / 4) + t));
+        const float4 qq = qv[u * (D / 4) + t];
+        acc += qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
+      }
+      sv[u] = acc;
+    }
+    const float4 g = ldg4(gate + (int64_t)e * ld_gi + lane * HPL);
+    const float4 a = make_float4(g.x * sv[0], g.y * sv[1], g.z * sv[2], g.w * sv[3]);
+    *reinterpret_cast<float4*>(beta + (int64_t)e * H + lane * HPL) = a;
+    m[0] = fmaxf(m[0], a.x); m[1] = fmaxf(m[1], a.y); m[2] = fmaxf(m[2], a.z); m[3] = fmaxf(m[3], a.w);
+  }
+  float S[HPL] = {0.f, 0.f, 0.f, 0.f};
+  for (int e = rs; e < re; ++e) {
+    float4* bp = reinterpret_cast<float4*>(beta + (int64_t)e * H + lane * HPL);
+    const float4 a = *bp;
+    const float p = poly[e];
+    const float4 x = make_float4(expf(a.x - m[0]) * p, expf(a.y - m[1]) * p, expf(a.z - m[2]) * p, expf(a.w - m[3]) * p);
+    *bp = x;
+    S[0] += x.x; S[1] += x.y; S[2] += x.z; S[3] += x.w;
+  }
+  const float den[HPL] = {S[0] + kSoftmaxEps, S[1] + kSoftmaxEps, S[2] + kSoftmaxEps, S[3] + kSoftmaxEps};
+  for (int e = rs; e < re; ++e) {
+    float4* bp = reinterpret_cast<float4*>(beta + (int64_t)e * H + lane * HPL);
+    const float4 x = *bp;
+    const float4 ih = ldg4(inputhead + (int64_t)e * ld_gi + lane * HPL);
+    const float rr = fmaxf(dist[e], kMinDist);
+    *bp = make_float4(x.x * ih.x / den[0] / rr, x.y * ih.y / den[1] / rr, x.z * ih.z / den[2] / rr,
+                      x.w * ih.w / den[3] / rr);
+  }
+  *reinterpret_cast<float4*>(row_max + (int64_t)i * H + lane * HPL) = make_float4(m[0], m[1], m[2], m[3]);
+  *reinterpret_cast<float4*>(row_sum + (int64_t)i * H + lane * HPL) = make_float4(S[0], S[1], S[2], S[3]);
+}
+
+template <int HPL, int D>
+__global__ void __launch_bounds__(kThreads)
+k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
+                   const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
+                   const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
+                   const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows,
+                   const float* __restrict__ beta, const float* __restrict__ row_max,
+                   const float* __restrict__ row_sum, float* __restrict__ d_gate, float* __restrict__ d_inputhead,
+                   int64_t ld_dgi, float* __restrict__ d_poly, float* __restrict__ d_dist,
+                   float* __restrict__ d_logit, const float* __restrict__ bufA, float* __restrict__ bufB) {
+  static_assert(HPL == 4, "float4 head groups");
+  constexpr int H = 32 * HPL, F4 = HPL * D / 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (r >= n_rows) return;
+  const int i = row_of(order, r);
+  const int rs = row_ptr[i], re = row_ptr[i + 1];
+  if (rs == re) return;
+  const int ho = lane * HPL;
+  float4 qv[F4];
+  const float* qr = q + (int64_t)i * H * D + ho * D;
+#pragma unroll
+  for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
+  const float4 mv = ldg4(row_max + (int64_t)i * H + ho), sv4 = ldg4(row_sum + (int64_t)i * H + ho);
+  const float m[HPL] = {mv.x, mv.y, mv.z, mv.w};
+  const float den[HPL] = {sv4.x + kSoftmaxEps, sv4.y + kSoftmaxEps, sv4.z + kSoftmaxEps, sv4.w + kSoftmaxEps};
+  // pass 1: s = q.k -> bufB; T_h = sum_e d_alpha * alpha
+  float T[HPL] = {0.f, 0.f, 0.f, 0.f};
+  for (int e = rs; e < re; ++e) {
+    const float* kr = k + (int64_t)col[e] * H * D + ho * D;
+    float s[HPL];
+#pragma unroll
+    for (int u = 0; u < HPL; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < D / 4; ++t) {
+        const float4 kv = ldg4(kr + 4 * (u * (D / 4) + t));
+        const float4 qq = qv[u * (D / 4) + t];
+        acc += qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
+      }
+      s[u] = acc;
+    }
+    *reinterpret_cast<float4*>(bufB + (int64_t)e * H + ho) = make_float4(s[0], s[1], s[2], s[3]);
+    const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho), ih4 = ldg4(inputhead + (int64_t)e * ld_gi + ho);
+    const float4 db4 = *reinterpret_cast<const float4*>(bufA + (int64_t)e * H + ho);
+    const float g[HPL] = {g4.x, g4.y, g4.z, g4.w}, ih[HPL] = {ih4.x, ih4.y, ih4.z, ih4.w};
+    const float db[HPL] = {db4.x, db4.y, db4.z, db4.w};
+    const float p = poly[e], rr = fmaxf(dist[e], kMinDist);
+#pragma unroll
+    for (int u = 0; u < HPL; ++u) {
+      const float x = expf(g[u] * s[u] - m[u]) * p;
+      const float al = x * ih[u] / den[u];
+      T[u] += (db[u] / rr) * al;
+    }
+  }
+  float dS[HPL];
+#pragma unroll
+  for (int u = 0; u < HPL; ++u) dS[u] = -T[u] / den[u];
+  // pass 2: dz, d_inputhead, d_dist, d_poly; dm and tie counts
+  float dmacc[HPL] = {0.f, 0.f, 0.f, 0.f}, nt[HPL] = {0.f, 0.f, 0.f, 0.f};
+  for (int e = rs; e < re; ++e) {
+    const float4 s4 = *reinterpret_cast<const float4*>(bufB + (int64_t)e * H + ho);
+    const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho), ih4 = ldg4(inputhead + (int64_t)e * ld_gi + ho);
+    const float4 db4 = *reinterpret_cast<const float4*>(bufA + (int64_t)e * H + ho);
+    const float4 b4 = ldg4(beta + (int64_t)e * H + ho);
+    const float s[HPL] = {s4.x, s4.y, s4.z, s4.w}, g[HPL] = {g4.x, g4.y, g4.z, g4.w};
+    const float ih[HPL] = {ih4.x, ih4.y, ih4.z, ih4.w}, db[HPL] = {db4.x, db4.y, db4.z, db4.w};
+    const float bt[HPL] = {b4.x, b4.y, b4.z, b4.w};
+    const float p = poly[e], d = dist[e], rr = fmaxf(d, kMinDist);
+    float dih[HPL], dz[HPL], sd = 0.f, sp = 0.f;
+#pragma unroll
+    for (int u = 0; u < HPL; ++u) {
+      const float a = g[u] * s[u];
+      const float ex = expf(a - m[u]);
+      const float x = ex * p;
+      const float dal = db[u] / rr;
+      const float dx = dal * ih[u] / den[u] + dS[u];
+      dih[u] = dal * x / den[u];
+      dz[u] = dx * x;
+      dmacc[u] -= dz[u];
+      nt[u] += (a == m[u]) ? 1.f : 0.f;
+      sd += db[u] * bt[u];
+      sp += dx * ex;
+    }
+    *reinterpret_cast<float4*>(d_inputhead + (int64_t)e * ld_dgi + ho) = make_float4(dih[0], dih[1], dih[2], dih[3]);
+    *reinterpret_cast<float4*>(d_logit + (int64_t)e * H + ho) = make_float4(dz[0], dz[1], dz[2], dz[3]);
+    sd = e2a_warp_sum(sd);
+    sp = e2a_warp_sum(sp);
+    if (lane == 0) {
+      d_dist[e] = d >= kMinDist ? -sd / rr : 0.f;
+      d_poly[e] = sp;
+    }
+  }
+  // pass 3: da = dz + [a == m] dm / n_ties (PyTorch's amax rule); d_gate = da * s; ds = da * gate
+  float share[HPL];
+#pragma unroll
+  for (int u = 0; u < HPL; ++u) share[u] = nt[u] > 0.f ? dmacc[u] / nt[u] : 0.f;
+  for (int e = rs; e < re; ++e) {
+    const float4 s4 = *reinterpret_cast<const float4*>(bufB + (int64_t)e * H + ho);
+    const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho);
+    float4* dl = reinterpret_cast<float4*>(d_logit + (int64_t)e * H + ho);
+    const float4 dz4 = *dl;
+    const float s[HPL] = {s4.x, s4.y, s4.z, s4.w}, g[HPL] = {g4.x, g4.y, g4.z, g4.w};
+    const float dz[HPL] = {dz4.x, dz4.y, dz4.z, dz4.w};
+    float dg[HPL], ds[HPL];
+#pragma unroll
+    for (int u = 0; u < HPL; ++u) {
+      const float a = g[u] * s[u];
+      const float da = dz[u] + ((a == m[u]) ? share[u] : 0.f);
+      dg[u] = da * s[u];
+      ds[u] = da * g[u];
+    }
+    *reinterpret_cast<float4*>(d_gate + (int64_t)e * ld_dgi + ho) = make_float4(dg[0], dg[1], dg[2], dg[3]);
+    *dl = make_float4(ds[0], ds[1], ds[2], ds[3]);
+  }
+}
+
 int check_dims(int H, int D, int C, Dims& dm, int& ks) {
   if (H <= 0 || D <= 0 || C <= 0) return E2A_ERR_ARG;
   if (H % 4 || kThreads % H) return E2A_ERR_UNSUPPORTED;
@@ -449,6 +633,9 @@ int launch_agg_hd(const float* X, const float* w, const Dims& dm, const int32_t*
   return E2A_OK;
 }
 
+// the warp-per-row softmax path: 128 heads of width 8 (4 heads per lane), 16-byte-aligned edge rows
+bool warp_softmax_ok(const Dims& dm, int64_t ld_gi) { return dm.H == 128 && dm.D == 8 && ld_gi % 4 == 0; }
+
 size_t softmax_smem(const Dims& dm, int extra_h) { return (size_t)dm.HD4 * 16 + (kThreads + extra_h * dm.H) * 4; }
 
 // Query-side backward with caller-provided scratch bufA/bufB ([E,H] each).
@@ -470,11 +657,17 @@ int bwd_query_launch(const float* q, const float* k, const float* value, const f
     });
   }
   E2A_CHECK_LAUNCH();
-  const size_t ssm = softmax_smem(dm, 3);
-  E2A_CUDA(prep_smem(k_softmax_bwd, ssm));
-  k_softmax_bwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                                         row_order, n_rows, dm, beta, row_max, row_sum, d_gate,
-                                                         d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
+  if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
+    k_softmax_bwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+        q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
+        d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
+  } else {
+    const size_t ssm = softmax_smem(dm, 3);
+    E2A_CUDA(prep_smem(k_softmax_bwd, ssm));
+    k_softmax_bwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                           row_order, n_rows, dm, beta, row_max, row_sum, d_gate,
+                                                           d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
+  }
   E2A_CHECK_LAUNCH();
   // d_q[i] = sum_e ds[e] k[j]  (isolated rows get zeros from the empty sum)
   return launch_agg_hd(k, d_logit, dm, row_ptr, col, nullptr, row_order, n_rows, d_q, st);
@@ -497,10 +690,15 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value, const float
   if (!q || !row_ptr || !out || !row_max || !row_sum) return E2A_ERR_ARG;
   if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t ssm = softmax_smem(dm, 2);
-  E2A_CUDA(prep_smem(k_softmax_fwd, ssm));
-  k_softmax_fwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                                         row_order, n_rows, dm, beta, row_max, row_sum);
+  if (warp_softmax_ok(dm, ld_gi)) {
+    k_softmax_fwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+        q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum);
+  } else {
+    const size_t ssm = softmax_smem(dm, 2);
+    E2A_CUDA(prep_smem(k_softmax_fwd, ssm));
+    k_softmax_fwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                           row_order, n_rows, dm, beta, row_max, row_sum);
+  }
   E2A_CHECK_LAUNCH();
   return launch_agg_ch(value, beta, dm, ks, row_ptr, col, nullptr, row_order, n_rows, out, st);
 }
