@@ -236,50 +236,50 @@ k_node_apply_fwd(const float* __restrict__ A, const float* __restrict__ h, int64
   }
 }
 
+// One CTA per node: dh[s,c] = sum_k A[k,s] dout[k,c] with one thread per channel; dA[k,s] with one
+// warp per output row k (lanes over channels, 9 warp sums per k, fixed order).  The node's rows are
+// read straight from global memory (they stay in L1 across the two loops).
 __global__ void __launch_bounds__(256)
 k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
-                 const float* __restrict__ dout, int64_t dout_node_stride, int64_t n_nodes, int C,
-                 float* __restrict__ dh, float* __restrict__ dA) {
+                        const float* __restrict__ dout, int64_t dout_node_stride, int64_t n_nodes, int C,
+                        float* __restrict__ dh, float* __restrict__ dA) {
   __shared__ float As[KO * KI];
-  __shared__ float red[KO * KI][8];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   for (int64_t n = blockIdx.x; n < n_nodes; n += gridDim.x) {
     __syncthreads();
     for (int t = threadIdx.x; t < KO * KI; t += blockDim.x) As[t] = A[n * KO * KI + t];
     __syncthreads();
     const float* hn = h + n * h_node_stride;
     const float* gn = dout + n * dout_node_stride;
-    float pa[KO * KI];
-#pragma unroll
-    for (int t = 0; t < KO * KI; ++t) pa[t] = 0.f;
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
-      float hv[KI], dv[KI];
+      float dv[KI];
 #pragma unroll
-      for (int s = 0; s < KI; ++s) { hv[s] = __ldg(hn + (int64_t)s * C + c); dv[s] = 0.f; }
+      for (int s = 0; s < KI; ++s) dv[s] = 0.f;
 #pragma unroll
       for (int k = 0; k < KO; ++k) {
         const float g = __ldg(gn + (int64_t)k * C + c);
 #pragma unroll
-        for (int s = 0; s < KI; ++s) {
-          dv[s] = fmaf(As[k * KI + s], g, dv[s]);
-          pa[k * KI + s] = fmaf(g, hv[s], pa[k * KI + s]);
-        }
+        for (int s = 0; s < KI; ++s) dv[s] = fmaf(As[k * KI + s], g, dv[s]);
       }
 #pragma unroll
       for (int s = 0; s < KI; ++s) dh[n * (int64_t)KI * C + (int64_t)s * C + c] = dv[s];
     }
     if (dA) {
-      // fixed-order reduction: warp shuffle, then the warp partials in order
+      for (int k = warp; k < KO; k += nwarp) {
+        float p[KI];
 #pragma unroll
-      for (int t = 0; t < KO * KI; ++t) {
-        const float v = e2a_warp_sum(pa[t]);
-        if (lane == 0) red[t][warp] = v;
-      }
-      __syncthreads();
-      for (int t = threadIdx.x; t < KO * KI; t += blockDim.x) {
-        float v = 0.f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[t][w];
-        dA[n * KO * KI + t] = v;
+        for (int s = 0; s < KI; ++s) p[s] = 0.f;
+        for (int c = lane; c < C; c += 32) {
+          const float g = __ldg(gn + (int64_t)k * C + c);
+#pragma unroll
+          for (int s = 0; s < KI; ++s) p[s] = fmaf(g, __ldg(hn + (int64_t)s * C + c), p[s]);
+        }
+#pragma unroll
+        for (int s = 0; s < KI; ++s) p[s] = e2a_warp_sum(p[s]);
+        if (lane == 0) {
+#pragma unroll
+          for (int s = 0; s < KI; ++s) dA[n * KO * KI + k * KI + s] = p[s];
+        }
       }
     }
   }

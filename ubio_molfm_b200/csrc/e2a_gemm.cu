@@ -251,16 +251,11 @@ k_gemm_tf32x3(const float* __restrict__ A, int64_t lda, const float* __restrict_
 
 
 // ------------------------------------------------------------------------------------------------
-// Pipelined variant for 16-byte-aligned operands: raw fp32 slabs arrive by cp.async (16-byte
-// copies, zero-filled past the matrix edge, destination already in the swizzled layout) RAW_STAGES
-// slabs ahead; each slab is split shared -> shared into one of two hi/lo operand buffers while the
-// tensor core works on the other.  Global-memory latency is off the critical path.
+// Pipelined kernel for 16-byte-aligned operands: raw fp32 slabs arrive by cp.async (16-byte copies,
+// zero-filled past the matrix edge, destination already in the swizzled layout) several slabs ahead;
+// each slab is split shared -> shared into one of two hi/lo operand buffers while the tensor core
+// works on the other.  Global-memory latency is off the critical path.
 // ------------------------------------------------------------------------------------------------
-constexpr int RAW_STAGES = 3;
-constexpr int kRawBytes = 2 * kTileBytes;                    // A and B raw slab
-constexpr int kOpBytes = 4 * kTileBytes;                     // A_hi, A_lo, B_hi, B_lo
-constexpr int kSmemAsync = RAW_STAGES * kRawBytes + 2 * kOpBytes + 1024 + 256;
-
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -268,23 +263,41 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ void issue_slab(const float* __restrict__ X, int64_t ld, int rows, int K, int r0, int k0,
-                                           uint32_t dst) {
+// ------------------------------------------------------------------------------------------------
+// v2: 16-wide k-slabs in the 64-byte-swizzled K-major layout (8-row atoms of 512 B, 16-byte chunk c
+// of row r at c ^ ((r >> 1) & 3)).  112 KB of shared memory and <= 128 registers per thread, so two
+// CTAs (two 256-column TMEM allocations) share an SM and overlap each other's stalls.
+// ------------------------------------------------------------------------------------------------
+constexpr int BK2 = 16;
+constexpr int kTile2 = BM * BK2 * 4;                 // 8 KB per operand part
+constexpr int kRaw2 = 2 * kTile2;                    // A and B raw slab
+constexpr int kOp2 = 4 * kTile2;                     // A_hi, A_lo, B_hi, B_lo
+constexpr int RAW2 = 3;
+constexpr int kSmem2 = RAW2 * kRaw2 + 2 * kOp2 + 256;
+constexpr int kF4PerThread2 = (BM * BK2 / 4) / kThreads;   // 2
+
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
+  // K-major, 64-byte swizzle: LBO unused (1), SBO = 512 B between 8-row atoms, version 1
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
+}
+
+__device__ __forceinline__ void issue_slab2(const float* __restrict__ X, int64_t ld, int rows, int K, int r0, int k0,
+                                            uint32_t dst) {
 #pragma unroll
-  for (int j = 0; j < kF4PerThread; ++j) {
+  for (int j = 0; j < kF4PerThread2; ++j) {
     const int c = threadIdx.x + j * kThreads;
-    const int r = c >> 3, ch = c & 7;
+    const int r = c >> 2, ch = c & 3;
     const int gr = r0 + r, gk = k0 + ch * 4;
     const int valid = (gr < rows && gk < K) ? min(4, K - gk) : 0;
     const float* src = valid ? X + (int64_t)gr * ld + gk : X;
-    cp_async16(dst + (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)), src, (uint32_t)valid * 4u);
+    cp_async16(dst + (uint32_t)(r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)), src, (uint32_t)valid * 4u);
   }
 }
 
-__device__ __forceinline__ void split_smem(const uint8_t* raw, uint8_t* hi, uint8_t* lo) {
+__device__ __forceinline__ void split_smem2(const uint8_t* raw, uint8_t* hi, uint8_t* lo) {
 #pragma unroll
-  for (int j = 0; j < kF4PerThread; ++j) {
-    const int off = (threadIdx.x + j * kThreads) * 16;  // same swizzled offset in and out
+  for (int j = 0; j < kF4PerThread2; ++j) {
+    const int off = (threadIdx.x + j * kThreads) * 16;
     const float4 v = *reinterpret_cast<const float4*>(raw + off);
     float4 h, l;
     h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
@@ -294,20 +307,21 @@ __device__ __forceinline__ void split_smem(const uint8_t* raw, uint8_t* hi, uint
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
-                    int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes,
-                    float* P, int64_t ldp) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = e2a_smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* raw = smem;                                        // RAW_STAGES x (A, B)
-  uint8_t* ops = smem + RAW_STAGES * kRawBytes;               // 2 x (A_hi, A_lo, B_hi, B_lo)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ops + 2 * kOpBytes);  // one per operand buffer
+__global__ void __launch_bounds__(kThreads, 2)
+k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
+                 int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes,
+                 float* P, int64_t ldp) {
+  extern __shared__ __align__(1024) uint8_t smem2[];
+  if ((e2a_smem_u32(smem2) & 1023u) != 0) {  // the descriptors assume 1 KB-aligned tiles
+    if (threadIdx.x == 0) atomicOr(&g_e2a_gemm_status, 2u);
+    return;
+  }
+  uint8_t* raw = smem2;
+  uint8_t* ops = smem2 + RAW2 * kRaw2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ops + 2 * kOp2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(e2a_smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
@@ -318,14 +332,13 @@ k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __res
     e2a_mbar_init(&bars[1], 1);
     e2a_fence_mbar_init();
   }
-  const int nk = (K + BK - 1) / BK;
-  // prologue: raw slabs 0 .. RAW_STAGES-2 in flight (one commit group each, possibly empty)
+  const int nk = (K + BK2 - 1) / BK2;
 #pragma unroll
-  for (int p = 0; p < RAW_STAGES - 1; ++p) {
+  for (int p = 0; p < RAW2 - 1; ++p) {
     if (p < nk) {
-      const uint32_t d = e2a_smem_u32(raw + p * kRawBytes);
-      issue_slab(A, lda, M, K, m0, p * BK, d);
-      issue_slab(B, ldb, N, K, n0, p * BK, d + kTileBytes);
+      const uint32_t d = e2a_smem_u32(raw + p * kRaw2);
+      issue_slab2(A, lda, M, K, m0, p * BK2, d);
+      issue_slab2(B, ldb, N, K, n0, p * BK2, d + kTile2);
     }
     cp_async_commit();
   }
@@ -340,38 +353,36 @@ k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __res
   for (int i = 0; i < BN / 2; ++i) acc[i] = 0.f;
   bool ok = true;
   for (int kb = 0; kb < nk; ++kb) {
-    // keep RAW_STAGES-1 slabs in flight: slab kb + RAW_STAGES - 1 into the stage freed last iteration
     {
-      const int p = kb + RAW_STAGES - 1;
+      const int p = kb + RAW2 - 1;
       if (p < nk) {
-        const uint32_t d = e2a_smem_u32(raw + (p % RAW_STAGES) * kRawBytes);
-        issue_slab(A, lda, M, K, m0, p * BK, d);
-        issue_slab(B, ldb, N, K, n0, p * BK, d + kTileBytes);
+        const uint32_t d = e2a_smem_u32(raw + (p % RAW2) * kRaw2);
+        issue_slab2(A, lda, M, K, m0, p * BK2, d);
+        issue_slab2(B, ldb, N, K, n0, p * BK2, d + kTile2);
       }
       cp_async_commit();
     }
-    cp_async_wait<RAW_STAGES - 1>();  // this thread's copies of slab kb have landed
-    __syncthreads();                  // ... and everybody's
-    // operand buffer kb & 1 was last read by the MMAs of slab kb-2, drained in iteration kb-1
-    const uint8_t* rs = raw + (kb % RAW_STAGES) * kRawBytes;
-    uint8_t* op = ops + (kb & 1) * kOpBytes;
-    split_smem(rs, op, op + kTileBytes);
-    split_smem(rs + kTileBytes, op + 2 * kTileBytes, op + 3 * kTileBytes);
+    cp_async_wait<RAW2 - 1>();
+    __syncthreads();
+    const uint8_t* rs = raw + (kb % RAW2) * kRaw2;
+    uint8_t* op = ops + (kb & 1) * kOp2;
+    split_smem2(rs, op, op + kTile2);
+    split_smem2(rs + kTile2, op + 2 * kTile2, op + 3 * kTile2);
     e2a_fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     if (threadIdx.x == 0) {
       tc_fence_after();
       const uint32_t d = tmem + (uint32_t)((kb & 1) * BN);
-      const uint32_t a_hi = e2a_smem_u32(op), a_lo = a_hi + kTileBytes;
-      const uint32_t b_hi = a_hi + 2 * kTileBytes, b_lo = a_hi + 3 * kTileBytes;
+      const uint32_t a_hi = e2a_smem_u32(op), a_lo = a_hi + kTile2;
+      const uint32_t b_hi = a_hi + 2 * kTile2, b_lo = a_hi + 3 * kTile2;
 #pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
+      for (int kk = 0; kk < BK2 / 8; ++kk) {
         const uint32_t koff = kk * 32;
-        mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_hi + koff), kk > 0 ? 1u : 0u);
+        mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_hi + koff), kk > 0 ? 1u : 0u);
         if (passes == 3) {
-          mma_tf32(d, smem_desc_sw128(a_hi + koff), smem_desc_sw128(b_lo + koff), 1u);
-          mma_tf32(d, smem_desc_sw128(a_lo + koff), smem_desc_sw128(b_hi + koff), 1u);
+          mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_lo + koff), 1u);
+          mma_tf32(d, smem_desc_sw64(a_lo + koff), smem_desc_sw64(b_hi + koff), 1u);
         }
       }
       mma_commit(&bars[kb & 1]);
@@ -409,10 +420,8 @@ k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __res
   }
   const bool all_ok = !__syncthreads_or(!ok);
   if (all_ok) {
-    // stage the tile through shared memory (row stride 132 floats: conflict-free 16-byte stores)
-    // so that every warp then writes whole 512-byte rows of C
     constexpr int kLd = BN + 4;
-    float* tile = reinterpret_cast<float*>(ops);
+    float* tile = reinterpret_cast<float*>(smem2);  // raw + operand region, idle now (67.6 KB used)
     {
       float* trow = tile + (32 * q + lane) * kLd + 64 * half;
 #pragma unroll
@@ -435,8 +444,6 @@ k_gemm_tf32x3_async(const float* __restrict__ A, int64_t lda, const float* __res
       float4 x = *reinterpret_cast<const float4*>(tile + r * kLd + 4 * lane);
       x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
       if (P) {
-        // pair-product mode: columns (2j, 2j+1) hold (o1_j, o2_j); P[row, j] (+)= o1_j * o2_j, and C
-        // (optional) receives the raw values for the backward
         float* pp = P + (int64_t)row * ldp + (gc >> 1);
         if (gc + 1 < N) pp[0] = (accumulate ? pp[0] : 0.f) + x.x * x.y;
         if (gc + 3 < N) pp[1] = (accumulate ? pp[1] : 0.f) + x.z * x.w;
@@ -492,9 +499,9 @@ int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, fl
                    ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
   dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
   if (vec) {
-    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_async, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAsync));
-    k_gemm_tf32x3_async<<<grid, kThreads, kSmemAsync, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                            accumulate, passes, nullptr, 0);
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
+    k_gemm_tf32x3_v2<<<grid, kThreads, kSmem2, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                     accumulate, passes, nullptr, 0);
   } else {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     k_gemm_tf32x3<false><<<grid, kThreads, kSmemBytes, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
@@ -516,9 +523,9 @@ int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_
   if (!vec) return E2A_ERR_UNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-  E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_async, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAsync));
-  k_gemm_tf32x3_async<<<grid, kThreads, kSmemAsync, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                          accumulate, passes, P, ldp);
+  E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
+  k_gemm_tf32x3_v2<<<grid, kThreads, kSmem2, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                   accumulate, passes, P, ldp);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }
