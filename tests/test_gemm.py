@@ -6,7 +6,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 200, 70), (1000, 512, 256), (4099, 1024, 1536),
-                                   (7, 3, 5), (129, 130, 0), (256, 128, 1)])
+                                   (7, 3, 5), (129, 130, 0), (256, 128, 1), (300, 260, 48), (200, 140, 64), (131, 129, 16)])
 def test_gemm_tf32x3_matches_fp64(M, N, K):
     from ubio_molfm_b200._lib import device_status_gemm
     from ubio_molfm_b200.linear import gemm

@@ -352,6 +352,19 @@ k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restri
 #pragma unroll
   for (int i = 0; i < BN / 2; ++i) acc[i] = 0.f;
   bool ok = true;
+  // Slabs kb = 2g, 2g+1 accumulate into TMEM buffer g & 1 (a 12-MMA chain, like a 32-wide slab);
+  // group g-1 is drained into the fp32 registers while group g runs.  Every wait targets the latest
+  // or the second-latest commit on its barrier, so a parity never wraps.
+  auto drain = [&](int g) {
+    tc_fence_after();
+#pragma unroll
+    for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + (uint32_t)((g & 1) * BN + 64 * half + c0), v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
+    }
+  };
   for (int kb = 0; kb < nk; ++kb) {
     {
       const int p = kb + RAW2 - 1;
@@ -361,6 +374,11 @@ k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restri
         issue_slab2(B, ldb, N, K, n0, p * BK2, d + kTile2);
       }
       cp_async_commit();
+    }
+    // operand buffer kb & 1 was read by the MMAs of slab kb-2
+    if (kb >= 2) {
+      ok = e2a_mbar_wait_bounded(&bars[kb & 1], ((kb - 2) >> 1) & 1, &g_e2a_gemm_status);
+      if (__syncthreads_or(!ok)) { ok = false; break; }
     }
     cp_async_wait<RAW2 - 1>();
     __syncthreads();
@@ -373,13 +391,14 @@ k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restri
     __syncthreads();
     if (threadIdx.x == 0) {
       tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)((kb & 1) * BN);
+      const uint32_t d = tmem + (uint32_t)(((kb >> 1) & 1) * BN);
       const uint32_t a_hi = e2a_smem_u32(op), a_lo = a_hi + kTile2;
       const uint32_t b_hi = a_hi + 2 * kTile2, b_lo = a_hi + 3 * kTile2;
 #pragma unroll
       for (int kk = 0; kk < BK2 / 8; ++kk) {
         const uint32_t koff = kk * 32;
-        mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_hi + koff), kk > 0 ? 1u : 0u);
+        const uint32_t first = ((kb & 1) == 0 && kk == 0) ? 0u : 1u;
+        mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_hi + koff), first);
         if (passes == 3) {
           mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_lo + koff), 1u);
           mma_tf32(d, smem_desc_sw64(a_lo + koff), smem_desc_sw64(b_hi + koff), 1u);
@@ -387,35 +406,24 @@ k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restri
       }
       mma_commit(&bars[kb & 1]);
     }
-    if (kb >= 1) {
-      const int pk = kb - 1;
-      ok = e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
-      if (__syncthreads_or(!ok)) { ok = false; break; }
-      tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
-      }
+    // drain group (kb >> 1) - 1 before its TMEM buffer is reused by the next group.  Its last slab,
+    // kb - 2, was awaited at the top of this iteration (waiting for it again here could see the
+    // barrier's parity already advanced by slab kb's commit).
+    if ((kb & 1) == 1 && kb >= 3) {
+      drain((kb >> 1) - 1);
+      tc_fence_before();
     }
   }
   cp_async_wait<0>();
+  // drain the remaining (one or two) groups
   if (ok && nk > 0) {
-    const int pk = nk - 1;
-    ok = e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
-    if (!__syncthreads_or(!ok)) {
-      tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)((pk & 1) * BN + 64 * half + c0), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
-      }
-    } else {
-      ok = false;
+    const int last_group = (nk - 1) >> 1;
+    const int first_left = (nk >= 4 && (((nk - 1) & 1) == 1)) ? last_group : (nk >= 3 ? last_group - 1 : 0);
+    for (int g = first_left; g <= last_group && ok; ++g) {
+      const int last = min(2 * g + 1, nk - 1);
+      ok = e2a_mbar_wait_bounded(&bars[last & 1], (last >> 1) & 1, &g_e2a_gemm_status);
+      if (__syncthreads_or(!ok)) { ok = false; break; }
+      drain(g);
     }
   }
   const bool all_ok = !__syncthreads_or(!ok);
