@@ -198,13 +198,17 @@ int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_
 int e2a_pair_grad(const float* O, const float* G, int64_t n_nodes, int R, int L1, int h, float* D, void* stream);
 /* Node-local map of irreps rows (both halves of the first-order SO(2) product,                   */
 /* so2_tensor_product.py:363-385, with A = W_inv diag(CG |pos|) S W precomputed per node):         */
-/* out[n,k,c] = sum_s A[n,k,s] h[n,s,c], A [n, 20, 9]; h / out rows of C floats with node strides. */
-/* Backward: dh [n,9,C] = A^T dout and (if dA != NULL) dA[n,k,s] = sum_c dout[n,k,c] h[n,s,c].     */
-int e2a_node_apply_fwd(const float* A, const float* h, int64_t h_node_stride, int64_t n_nodes, int ko, int ki,
-                       int C, float* out, int64_t out_node_stride, void* stream);
+/* out[n,k,c] = sum_s A[n,k,s] h[n,s,c] - sub[n,k,c] (sub may be NULL), A [n, 20, 9]; h / sub / out */
+/* rows of C floats with node strides; append_h != 0 also copies h into out rows 20..28.           */
+/* Backward: dh[n,s,c] = sum_k A[n,k,s] dout[n,k,c] + dh_add[n,s,c] (dh_add may be NULL),          */
+/* dsub = -dout (if dsub != NULL) and dA[n,k,s] = sum_c dout[n,k,c] h[n,s,c] (if dA != NULL).      */
+int e2a_node_apply_fwd(const float* A, const float* h, int64_t h_node_stride, const float* sub,
+                       int64_t sub_node_stride, int64_t n_nodes, int ko, int ki, int C, float* out,
+                       int64_t out_node_stride, int append_h, void* stream);
 int e2a_node_apply_bwd(const float* A, const float* h, int64_t h_node_stride, const float* dout,
-                       int64_t dout_node_stride, int64_t n_nodes, int ko, int ki, int C, float* dh, float* dA,
-                       void* stream);
+                       int64_t dout_node_stride, const float* dh_add, int64_t dh_add_node_stride, int64_t n_nodes,
+                       int ko, int ki, int C, float* dh, int64_t dh_node_stride, float* dsub, int64_t dsub_node_stride,
+                       float* dA, void* stream);
 /* Status bits of the GEMM's bounded waits (1 = a wait timed out); copies and optionally clears. */
 int e2a_gemm_status(unsigned int* status, int reset, void* stream);
 

@@ -383,3 +383,82 @@ def test_node_half_fused_matches_torch():
     gg = torch.autograd.grad(out, ag, w.float().to(DEV))
     for a, b in zip(gg, gr):
         assert (a.double().cpu() - b).abs().max().item() < 2e-5 * max(1.0, b.abs().max().item())
+
+
+@pytest.mark.parametrize("mode", ["plain", "merge", "sub"])
+def test_node_apply_modes_match_torch(mode):
+    from ubio_molfm_b200.linear import node_apply
+
+    g = torch.Generator().manual_seed(11)
+    n, C = 257, 96
+    A = torch.randn(n, 20, 9, generator=g, dtype=torch.float64)
+    x = torch.randn(n, 29 if mode == "sub" else 9, C, generator=g, dtype=torch.float64)
+
+    def ref_fn(A, x):
+        if mode == "sub":
+            return torch.einsum("nks,nsc->nkc", A, x[:, 20:]) - x[:, :20]
+        y = torch.einsum("nks,nsc->nkc", A, x)
+        return torch.cat([y, x], dim=1) if mode == "merge" else y
+
+    ar = [A.clone().requires_grad_(True), x.clone().requires_grad_(True)]
+    ref = ref_fn(*ar)
+    ag = [A.float().to(DEV).requires_grad_(True), x.float().to(DEV).requires_grad_(True)]
+    out = node_apply(ag[0], ag[1], mode)
+    assert out.shape == ref.shape
+    assert (out.double().cpu() - ref).abs().max().item() < 2e-5 * ref.abs().max().item()
+    w = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    gr = torch.autograd.grad(ref, ar, w)
+    gg = torch.autograd.grad(out, ag, w.float().to(DEV))
+    for a, b in zip(gg, gr):
+        assert (a.double().cpu() - b).abs().max().item() < 2e-5 * b.abs().max().item()
+
+
+def test_rowblock_linear_matches_torch():
+    from ubio_molfm_b200.linear import rowblock_linear
+    from ubio_molfm_b200.nn import SO2_TP_givenl2
+
+    g = torch.Generator().manual_seed(12)
+    n, C, Co = 300, 64, 48
+    so2 = SO2_TP_givenl2(2, C, Co)
+    _, tasks = so2.mc_row_order()
+    ws = [torch.randn(Co, cnt * C, generator=g, dtype=torch.float64) / 8 for _, cnt in so2.l3_sequential]
+    bias = torch.randn(Co, generator=g, dtype=torch.float64)
+    x = torch.randn(n, 20, C, generator=g, dtype=torch.float64, requires_grad=True)
+    ref = torch.zeros(n, 9, Co, dtype=torch.float64)
+    outs = []
+    for r0, k, o, wi in tasks:
+        y = x[:, r0:r0 + k].reshape(n, -1) @ ws[wi].t()
+        outs.append((o, y + bias if o == 0 else y))
+    ref = torch.stack([y for _, y in sorted(outs, key=lambda t: t[0])], dim=1)
+    xg = x.detach().float().to(DEV).requires_grad_(True)
+    out = rowblock_linear(xg, tasks, [w.float().to(DEV) for w in ws], bias.float().to(DEV), 9)
+    assert (out.double().cpu() - ref).abs().max().item() < 1e-5 * ref.abs().max().item()
+    w = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    (gr,) = torch.autograd.grad(ref, x, w)
+    (gg,) = torch.autograd.grad(out, xg, w.float().to(DEV))
+    assert (gg.double().cpu() - gr).abs().max().item() < 1e-5 * gr.abs().max().item()
+
+
+def test_layer_fused_eval_path_equals_module_path():
+    """The inference-only row reordering, merged value rows and merged output linears reproduce the
+    module-by-module CUDA path (used in training mode) on the same weights."""
+    rec = load("layer_small_pbc")
+    cfg = layer_cfg(rec)
+    layer = build_product_layer(cfg, DEV)
+    leaves, bd, Z = layer_inputs(rec, DEV)
+    kw = dict(node_pos=leaves["node_pos"], node_irreps_input=leaves["node_irreps_input"], edge_dis=leaves["edge_dis"],
+              edge_vec=None, attn_weight=leaves["attn_weight"], atomic_numbers=Z, poly_dist=leaves["poly_dist"])
+    out_e, _ = layer(batched_data=dict(bd), **kw)
+    layer.train()
+    out_t, _ = layer(batched_data=dict(bd), **kw)
+    layer.eval()
+    scale = max(out_t.abs().max().item(), 1.0)
+    assert (out_e - out_t).abs().max().item() <= 1e-5 * scale
+    dout = torch.randn_like(out_e)
+    ge = torch.autograd.grad(out_e, [leaves[k] for k in LEAVES], dout, allow_unused=True)
+    gt = torch.autograd.grad(out_t, [leaves[k] for k in LEAVES], dout, allow_unused=True)
+    for k, a, b in zip(LEAVES, ge, gt):
+        if a is None or b is None:
+            assert a is None and b is None, k
+            continue
+        assert (a - b).abs().max().item() <= 1e-5 * max(b.abs().max().item(), 1.0), k

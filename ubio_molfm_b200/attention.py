@@ -21,6 +21,7 @@ from torch import nn
 
 from .nn import (E2TensorProductSO2_FirstOrder, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
                  irreps_channels_lmax, lin, parse_irreps, run_mlp)
+from . import linear as tc
 from .ops import attention_span
 
 
@@ -64,6 +65,27 @@ class E2AttentionArbOrder_sparse(nn.Module):
         if (29 * C) % num_attn_heads:
             raise NotImplementedError("29*C must be divisible by the number of heads")
 
+    def _fused_rows(self):
+        if getattr(self, "_fused_rows_cache", None) is None:
+            perm, tasks = self.first_order_tp.so2_tp.mc_row_order()
+            self._fused_rows_cache = (perm, tasks)
+        return self._fused_rows_cache
+
+    def _fused_out_weights(self):
+        """Per l3: proj_first.weight[l3] @ (out_linear[l3].weight * path_norm[l3]) -> [C, cnt*C'].
+        The SO(2) output linear and proj_first are consecutive linear maps (no bias or activation
+        between them), so one product per output row replaces the two."""
+        so2 = self.first_order_tp.so2_tp
+        pw = self.proj_first.weight.detach()
+        norm = so2.path_norm.detach().reshape(-1)
+        ws = []
+        for idx, (l3, cnt) in enumerate(so2.l3_sequential):
+            nl = norm[l3 * l3:(l3 + 1) ** 2]
+            if not bool((nl == nl[0]).all()):
+                raise NotImplementedError("path_norm must be constant within an l3 block")
+            ws.append(pw[l3] @ (so2.out_linear[idx].weight.detach() * nl[0]))
+        return ws
+
     # -- edge radial MLP with the first layer split as W_r rbf + (W_t T)[Z_i] + (W_s S)[Z_j] + b --
     def edge_gate(self, attn_weight, atomic_numbers, f_outcell_index, query_idx, neighbor_idx):
         net = self.fc_easy.net
@@ -103,9 +125,18 @@ class E2AttentionArbOrder_sparse(nn.Module):
 
         value = self.proj_value(x)[outcell]                                          # [N2, 9, C]
         tp = self.first_order_tp
-        h_b = tp.node_half(bd["wigner_exp"], bd["wigner_inv_exp"], value, bd["f_exp_node_pos"])  # [N2, 20, C]
-        n_b = h_b.shape[1]
-        merged = torch.cat([h_b, value], dim=1).reshape(N2, -1, H)                   # [N2, 29*C/H, H]
+        fused = x.is_cuda and not self.training
+        if fused:
+            # rows of both halves in the (m, c) order of the output linear; [A_b v ; v] in one kernel
+            row_perm, tasks = self._fused_rows()
+            A_b = tp.node_map(bd["wigner_exp"], bd["wigner_inv_exp"], bd["f_exp_node_pos"], row_perm)
+            merged = tc.node_apply(A_b, value, "merge")                               # [N2, 29, C]
+            n_b = A_b.shape[1]
+        else:
+            h_b = tp.node_half(bd["wigner_exp"], bd["wigner_inv_exp"], value, bd["f_exp_node_pos"])  # [N2, 20, C]
+            n_b = h_b.shape[1]
+            merged = torch.cat([h_b, value], dim=1)
+        merged = merged.reshape(N2, -1, H)                                              # [N2, 29*C/H, H]
 
         poly = poly_dist if poly_dist is not None else torch.ones_like(edge_dis)
         if bd.get("query_sorted", None) is None:
@@ -122,6 +153,13 @@ class E2AttentionArbOrder_sparse(nn.Module):
             agg = attention_span(q_scaled, key, merged, gate[perm], poly[perm], edge_dis[perm], md,
                                  bd.get("row_order"), bd.get("key_order"))
         agg = agg.reshape(N1, -1, C)
+        if fused:
+            # A_a agg_v - agg_b, then output linear and proj_first as one GEMM per output row
+            A_a = tp.node_map(bd["wigner"], bd["wigner_inv"], node_pos, row_perm)
+            diff = tc.node_apply(A_a, agg, "sub")                                          # [N1, 20, C]
+            out = tc.rowblock_linear(diff, tasks, self._fused_out_weights(), self.proj_first.bias,
+                                     (self.lmax + 1) ** 2)
+            return out, attn_weight
         h_b_agg, h_a = agg[:, :n_b], agg[:, n_b:]
         h_a = tp.node_half(bd["wigner"], bd["wigner_inv"], h_a, node_pos)
         out = tp.so2_tp.forward_linear(h_a - h_b_agg)

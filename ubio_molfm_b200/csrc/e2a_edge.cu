@@ -213,7 +213,8 @@ constexpr int KO = 20, KI = 9;
 
 __global__ void __launch_bounds__(256)
 k_node_apply_fwd(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
-                 int64_t n_nodes, int C, float* __restrict__ out, int64_t out_node_stride) {
+                 const float* __restrict__ sub, int64_t sub_node_stride, int64_t n_nodes, int C,
+                 float* __restrict__ out, int64_t out_node_stride, int append_h) {
   __shared__ float As[KO * KI];
   for (int64_t n = blockIdx.x; n < n_nodes; n += gridDim.x) {
     __syncthreads();
@@ -230,19 +231,26 @@ k_node_apply_fwd(const float* __restrict__ A, const float* __restrict__ h, int64
         float acc = 0.f;
 #pragma unroll
         for (int s = 0; s < KI; ++s) acc = fmaf(As[k * KI + s], hv[s], acc);
+        if (sub) acc -= __ldg(sub + n * sub_node_stride + (int64_t)k * C + c);
         on[(int64_t)k * C + c] = acc;
+      }
+      if (append_h) {
+#pragma unroll
+        for (int s = 0; s < KI; ++s) on[(int64_t)(KO + s) * C + c] = hv[s];
       }
     }
   }
 }
 
-// One CTA per node: dh[s,c] = sum_k A[k,s] dout[k,c] with one thread per channel; dA[k,s] with one
-// warp per output row k (lanes over channels, 9 warp sums per k, fixed order).  The node's rows are
-// read straight from global memory (they stay in L1 across the two loops).
+// One CTA per node: dh[s,c] = sum_k A[k,s] dout[k,c] (+ dh_add[s,c]) with one thread per channel,
+// dsub = -dout, and dA[k,s] with one warp per output row k (lanes over channels, 9 warp sums per k,
+// fixed order).  The node's rows are read straight from global memory (they stay in L1 across the
+// two loops).
 __global__ void __launch_bounds__(256)
 k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
-                        const float* __restrict__ dout, int64_t dout_node_stride, int64_t n_nodes, int C,
-                        float* __restrict__ dh, float* __restrict__ dA) {
+                 const float* __restrict__ dout, int64_t dout_node_stride, const float* __restrict__ dh_add,
+                 int64_t dh_add_node_stride, int64_t n_nodes, int C, float* __restrict__ dh, int64_t dh_node_stride,
+                 float* __restrict__ dsub, int64_t dsub_node_stride, float* __restrict__ dA) {
   __shared__ float As[KO * KI];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   for (int64_t n = blockIdx.x; n < n_nodes; n += gridDim.x) {
@@ -254,15 +262,16 @@ k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
       float dv[KI];
 #pragma unroll
-      for (int s = 0; s < KI; ++s) dv[s] = 0.f;
+      for (int s = 0; s < KI; ++s) dv[s] = dh_add ? __ldg(dh_add + n * dh_add_node_stride + (int64_t)s * C + c) : 0.f;
 #pragma unroll
       for (int k = 0; k < KO; ++k) {
         const float g = __ldg(gn + (int64_t)k * C + c);
+        if (dsub) dsub[n * dsub_node_stride + (int64_t)k * C + c] = -g;
 #pragma unroll
         for (int s = 0; s < KI; ++s) dv[s] = fmaf(As[k * KI + s], g, dv[s]);
       }
 #pragma unroll
-      for (int s = 0; s < KI; ++s) dh[n * (int64_t)KI * C + (int64_t)s * C + c] = dv[s];
+      for (int s = 0; s < KI; ++s) dh[n * dh_node_stride + (int64_t)s * C + c] = dv[s];
     }
     if (dA) {
       for (int k = warp; k < KO; k += nwarp) {
@@ -288,28 +297,35 @@ k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64
 
 extern "C" {
 
-int e2a_node_apply_fwd(const float* A, const float* h, int64_t h_node_stride, int64_t n_nodes, int ko, int ki, int C,
-                       float* out, int64_t out_node_stride, void* stream) {
+int e2a_node_apply_fwd(const float* A, const float* h, int64_t h_node_stride, const float* sub,
+                       int64_t sub_node_stride, int64_t n_nodes, int ko, int ki, int C, float* out,
+                       int64_t out_node_stride, int append_h, void* stream) {
   if (n_nodes < 0 || C <= 0) return E2A_ERR_ARG;
   if (ko != KO || ki != KI) return E2A_ERR_UNSUPPORTED;
   if (n_nodes == 0) return E2A_OK;
-  if (!A || !h || !out || h_node_stride < (int64_t)KI * C || out_node_stride < (int64_t)KO * C) return E2A_ERR_ARG;
+  if (!A || !h || !out || h_node_stride < (int64_t)KI * C ||
+      out_node_stride < (int64_t)(append_h ? KO + KI : KO) * C || (sub && sub_node_stride < (int64_t)KO * C))
+    return E2A_ERR_ARG;
   const int64_t g = n_nodes < (1 << 30) ? n_nodes : (1 << 30);
-  k_node_apply_fwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, n_nodes, C, out, out_node_stride);
+  k_node_apply_fwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, sub, sub_node_stride, n_nodes, C,
+                                                             out, out_node_stride, append_h ? 1 : 0);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }
 
 int e2a_node_apply_bwd(const float* A, const float* h, int64_t h_node_stride, const float* dout,
-                       int64_t dout_node_stride, int64_t n_nodes, int ko, int ki, int C, float* dh, float* dA,
-                       void* stream) {
+                       int64_t dout_node_stride, const float* dh_add, int64_t dh_add_node_stride, int64_t n_nodes,
+                       int ko, int ki, int C, float* dh, int64_t dh_node_stride, float* dsub, int64_t dsub_node_stride,
+                       float* dA, void* stream) {
   if (n_nodes < 0 || C <= 0) return E2A_ERR_ARG;
   if (ko != KO || ki != KI) return E2A_ERR_UNSUPPORTED;
   if (n_nodes == 0) return E2A_OK;
-  if (!A || !h || !dout || !dh) return E2A_ERR_ARG;
+  if (!A || !h || !dout || !dh || dh_node_stride < (int64_t)KI * C || (dsub && dsub_node_stride < (int64_t)KO * C))
+    return E2A_ERR_ARG;
   const int64_t g = n_nodes < (1 << 30) ? n_nodes : (1 << 30);
-  k_node_apply_bwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, dout, dout_node_stride, n_nodes, C,
-                                                             dh, dA);
+  k_node_apply_bwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, dout, dout_node_stride, dh_add,
+                                                             dh_add_node_stride, n_nodes, C, dh, dh_node_stride,
+                                                             dsub, dsub_node_stride, dA);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }

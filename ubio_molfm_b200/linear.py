@@ -216,20 +216,34 @@ def so3_pair_product(x, w1, w2, bias, lidx):
 
 
 class _NodeApplyFn(torch.autograd.Function):
-    """out[n] = A[n] @ h[n] for A [n, 20, 9] and h [n, 9, C] (h may be a row-strided view)."""
+    """Per-node [20 x 9] map of irreps rows, A [n, 20, 9]:
+
+    * ``plain``: out [n, 20, C] = A h for h [n, 9, C] (h may be a row-strided view);
+    * ``merge``: out [n, 29, C] = [A h ; h]  (the value rows appended after the product rows);
+    * ``sub``:   out [n, 20, C] = A x[:, 20:] - x[:, :20] for x [n, 29, C]  (gradient w.r.t. x).
+    """
 
     @staticmethod
-    def forward(ctx, A, h):
+    def forward(ctx, A, h, mode):
         lib = _lib.load()
         A = A.contiguous()
         n, KO, KI = A.shape
         C = h.shape[2]
         if h.stride(2) != 1 or h.stride(1) != C:
             h = h.contiguous()
-        out = torch.empty((n, KO, C), device=h.device, dtype=torch.float32)
-        check(lib.e2a_node_apply_fwd(ptr(A), ptr(h), h.stride(0), n, KO, KI, C, ptr(out), out.stride(0),
-                                     stream_of(h.device)), "e2a_node_apply_fwd")
+        dev = h.device
+        if mode == "sub":
+            src, sub = h[:, KO:], h
+            out = torch.empty((n, KO, C), device=dev, dtype=torch.float32)
+            check(lib.e2a_node_apply_fwd(ptr(A), ptr(src), h.stride(0), ptr(sub), h.stride(0), n, KO, KI, C, ptr(out),
+                                         out.stride(0), 0, stream_of(dev)), "e2a_node_apply_fwd")
+        else:
+            rows = KO + KI if mode == "merge" else KO
+            out = torch.empty((n, rows, C), device=dev, dtype=torch.float32)
+            check(lib.e2a_node_apply_fwd(ptr(A), ptr(h), h.stride(0), None, 0, n, KO, KI, C, ptr(out), out.stride(0),
+                                         1 if mode == "merge" else 0, stream_of(dev)), "e2a_node_apply_fwd")
         ctx.save_for_backward(A, h)
+        ctx.mode = mode
         return out
 
     @staticmethod
@@ -239,13 +253,70 @@ class _NodeApplyFn(torch.autograd.Function):
         g = g.contiguous()
         n, KO, KI = A.shape
         C = h.shape[2]
-        dh = torch.empty((n, KI, C), device=h.device, dtype=torch.float32)
+        dev = h.device
         dA = torch.empty_like(A) if ctx.needs_input_grad[0] else None
-        check(lib.e2a_node_apply_bwd(ptr(A), ptr(h), h.stride(0), ptr(g), g.stride(0), n, KO, KI, C, ptr(dh), ptr(dA),
-                                     stream_of(h.device)), "e2a_node_apply_bwd")
-        return dA, dh
+        if ctx.mode == "sub":
+            dx = torch.empty((n, KO + KI, C), device=dev, dtype=torch.float32)
+            check(lib.e2a_node_apply_bwd(ptr(A), ptr(h[:, KO:]), h.stride(0), ptr(g), g.stride(0), None, 0, n, KO, KI,
+                                         C, ptr(dx[:, KO:]), dx.stride(0), ptr(dx), dx.stride(0), ptr(dA),
+                                         stream_of(dev)), "e2a_node_apply_bwd")
+            return dA, dx, None
+        dh = torch.empty((n, KI, C), device=dev, dtype=torch.float32)
+        add = g[:, KO:] if ctx.mode == "merge" else None
+        check(lib.e2a_node_apply_bwd(ptr(A), ptr(h), h.stride(0), ptr(g), g.stride(0), ptr(add),
+                                     g.stride(0) if add is not None else 0, n, KO, KI, C, ptr(dh), dh.stride(0),
+                                     None, 0, ptr(dA), stream_of(dev)), "e2a_node_apply_bwd")
+        return dA, dh, None
 
 
-def node_apply(A, h):
-    """Per-node [20 x 9] map of irreps rows (CUDA)."""
-    return _NodeApplyFn.apply(A.float(), h.float())
+def node_apply(A, h, mode="plain"):
+    """Per-node [20 x 9] map of irreps rows (CUDA); ``mode`` as in :class:`_NodeApplyFn`."""
+    if mode not in ("plain", "merge", "sub"):
+        raise ValueError(f"unknown node_apply mode {mode!r}")
+    return _NodeApplyFn.apply(A.float(), h.float(), mode)
+
+
+def _gemm_raw(lib, a, lda, b, ldb, c, ldc, bias, M, N, K, dev):
+    check(lib.e2a_gemm_tf32x3(a, lda, b, ldb, c, ldc, bias, M, N, K, 0, PASSES, stream_of(dev)), "e2a_gemm_tf32x3")
+
+
+class _RowBlockLinearFn(torch.autograd.Function):
+    """out[n, o_t, :] = x[n, r_t : r_t + k_t, :].flatten() @ W_t^T (+ bias on output row 0), one
+    tensor-core GEMM per task t = (r_t, k_t, o_t, w_t) with node-strided operands (no copies).  The
+    tasks partition the rows of x, so the input gradient is written, not accumulated.  Weights are
+    constants (inference path)."""
+
+    @staticmethod
+    def forward(ctx, x, tasks, weights, weights_t, bias, out_rows):
+        lib = _lib.load()
+        x = x.contiguous()
+        n, R, C = x.shape
+        Co = weights[0].shape[0]
+        out = torch.empty((n, out_rows, Co), device=x.device, dtype=torch.float32)
+        for r0, k, o, wi in tasks:
+            _gemm_raw(lib, x.data_ptr() + 4 * r0 * C, R * C, ptr(weights[wi]), k * C, out.data_ptr() + 4 * o * Co,
+                      out_rows * Co, ptr(bias) if (bias is not None and o == 0) else None, n, Co, k * C, x.device)
+        ctx.tasks, ctx.weights_t, ctx.shape = tasks, weights_t, (n, R, C, out_rows, Co)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        g = g.contiguous()
+        n, R, C, out_rows, Co = ctx.shape
+        dx = torch.empty((n, R, C), device=g.device, dtype=torch.float32)
+        for r0, k, o, wi in ctx.tasks:
+            _gemm_raw(lib, g.data_ptr() + 4 * o * Co, out_rows * Co, ptr(ctx.weights_t[wi]), Co,
+                      dx.data_ptr() + 4 * r0 * C, R * C, None, n, k * C, Co, g.device)
+        return dx, None, None, None, None, None
+
+
+def rowblock_linear(x, tasks, weights, bias, out_rows):
+    """See :class:`_RowBlockLinearFn`; ``weights`` are [Co, k*C] fp32 CUDA tensors."""
+    rows = sorted((r0, r0 + k) for r0, k, _, _ in tasks)
+    if rows[0][0] != 0 or rows[-1][1] != x.shape[1] or any(a[1] != b[0] for a, b in zip(rows, rows[1:])):
+        raise ValueError("rowblock_linear tasks must partition the input rows")
+    weights = [w.detach().float().contiguous() for w in weights]
+    weights_t = [w.t().contiguous() for w in weights]
+    b = bias.detach().float().contiguous() if bias is not None else None
+    return _RowBlockLinearFn.apply(x.float(), tuple(tasks), weights, weights_t, b, out_rows)

@@ -240,6 +240,21 @@ class SO2_TP_givenl2(nn.Module):
             return self.forward_linear(y)
         return y
 
+    def mc_row_order(self):
+        """Row permutation (new -> old) that stores each l3 block m-major, (m, c) instead of (c, m), so
+        that the ``cnt`` rows feeding output row m of an l3 block are contiguous, and the row-block
+        tasks (first row, rows, output row, l3 index) of the output linear in that order."""
+        perm, tasks = [], []
+        start = 0
+        for idx, (l3, cnt) in enumerate(self.l3_sequential):
+            d = 2 * l3 + 1
+            for m in range(d):
+                tasks.append((start + m * cnt, cnt, l3 * l3 + m, idx))
+                for c in range(cnt):
+                    perm.append(start + c * d + m)
+            start += d * cnt
+        return perm, tasks
+
     def forward_linear(self, y):
         bs = y.shape[0]
         start = 0
@@ -262,6 +277,13 @@ class E2TensorProductSO2_FirstOrder(nn.Module):
         self.in_c, self.out_c, self.lmax, self.head = in_c, out_c, lmax, head
         self.so2_tp = SO2_TP_givenl2(lmax, in_c, out_c, with_linear=True)
 
+    def node_map(self, wigner, wigner_inv, pos, row_perm=None):
+        """A = W_inv diag(CG |pos|) S W per node, [n, 20, 9] (rows optionally permuted)."""
+        tp = self.so2_tp
+        scale = tp.CG_weight.reshape(1, -1, 1) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
+        A = torch.bmm(wigner_inv, wigner[:, tp.selected_idx, :] * scale)
+        return A if row_perm is None else A[:, row_perm]
+
     def node_half(self, wigner, wigner_inv, h, pos):
         """W_inv @ (CG-select(W @ h) * |pos|): the per-node half of h (x) r.
 
@@ -270,8 +292,6 @@ class E2TensorProductSO2_FirstOrder(nn.Module):
         [9, C] rows by one kernel."""
         tp = self.so2_tp
         if h.is_cuda:
-            scale = tp.CG_weight.reshape(1, -1, 1) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
-            A = torch.bmm(wigner_inv, wigner[:, tp.selected_idx, :] * scale)          # [n, 20, 9]
-            return tc.node_apply(A, h)
+            return tc.node_apply(self.node_map(wigner, wigner_inv, pos), h)
         y = tp(torch.bmm(wigner, h), with_linear=False) * torch.norm(pos, dim=-1).reshape(-1, 1, 1)
         return torch.bmm(wigner_inv, y)
