@@ -184,14 +184,19 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
 /* SO3_Linear2Scalar_e2former (2240-2274), RadialProfile (2151-2178) and forward_linear          */
 /* (so2_tensor_product.py:273-290).                                                             */
 /* ------------------------------------------------------------------------------------------ */
-int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                    const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes,
+int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                    int64_t ldc, const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes,
                     void* stream);
+/* B_lo != NULL: B holds tf32(B) and B_lo tf32(B - tf32(B)) (e2a_tf32_split; worth it when B, the    */
+/* weight operand, is reused); then 16-byte-aligned rows are required, else E2A_ERR_UNSUPPORTED.    */
+int e2a_tf32_split(const float* B, int64_t ldb, int64_t N, int64_t K, float* B_hi, float* B_lo, int64_t ldo,
+                   void* stream);
 /* Pair-product epilogue for SO3_Linear2Scalar_e2former (module_utils.py:2240-2274): B's rows come */
 /* interleaved (o1_j, o2_j); P[r, j] = (P[r, j] if accumulate) + o1_j * o2_j with leading dim ldp, */
-/* C (may be NULL) receives the raw [M, N] values.  N even; 16-byte-aligned A / B rows required.  */
-int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                             const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
+/* C (may be NULL) receives the raw [M, N] values.  N even, K > 0; 16-byte-aligned A / B rows     */
+/* (lda, ldb multiples of 4) required, else E2A_ERR_UNSUPPORTED.  B_lo as for e2a_gemm_tf32x3.     */
+int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                             int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
                              int accumulate, int passes, void* stream);
 /* Backward of the pair product: D[n,m,2j] = G[n,l(m),j] O[n,m,2j+1], D[n,m,2j+1] = G[n,l(m),j] O[n,m,2j] */
 /* for O, D [n_nodes, R, 2h], G [n_nodes, L1, h], l(m) the degree of row m.                      */

@@ -47,9 +47,10 @@ SIGNATURES = {
     "e2a_attn_bwd_workspace_bytes": (SZ, [I64, I32]),
     "e2a_attn_bwd_query": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                  P, P, P, P, P, P, P, I64, P, P, P, P, SZ, P]),
-    "e2a_gemm_tf32x3": (I32, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, I32, P]),
+    "e2a_gemm_tf32x3": (I32, [P, I64, P, P, I64, P, I64, P, I64, I64, I64, I32, I32, P]),
+    "e2a_tf32_split": (I32, [P, I64, I64, I64, P, P, I64, P]),
     "e2a_gemm_status": (I32, [P, I32, P]),
-    "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
+    "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
     "e2a_pair_grad": (I32, [P, P, I64, I32, I32, I32, P, P]),
     "e2a_node_apply_fwd": (I32, [P, P, I64, P, I64, I64, I32, I32, I32, P, I64, I32, P]),
     "e2a_node_apply_bwd": (I32, [P, P, I64, P, I64, P, I64, I64, I32, I32, I32, P, I64, P, I64, P, P]),

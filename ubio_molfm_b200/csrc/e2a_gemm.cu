@@ -21,6 +21,7 @@
 // The dropped lo*lo term is below fp32 resolution (|error| ~ 2^-22 relative per product).
 // Every mbarrier wait is bounded in time; on a timeout the kernel records E2A_DEV_WAIT_TIMEOUT,
 // still waits (bounded) for its MMAs, frees its tensor memory and returns.
+#include <cuda.h>  // CUtensorMap; the encoder is fetched from the driver at run time
 #include "e2a_common.cuh"
 
 __device__ unsigned int g_e2a_gemm_status = 0;
@@ -249,294 +250,478 @@ k_gemm_tf32x3(const float* __restrict__ A, int64_t lda, const float* __restrict_
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Warp-specialised persistent kernel for 16-byte-aligned operands.  One CTA per SM walks 128 x 128
+// output tiles (n fastest, so CTAs running together share A rows in L2).  Roles:
+//  * warp 0 (one lane): TMA producer -- per k-slab one 2-D tensor copy each of raw fp32 A and of B
+//    (or of B_hi and B_lo when the caller pre-split the weight operand) into a stage ring, already
+//    in the swizzled K-major layout the tensor core reads;
+//  * warps 2-3 (and 8-9 for 32-wide slabs): splitters -- turn each raw slab into hi = tf32(x) (in
+//    place) and lo = tf32(x - hi)
+//    (A only when B arrives pre-split, which measured faster: shared-memory traffic per slab is the
+//    tighter resource);
+//  * warp 1 (one lane): MMA issuer -- tcgen05.mma kind::tf32 hi*hi + hi*lo + lo*hi into one of four
+//    128-column TMEM chain buffers (a chain = 32 k, 12 MMAs), then tcgen05.commit frees the
+//    stage and, at a chain end, hands the buffer to the drain warps;
+//  * warps 4-7: drain every chain into fp32 registers with round-to-nearest adds (the tensor core's
+//    own accumulation truncates, so chains are kept short), then run the tile's epilogue (bias /
+//    accumulate / pair product) through a per-warp staging area with coalesced row stores.
+// The roles meet only at mbarriers; there is no block-wide barrier in the loop.  Every wait is
+// bounded (~2 s): a timeout sets E2A_DEV_WAIT_TIMEOUT and an abort flag that ends every role, and
+// the producer / issuer then wait (bounded) for their copies / MMAs in flight before TMEM is freed.
+// ------------------------------------------------------------------------------------------------
+template <int V>
+struct IntC { static constexpr int value = V; };
 
-// ------------------------------------------------------------------------------------------------
-// Pipelined kernel for 16-byte-aligned operands: raw fp32 slabs arrive by cp.async (16-byte copies,
-// zero-filled past the matrix edge, destination already in the swizzled layout) several slabs ahead;
-// each slab is split shared -> shared into one of two hi/lo operand buffers while the tensor core
-// works on the other.  Global-memory latency is off the critical path.
-// ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+// Two slab shapes: 16-wide slabs (64-byte rows and swizzle, six stages) suit K <= 256, where tiles
+// turn over quickly; 32-wide slabs (128-byte rows and swizzle, three stages) move more bytes per
+// TMA request and suit long K.
+template <int BK_>
+struct WsCfg {
+  static constexpr int BK = BK_;
+  static constexpr int SPC = 32 / BK;                    // slabs per TMEM chain (32 k = 12 MMAs)
+  static constexpr int STAGES = BK == 16 ? 6 : 3;
+  static constexpr int TILE = BM * BK * 4;               // bytes per operand part
+  static constexpr int STAGE = 4 * TILE;                 // A (raw, then hi in place), A_lo, B (same), B_lo
+  static constexpr int NBARS = 3 * STAGES + 8;           // + 2 x WS_CHAINS
+  static constexpr int SPLIT = BK == 16 ? 64 : 128;      // splitter threads (warps 2-3, and 8-9 for BK 32)
+  static constexpr int THREADS = 256 + (SPLIT - 64);
+  static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
+    // K-major; LBO unused (1); SBO = 8 rows x row bytes; version 1; swizzle 64 B (4) or 128 B (2)
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(BK * 4 * 8 / 16) << 32) | (1ull << 46) |
+           ((BK == 16 ? 4ull : 2ull) << 61);
+  }
+};
+constexpr int WS_CHAINS = 4;                     // TMEM chain buffers of BN columns (512 columns)
+constexpr int WS_EH = BN / 4;                    // epilogue staged in four column quarters
+constexpr int WS_LD = WS_EH + 4;                 // staging row stride (floats)
+constexpr int WS_EPI = 4 * 32 * WS_LD * 4;       // four drain warps x 32 rows x one quarter
+constexpr uint32_t kWsTmemCols = WS_CHAINS * BN;
+template <int BK>
+constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024; }
+
+__device__ __forceinline__ float tf32_lo(float a, float h) { return tf32_hi(a - h); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(e2a_smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// ------------------------------------------------------------------------------------------------
-// v2: 16-wide k-slabs in the 64-byte-swizzled K-major layout (8-row atoms of 512 B, 16-byte chunk c
-// of row r at c ^ ((r >> 1) & 3)).  112 KB of shared memory and <= 128 registers per thread, so two
-// CTAs (two 256-column TMEM allocations) share an SM and overlap each other's stalls.
-// ------------------------------------------------------------------------------------------------
-constexpr int BK2 = 16;
-constexpr int kTile2 = BM * BK2 * 4;                 // 8 KB per operand part
-constexpr int kRaw2 = 2 * kTile2;                    // A and B raw slab
-constexpr int kOp2 = 4 * kTile2;                     // A_hi, A_lo, B_hi, B_lo
-constexpr int RAW2 = 3;
-constexpr int kSmem2 = RAW2 * kRaw2 + 2 * kOp2 + 256;
-constexpr int kF4PerThread2 = (BM * BK2 / 4) / kThreads;   // 2
-
-__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
-  // K-major, 64-byte swizzle: LBO unused (1), SBO = 512 B between 8-row atoms, version 1
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(e2a_smem_u32(bar)) : "memory");
+}
+// 2-D tensor copy global -> this CTA's shared memory (no multicast), completion on `bar`
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(e2a_smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(e2a_smem_u32(bar))
+      : "memory");
 }
 
-__device__ __forceinline__ void issue_slab2(const float* __restrict__ X, int64_t ld, int rows, int K, int r0, int k0,
-                                            uint32_t dst) {
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
 #pragma unroll
-  for (int j = 0; j < kF4PerThread2; ++j) {
-    const int c = threadIdx.x + j * kThreads;
-    const int r = c >> 2, ch = c & 3;
-    const int gr = r0 + r, gk = k0 + ch * 4;
-    const int valid = (gr < rows && gk < K) ? min(4, K - gk) : 0;
-    const float* src = valid ? X + (int64_t)gr * ld + gk : X;
-    cp_async16(dst + (uint32_t)(r * 64 + ((ch ^ ((r >> 1) & 3)) << 4)), src, (uint32_t)valid * 4u);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded wait that also gives up when another role has set the abort flag.
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (e2a_mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = e2a_globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (e2a_mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (e2a_globaltimer() - t0 > 2000000000ull) {
+        *abort_flag = 1;
+        atomicOr(&g_e2a_gemm_status, E2A_DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
   }
 }
 
-__device__ __forceinline__ void split_smem2(const uint8_t* raw, uint8_t* hi, uint8_t* lo) {
-#pragma unroll
-  for (int j = 0; j < kF4PerThread2; ++j) {
-    const int off = (threadIdx.x + j * kThreads) * 16;
-    const float4 v = *reinterpret_cast<const float4*>(raw + off);
-    float4 h, l;
-    h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
-    l.x = v.x - h.x; l.y = v.y - h.y; l.z = v.z - h.z; l.w = v.w - h.w;
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) = l;
-  }
-}
+#ifdef E2A_GEMM_TRACE
+__device__ unsigned long long g_ws_trace[8][512];
+#define WS_TRACE(k, i) do { if (blockIdx.x == 0 && (i) < 512) g_ws_trace[k][i] = e2a_globaltimer(); } while (0)
+#else
+#define WS_TRACE(k, i) do { } while (0)
+#endif
 
-__global__ void __launch_bounds__(kThreads, 2)
-k_gemm_tf32x3_v2(const float* __restrict__ A, int64_t lda, const float* __restrict__ B, int64_t ldb, float* C,
-                 int64_t ldc, const float* __restrict__ bias, int M, int N, int K, int accumulate, int passes,
-                 float* P, int64_t ldp) {
-  extern __shared__ __align__(1024) uint8_t smem2[];
-  if ((e2a_smem_u32(smem2) & 1023u) != 0) {  // the descriptors assume 1 KB-aligned tiles
-    if (threadIdx.x == 0) atomicOr(&g_e2a_gemm_status, 2u);
-    return;
-  }
-  uint8_t* raw = smem2;
-  uint8_t* ops = smem2 + RAW2 * kRaw2;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ops + 2 * kOp2);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+template <int BK_>
+__global__ void __launch_bounds__(WsCfg<BK_>::THREADS, 1)
+k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+          const __grid_constant__ CUtensorMap tmBl, int b_split, float* C, int64_t ldc, const float* __restrict__ bias, float* P,
+          int64_t ldp, int M, int N, int K, int accumulate, int passes) {
+  using Cfg = WsCfg<BK_>;
+  extern __shared__ uint8_t ws_raw[];
+  uint8_t* smem = ws_raw + ((1024u - (e2a_smem_u32(ws_raw) & 1023u)) & 1023u);
+  uint8_t* stages = smem;
+  float* epi = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE + WS_EPI);
+  uint64_t* full = bars;                          // TMA landed            (1 arrive + tx bytes)
+  uint64_t* split_done = bars + Cfg::STAGES;        // A hi / lo written     (one per splitter)
+  uint64_t* empty = bars + 2 * Cfg::STAGES;         // MMAs of the slab done (tcgen05.commit)
+  uint64_t* tfull = bars + 3 * Cfg::STAGES;         // chain buffer ready    (tcgen05.commit)
+  uint64_t* tempty = tfull + WS_CHAINS;           // chain buffer drained  (128 arrives)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int tiles = ((M + BM - 1) / BM) * tiles_n;
+  const int nk = (K + Cfg::BK - 1) / Cfg::BK;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(e2a_smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
+                 ::"r"(e2a_smem_u32(tmem_slot)), "r"(kWsTmemCols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (threadIdx.x == 0) {
-    e2a_mbar_init(&bars[0], 1);
-    e2a_mbar_init(&bars[1], 1);
-    e2a_fence_mbar_init();
-  }
-  const int nk = (K + BK2 - 1) / BK2;
-#pragma unroll
-  for (int p = 0; p < RAW2 - 1; ++p) {
-    if (p < nk) {
-      const uint32_t d = e2a_smem_u32(raw + p * kRaw2);
-      issue_slab2(A, lda, M, K, m0, p * BK2, d);
-      issue_slab2(B, ldb, N, K, n0, p * BK2, d + kTile2);
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      e2a_mbar_init(&full[s], 1);
+      e2a_mbar_init(&split_done[s], Cfg::SPLIT);
+      e2a_mbar_init(&empty[s], 1);
     }
-    cp_async_commit();
+    for (int c = 0; c < WS_CHAINS; ++c) {
+      e2a_mbar_init(&tfull[c], 1);
+      e2a_mbar_init(&tempty[c], 128);
+    }
+    *abort_flag = 0;
+    e2a_fence_mbar_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int q = warp & 3, half = warp >> 2;
-  const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-  float acc[BN / 2];
-#pragma unroll
-  for (int i = 0; i < BN / 2; ++i) acc[i] = 0.f;
-  bool ok = true;
-  // Slabs kb = 2g, 2g+1 accumulate into TMEM buffer g & 1 (a 12-MMA chain, like a 32-wide slab);
-  // group g-1 is drained into the fp32 registers while group g runs.  Every wait targets the latest
-  // or the second-latest commit on its barrier, so a parity never wraps.
-  auto drain = [&](int g) {
-    tc_fence_after();
-#pragma unroll
-    for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + (uint32_t)((g & 1) * BN + 64 * half + c0), v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[c0 + i] += v[i];
-    }
-  };
-  for (int kb = 0; kb < nk; ++kb) {
-    {
-      const int p = kb + RAW2 - 1;
-      if (p < nk) {
-        const uint32_t d = e2a_smem_u32(raw + (p % RAW2) * kRaw2);
-        issue_slab2(A, lda, M, K, m0, p * BK2, d);
-        issue_slab2(B, ldb, N, K, n0, p * BK2, d + kTile2);
-      }
-      cp_async_commit();
-    }
-    // operand buffer kb & 1 was read by the MMAs of slab kb-2
-    if (kb >= 2) {
-      ok = e2a_mbar_wait_bounded(&bars[kb & 1], ((kb - 2) >> 1) & 1, &g_e2a_gemm_status);
-      if (__syncthreads_or(!ok)) { ok = false; break; }
-    }
-    cp_async_wait<RAW2 - 1>();
-    __syncthreads();
-    const uint8_t* rs = raw + (kb % RAW2) * kRaw2;
-    uint8_t* op = ops + (kb & 1) * kOp2;
-    split_smem2(rs, op, op + kTile2);
-    split_smem2(rs + kTile2, op + 2 * kTile2, op + 3 * kTile2);
-    e2a_fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)(((kb >> 1) & 1) * BN);
-      const uint32_t a_hi = e2a_smem_u32(op), a_lo = a_hi + kTile2;
-      const uint32_t b_hi = a_hi + 2 * kTile2, b_lo = a_hi + 3 * kTile2;
-#pragma unroll
-      for (int kk = 0; kk < BK2 / 8; ++kk) {
-        const uint32_t koff = kk * 32;
-        const uint32_t first = ((kb & 1) == 0 && kk == 0) ? 0u : 1u;
-        mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_hi + koff), first);
-        if (passes == 3) {
-          mma_tf32(d, smem_desc_sw64(a_hi + koff), smem_desc_sw64(b_lo + koff), 1u);
-          mma_tf32(d, smem_desc_sw64(a_lo + koff), smem_desc_sw64(b_hi + koff), 1u);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+      if (b_split) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmBl)) : "memory");
+      const uint32_t bytes = (b_split ? 3 : 2) * Cfg::TILE;
+      uint32_t n = 0;
+      bool run = true;
+      for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++n) {
+          const uint32_t s = n % Cfg::STAGES;
+          if (!ws_wait(&empty[s], ((n / Cfg::STAGES) & 1) ^ 1, abort_flag)) { run = false; break; }
+          WS_TRACE(0, n);
+          uint8_t* st = stages + s * Cfg::STAGE;
+          mbar_expect_tx(&full[s], bytes);
+          tma_load_2d(st, &tmA, kb * Cfg::BK, m0, &full[s]);
+          tma_load_2d(st + 2 * Cfg::TILE, &tmB, kb * Cfg::BK, n0, &full[s]);
+          if (b_split) tma_load_2d(st + 3 * Cfg::TILE, &tmBl, kb * Cfg::BK, n0, &full[s]);
         }
       }
-      mma_commit(&bars[kb & 1]);
-    }
-    // drain group (kb >> 1) - 1 before its TMEM buffer is reused by the next group.  Its last slab,
-    // kb - 2, was awaited at the top of this iteration (waiting for it again here could see the
-    // barrier's parity already advanced by slab kb's commit).
-    if ((kb & 1) == 1 && kb >= 3) {
-      drain((kb >> 1) - 1);
-      tc_fence_before();
-    }
-  }
-  cp_async_wait<0>();
-  // drain the remaining (one or two) groups
-  if (ok && nk > 0) {
-    const int last_group = (nk - 1) >> 1;
-    const int first_left = (nk >= 4 && (((nk - 1) & 1) == 1)) ? last_group : (nk >= 3 ? last_group - 1 : 0);
-    for (int g = first_left; g <= last_group && ok; ++g) {
-      const int last = min(2 * g + 1, nk - 1);
-      ok = e2a_mbar_wait_bounded(&bars[last & 1], (last >> 1) & 1, &g_e2a_gemm_status);
-      if (__syncthreads_or(!ok)) { ok = false; break; }
-      drain(g);
-    }
-  }
-  const bool all_ok = !__syncthreads_or(!ok);
-  if (all_ok) {
-    constexpr int kLd = BN + 4;
-    float* tile = reinterpret_cast<float*>(smem2);  // raw + operand region, idle now (67.6 KB used)
-    {
-      float* trow = tile + (32 * q + lane) * kLd + 64 * half;
-#pragma unroll
-      for (int i = 0; i < BN / 2; i += 4)
-        *reinterpret_cast<float4*>(trow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-    }
-    __syncthreads();
-    const int gc = n0 + 4 * lane;
-    float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (bias) {
-      if (gc < N) bv.x = bias[gc];
-      if (gc + 1 < N) bv.y = bias[gc + 1];
-      if (gc + 2 < N) bv.z = bias[gc + 2];
-      if (gc + 3 < N) bv.w = bias[gc + 3];
-    }
-    const bool cvec = C && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
-    for (int r = warp; r < BM; r += kThreads / 32) {
-      const int row = m0 + r;
-      if (row >= M) break;
-      float4 x = *reinterpret_cast<const float4*>(tile + r * kLd + 4 * lane);
-      x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
-      if (P) {
-        float* pp = P + (int64_t)row * ldp + (gc >> 1);
-        if (gc + 1 < N) pp[0] = (accumulate ? pp[0] : 0.f) + x.x * x.y;
-        if (gc + 3 < N) pp[1] = (accumulate ? pp[1] : 0.f) + x.z * x.w;
-        if (!C) continue;
-        float* cp = C + (int64_t)row * ldc + gc;
-        if (cvec) {
-          *reinterpret_cast<float4*>(cp) = x;
-        } else {
-          const float xv[4] = {x.x, x.y, x.z, x.w};
-          for (int t = 0; t < 4; ++t)
-            if (gc + t < N) cp[t] = xv[t];
-        }
-        continue;
-      }
-      float* cp = C + (int64_t)row * ldc + gc;
-      if (cvec) {
-        if (accumulate) {
-          const float4 o = *reinterpret_cast<const float4*>(cp);
-          x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-        }
-        *reinterpret_cast<float4*>(cp) = x;
-      } else {
-        const float xv[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (gc + t < N) cp[t] = accumulate ? cp[t] + xv[t] : xv[t];
+      if (!run) {  // copies still in flight must land before the CTA exits
+        for (uint32_t j = (n >= Cfg::STAGES ? n - Cfg::STAGES : 0); j < n; ++j)
+          e2a_mbar_wait_bounded(&full[j % Cfg::STAGES], (j / Cfg::STAGES) & 1, &g_e2a_gemm_status);
       }
     }
-  } else if (threadIdx.x == 0 && nk > 0) {
-    for (int pk = (nk >= 2 ? nk - 2 : 0); pk < nk; ++pk)
-      e2a_mbar_wait_bounded(&bars[pk & 1], (pk >> 1) & 1, &g_e2a_gemm_status);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t n = 0, c = 0;
+      int64_t last = -1;  // last slab whose MMAs were committed
+      bool run = true;
+      for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
+        for (int kb = 0; kb < nk; ++kb, ++n) {
+          const uint32_t s = n % Cfg::STAGES, cb = c % WS_CHAINS;
+          if ((kb % Cfg::SPC) == 0 && !ws_wait(&tempty[cb], ((c / WS_CHAINS) & 1) ^ 1, abort_flag)) { run = false; break; }
+          if (!ws_wait(&split_done[s], (n / Cfg::STAGES) & 1, abort_flag)) { run = false; break; }
+          WS_TRACE(3, n);
+          tc_fence_after();
+          const uint32_t d = tmem + cb * BN;
+          const uint32_t a_hi = e2a_smem_u32(stages + s * Cfg::STAGE), a_lo = a_hi + Cfg::TILE;
+          const uint32_t b_hi = a_hi + 2 * Cfg::TILE, b_lo = a_hi + 3 * Cfg::TILE;
+#pragma unroll
+          for (int kk = 0; kk < Cfg::BK / 8; ++kk) {
+            const uint32_t koff = kk * 32;
+            mma_tf32(d, Cfg::desc(a_hi + koff), Cfg::desc(b_hi + koff), ((kb % Cfg::SPC) == 0 && kk == 0) ? 0u : 1u);
+            if (passes == 3) {
+              mma_tf32(d, Cfg::desc(a_hi + koff), Cfg::desc(b_lo + koff), 1u);
+              mma_tf32(d, Cfg::desc(a_lo + koff), Cfg::desc(b_hi + koff), 1u);
+            }
+          }
+          mma_commit(&empty[s]);
+          last = n;
+          if ((kb % Cfg::SPC) == Cfg::SPC - 1 || kb == nk - 1) {
+            mma_commit(&tfull[cb]);
+            ++c;
+          }
+        }
+      }
+      if (!run && last >= 0)  // let the committed MMAs finish before the tensor memory is freed
+        e2a_mbar_wait_bounded(&empty[last % Cfg::STAGES], (uint32_t)((last / Cfg::STAGES) & 1), &g_e2a_gemm_status);
+    }
+  } else if (warp < 4 || warp >= 8) {
+    // ------------------------------------------------------------------ splitters (128 threads)
+    const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 192;
+    uint32_t n = 0;
+    bool run = true;
+    for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
+      for (int kb = 0; kb < nk; ++kb, ++n) {
+        const uint32_t s = n % Cfg::STAGES;
+        if (!ws_wait(&full[s], (n / Cfg::STAGES) & 1, abort_flag)) { run = false; break; }
+        if (t == 0) WS_TRACE(1, n);
+        uint8_t* st = stages + s * Cfg::STAGE;
+        auto split = [&](auto count) {
+#pragma unroll
+          for (int j = 0; j < decltype(count)::value; ++j) {      // float4 index over A then B
+            const int idx = t + j * Cfg::SPLIT;
+            const int off = (idx & (Cfg::TILE / 16 - 1)) * 16 + (idx >= Cfg::TILE / 16 ? 2 * Cfg::TILE : 0);
+            const float4 v = *reinterpret_cast<const float4*>(st + off);
+            float4 h, l;
+            h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
+            l.x = tf32_lo(v.x, h.x); l.y = tf32_lo(v.y, h.y); l.z = tf32_lo(v.z, h.z); l.w = tf32_lo(v.w, h.w);
+            *reinterpret_cast<float4*>(st + off) = h;
+            *reinterpret_cast<float4*>(st + Cfg::TILE + off) = l;
+          }
+        };
+        if (b_split) split(IntC<Cfg::TILE / 16 / Cfg::SPLIT>{});
+        else split(IntC<2 * Cfg::TILE / 16 / Cfg::SPLIT>{});
+        e2a_fence_proxy_async();
+        mbar_arrive(&split_done[s]);
+        if (t == 0) WS_TRACE(2, n);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ drain + epilogue (128 threads)
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    float* stg = epi + q * 32 * WS_LD;
+    uint32_t c = 0;
+    bool run = true;
+    const int nch = (nk + Cfg::SPC - 1) / Cfg::SPC;
+    for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      float acc[BN];
+#pragma unroll
+      for (int i = 0; i < BN; ++i) acc[i] = 0.f;
+      for (int ch = 0; ch < nch; ++ch, ++c) {
+        const uint32_t cb = c % WS_CHAINS;
+        if (!ws_wait(&tfull[cb], (c / WS_CHAINS) & 1, abort_flag)) { run = false; break; }
+        if (threadIdx.x == 128) WS_TRACE(4, c);
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float v[64];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_ld16_nowait(tmem + lane_base + cb * BN + h * 64 + 16 * j, v + 16 * j);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 64; ++i) acc[h * 64 + i] += v[i];
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[cb]);
+        if (threadIdx.x == 128) WS_TRACE(5, c);
+      }
+      if (!run) break;
+      // epilogue: stage this warp's 32 rows one column quarter at a time, then write them row by row
+      // (lanes across columns)
+#pragma unroll
+      for (int hh = 0; hh < BN / WS_EH; ++hh) {
+#pragma unroll
+        for (int i = 0; i < WS_EH; i += 4)
+          *reinterpret_cast<float4*>(stg + lane * WS_LD + i) =
+              make_float4(acc[hh * WS_EH + i], acc[hh * WS_EH + i + 1], acc[hh * WS_EH + i + 2], acc[hh * WS_EH + i + 3]);
+        __syncwarp();
+        constexpr int kLanesPerRow = WS_EH / 4, kRowsPerStep = 32 / kLanesPerRow;
+        const int sub = lane % kLanesPerRow, rr = lane / kLanesPerRow;
+        const int gc = n0 + hh * WS_EH + 4 * sub;
+        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (bias) {
+          if (gc < N) bv.x = bias[gc];
+          if (gc + 1 < N) bv.y = bias[gc + 1];
+          if (gc + 2 < N) bv.z = bias[gc + 2];
+          if (gc + 3 < N) bv.w = bias[gc + 3];
+        }
+        const bool cvec = C && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
+        for (int r2 = 0; r2 < 32; r2 += kRowsPerStep) {
+          const int r = r2 + rr;
+          const int row = m0 + 32 * q + r;
+          if (row >= M) continue;
+          float4 x = *reinterpret_cast<const float4*>(stg + r * WS_LD + 4 * sub);
+          x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
+          if (P) {
+            float* pp = P + (int64_t)row * ldp + (gc >> 1);
+            if (gc + 1 < N) pp[0] = (accumulate ? pp[0] : 0.f) + x.x * x.y;
+            if (gc + 3 < N) pp[1] = (accumulate ? pp[1] : 0.f) + x.z * x.w;
+            if (!C) continue;
+            float* cp = C + (int64_t)row * ldc + gc;
+            if (cvec) {
+              *reinterpret_cast<float4*>(cp) = x;
+            } else {
+              const float xv[4] = {x.x, x.y, x.z, x.w};
+              for (int u = 0; u < 4; ++u)
+                if (gc + u < N) cp[u] = xv[u];
+            }
+            continue;
+          }
+          float* cp = C + (int64_t)row * ldc + gc;
+          if (cvec) {
+            if (accumulate) {
+              const float4 o = *reinterpret_cast<const float4*>(cp);
+              x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+            }
+            *reinterpret_cast<float4*>(cp) = x;
+          } else {
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+            for (int u = 0; u < 4; ++u)
+              if (gc + u < N) cp[u] = accumulate ? cp[u] + xv[u] : xv[u];
+          }
+        }
+        __syncwarp();
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWsTmemCols) : "memory");
   }
 }
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                    const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes, void* stream) {
-  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
-  if (M == 0 || N == 0) return E2A_OK;
-  if (!C || (K > 0 && (!A || !B)) || lda < K || ldb < K || ldc < N) return E2A_ERR_ARG;
-  if ((M + BM - 1) / BM > INT32_MAX || (N + BN - 1) / BN > 65535 || K > INT32_MAX) return E2A_ERR_ARG;
-  cudaStream_t st = (cudaStream_t)stream;
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver through the runtime (no link against libcuda)
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [rows, cols] fp32 row-major with leading dim ld: bk x 128 boxes, (bk * 4)-byte swizzle, zero fill
+bool make_map_2d(EncodeTiledFn enc, CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld,
+                 int bk) {
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)BM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, bk == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+__global__ void k_tf32_split(const float* __restrict__ B, int64_t ldb, int64_t N, int K, float* __restrict__ hi,
+                             float* __restrict__ lo, int64_t ldo) {
+  const int64_t total = N * (int64_t)K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K;
+    const int c = (int)(i - r * K);
+    const float x = B[r * ldb + c];
+    const float h = tf32_hi(x);
+    hi[r * ldo + c] = h;
+    lo[r * ldo + c] = tf32_lo(x, h);
+  }
+}
+
+}  // namespace
+
+// Launches the warp-specialised kernel; E2A_ERR_UNSUPPORTED when the operands do not suit it.
+static int launch_ws(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                     int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
+                     int accumulate, int passes, cudaStream_t st) {
   const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
-                   ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
-  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-  if (vec) {
-    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
-    k_gemm_tf32x3_v2<<<grid, kThreads, kSmem2, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                     accumulate, passes, nullptr, 0);
+                   ((reinterpret_cast<uintptr_t>(B) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(B_lo) & 15u) == 0);
+  if (!vec || K == 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return E2A_ERR_UNSUPPORTED;
+  EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return E2A_ERR_UNSUPPORTED;
+  const int bk = K <= 256 ? 16 : 32;
+  CUtensorMap ta, tb, tbl;
+  if (!make_map_2d(enc, &ta, A, M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
+      !make_map_2d(enc, &tbl, B_lo ? B_lo : B, N, K, ldb, bk))
+    return E2A_ERR_UNSUPPORTED;
+  int dev = 0, sms = 0;
+  E2A_CUDA(cudaGetDevice(&dev));
+  E2A_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  if (tiles > INT32_MAX) return E2A_ERR_ARG;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  if (bk == 16) {
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<16>()));
+    k_gemm_ws<16><<<grid, WsCfg<16>::THREADS, ws_smem<16>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
+                                                            (int)N, (int)K, accumulate, passes);
   } else {
-    E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    k_gemm_tf32x3<false><<<grid, kThreads, kSmemBytes, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                             accumulate, passes);
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32>()));
+    k_gemm_ws<32><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
+                                                            (int)N, (int)K, accumulate, passes);
   }
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }
 
-int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                             const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
+extern "C" {
+
+int e2a_gemm_tf32x3(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                    int64_t ldc, const float* bias, int64_t M, int64_t N, int64_t K, int accumulate, int passes,
+                    void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!C || (K > 0 && (!A || !B)) || lda < K || ldb < K || ldc < N) return E2A_ERR_ARG;
+  if ((M + BM - 1) / BM > INT32_MAX || (N + BN - 1) / BN > 65535 || K > INT32_MAX) return E2A_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int r = launch_ws(A, lda, B, B_lo, ldb, C, ldc, bias, nullptr, 0, M, N, K, accumulate, passes, st);
+  if (r != E2A_ERR_UNSUPPORTED) return r;
+  if (B_lo) return E2A_ERR_UNSUPPORTED;  // a pre-split B needs the pipelined kernel
+  // general operands (unaligned rows, K = 0): the register-staged kernel
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  k_gemm_tf32x3<false><<<grid, kThreads, kSmemBytes, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
+                                                           accumulate, passes);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                             int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
                              int accumulate, int passes, void* stream) {
   if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3) || (N & 1)) return E2A_ERR_ARG;
   if (M == 0 || N == 0) return E2A_OK;
   if (!P || (K > 0 && (!A || !B)) || lda < K || ldb < K || (C && ldc < N) || ldp < N / 2) return E2A_ERR_ARG;
-  if ((M + BM - 1) / BM > INT32_MAX || (N + BN - 1) / BN > 65535 || K > INT32_MAX) return E2A_ERR_ARG;
-  const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
-                   ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
-  if (!vec) return E2A_ERR_UNSUPPORTED;
-  cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
-  E2A_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2));
-  k_gemm_tf32x3_v2<<<grid, kThreads, kSmem2, st>>>(A, lda, B, ldb, C, ldc, bias, (int)M, (int)N, (int)K,
-                                                   accumulate, passes, P, ldp);
+  return launch_ws(A, lda, B, B_lo, ldb, C, ldc, bias, P, ldp, M, N, K, accumulate, passes, (cudaStream_t)stream);
+}
+
+int e2a_tf32_split(const float* B, int64_t ldb, int64_t N, int64_t K, float* B_hi, float* B_lo, int64_t ldo,
+                   void* stream) {
+  if (N < 0 || K < 0 || K > INT32_MAX) return E2A_ERR_ARG;
+  if (N == 0 || K == 0) return E2A_OK;
+  if (!B || !B_hi || !B_lo || ldb < K || ldo < K) return E2A_ERR_ARG;
+  const int64_t total = N * K;
+  const int64_t blocks = (total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096;
+  k_tf32_split<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(B, ldb, N, (int)K, B_hi, B_lo, ldo);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }
+
+#ifdef E2A_GEMM_TRACE
+int e2a_gemm_trace(unsigned long long* out) {
+  E2A_CUDA(cudaMemcpyFromSymbol(out, g_ws_trace, sizeof(g_ws_trace)));
+  return E2A_OK;
+}
+#endif
 
 int e2a_gemm_status(unsigned int* status, int reset, void* stream) {
   if (!status) return E2A_ERR_ARG;

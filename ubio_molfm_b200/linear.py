@@ -12,10 +12,49 @@ from . import _lib
 from ._lib import check, ptr, stream_of
 
 PASSES = 3
+# Pre-split the weight operand (B) into tf32 hi / lo once per call (one small launch) instead of
+# splitting it on chip in every tile.
+PRESPLIT_WEIGHTS = True
 
 
-def gemm(a, b, bias=None, out=None, accumulate=False, passes=None):
-    """``a [M,K] @ b[N,K]^T (+ bias)`` -> [M,N] (fp32, CUDA, row-major with unit inner stride)."""
+def split_tf32(b):
+    """``b`` (fp32, rows of K) -> (hi, lo) contiguous with hi = tf32(b), lo = tf32(b - hi): the
+    pre-split weight operand of the GEMM (one small launch, reused by every product with ``b`` or a
+    row block of it)."""
+    lib = _lib.load()
+    b = b.contiguous().float()
+    hi = torch.empty_like(b)
+    lo = torch.empty_like(b)
+    K = b.shape[-1]
+    check(lib.e2a_tf32_split(ptr(b), K, b.numel() // max(K, 1), K, ptr(hi), ptr(lo), K, stream_of(b.device)),
+          "e2a_tf32_split")
+    return hi, lo
+
+
+def _maybe_split(b):
+    """``split_tf32(b)`` when weights are pre-split, else ``(b, None)`` (split on chip)."""
+    return split_tf32(b) if PRESPLIT_WEIGHTS else (b.contiguous(), None)
+
+
+def _presplit_ok(a_ptr, lda, K):
+    return PRESPLIT_WEIGHTS and K > 0 and K % 4 == 0 and a_ptr % 16 == 0 and lda % 4 == 0
+
+
+def _gemm_ptrs(lib, a, lda, b, b_lo, ldb, c, ldc, bias, M, N, K, accumulate, passes, dev, P=None, ldp=0):
+    """Raw-pointer GEMM (pair-product epilogue when ``P`` is given; ``b_lo`` = pre-split low part)."""
+    st = stream_of(dev)
+    if P is not None:
+        check(lib.e2a_gemm_tf32x3_pairprod(a, lda, b, b_lo, ldb, c, ldc, bias, P, ldp, M, N, K,
+                                           1 if accumulate else 0, passes, st), "e2a_gemm_tf32x3_pairprod")
+        return
+    check(lib.e2a_gemm_tf32x3(a, lda, b, b_lo, ldb, c, ldc, bias, M, N, K, 1 if accumulate else 0, passes, st),
+          "e2a_gemm_tf32x3")
+
+
+def gemm(a, b, bias=None, out=None, accumulate=False, passes=None, b_split=None):
+    """``a [M,K] @ b[N,K]^T (+ bias)`` -> [M,N] (fp32, CUDA, row-major with unit inner stride).
+    ``b_split`` = rows of ``split_tf32`` output matching ``b`` when the caller reuses ``b``; with
+    aligned operands ``b`` is split here otherwise."""
     lib = _lib.load()
     if a.dtype != torch.float32 or b.dtype != torch.float32:
         raise TypeError("gemm expects float32 operands")
@@ -31,9 +70,15 @@ def gemm(a, b, bias=None, out=None, accumulate=False, passes=None):
         out = torch.empty((M, N), device=a.device, dtype=torch.float32)
     if bias is not None:
         bias = bias.contiguous()
-    check(lib.e2a_gemm_tf32x3(ptr(a), max(a.stride(0), K), ptr(b), max(b.stride(0), K), ptr(out), out.stride(0),
-                              ptr(bias), M, N, K, 1 if accumulate else 0, PASSES if passes is None else passes,
-                              stream_of(a.device)), "e2a_gemm_tf32x3")
+    lda = max(a.stride(0), K)
+    passes = PASSES if passes is None else passes
+    if _presplit_ok(a.data_ptr(), lda, K):
+        hi, lo = b_split if b_split is not None else split_tf32(b)
+        _gemm_ptrs(lib, ptr(a), lda, ptr(hi), ptr(lo), K, ptr(out), out.stride(0), ptr(bias), M, N, K, accumulate,
+                   passes, a.device)
+    else:
+        _gemm_ptrs(lib, ptr(a), lda, ptr(b), None, max(b.stride(0), K), ptr(out), out.stride(0), ptr(bias), M, N, K,
+                   accumulate, passes, a.device)
     return out
 
 
@@ -81,8 +126,10 @@ class _SO3LinearFn(torch.autograd.Function):
         Co = w.shape[1]
         x = x.contiguous()
         out = torch.empty((N, R, Co), device=x.device, dtype=torch.float32)
+        whi, wlo = _maybe_split(w)
         for m in range(R):
-            gemm(x[:, m, :], w[lidx[m]], bias if (m == 0 and bias is not None) else None, out=out[:, m, :])
+            gemm(x[:, m, :], w[lidx[m]], bias if (m == 0 and bias is not None) else None, out=out[:, m, :],
+                 b_split=(whi[lidx[m]], wlo[lidx[m]]))
         ctx.save_for_backward(x if w.requires_grad else None, w)
         ctx.lidx = lidx
         ctx.has_bias = bias is not None
@@ -97,9 +144,10 @@ class _SO3LinearFn(torch.autograd.Function):
         dx = dw = db = None
         if ctx.needs_input_grad[0]:
             wt = w.transpose(1, 2).contiguous()  # [L, C, Co]
+            thi, tlo = _maybe_split(wt)
             dx = torch.empty((N, R, C), device=g.device, dtype=torch.float32)
             for m in range(R):
-                gemm(g[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :])
+                gemm(g[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :], b_split=(thi[ctx.lidx[m]], tlo[ctx.lidx[m]]))
         if ctx.needs_input_grad[1]:
             dw = torch.zeros_like(w)
             for m in range(R):
@@ -176,14 +224,13 @@ class _SO3PairProdFn(torch.autograd.Function):
         dev = x.device
         O = torch.empty((N, R, h2), device=dev, dtype=torch.float32)
         P = torch.empty((N, L1, h), device=dev, dtype=torch.float32)
-        st = stream_of(dev)
+        whi, wlo = split_tf32(w12) if _presplit_ok(x.data_ptr(), R * C, C) else (w12, None)
         for m in range(R):
             l = lidx[m]
             first = m == l * l
-            xm = x[:, m, :]
-            check(lib.e2a_gemm_tf32x3_pairprod(ptr(xm), R * C, ptr(w12[l]), C, ptr(O[:, m, :]), R * h2,
-                                               ptr(b12) if m == 0 else None, ptr(P[:, l, :]), L1 * h, N, h2, C,
-                                               0 if first else 1, PASSES, st), "e2a_gemm_tf32x3_pairprod")
+            _gemm_ptrs(lib, x[:, m, :].data_ptr(), R * C, ptr(whi[l]), ptr(wlo[l]) if wlo is not None else None, C,
+                       ptr(O[:, m, :]), R * h2,
+                       ptr(b12) if m == 0 else None, N, h2, C, not first, PASSES, dev, P=ptr(P[:, l, :]), ldp=L1 * h)
         ctx.save_for_backward(O, w12)
         ctx.lidx = lidx
         return P
@@ -199,9 +246,10 @@ class _SO3PairProdFn(torch.autograd.Function):
         D = torch.empty_like(O)
         check(lib.e2a_pair_grad(ptr(O), ptr(G), N, R, L1, h2 // 2, ptr(D), stream_of(O.device)), "e2a_pair_grad")
         wt = w12.transpose(1, 2).contiguous()  # [L+1, C, 2h]
+        thi, tlo = _maybe_split(wt)
         dx = torch.empty((N, R, C), device=O.device, dtype=torch.float32)
         for m in range(R):
-            gemm(D[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :])
+            gemm(D[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :], b_split=(thi[ctx.lidx[m]], tlo[ctx.lidx[m]]))
         return dx, None, None, None
 
 
@@ -276,10 +324,6 @@ def node_apply(A, h, mode="plain"):
     return _NodeApplyFn.apply(A.float(), h.float(), mode)
 
 
-def _gemm_raw(lib, a, lda, b, ldb, c, ldc, bias, M, N, K, dev):
-    check(lib.e2a_gemm_tf32x3(a, lda, b, ldb, c, ldc, bias, M, N, K, 0, PASSES, stream_of(dev)), "e2a_gemm_tf32x3")
-
-
 class _RowBlockLinearFn(torch.autograd.Function):
     """out[n, o_t, :] = x[n, r_t : r_t + k_t, :].flatten() @ W_t^T (+ bias on output row 0), one
     tensor-core GEMM per task t = (r_t, k_t, o_t, w_t) with node-strided operands (no copies).  The
@@ -293,9 +337,11 @@ class _RowBlockLinearFn(torch.autograd.Function):
         n, R, C = x.shape
         Co = weights[0].shape[0]
         out = torch.empty((n, out_rows, Co), device=x.device, dtype=torch.float32)
+        splits = [_maybe_split(w) for w in weights]
         for r0, k, o, wi in tasks:
-            _gemm_raw(lib, x.data_ptr() + 4 * r0 * C, R * C, ptr(weights[wi]), k * C, out.data_ptr() + 4 * o * Co,
-                      out_rows * Co, ptr(bias) if (bias is not None and o == 0) else None, n, Co, k * C, x.device)
+            _gemm_ptrs(lib, x.data_ptr() + 4 * r0 * C, R * C, ptr(splits[wi][0]), ptr(splits[wi][1]), k * C,
+                       out.data_ptr() + 4 * o * Co, out_rows * Co, ptr(bias) if (bias is not None and o == 0) else None,
+                       n, Co, k * C, False, PASSES, x.device)
         ctx.tasks, ctx.weights_t, ctx.shape = tasks, weights_t, (n, R, C, out_rows, Co)
         return out
 
@@ -305,9 +351,10 @@ class _RowBlockLinearFn(torch.autograd.Function):
         g = g.contiguous()
         n, R, C, out_rows, Co = ctx.shape
         dx = torch.empty((n, R, C), device=g.device, dtype=torch.float32)
+        splits = [_maybe_split(w) for w in ctx.weights_t]
         for r0, k, o, wi in ctx.tasks:
-            _gemm_raw(lib, g.data_ptr() + 4 * o * Co, out_rows * Co, ptr(ctx.weights_t[wi]), Co,
-                      dx.data_ptr() + 4 * r0 * C, R * C, None, n, k * C, Co, g.device)
+            _gemm_ptrs(lib, g.data_ptr() + 4 * o * Co, out_rows * Co, ptr(splits[wi][0]), ptr(splits[wi][1]), Co,
+                       dx.data_ptr() + 4 * r0 * C, R * C, None, n, k * C, Co, False, PASSES, g.device)
         return dx, None, None, None, None, None
 
 
