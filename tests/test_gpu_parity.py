@@ -386,11 +386,12 @@ def test_node_half_fused_matches_torch():
 
 
 @pytest.mark.parametrize("mode", ["plain", "merge", "sub"])
-def test_node_apply_modes_match_torch(mode):
+@pytest.mark.parametrize("C", [96, 256])   # 256: the vectorised warp-per-node backward
+def test_node_apply_modes_match_torch(mode, C):
     from ubio_molfm_b200.linear import node_apply
 
     g = torch.Generator().manual_seed(11)
-    n, C = 257, 96
+    n = 257
     A = torch.randn(n, 20, 9, generator=g, dtype=torch.float64)
     x = torch.randn(n, 29 if mode == "sub" else 9, C, generator=g, dtype=torch.float64)
 

@@ -293,6 +293,106 @@ k_node_apply_bwd(const float* __restrict__ A, const float* __restrict__ h, int64
     }
   }
 }
+
+// Butterfly reduce-scatter of 36 per-lane partials over the warp: 37 shuffles instead of 36 x 5.
+// On return lane holds in v[0..1] the full sums of the indices given by rs36_index.
+__device__ __forceinline__ void rs36(float (&v)[36], int lane) {
+#define E2A_RS_STEP(H, W)                                              \
+  {                                                                    \
+    const bool up = (lane & (W)) != 0;                                 \
+    _Pragma("unroll") for (int i = 0; i < (H); ++i) {                  \
+      const float send = up ? v[i] : v[i + (H)];                       \
+      const float keep = up ? v[i + (H)] : v[i];                       \
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, (W));           \
+    }                                                                  \
+  }
+  E2A_RS_STEP(18, 16)
+  E2A_RS_STEP(9, 8)
+  v[9] = 0.f;
+  E2A_RS_STEP(5, 4)
+  v[5] = 0.f;
+  E2A_RS_STEP(3, 2)
+  v[3] = 0.f;
+  E2A_RS_STEP(2, 1)
+#undef E2A_RS_STEP
+}
+// index (0..35) of this lane's v[j] after rs36, or -1 for a padding slot
+__device__ __forceinline__ int rs36_index(int lane, int j) {
+  int p = j + ((lane & 1) ? 2 : 0);
+  if (p >= 3) return -1;
+  p += (lane & 2) ? 3 : 0;
+  if (p >= 5) return -1;
+  p += (lane & 4) ? 5 : 0;
+  if (p >= 9) return -1;
+  p += (lane & 8) ? 9 : 0;
+  return p + ((lane & 16) ? 18 : 0);
+}
+
+// Vectorised backward, one warp per node, lanes over float4 channel groups (C % 128 == 0, rows
+// 16-byte aligned): dh (+ dh_add) = A^T dout with A from shared memory, dsub = -dout, and
+// dA[k,s] = <dout[k,:], h[s,:]> accumulated per lane for four k rows at a time and summed across
+// the warp by one reduce-scatter per group.
+__global__ void __launch_bounds__(256, 2)
+k_node_apply_bwd_warp(const float* __restrict__ A, const float* __restrict__ h, int64_t h_node_stride,
+                      const float* __restrict__ dout, int64_t dout_node_stride, const float* __restrict__ dh_add,
+                      int64_t dh_add_node_stride, int64_t n_nodes, int C, float* __restrict__ dh,
+                      int64_t dh_node_stride, float* __restrict__ dsub, int64_t dsub_node_stride,
+                      float* __restrict__ dA) {
+  __shared__ float As[8][KO * KI];
+  __shared__ float dAs[8][KO * KI];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int64_t n = (int64_t)blockIdx.x * 8 + w; n < n_nodes; n += (int64_t)gridDim.x * 8) {
+    for (int t = lane; t < KO * KI; t += 32) {
+      As[w][t] = A[n * KO * KI + t];
+      dAs[w][t] = 0.f;
+    }
+    __syncwarp();
+    const float* hn = h + n * h_node_stride;
+    const float* gn = dout + n * dout_node_stride;
+    for (int c = 4 * lane; c < C; c += 128) {
+      float4 hv[KI], dv[KI];
+#pragma unroll
+      for (int s = 0; s < KI; ++s) {
+        hv[s] = __ldg(reinterpret_cast<const float4*>(hn + (int64_t)s * C + c));
+        dv[s] = dh_add ? __ldg(reinterpret_cast<const float4*>(dh_add + n * dh_add_node_stride + (int64_t)s * C + c))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll 1
+      for (int kg = 0; kg < KO / 4; ++kg) {
+        float p[36];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int k = 4 * kg + kk;
+          const float4 g = __ldg(reinterpret_cast<const float4*>(gn + (int64_t)k * C + c));
+          if (dsub)
+            *reinterpret_cast<float4*>(dsub + n * dsub_node_stride + (int64_t)k * C + c) =
+                make_float4(-g.x, -g.y, -g.z, -g.w);
+#pragma unroll
+          for (int s = 0; s < KI; ++s) {
+            const float a = As[w][k * KI + s];
+            dv[s].x = fmaf(a, g.x, dv[s].x); dv[s].y = fmaf(a, g.y, dv[s].y);
+            dv[s].z = fmaf(a, g.z, dv[s].z); dv[s].w = fmaf(a, g.w, dv[s].w);
+            p[kk * KI + s] = g.x * hv[s].x + g.y * hv[s].y + g.z * hv[s].z + g.w * hv[s].w;
+          }
+        }
+        if (dA) {
+          rs36(p, lane);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int idx = rs36_index(lane, j);
+            if (idx >= 0) dAs[w][(4 * kg) * KI + idx] += p[j];
+          }
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < KI; ++s) *reinterpret_cast<float4*>(dh + n * dh_node_stride + (int64_t)s * C + c) = dv[s];
+    }
+    __syncwarp();
+    if (dA)
+      for (int t = lane; t < KO * KI; t += 32) dA[n * KO * KI + t] = dAs[w][t];
+    __syncwarp();
+  }
+}
 }  // namespace
 
 extern "C" {
@@ -322,6 +422,17 @@ int e2a_node_apply_bwd(const float* A, const float* h, int64_t h_node_stride, co
   if (n_nodes == 0) return E2A_OK;
   if (!A || !h || !dout || !dh || dh_node_stride < (int64_t)KI * C || (dsub && dsub_node_stride < (int64_t)KO * C))
     return E2A_ERR_ARG;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (C % 128 == 0 && h_node_stride % 4 == 0 && dout_node_stride % 4 == 0 && dh_node_stride % 4 == 0 &&
+      (!dh_add || dh_add_node_stride % 4 == 0) && (!dsub || dsub_node_stride % 4 == 0) && al(h) && al(dout) &&
+      al(dh) && al(dh_add) && al(dsub)) {
+    const int64_t blocks = (n_nodes + 7) / 8 < 148 * 16 ? (n_nodes + 7) / 8 : 148 * 16;
+    k_node_apply_bwd_warp<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, dout, dout_node_stride,
+                                                                         dh_add, dh_add_node_stride, n_nodes, C, dh,
+                                                                         dh_node_stride, dsub, dsub_node_stride, dA);
+    E2A_CHECK_LAUNCH();
+    return E2A_OK;
+  }
   const int64_t g = n_nodes < (1 << 30) ? n_nodes : (1 << 30);
   k_node_apply_bwd<<<(int)g, 256, 0, (cudaStream_t)stream>>>(A, h, h_node_stride, dout, dout_node_stride, dh_add,
                                                              dh_add_node_stride, n_nodes, C, dh, dh_node_stride,
