@@ -504,34 +504,41 @@ k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   float dS[HPL];
 #pragma unroll
   for (int u = 0; u < HPL; ++u) dS[u] = -T[u] / den[u];
-  // pass 2: dz, d_inputhead, d_dist, d_poly; dm and tie counts
+  // pass 2: dz, d_inputhead, d_dist, d_poly, and d_gate = dz * s, ds = dz * gate (beta recomputed in
+  // registers); row max gradient dm = -sum dz and tie counts
   float dmacc[HPL] = {0.f, 0.f, 0.f, 0.f}, nt[HPL] = {0.f, 0.f, 0.f, 0.f};
+  int em[HPL] = {-1, -1, -1, -1};   // first edge attaining the row max, per head
   for (int e = rs; e < re; ++e) {
     const float4 s4 = *reinterpret_cast<const float4*>(bufB + (int64_t)e * H + ho);
     const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho), ih4 = ldg4(inputhead + (int64_t)e * ld_gi + ho);
     const float4 db4 = *reinterpret_cast<const float4*>(bufA + (int64_t)e * H + ho);
-    const float4 b4 = ldg4(beta + (int64_t)e * H + ho);
     const float s[HPL] = {s4.x, s4.y, s4.z, s4.w}, g[HPL] = {g4.x, g4.y, g4.z, g4.w};
     const float ih[HPL] = {ih4.x, ih4.y, ih4.z, ih4.w}, db[HPL] = {db4.x, db4.y, db4.z, db4.w};
-    const float bt[HPL] = {b4.x, b4.y, b4.z, b4.w};
     const float p = poly[e], d = dist[e], rr = fmaxf(d, kMinDist);
-    float dih[HPL], dz[HPL], sd = 0.f, sp = 0.f;
+    float dih[HPL], dg[HPL], ds[HPL], sd = 0.f, sp = 0.f;
 #pragma unroll
     for (int u = 0; u < HPL; ++u) {
       const float a = g[u] * s[u];
       const float ex = expf(a - m[u]);
       const float x = ex * p;
+      const float bt = x * ih[u] / den[u] / rr;   // beta, as the forward computes it
       const float dal = db[u] / rr;
       const float dx = dal * ih[u] / den[u] + dS[u];
       dih[u] = dal * x / den[u];
-      dz[u] = dx * x;
-      dmacc[u] -= dz[u];
-      nt[u] += (a == m[u]) ? 1.f : 0.f;
-      sd += db[u] * bt[u];
+      const float dz = dx * x;
+      dmacc[u] -= dz;
+      if (a == m[u]) {
+        nt[u] += 1.f;
+        if (em[u] < 0) em[u] = e;
+      }
+      sd += db[u] * bt;
       sp += dx * ex;
+      dg[u] = dz * s[u];
+      ds[u] = dz * g[u];
     }
     *reinterpret_cast<float4*>(d_inputhead + (int64_t)e * ld_dgi + ho) = make_float4(dih[0], dih[1], dih[2], dih[3]);
-    *reinterpret_cast<float4*>(d_logit + (int64_t)e * H + ho) = make_float4(dz[0], dz[1], dz[2], dz[3]);
+    *reinterpret_cast<float4*>(d_gate + (int64_t)e * ld_dgi + ho) = make_float4(dg[0], dg[1], dg[2], dg[3]);
+    *reinterpret_cast<float4*>(d_logit + (int64_t)e * H + ho) = make_float4(ds[0], ds[1], ds[2], ds[3]);
     sd = e2a_warp_sum(sd);
     sp = e2a_warp_sum(sp);
     if (lane == 0) {
@@ -539,27 +546,28 @@ k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
       d_poly[e] = sp;
     }
   }
-  // pass 3: da = dz + [a == m] dm / n_ties (PyTorch's amax rule); d_gate = da * s; ds = da * gate
-  float share[HPL];
+  // the row max passes dm to the edges attaining it, shared equally among ties (PyTorch's amax
+  // rule): da = dz + dm / n_ties there, so d_gate += share * s and ds += share * gate.  One edge per
+  // head in the common case; a tie re-walks the row for that head only.
 #pragma unroll
-  for (int u = 0; u < HPL; ++u) share[u] = nt[u] > 0.f ? dmacc[u] / nt[u] : 0.f;
-  for (int e = rs; e < re; ++e) {
-    const float4 s4 = *reinterpret_cast<const float4*>(bufB + (int64_t)e * H + ho);
-    const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho);
-    float4* dl = reinterpret_cast<float4*>(d_logit + (int64_t)e * H + ho);
-    const float4 dz4 = *dl;
-    const float s[HPL] = {s4.x, s4.y, s4.z, s4.w}, g[HPL] = {g4.x, g4.y, g4.z, g4.w};
-    const float dz[HPL] = {dz4.x, dz4.y, dz4.z, dz4.w};
-    float dg[HPL], ds[HPL];
-#pragma unroll
-    for (int u = 0; u < HPL; ++u) {
-      const float a = g[u] * s[u];
-      const float da = dz[u] + ((a == m[u]) ? share[u] : 0.f);
-      dg[u] = da * s[u];
-      ds[u] = da * g[u];
+  for (int u = 0; u < HPL; ++u) {
+    if (nt[u] <= 0.f) continue;
+    const float share = dmacc[u] / nt[u];
+    const int h = ho + u;
+    if (nt[u] == 1.f) {
+      const int e = em[u];
+      const float sv = bufB[(int64_t)e * H + h], gv = __ldg(gate + (int64_t)e * ld_gi + h);
+      d_gate[(int64_t)e * ld_dgi + h] += share * sv;
+      d_logit[(int64_t)e * H + h] += share * gv;
+    } else {
+      for (int e = em[u]; e < re; ++e) {
+        const float sv = bufB[(int64_t)e * H + h], gv = __ldg(gate + (int64_t)e * ld_gi + h);
+        if (gv * sv == m[u]) {
+          d_gate[(int64_t)e * ld_dgi + h] += share * sv;
+          d_logit[(int64_t)e * H + h] += share * gv;
+        }
+      }
     }
-    *reinterpret_cast<float4*>(d_gate + (int64_t)e * ld_dgi + ho) = make_float4(dg[0], dg[1], dg[2], dg[3]);
-    *dl = make_float4(ds[0], ds[1], ds[2], ds[3]);
   }
 }
 
