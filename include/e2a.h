@@ -45,6 +45,8 @@ int e2a_version(void);
 const char* e2a_status_string(int status);
 /* cudaError_t of the most recent E2A_ERR_CUDA on this host thread (0 if none). */
 int e2a_last_cuda_error(void);
+/* Number of kernels this library has launched in this process (all host threads). */
+uint64_t e2a_launch_count(void);
 
 /* ------------------------------------------------------------------------------------------ */
 /* CSR metadata: prepare_sparse_qk_edge_index_metadata (triton_sparse_qk_autograd.py:635-652). */
@@ -174,6 +176,29 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
                      const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm,
                      const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,
                      int H, int D, int C, float* d_k, float* d_value, void* stream);
+
+/* The backward as three stages, the first one fused (preferred; e2a_attn_bwd_query + _key remain):   */
+/* 1. key side, one pass over the key CSR gathering each destination cotangent row once:               */
+/*    d_value[k] = sum_e beta[e] dout[i_e] (sparse_v_agg_edge_index backward, d value) and             */
+/*    d_beta[e,h] = <dout[i_e], value[k]>_h (its d alpha).  H must divide 1024 and be <= 128, else       */
+/*    E2A_ERR_UNSUPPORTED.                                                                               */
+int e2a_attn_bwd_value(const float* value, const float* dout, const float* beta, const int32_t* k_row_ptr,
+                       const int32_t* k_col, const int32_t* k_perm, const int32_t* key_order, int64_t n_rows,
+                       int64_t n_keys, int64_t n_edges, int H, int D, int C, float* d_value, float* d_beta,
+                       void* stream);
+/* 2. query side from d_beta: softmax backward (PyTorch amax tie rule) -> d_gate, d_inputhead, d_poly,  */
+/*    d_dist, ds = d_logit, and d_q = sum_e ds k.  Workspace: e2a_attn_bwd_softmax_workspace_bytes.      */
+size_t e2a_attn_bwd_softmax_workspace_bytes(int64_t n_edges, int H);
+int e2a_attn_bwd_softmax(const float* q, const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
+                         const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                         const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D,
+                         int C, const float* beta, const float* row_max, const float* row_sum, const float* d_beta,
+                         float* d_q, float* d_gate, float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist,
+                         float* d_logit, void* workspace, size_t workspace_bytes, void* stream);
+/* 3. key side: d_k[k] = sum_e ds[e] q[i_e]. */
+int e2a_attn_bwd_dk(const float* q, const float* d_logit, const int32_t* k_row_ptr, const int32_t* k_col,
+                    const int32_t* k_perm, const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,
+                    int H, int D, int C, float* d_k, void* stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Dense fp32 projection on tcgen05 tensor cores: C[M,N] = A[M,K] B[N,K]^T (+bias[N]) (+C when  */

@@ -463,3 +463,51 @@ def test_layer_fused_eval_path_equals_module_path():
             assert a is None and b is None, k
             continue
         assert (a - b).abs().max().item() <= 1e-5 * max(b.abs().max().item(), 1.0), k
+
+
+def test_three_stage_backward_equals_two_entry_backward():
+    """e2a_attn_bwd_value + _softmax + _dk (the fused path the layer uses) produce the same gradients
+    as e2a_attn_bwd_query + e2a_attn_bwd_key on the same inputs."""
+    from ubio_molfm_b200 import _lib
+    from ubio_molfm_b200._lib import check, ptr, stream_of
+    from ubio_molfm_b200.ops import attention_span, prepare_sparse_qk_edge_index_metadata
+
+    g = torch.Generator().manual_seed(21)
+    N, M, E, H, D, C = 300, 420, 4000, 128, 8, 58
+    qi = torch.sort(torch.randint(0, N, (E,), generator=g)).values
+    ki = torch.randint(0, M, (E,), generator=g)
+    md = prepare_sparse_qk_edge_index_metadata(qi.to(DEV), ki.to(DEV), N, M)
+    q = torch.randn(N, H, D, generator=g).to(DEV).requires_grad_(True)
+    k = torch.randn(M, H, D, generator=g).to(DEV).requires_grad_(True)
+    v = torch.randn(M, C, H, generator=g).to(DEV).requires_grad_(True)
+    gate = torch.randn(E, 2 * H, generator=g).to(DEV).requires_grad_(True)
+    poly = torch.rand(E, generator=g).to(DEV).requires_grad_(True)
+    dist = (torch.rand(E, generator=g) * 5 + 0.5).to(DEV).requires_grad_(True)
+    out = attention_span(q, k, v, gate, poly, dist, md)
+    dout = torch.randn_like(out)
+    grads = torch.autograd.grad(out, [q, k, v, gate, poly, dist], dout)
+    # the two-entry path on the same saved tensors
+    lib = _lib.load()
+    st = stream_of(q.device)
+    from ubio_molfm_b200.ops import TIMER  # noqa: F401  (imported for parity with the layer path)
+    beta = torch.empty(E, H, device=DEV)
+    rmax = torch.empty(N, H, device=DEV)
+    rsum = torch.empty(N, H, device=DEV)
+    o2 = torch.empty(N, C, H, device=DEV)
+    md32 = [t.to(torch.int32) for t in md]
+    check(lib.e2a_attn_fwd(ptr(q), ptr(k), ptr(v), ptr(gate), ptr(gate[:, H:]), 2 * H, ptr(poly), ptr(dist),
+                           ptr(md32[0]), ptr(md32[1]), None, N, M, E, H, D, C, ptr(o2), ptr(beta), ptr(rmax), ptr(rsum),
+                           st), "e2a_attn_fwd")
+    ws = torch.empty(lib.e2a_attn_bwd_workspace_bytes(E, H), dtype=torch.uint8, device=DEV)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(E, 2 * H, device=DEV)
+    dp, dd, dl = torch.empty(E, device=DEV), torch.empty(E, device=DEV), torch.empty(E, H, device=DEV)
+    check(lib.e2a_attn_bwd_query(ptr(q), ptr(k), ptr(v), ptr(gate), ptr(gate[:, H:]), 2 * H, ptr(poly), ptr(dist),
+                                 ptr(md32[0]), ptr(md32[1]), None, N, M, E, H, D, C, ptr(beta), ptr(rmax), ptr(rsum),
+                                 ptr(dout), ptr(dq), ptr(dg), ptr(dg[:, H:]), 2 * H, ptr(dp), ptr(dd), ptr(dl), ptr(ws),
+                                 ws.numel(), st), "e2a_attn_bwd_query")
+    check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(dl), ptr(md32[3]), ptr(md32[4]), ptr(md32[5]), None,
+                               N, M, E, H, D, C, ptr(dk), ptr(dv), st), "e2a_attn_bwd_key")
+    # d(beta) is summed in a different order on the two paths (fp32 rounding only)
+    for a, b in zip(grads, [dq, dk, dv, dg, dp, dd]):
+        assert (a - b).abs().max().item() <= 1e-4 * max(b.abs().max().item(), 1.0)

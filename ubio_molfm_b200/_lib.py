@@ -16,6 +16,7 @@ LIB_PATH = os.environ.get("E2A_LIB", os.path.join(_HERE, "libe2a.so"))
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
 I32 = ctypes.c_int
+U64 = ctypes.c_uint64
 F32 = ctypes.c_float
 SZ = ctypes.c_size_t
 
@@ -24,6 +25,7 @@ SIGNATURES = {
     "e2a_version": (I32, []),
     "e2a_status_string": (ctypes.c_char_p, [I32]),
     "e2a_last_cuda_error": (I32, []),
+    "e2a_launch_count": (U64, []),
     "e2a_csr_workspace_bytes": (SZ, [I64, I64, I64]),
     "e2a_csr_build": (I32, [P, P, I64, I64, I64, P, P, P, P, P, P, P, SZ, P]),
     "e2a_pbc_expand_workspace_bytes": (SZ, [I64, I32]),
@@ -59,6 +61,11 @@ SIGNATURES = {
     "e2a_attn_bwd_query_noalloc": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                          P, P, P, P, P, P, P, I64, P, P, P, P]),
     "e2a_attn_bwd_key": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
+    "e2a_attn_bwd_value": (I32, [P, P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P]),
+    "e2a_attn_bwd_softmax_workspace_bytes": (SZ, [I64, I32]),
+    "e2a_attn_bwd_softmax": (I32, [P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P, P, P, P, P,
+                                   I64, P, P, P, P, SZ, P]),
+    "e2a_attn_bwd_dk": (I32, [P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P]),
 }
 
 _lib = None
@@ -83,6 +90,11 @@ def load():
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+def launch_count() -> int:
+    """Kernels launched by this library so far in this process."""
+    return int(load().e2a_launch_count())
 
 
 def check(status: int, what: str):

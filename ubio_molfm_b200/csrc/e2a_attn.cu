@@ -120,6 +120,88 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
 }
 
 // ------------------------------------------------------------------------------------------------
+// Key-side value backward, fused: one CTA per key row k (key CSR, spatial key order).  For every edge
+// e = (i -> k) the destination cotangent row dout[i] ([C,H] layout, channel = c*H + h) is gathered
+// once and serves both products:
+//   d_value[k] += beta[e,h] dout[i]                       (the value aggregation's transpose)
+//   d_beta[e,h] = sum_c dout[i,c,h] value[k,c,h]          (the aggregation's weight gradient)
+// The key's own value row stays in registers (each thread owns KS float4 slots, all of the same four
+// heads); d_beta partials of a batch of kVB edges are combined across the warps in shared memory.
+// Requires H dividing 1024 and H <= 128 (a thread's slots share heads, every warp covers all head
+// quads, one batch is one float4 per thread) and the [C,H] channel layout.
+// ------------------------------------------------------------------------------------------------
+template <int KS>
+__global__ void __launch_bounds__(kThreads)
+k_value_bwd(const float* __restrict__ value, const float* __restrict__ dout, const float* __restrict__ beta, int H,
+            int row_f4, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
+            const int32_t* __restrict__ perm, const int32_t* __restrict__ order, int64_t n_rows,
+            float* __restrict__ d_value, float* __restrict__ d_beta) {
+  extern __shared__ float4 smem4[];
+  float4* part = smem4;                       // [kWarps][kVB = 1024 / H][H / 4]
+  const int H4 = H / 4, vb = kThreads / H4;   // edges per batch
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int hq = threadIdx.x % H4;            // this thread's head quad (heads 4 hq .. 4 hq + 3)
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const int kk = row_of(order, r);
+    const int rs = row_ptr[kk], re = row_ptr[kk + 1];
+    const float4* vr = reinterpret_cast<const float4*>(value + (int64_t)kk * row_f4 * 4);
+    float4 vv[KS], acc[KS];
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int f = threadIdx.x + s * kThreads;
+      vv[s] = f < row_f4 ? __ldg(vr + f) : f4_zero();
+      acc[s] = f4_zero();
+    }
+    for (int p0 = rs; p0 < re; p0 += vb) {
+      const int nb = min(vb, re - p0);
+      for (int b = 0; b < nb; ++b) {
+        const int p = p0 + b;
+        const int64_t e = perm[p];
+        const float4* xr = reinterpret_cast<const float4*>(dout + (int64_t)col[p] * row_f4 * 4);
+        const float4 bw = ldg4(beta + e * H + 4 * hq);
+        float4 pt = f4_zero();
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const int f = threadIdx.x + s * kThreads;
+          if (f < row_f4) {
+            const float4 x = __ldg(xr + f);
+            acc[s] = f4_fma4(bw, x, acc[s]);
+            pt = f4_fma4(x, vv[s], pt);
+          }
+        }
+        // lanes of one warp cover head quads (32 * warp + lane) % H4; fold the warp's duplicates
+        for (int o = H4; o < 32; o <<= 1) {
+          pt.x += __shfl_xor_sync(0xffffffffu, pt.x, o);
+          pt.y += __shfl_xor_sync(0xffffffffu, pt.y, o);
+          pt.z += __shfl_xor_sync(0xffffffffu, pt.z, o);
+          pt.w += __shfl_xor_sync(0xffffffffu, pt.w, o);
+        }
+        if (lane < H4 || H4 >= 32) part[(warp * vb + b) * H4 + hq] = pt;
+      }
+      __syncthreads();
+      {  // thread t finalises head quad t % H4 of batch edge t / H4 (warp partials in fixed order)
+        const int b = threadIdx.x / H4;
+        if (b < nb) {
+          float4 sum = f4_zero();
+          for (int w = 0; w < kWarps; ++w) {
+            const float4 v = part[(w * vb + b) * H4 + hq];
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+          }
+          *reinterpret_cast<float4*>(d_beta + (int64_t)perm[p0 + b] * H + 4 * hq) = sum;
+        }
+      }
+      __syncthreads();
+    }
+    float4* orow = reinterpret_cast<float4*>(d_value + (int64_t)kk * row_f4 * 4);
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int f = threadIdx.x + s * kThreads;
+      if (f < row_f4) orow[f] = acc[s];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Forward softmax: beta[e,h] = exp(g s - m) poly ih / (S + eps) / max(d, 1e-6), plus row stats
 // ------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
@@ -681,6 +763,43 @@ int bwd_query_launch(const float* q, const float* k, const float* value, const f
   return launch_agg_hd(k, d_logit, dm, row_ptr, col, nullptr, row_order, n_rows, d_q, st);
 }
 
+// fused key-side value backward (d_value and d_beta); E2A_ERR_UNSUPPORTED outside its layout
+int value_bwd_launch(const float* value, const float* dout, const float* beta, const Dims& dm, int ks,
+                     const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm, const int32_t* key_order,
+                     int64_t n_keys, float* d_value, float* d_beta, cudaStream_t st) {
+  if (1024 % dm.H != 0 || dm.H > 128) return E2A_ERR_UNSUPPORTED;  // every warp covers all head quads
+  const size_t sm = (size_t)kWarps * kThreads * 16;  // kWarps x (1024 / H edges x H / 4 quads) float4
+  E2A_DISPATCH_KS(ks, k_value_bwd, {
+    E2A_CUDA(prep_smem(kf, sm));
+    kf<<<grid_for(n_keys), kThreads, sm, st>>>(value, dout, beta, dm.H, dm.CH4, k_row_ptr, k_col, k_perm, key_order,
+                                               n_keys, d_value, d_beta);
+  });
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+// query-side backward from a given d_beta: softmax backward + d_q; scratch bufB ([E,H])
+int softmax_bwd_dq_launch(const float* q, const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
+                          const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                          const int32_t* row_order, int64_t n_rows, const Dims& dm, const float* beta,
+                          const float* row_max, const float* row_sum, const float* d_beta, float* d_q, float* d_gate,
+                          float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
+                          float* bufB, cudaStream_t st) {
+  if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
+    k_softmax_bwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+        q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
+        d_inputhead, ld_dgi, d_poly, d_dist, d_logit, d_beta, bufB);
+  } else {
+    const size_t ssm = softmax_smem(dm, 3);
+    E2A_CUDA(prep_smem(k_softmax_bwd, ssm));
+    k_softmax_bwd<<<grid_for(n_rows), kThreads, ssm, st>>>(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
+                                                           row_order, n_rows, dm, beta, row_max, row_sum, d_gate,
+                                                           d_inputhead, ld_dgi, d_poly, d_dist, d_logit, d_beta, bufB);
+  }
+  E2A_CHECK_LAUNCH();
+  return launch_agg_hd(k, d_logit, dm, row_ptr, col, nullptr, row_order, n_rows, d_q, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -759,6 +878,66 @@ int e2a_attn_bwd_key(const float* q, const float* dout, const float* beta, const
   rc = launch_agg_ch(dout, beta, dm, ks, k_row_ptr, k_col, k_perm, key_order, n_keys, d_value, st);
   if (rc) return rc;
   return launch_agg_hd(q, d_logit, dm, k_row_ptr, k_col, k_perm, key_order, n_keys, d_k, st);
+}
+
+
+int e2a_attn_bwd_value(const float* value, const float* dout, const float* beta, const int32_t* k_row_ptr,
+                       const int32_t* k_col, const int32_t* k_perm, const int32_t* key_order, int64_t n_rows,
+                       int64_t n_keys, int64_t n_edges, int H, int D, int C, float* d_value, float* d_beta,
+                       void* stream) {
+  Dims dm;
+  int ks;
+  int rc = check_dims(H, D, C, dm, ks);
+  if (rc) return rc;
+  if (n_rows < 0 || n_keys < 0 || n_edges < 0 || n_edges > INT32_MAX) return E2A_ERR_ARG;
+  if (n_keys == 0) return E2A_OK;
+  if (!k_row_ptr || !d_value || !value) return E2A_ERR_ARG;
+  if (n_edges > 0 && (!dout || !beta || !k_col || !k_perm || !d_beta)) return E2A_ERR_ARG;
+  return value_bwd_launch(value, dout, beta, dm, ks, k_row_ptr, k_col, k_perm, key_order, n_keys, d_value, d_beta,
+                          (cudaStream_t)stream);
+}
+
+size_t e2a_attn_bwd_softmax_workspace_bytes(int64_t n_edges, int H) {
+  return e2a_align_up((size_t)(n_edges > 0 ? n_edges : 1) * H * 4, 256) + 256;
+}
+
+int e2a_attn_bwd_softmax(const float* q, const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
+                         const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                         const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D,
+                         int C, const float* beta, const float* row_max, const float* row_sum, const float* d_beta,
+                         float* d_q, float* d_gate, float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist,
+                         float* d_logit, void* workspace, size_t workspace_bytes, void* stream) {
+  Dims dm;
+  int ks;
+  int rc = check_dims(H, D, C, dm, ks);
+  if (rc) return rc;
+  if (n_rows < 0 || n_keys < 0 || n_edges < 0 || ld_gi < H || ld_dgi < H || n_edges > INT32_MAX) return E2A_ERR_ARG;
+  if (n_rows == 0) return E2A_OK;
+  if (!q || !row_ptr || !d_q) return E2A_ERR_ARG;
+  if (n_edges > 0 && (!k || !gate || !inputhead || !poly || !dist || !col || !beta || !d_beta || !d_gate ||
+                      !d_inputhead || !d_poly || !d_dist || !d_logit))
+    return E2A_ERR_ARG;
+  if (workspace_bytes < e2a_attn_bwd_softmax_workspace_bytes(n_edges, H)) return E2A_ERR_WORKSPACE;
+  E2aArena ar{(char*)workspace, workspace_bytes, 0};
+  float* bufB = (float*)ar.take((size_t)(n_edges > 0 ? n_edges : 1) * H * 4);
+  if (!bufB) return E2A_ERR_WORKSPACE;
+  return softmax_bwd_dq_launch(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm, beta,
+                               row_max, row_sum, d_beta, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,
+                               bufB, (cudaStream_t)stream);
+}
+
+int e2a_attn_bwd_dk(const float* q, const float* d_logit, const int32_t* k_row_ptr, const int32_t* k_col,
+                    const int32_t* k_perm, const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,
+                    int H, int D, int C, float* d_k, void* stream) {
+  Dims dm;
+  int ks;
+  int rc = check_dims(H, D, C, dm, ks);
+  if (rc) return rc;
+  if (n_rows < 0 || n_keys < 0 || n_edges < 0) return E2A_ERR_ARG;
+  if (n_keys == 0) return E2A_OK;
+  if (!k_row_ptr || !d_k) return E2A_ERR_ARG;
+  if (n_edges > 0 && (!q || !d_logit || !k_col || !k_perm)) return E2A_ERR_ARG;
+  return launch_agg_hd(q, d_logit, dm, k_row_ptr, k_col, k_perm, key_order, n_keys, d_k, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -6,6 +6,7 @@
 
 #define E2A_CHECK_LAUNCH()                                   \
   do {                                                       \
+    e2a_note_launch();                                       \
     cudaError_t _e = cudaGetLastError();                     \
     if (_e != cudaSuccess) { e2a_set_cuda_error(_e); return E2A_ERR_CUDA; } \
   } while (0)
@@ -17,6 +18,7 @@
   } while (0)
 
 void e2a_set_cuda_error(cudaError_t e);
+void e2a_note_launch();  // counts kernel launches for e2a_launch_count
 
 static inline size_t e2a_align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

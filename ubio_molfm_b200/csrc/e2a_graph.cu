@@ -4,6 +4,7 @@
 // no float atomics; grouping uses integer atomics followed by a deterministic in-segment ordering.
 #include <cub/cub.cuh>
 #include <stdio.h>
+#include <atomic>
 #include "e2a_common.cuh"
 
 namespace {
@@ -488,6 +489,8 @@ int rg_prepare(const float* pts, const int64_t* p_ptr, int64_t NQ, int64_t P, in
 
 static thread_local int g_last_cuda_error = 0;
 void e2a_set_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+static std::atomic<unsigned long long> g_launches{0};
+void e2a_note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 extern "C" {
 
@@ -505,6 +508,8 @@ const char* e2a_status_string(int status) {
 }
 
 int e2a_last_cuda_error(void) { return g_last_cuda_error; }
+
+uint64_t e2a_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 size_t e2a_csr_workspace_bytes(int64_t E, int64_t N, int64_t M) {
   int64_t R = N > M ? N : M;

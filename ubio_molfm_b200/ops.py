@@ -335,6 +335,29 @@ class AttnSpanFn(torch.autograd.Function):
         d_poly = torch.empty(E, device=dev, dtype=torch.float32)
         d_dist = torch.empty(E, device=dev, dtype=torch.float32)
         d_logit = torch.empty((E, H), device=dev, dtype=torch.float32)
+        d_k = torch.empty_like(key)
+        d_v = torch.empty_like(value)
+        if H <= 128 and 1024 % H == 0:
+            # fused key-side pass first (d_value and d_beta from one gather of each cotangent row)
+            d_beta = torch.empty((E, H), device=dev, dtype=torch.float32)
+            tok = TIMER.start("e2a_attn_bwd_value")
+            check(lib.e2a_attn_bwd_value(ptr(value), ptr(dout), ptr(beta), ptr(md[3]), ptr(md[4]), ptr(md[5]),
+                                         ptr(key_order), N, M, E, H, D, C, ptr(d_v), ptr(d_beta), st),
+                  "e2a_attn_bwd_value")
+            TIMER.stop(tok)
+            ws = _workspace(lib.e2a_attn_bwd_softmax_workspace_bytes(E, H), dev)
+            tok = TIMER.start("e2a_attn_bwd_softmax")
+            check(lib.e2a_attn_bwd_softmax(ptr(q), ptr(key), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H, ptr(poly),
+                                           ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
+                                           ptr(beta), ptr(rmax), ptr(rsum), ptr(d_beta), ptr(d_q), ptr(d_gate),
+                                           ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit), ptr(ws),
+                                           ws.numel(), st), "e2a_attn_bwd_softmax")
+            TIMER.stop(tok)
+            tok = TIMER.start("e2a_attn_bwd_dk")
+            check(lib.e2a_attn_bwd_dk(ptr(q), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]), ptr(key_order), N, M,
+                                      E, H, D, C, ptr(d_k), st), "e2a_attn_bwd_dk")
+            TIMER.stop(tok)
+            return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None
         ws = _workspace(lib.e2a_attn_bwd_workspace_bytes(E, H), dev)
         tok = TIMER.start("e2a_attn_bwd_query")
         check(lib.e2a_attn_bwd_query(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
@@ -343,8 +366,6 @@ class AttnSpanFn(torch.autograd.Function):
                                      ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit), ptr(ws),
                                      ws.numel(), st), "e2a_attn_bwd_query")
         TIMER.stop(tok)
-        d_k = torch.empty_like(key)
-        d_v = torch.empty_like(value)
         tok = TIMER.start("e2a_attn_bwd_key")
         check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]),
                                    ptr(key_order), N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
