@@ -199,6 +199,12 @@ def bwdk_algorithmic_bytes(N, N2, E):
     return 4 * (reads + writes)
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each span entry point (sum over its kernels),
+# one ncu capture of the default workload (1e5 atoms, k = 32); summary in profiles/attn_kernels_dram_100k.txt.
+MEASURED_TRAFFIC_DEFAULT = {"e2a_attn_fwd": 20.52e9, "e2a_attn_bwd_value": 16.78e9,
+                            "e2a_attn_bwd_softmax": 25.52e9, "e2a_attn_bwd_dk": 2.74e9}
+
+
 def bwdv_algorithmic_bytes(N, N2, E):
     """e2a_attn_bwd_value: own value row and each cotangent row once, beta, key CSR; d_value, d_beta."""
     CH = 58 * HEADS
@@ -369,7 +375,9 @@ def run_ours(args, ws, rank, local):
     peak, peak_kind = measured_peaks()
     achieved = alg / (per_launch_ms * 1e-3) / 1e9
     roof = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+            "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+            "traffic": (MEASURED_TRAFFIC_DEFAULT.get(name)
+                        if (args.atoms, args.k) == (100_000, 32) else None),
             "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
             "kernels_ms_per_step": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
             "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
