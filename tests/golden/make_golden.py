@@ -212,6 +212,93 @@ def layer_cases(mods):
     return cases
 
 
+BACKBONE_CFG = dict(irreps_node_embedding="32x0e+32x1e+32x2e", num_layers=2, max_neighbors=None,
+                    max_radius=5.0, number_of_basis=32, num_attn_heads=8, attn_scalar_head=8,
+                    irreps_head="4x0e+4x1e+4x2e", norm_layer="rms_norm_sh", alpha_drop=0.0,
+                    tp_type="QK_alpha", attn_type="so2-first-order", atom_type_cnt=256, avg_degree=23.0)
+
+
+def _energy_head(embedding_dim):
+    """The reference's MLP_energy_head (pipeline/head.py:330-341), imported when its module loads
+    under the shim; its three-layer MLP otherwise (same parameter names)."""
+    try:
+        import importlib
+        head = importlib.import_module("molfm.pipeline.head")
+        return head.MLP_energy_head(embedding_dim, 2), "reference"
+    except Exception:  # noqa: BLE001 -- the head module pulls in optional dependencies
+        m = torch.nn.Module()
+        m.mlp = torch.nn.Sequential(torch.nn.Linear(embedding_dim, embedding_dim), torch.nn.SiLU(),
+                                    torch.nn.Linear(embedding_dim, embedding_dim), torch.nn.SiLU(),
+                                    torch.nn.Linear(embedding_dim, 1))
+        m.forward = lambda emb, irreps=None: m.mlp(emb)
+        return m, "restated"
+
+
+def backbone_case(mods, P, ZZ, cell, pbc, seed, max_neighbors=None):
+    """The reference E2former (e2former.py:756-1145) + energy head, energies and forces = -dE/dpos by
+    autograd through its own PBC expansion and radius graph (the wrapper's path, e2former_wrapper.py:
+    140-339, and GradientHead, pipeline/head.py:305-328)."""
+    mu, e2f = mods["mu"], mods["e2f"]
+    cfg = dict(BACKBONE_CFG, max_neighbors=max_neighbors)
+    dec = e2f.E2former(**cfg).eval()
+    synthetic.seeded_params_(dec, seed)
+    C = int(cfg["irreps_node_embedding"].split("x")[0])
+    head, head_kind = _energy_head(C)
+    synthetic.seeded_params_(head, seed + 1)
+    P = torch.tensor(P, dtype=torch.float32)
+    Z = torch.tensor(ZZ, dtype=torch.long)
+    B, L = Z.shape
+    node_mask = Z != 0
+    padding_mask = ~node_mask
+    pos = P.clone().requires_grad_(True)
+    posm = torch.where(padding_mask.unsqueeze(-1).repeat(1, 1, 3), 999.0, pos)
+    cell_t = torch.tensor(cell, dtype=torch.float32).reshape(1, 3, 3).repeat(B, 1, 1)
+    pbc_t = torch.tensor(pbc, dtype=torch.bool).reshape(1, 3).repeat(B, 1)
+    bd = {"pos": posm, "atom_masks": node_mask, "atomic_numbers": Z, "pbc": pbc_t, "cell": cell_t}
+    if bool(pbc_t.any()):
+        ce = mu.CellExpander(cfg["max_radius"], 512, 4)
+        ex = ce.expand_includeself(posm, pbc_t, Z, cell_t, neighbors_radius=(None, cfg["max_radius"]),
+                                   use_grad=True, padding_mask=padding_mask)
+    else:
+        ex = {"expand_node_pos": posm, "outcell_index": torch.arange(L).unsqueeze(0).repeat(B, 1),
+              "expand_node_mask": node_mask}
+    bd.update(ex)
+    exp_pos = bd["expand_node_pos"].masked_fill(~bd["expand_node_mask"].unsqueeze(-1), 999)
+    bd["expand_node_pos"] = exp_pos
+    ptr = torch.nn.functional.pad(node_mask.sum(-1).to(torch.int32).cumsum(0), (1, 0))
+    bd["f_exp_node_pos"] = exp_pos[bd["expand_node_mask"]]
+    bd["f_outcell_index"] = (bd["outcell_index"] + ptr[:B, None])[bd["expand_node_mask"]]
+    nb = mu.construct_radius_neighbor(posm, node_mask, exp_pos, bd["expand_node_mask"],
+                                      max_dist=cfg["max_radius"], min_dist=1e-4, max_neighbors=max_neighbors)
+    tok = torch.zeros(B, L, C)
+    node_attr, _, node_irreps = dec(bd, tok, None, neighbor_info=nb)
+    e_atom = head(node_attr, node_irreps).squeeze(-1).masked_fill(~node_mask, 0.0)
+    energy = e_atom.sum(dim=-1)
+    (grad,) = torch.autograd.grad(energy.sum(), pos)
+    return {
+        "cfg": np.array(json.dumps(dict(cfg, seed=seed, head=head_kind))),
+        "pos": _np(P[node_mask]), "Z": _np(Z[node_mask]),
+        "batch": _np(torch.arange(B).unsqueeze(1).repeat(1, L)[node_mask]),
+        "cell": np.asarray(cell, np.float32), "pbc": np.asarray(pbc, bool),
+        "energy": _np(energy), "forces": _np(-grad[node_mask]),
+        "node_irreps": _np(node_irreps[node_mask]), "n_edges": np.array(int(nb["query_idx"].numel())),
+    }
+
+
+def backbone_cases(mods):
+    cases = {}
+    rng = np.random.default_rng(8)
+    pos = rng.uniform(0, 8.0, size=(40, 3)).astype(np.float32)
+    Z = rng.choice([1, 6, 7, 8], size=40)
+    cases["backbone_pbc40"] = backbone_case(mods, pos[None], Z[None], np.eye(3, dtype=np.float32) * 8.0,
+                                            [True, True, True], seed=31)
+    mols = synthetic.molecule_batch(3, 8, 20, seed=9)
+    P, ZZ = pad_systems([(m[0], m[1]) for m in mols])
+    cases["backbone_mol3"] = backbone_case(mods, P, ZZ, np.zeros((3, 3), np.float32), [False] * 3, seed=32,
+                                           max_neighbors=12)
+    return cases
+
+
 def so2_pin(mods):
     mu, so2tp = mods["mu"], mods["so2tp"]
     torch.manual_seed(0)
@@ -250,17 +337,23 @@ def so2_pin(mods):
     }
 
 
-def main():
+def main(only=None):
+    """Write every fixture, or only those whose name starts with ``only``."""
     mods = refshim.load_reference()
-    pin = so2_pin(mods)
-    assert pin["max_abs_diff"] < 1e-5, pin
-    with open(os.path.join(HERE, "so2_pin.json"), "w") as f:
-        json.dump(pin, f, indent=1)
-    print("so2 pin", pin["max_abs_diff"])
-    for name, rec in {**graph_cases(mods), **layer_cases(mods)}.items():
-        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
-        print(name, "E=", len(rec["query_idx"]), "N=", len(rec["pos"]), "N2=", len(rec["f_exp_node_pos"]))
+    if only is None:
+        pin = so2_pin(mods)
+        assert pin["max_abs_diff"] < 1e-5, pin
+        with open(os.path.join(HERE, "so2_pin.json"), "w") as f:
+            json.dump(pin, f, indent=1)
+        print("so2 pin", pin["max_abs_diff"])
+    makers = {"graph": graph_cases, "layer": layer_cases, "backbone": backbone_cases}
+    for prefix, make in makers.items():
+        if only is not None and prefix != only:
+            continue
+        for name, rec in make(mods).items():
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
+            print(name, "N=", len(rec["pos"]), "E=", len(rec["query_idx"]) if "query_idx" in rec else int(rec["n_edges"]))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else None)

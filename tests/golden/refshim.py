@@ -162,6 +162,14 @@ class Irreps(tuple):
                 out.append((mul, ir))
         return Irreps(out)
 
+    def __contains__(self, ir):
+        """``Irrep in Irreps`` (e3nn semantics: some block carries that irrep)."""
+        try:
+            ir = Irrep(ir)
+        except (ValueError, KeyError, TypeError):
+            return tuple.__contains__(self, ir)
+        return any(m.ir == ir for m in self)
+
     def __repr__(self):
         return "+".join(repr(m) for m in self)
 
