@@ -96,3 +96,24 @@ def test_gemm_general_kernel_matches_pipelined_kernel(M, N, K):
     err32 = ((a @ b.t()).double() - ref).abs().max().item() / scale
     for out in (out_ws, out_gen):
         assert (out.double() - ref).abs().max().item() / scale < 4 * err32 + 2e-6
+
+
+def test_pair_product_recompute_matches_saved():
+    """so3_pair_product with the projections formed again in the backward gives the same gradient
+    as keeping them (same GEMMs, same values)."""
+    from ubio_molfm_b200.linear import so3_pair_product
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    N, C, h = 300, 64, 48
+    x = torch.randn(N, 9, C, device="cuda", generator=g, requires_grad=True)
+    w1 = torch.randn(3, h, C, device="cuda", generator=g) / 8
+    w2 = torch.randn(3, h, C, device="cuda", generator=g) / 8
+    b = torch.randn(h, device="cuda", generator=g)
+    lidx = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+    G = torch.randn(N, 3, h, device="cuda", generator=g)
+    p0 = so3_pair_product(x, w1, w2, b, lidx)
+    (d0,) = torch.autograd.grad(p0, x, G)
+    p1 = so3_pair_product(x, w1, w2, b, lidx, recompute=True)
+    (d1,) = torch.autograd.grad(p1, x, G)
+    assert torch.equal(p0, p1)
+    assert torch.equal(d0, d1)

@@ -212,10 +212,26 @@ def ln_silu(h, ln, tables=None):
 class _SO3PairProdFn(torch.autograd.Function):
     """``P[n, l, j] = sum_{m in degree l} o1[n,m,j] * o2[n,m,j]`` with ``o1 = x W1[l]^T (+b on m=0)``,
     ``o2 = x W2[l]^T`` (the inner product of SO3_Linear2Scalar_e2former), fused into the GEMM
-    epilogue.  ``w12`` [L+1, 2h, C] holds W1 / W2 rows interleaved; ``b12`` [2h] the bias (0 on odd)."""
+    epilogue.  ``w12`` [L+1, 2h, C] holds W1 / W2 rows interleaved; ``b12`` [2h] the bias (0 on odd).
+    With ``recompute`` the projections O are not kept for the backward (they are 4h floats per row,
+    the largest per-node activation of the layer) but formed again there from ``x`` by the same GEMMs,
+    so the backward sees the same values."""
 
     @staticmethod
-    def forward(ctx, x, w12, b12, lidx):
+    def _project(lib, x, whi, wlo, b12, lidx, O, P=None):
+        N, R, C = x.shape
+        L1, h2 = whi.shape[0], whi.shape[1]
+        dev = x.device
+        for m in range(R):
+            l = lidx[m]
+            first = m == l * l
+            _gemm_ptrs(lib, x[:, m, :].data_ptr(), R * C, ptr(whi[l]), ptr(wlo[l]) if wlo is not None else None, C,
+                       ptr(O[:, m, :]), R * h2, ptr(b12) if m == 0 else None, N, h2, C,
+                       P is not None and not first, PASSES, dev,
+                       P=ptr(P[:, l, :]) if P is not None else None, ldp=L1 * (h2 // 2))
+
+    @staticmethod
+    def forward(ctx, x, w12, b12, lidx, recompute=False):
         lib = _lib.load()
         x = x.contiguous()
         N, R, C = x.shape
@@ -225,20 +241,27 @@ class _SO3PairProdFn(torch.autograd.Function):
         O = torch.empty((N, R, h2), device=dev, dtype=torch.float32)
         P = torch.empty((N, L1, h), device=dev, dtype=torch.float32)
         whi, wlo = split_tf32(w12) if _presplit_ok(x.data_ptr(), R * C, C) else (w12, None)
-        for m in range(R):
-            l = lidx[m]
-            first = m == l * l
-            _gemm_ptrs(lib, x[:, m, :].data_ptr(), R * C, ptr(whi[l]), ptr(wlo[l]) if wlo is not None else None, C,
-                       ptr(O[:, m, :]), R * h2,
-                       ptr(b12) if m == 0 else None, N, h2, C, not first, PASSES, dev, P=ptr(P[:, l, :]), ldp=L1 * h)
-        ctx.save_for_backward(O, w12)
+        _SO3PairProdFn._project(lib, x, whi, wlo, b12, lidx, O, P)
+        if recompute:
+            del O
+            ctx.save_for_backward(x, w12, b12)
+        else:
+            ctx.save_for_backward(O, w12, b12)
+        ctx.recompute = recompute
         ctx.lidx = lidx
         return P
 
     @staticmethod
     def backward(ctx, G):
         lib = _lib.load()
-        O, w12 = ctx.saved_tensors
+        t0, w12, b12 = ctx.saved_tensors
+        if ctx.recompute:
+            x = t0
+            O = torch.empty((x.shape[0], x.shape[1], w12.shape[1]), device=x.device, dtype=torch.float32)
+            whi, wlo = split_tf32(w12) if _presplit_ok(x.data_ptr(), x.shape[1] * x.shape[2], x.shape[2]) else (w12, None)
+            _SO3PairProdFn._project(lib, x, whi, wlo, b12, ctx.lidx, O)
+        else:
+            O = t0
         G = G.contiguous()
         N, R, h2 = O.shape
         L1 = w12.shape[0]
@@ -250,17 +273,17 @@ class _SO3PairProdFn(torch.autograd.Function):
         dx = torch.empty((N, R, C), device=O.device, dtype=torch.float32)
         for m in range(R):
             gemm(D[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :], b_split=(thi[ctx.lidx[m]], tlo[ctx.lidx[m]]))
-        return dx, None, None, None
+        return dx, None, None, None, None
 
 
-def so3_pair_product(x, w1, w2, bias, lidx):
+def so3_pair_product(x, w1, w2, bias, lidx, recompute=False):
     """Fused per-degree inner product of two per-degree linears (constant weights)."""
     if not x.is_cuda:
         raise ValueError("ubio_molfm_b200 kernels need CUDA tensors (there is no CPU path)")
     L1, h, C = w1.shape
     w12 = torch.stack([w1, w2], dim=2).reshape(L1, 2 * h, C).contiguous()
     b12 = torch.stack([bias.reshape(-1), torch.zeros_like(bias.reshape(-1))], dim=1).reshape(2 * h).contiguous()
-    return _SO3PairProdFn.apply(x.float(), w12, b12, tuple(int(v) for v in lidx))
+    return _SO3PairProdFn.apply(x.float(), w12, b12, tuple(int(v) for v in lidx), bool(recompute))
 
 
 class _NodeApplyFn(torch.autograd.Function):
@@ -285,6 +308,7 @@ class _NodeApplyFn(torch.autograd.Function):
             out = torch.empty((n, KO, C), device=dev, dtype=torch.float32)
             check(lib.e2a_node_apply_fwd(ptr(A), ptr(src), h.stride(0), ptr(sub), h.stride(0), n, KO, KI, C, ptr(out),
                                          out.stride(0), 0, stream_of(dev)), "e2a_node_apply_fwd")
+            h = src.contiguous()   # the backward reads only the value rows; keep [n, 9, C], not all 29
         else:
             rows = KO + KI if mode == "merge" else KO
             out = torch.empty((n, rows, C), device=dev, dtype=torch.float32)
@@ -305,7 +329,7 @@ class _NodeApplyFn(torch.autograd.Function):
         dA = torch.empty_like(A) if ctx.needs_input_grad[0] else None
         if ctx.mode == "sub":
             dx = torch.empty((n, KO + KI, C), device=dev, dtype=torch.float32)
-            check(lib.e2a_node_apply_bwd(ptr(A), ptr(h[:, KO:]), h.stride(0), ptr(g), g.stride(0), None, 0, n, KO, KI,
+            check(lib.e2a_node_apply_bwd(ptr(A), ptr(h), h.stride(0), ptr(g), g.stride(0), None, 0, n, KO, KI,
                                          C, ptr(dx[:, KO:]), dx.stride(0), ptr(dx), dx.stride(0), ptr(dA),
                                          stream_of(dev)), "e2a_node_apply_bwd")
             return dA, dx, None

@@ -331,10 +331,15 @@ class E2FormerPotential(nn.Module):
     ``(energy [B], forces [N,3])``.  Periodic systems are one per call; non-periodic molecules may be
     batched (``batch`` sorted, systems do not see each other)."""
 
-    def __init__(self, **backbone_kwargs):
+    def __init__(self, memory_saving=True, **backbone_kwargs):
         super().__init__()
         self.decoder = E2former(**backbone_kwargs)
         self.energy_head = MLP_energy_head(self.decoder.scalar_dim, self.decoder.lmax)
+        # large systems: the Q / K projections are formed again in the backward (saves 2 x 4 x hidden
+        # floats per irreps row per layer; ~29 GB at 1e5 atoms with the full-size model)
+        for blk in self.decoder.blocks:
+            blk.ga.query_linear.recompute_pair_product = memory_saving
+            blk.ga.key_linear.recompute_pair_product = memory_saving
 
     def build_graph(self, pos, cell, pbc, batch):
         dec = self.decoder

@@ -111,6 +111,9 @@ class SO3_Linear2Scalar_e2former(nn.Module):
         self.register_buffer("expand_index", expand_index)
         self.final_linear = nn.Sequential(
             nn.Linear(hidden * (lmax + 1), hidden), nn.LayerNorm(hidden), nn.SiLU(), nn.Linear(hidden, out_features))
+        # inference memory mode: form the per-degree projections again in the backward instead of
+        # keeping them (4 x hidden floats per irreps row)
+        self.recompute_pair_product = False
 
     def forward(self, x):
         shape = x.shape[:-2]
@@ -118,7 +121,7 @@ class SO3_Linear2Scalar_e2former(nn.Module):
         if x.is_cuda and not self.training:
             # both projections and the inner product over m in one tensor-core GEMM per row
             h = tc.so3_pair_product(x, self.weight.detach(), self.weight2.detach(), self.bias.detach(),
-                                    _degree_of_rows(self.lmax)[: x.shape[1]])
+                                    _degree_of_rows(self.lmax)[: x.shape[1]], recompute=self.recompute_pair_product)
             h = h.reshape(x.shape[0], -1)
             fl = self.final_linear
             cwt = not self.training

@@ -133,6 +133,46 @@ def bio_box(n_atoms=1500, density=1.0, dmin=0.9, seed=0,
     return pos, Z, np.eye(3) * side
 
 
+def blob_in_water(box=100.0, n_blob=8000, blob_density=1.35, water_density=1.0, dmin=0.9, jitter=0.3, seed=0,
+                  fractions=((1, 0.50), (6, 0.30), (7, 0.08), (16, 0.01), (8, 0.11))):
+    """Large periodic system: a spherical H/C/N/O/S blob of ``n_blob`` atoms at ``blob_density``
+    (g/cm^3, min distance ``dmin``) in the centre of a cubic box of rigid water at ``water_density``
+    (molecules on a jittered lattice with random orientations; molecules whose oxygen lies within the
+    blob radius + 1.5 A are left out).  About 1e5 atoms at the defaults."""
+    rng = _rng(seed)
+    els = np.array([e for e, _ in fractions])
+    fr = np.array([f for _, f in fractions])
+    counts = np.floor(fr / fr.sum() * n_blob).astype(int)
+    counts[0] += n_blob - counts.sum()
+    Zb = np.repeat(els, counts)
+    rng.shuffle(Zb)
+    mass_g = sum(MASS[int(z)] for z in Zb) / AVOGADRO
+    radius = (3.0 * mass_g / blob_density * 1e24 / (4.0 * math.pi)) ** (1.0 / 3.0)
+    side = 2.0 * radius
+    centre = np.full(3, side / 2.0)
+    pb = _poisson_fill(rng, n_blob, side, dmin, inside=lambda p: np.linalg.norm(p - centre) <= radius)
+    pb = pb - centre + box / 2.0
+    # water lattice at the requested density
+    mol_mass_g = (MASS[8] + 2 * MASS[1]) / AVOGADRO
+    spacing = (mol_mass_g / water_density * 1e24) ** (1.0 / 3.0)
+    n_side = max(1, int(round(box / spacing)))
+    g = (np.arange(n_side) + 0.5) * (box / n_side)
+    centres = np.stack(np.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3)
+    centres = centres + rng.uniform(-jitter, jitter, size=centres.shape)
+    keep = np.linalg.norm(centres - box / 2.0, axis=1) > radius + 1.5
+    centres = centres[keep]
+    th = math.radians(104.52) / 2
+    r = 0.9572
+    local = np.array([[0.0, 0.0, 0.0], [r * math.sin(th), r * math.cos(th), 0.0],
+                      [-r * math.sin(th), r * math.cos(th), 0.0]])
+    rot = random_rotations(rng, len(centres))
+    pw = (centres[:, None, :] + np.einsum("nij,aj->nai", rot, local)).reshape(-1, 3)
+    Zw = np.tile(np.array([8, 1, 1]), len(centres))
+    pos = np.mod(np.concatenate([pb, pw], axis=0), box)
+    Z = np.concatenate([Zb, Zw])
+    return pos, Z, np.eye(3) * box
+
+
 def molecule_batch(n_mol, min_atoms=10, max_atoms=60, seed=0,
                    elements=(1, 6, 7, 8, 9, 16, 17)):
     """Non-periodic random-tree conformers: bonds 1.0-1.6 A with +-0.05 A noise, seeded.
