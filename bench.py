@@ -1,24 +1,25 @@
-"""Benchmark of the E2Former-V2 sparse equivariant attention layer on B200.
+"""Benchmark of the E2Former-V2 energy + forces evaluation on B200 (the path's headline metric).
 
-Workload (the attention-layer microbenchmark): one ``E2AttentionArbOrder_sparse`` forward + the
-first-order backward autograd runs for forces, at the full layer size (node irreps
-256x0e+256x1e+256x2e, 128 heads, 8 scalar dims, head irreps 2x0e+2x1e+2x2e, 256 RBF), fp32, on a
-periodic box of seeded uniform positions (default 1e5 atoms, ~32 neighbours within 6 A).  Weights are
-seeded random (no checkpoint).  Metric: atom-steps/s = atoms x steps / device seconds.
+Default workload (``--workload model``): the full-size random-init E2Former-V2 backbone (4 layers,
+node irreps 256x0e+256x1e+256x2e, 128 heads, 8 scalar dims, head irreps 2x0e+2x1e+2x2e, 256 RBF,
+cutoff 6 A, at most 32 neighbours) on a ~1e5-atom periodic system (a seeded 8,000-atom H/C/N/O/S
+blob in rigid water, 100 A cube).  One step = one energy + forces evaluation as the MD / ASE
+interfaces call it: CUDA PBC images, radius graph and CSR, Wigner matrices, the backbone, the
+energy head and forces = -dE/dpos by autograd.  fp32 throughout (3xTF32 tensor-core GEMMs).
+Metric: atom-steps/s = atoms x steps / device seconds.  ``--workload layer`` is the isolated
+attention-layer microbenchmark (one layer forward + backward on a uniform box).
 
-* ``value``: inputs resident in HBM (graph, Wigner matrices, RBF built once), CUDA events around
-  exactly K steps, barrier + synchronize on both sides, max over ranks.  All inputs are larger than L2.
-* ``e2e``: the same step through the public API from pinned HOST buffers each step: copy positions,
-  atomic numbers, node features and the output cotangent to the device, build the periodic images,
-  radius graph, CSR metadata, Wigner matrices and RBF, run the layer forward + backward, and copy the
-  output, d(features) and d(positions) back.
-* ``roofline``: the dominant kernel of this package, timed with CUDA events on its launch stream
-  inside the timed region, against its compulsory (algorithmic) bytes.
+* ``value``: positions resident in HBM, CUDA events around exactly K steps, barrier + synchronize
+  on both sides, max over ranks.  All inputs are larger than L2.
+* ``e2e``: the same step through the public API (``E2FormerPotential.forward``) from pinned HOST
+  buffers each step: H2D of positions and atomic numbers, D2H of energy and forces.
+* ``roofline``: the dominant attention kernel entry point of this package, timed with CUDA events on
+  its launch stream inside the timed region, against its compulsory (algorithmic) bytes.
 * ``cpu_baseline``: the CPU oracle (the reference algorithm restated) on a bounded sample.
 
-Multi-GPU: ``--gpus N`` under torchrun runs one independent replica per rank (the layer has no
-exchange step), ``scaling: weak``.  ``--impl reference`` times the CPU restatement of the reference
-path (the reference itself is pure Python and is not installed on the GPU box).
+Multi-GPU: ``--gpus N`` under torchrun runs one independent system per rank (``scaling: weak``).
+``--impl reference`` times the CPU restatement of the reference path (the reference itself is pure
+Python and is not installed on the GPU box).
 """
 from __future__ import annotations
 
@@ -48,9 +49,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--atoms", type=int, default=100_000)
+    ap.add_argument("--workload", default="model", choices=["model", "layer"])
+    ap.add_argument("--atoms", type=int, default=100_000, help="layer workload: atoms")
     ap.add_argument("--k", type=int, default=32)
-    ap.add_argument("--cpu-atoms", type=int, default=1500, help="CPU baseline sample size")
+    ap.add_argument("--cpu-atoms", type=int, default=None,
+                    help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -203,6 +206,9 @@ def bwdk_algorithmic_bytes(N, N2, E):
 # one ncu capture of the default workload (1e5 atoms, k = 32); summary in profiles/attn_kernels_dram_100k.txt.
 MEASURED_TRAFFIC_DEFAULT = {"e2a_attn_fwd": 20.52e9, "e2a_attn_bwd_value": 16.78e9,
                             "e2a_attn_bwd_softmax": 25.52e9, "e2a_attn_bwd_dk": 2.74e9}
+# the same per-launch figures for the default model workload (blob in water, 97,862 atoms); filled from
+# one ncu capture of that workload (profiles/model_100k_launches.md), empty until captured
+MEASURED_TRAFFIC_MODEL = {}
 
 
 def bwdv_algorithmic_bytes(N, N2, E):
@@ -299,13 +305,14 @@ def _cpu_model():
 def run_reference(args, ws, rank):
     if rank != 0:
         return
-    cb = run_cpu_baseline(args.cpu_atoms, args.k, args.steps, min(args.warmup, 1))
+    n = args.cpu_atoms or 1500
+    cb = run_cpu_baseline(n, args.k, args.steps, min(args.warmup, 1))
     v = cb["value"]
     line = {"impl": "reference", "metric": "atom-steps/s", "value": v, "unit": "atom-steps/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.cpu_atoms / v,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * n / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded uniform periodic box, seeded random weights)",
-            "config": config_dict(args, extra={"reference_sample_atoms": args.cpu_atoms}),
+            "config": config_dict(args, extra={"reference_sample_atoms": n}),
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -428,7 +435,7 @@ def run_ours(args, ws, rank, local):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = run_cpu_baseline(args.cpu_atoms, args.k, 1, 0)
+        cpu = run_cpu_baseline(args.cpu_atoms or 1500, args.k, 1, 0)
 
     if rank == 0:
         line = {"metric": "atom-steps/s", "value": round(value, 1), "unit": "atom-steps/s", "n_gpus": ws,
@@ -440,10 +447,212 @@ def run_ours(args, ws, rank, local):
         print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------
+# Full energy + forces workload
+# ------------------------------------------------------------------------------------------------
+MODEL_CFG = dict(irreps_node_embedding=f"{C_CH}x0e+{C_CH}x1e+{C_CH}x2e", num_layers=4, max_neighbors=32,
+                 max_radius=CUTOFF, number_of_basis=NB, num_attn_heads=HEADS, attn_scalar_head=DHEAD,
+                 irreps_head=HEAD_IRREPS, norm_layer="rms_norm_sh", alpha_drop=0.0, avg_degree=23.01)
+
+
+def model_config_dict(args, N=None, E=None, N2=None, extra=None):
+    d = {"workload": "E2Former-V2 energy+forces (full-size backbone, 4 layers) on a ~1e5-atom periodic "
+                     "system: 8,000-atom H/C/N/O/S blob in rigid water, 100 A cube, cutoff 6 A, <= 32 neighbours",
+         "layers": 4, "irreps": MODEL_CFG["irreps_node_embedding"], "heads": HEADS, "attn_scalar_head": DHEAD,
+         "irreps_head": HEAD_IRREPS, "rbf": NB, "cutoff": CUTOFF, "max_neighbors": 32,
+         "l2": "inputs larger than L2 (value rows alone are GBs per layer)", "parallelism": f"replicas x{args.gpus}",
+         "graph": "rebuilt every step (PBC images, radius graph, CSR)"}
+    if N is not None:
+        d.update({"atoms_per_rank": N, "edges_per_rank": E, "expanded_nodes_per_rank": N2})
+    if extra:
+        d.update(extra)
+    return d
+
+
+def make_model(dev, seed=0):
+    from ubio_molfm_b200.model import E2FormerPotential
+    from ubio_molfm_b200.synthetic import seeded_params_
+
+    m = E2FormerPotential(**MODEL_CFG)
+    seeded_params_(m, seed)
+    return m.to(dev).eval()
+
+
+def cpu_model_setup(n_atoms):
+    """The CPU oracle of the full energy + forces evaluation on a bounded sample (an ``n_atoms``
+    biomolecular box at the model's cutoff and neighbour cap); returns a closure and a description."""
+    from oracle import graph_ref
+    from oracle import model_ref as M
+    from ubio_molfm_b200.graph import pbc_image_offsets
+    from ubio_molfm_b200.synthetic import bio_box
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    m = make_model("cpu")
+    p = {k: v.detach() for k, v in m.decoder.state_dict().items()}
+    ph = {k: v.detach() for k, v in m.energy_head.state_dict().items()}
+    pos, Z, cell = bio_box(n_atoms, seed=3)
+    pos = pos.astype(np.float32)
+    off = pbc_image_offsets(cell, [True] * 3, CUTOFF).numpy()
+    ia = graph_ref.pbc_expand(pos, off, CUTOFF)
+    oc, offs = ia % n_atoms, off[ia // n_atoms]
+    exp = (pos[oc] + offs).astype(np.float32)
+    qi, ni, _ = graph_ref.radius_graph(pos, exp, [0, n_atoms], [0, len(exp)], CUTOFF, 1e-4, 32)
+    graph = (torch.tensor(qi), torch.tensor(ni), torch.tensor(oc), torch.tensor(offs), True)
+    pos_t, Z_t = torch.tensor(pos), torch.tensor(Z)
+
+    def run():
+        M.energy_forces(p, ph, MODEL_CFG, pos_t, Z_t, graph)
+
+    desc = (f"{n_atoms}-atom biomolecular box, {len(qi)} edges: energy+forces of the full-size model by the "
+            f"CPU oracle (the reference's pure-PyTorch path restated), fp32")
+    return run, desc
+
+
+def run_cpu_model(n_atoms, steps=1, warmup=0):
+    run, desc = cpu_model_setup(n_atoms)
+    for _ in range(warmup):
+        run()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{desc}; median of {steps} steps, {t:.2f} s/step", "cpu_model": _cpu_model()}
+
+
+def run_reference_model(args, ws, rank):
+    if rank != 0:
+        return
+    n = args.cpu_atoms or 500
+    cb = run_cpu_model(n, args.steps, min(args.warmup, 1))
+    v = cb["value"]
+    line = {"impl": "reference", "metric": "atom-steps/s", "value": v, "unit": "atom-steps/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * n / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded periodic systems, seeded random weights)",
+            "config": model_config_dict(args, extra={"reference_sample_atoms": n}), "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_model(args, ws, rank, local):
+    from ubio_molfm_b200 import _lib, ops
+    from ubio_molfm_b200.synthetic import blob_in_water
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    model = make_model(dev)
+    pos_np, Z_np, cell_np = blob_in_water(seed=100 + rank)
+    pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
+    Z = torch.tensor(Z_np, device=dev)
+    cell = torch.tensor(cell_np, dtype=torch.float32)
+    pbc = (True, True, True)
+    N = pos.shape[0]
+    g, _ = model.build_graph(pos, cell, pbc, None)
+    E, N2 = g["query_idx"].numel(), g["f_exp_node_pos"].shape[0]
+    del g
+
+    def step():
+        return model(pos, Z, cell, pbc)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    ops.TIMER.enabled = True
+    ops.TIMER.events = {}
+    launches0 = _lib.launch_count()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    ops.TIMER.enabled = False
+    launches_timed = _lib.launch_count() - launches0
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, ws, dev)
+    kern = ops.TIMER.summary()
+    name, (nl, tot) = max(kern.items(), key=lambda kv: kv[1][1])
+    alg = {"e2a_attn_fwd": fwd_algorithmic_bytes, "e2a_attn_bwd_query": bwdq_algorithmic_bytes,
+           "e2a_attn_bwd_key": bwdk_algorithmic_bytes, "e2a_attn_bwd_value": bwdv_algorithmic_bytes,
+           "e2a_attn_bwd_softmax": bwds_algorithmic_bytes, "e2a_attn_bwd_dk": bwddk_algorithmic_bytes}[name](N, N2, E)
+    per_launch_ms = tot / nl
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (per_launch_ms * 1e-3) / 1e9
+    roof = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+            "traffic": MEASURED_TRAFFIC_MODEL.get(name),
+            "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
+            "kernels_ms_per_launch": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
+            "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
+    value = ws * N * 1e3 / ms
+
+    e2e = None
+    if not args.no_e2e:
+        h_pos = torch.tensor(pos_np, dtype=torch.float32).pin_memory()
+        h_Z = torch.tensor(Z_np).pin_memory()
+        h_e = torch.empty(1, dtype=torch.float32).pin_memory()
+        h_f = torch.empty((N, 3), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            p = h_pos.to(dev, non_blocking=True)
+            z = h_Z.to(dev, non_blocking=True)
+            e, f = model(p, z, cell, pbc)
+            h_e.copy_(e, non_blocking=True)
+            h_f.copy_(f, non_blocking=True)
+
+        for _ in range(max(1, min(args.warmup, 2))):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        ems = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
+        e2e = {"value": ws * N * 1e3 / ems, "unit": "atom-steps/s",
+               "h2d_bytes_per_step": h_pos.numel() * 4 + h_Z.numel() * 8,
+               "d2h_bytes_per_step": h_e.numel() * 4 + h_f.numel() * 4, "ms_per_step": round(ems, 3),
+               "includes": "H2D positions + atomic numbers, PBC images, radius graph + CSR, Wigner, backbone, "
+                           "energy head, forces, D2H energy + forces"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = run_cpu_model(args.cpu_atoms or 500, 1, 0)
+
+    if rank == 0:
+        line = {"metric": "atom-steps/s", "value": round(value, 1), "unit": "atom-steps/s", "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded blob-in-water periodic system, seeded random weights)",
+                "config": model_config_dict(args, N, E, N2), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches_timed, "clocks": clk}
+        print(json.dumps(line))
+
+
 def main():
     args = parse()
     ws, rank, local = dist_init(args)
-    if args.impl == "reference":
+    if args.workload == "model":
+        if args.impl == "reference":
+            run_reference_model(args, ws, rank)
+        else:
+            run_model(args, ws, rank, local)
+    elif args.impl == "reference":
         run_reference(args, ws, rank)
     else:
         run_ours(args, ws, rank, local)
