@@ -273,6 +273,24 @@ int e2a_attn_bwd_query_noalloc(const float* q, const float* k, const float* valu
                                int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
                                void* stream);
 
+/* ------------------------------------------------------------------------------------------ */
+/* Node-wise irreps kernels of the transformer block (one warp per node; rows = (lmax+1)^2).    */
+/* Equivariant RMS norm, EquivariantRMSNormArraySphericalHarmonicsV2_BL (module_utils.py:      */
+/* 1720-1772): f = x with row 0 centred over channels, rstd = (sum_r bw_r mean_c f^2 + eps)^-1/2 */
+/* (bw_r = 1/((2l+1)(lmax+1))), y = f rstd w[l(r)] (+ b on row 0); stats [n, 2] = (mean0, rstd). */
+/* C % 128 == 0, C <= 256, 16-byte-aligned rows, else E2A_ERR_UNSUPPORTED.                     */
+int e2a_rms_norm_fwd(const float* x, int64_t n_nodes, int rows, int C, const float* weight, const float* bias,
+                     float eps, float* y, float* stats, void* stream);
+int e2a_rms_norm_bwd(const float* x, const float* dy, int64_t n_nodes, int rows, int C, const float* weight,
+                     const float* stats, float* dx, void* stream);
+/* Gate_s3 (module_utils.py:2694-2745): y[0] = cs silu(s[0]), y[r] = cv sigmoid(s[l(r)]) h[r] for  */
+/* r >= 1; s [n, 3, C] is the gate linear of row 0, h / y [n, 9, C].  Backward gives ds and dh   */
+/* (dh row 0 = 0).                                                                                 */
+int e2a_gate_fwd(const float* s, const float* h, int64_t n_nodes, int rows, int C, float c_scalar, float c_vector,
+                 float* y, void* stream);
+int e2a_gate_bwd(const float* s, const float* h, const float* dy, int64_t n_nodes, int rows, int C, float c_scalar,
+                 float c_vector, float* ds, float* dh, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,293 @@
+// Node-wise irreps kernels of the E2Former-V2 block: the equivariant RMS norm and the gated
+// activation of the feed-forward network, forward and backward, one warp per node with float4
+// lanes over the channels (memory bound: each node's [R, C] rows are read and written once).
+//
+//  * e2a_rms_norm_fwd / _bwd -- EquivariantRMSNormArraySphericalHarmonicsV2_BL (module_utils.py:
+//    1720-1772; component normalisation, degree-balanced, centred, affine):
+//      f = x with the l=0 row centred over channels,
+//      rstd = (sum_r bw_r mean_c f[r,c]^2 + eps)^-1/2,  bw_r = 1 / ((2 l(r) + 1)(lmax + 1)),
+//      y[r,c] = f[r,c] rstd w[l(r),c]  (+ b[c] on r = 0).
+//  * e2a_gate_fwd / _bwd -- Gate_s3 (module_utils.py:2694-2745):
+//      y[0,c] = cs silu(s[c]),  y[r,c] = cv sigmoid(s[l(r) C + c]) h[r,c]  (r >= 1),
+//    s = the gate linear of the l=0 row, [lmax+1, C] per node; cs, cv the normalising constants.
+#include "e2a_common.cuh"
+
+namespace {
+
+constexpr int kNodeThreads = 256;
+constexpr int kMaxRows = 9;       // lmax <= 2
+
+__device__ __forceinline__ int degree_of_row(int r) { return r == 0 ? 0 : (r < 4 ? 1 : 2); }
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// CPR = float4 groups per lane per row (C = 128 * CPR)
+template <int CPR>
+__global__ void __launch_bounds__(kNodeThreads)
+k_rms_norm_fwd(const float* __restrict__ x, int64_t n, int R, int lmax, const float* __restrict__ w,
+               const float* __restrict__ b, float eps, float* __restrict__ y, float* __restrict__ stats) {
+  constexpr int C = 128 * CPR;
+  const int lane = threadIdx.x & 31;
+  const int64_t node = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (node >= n) return;
+  const float* xn = x + node * R * C;
+  float4 v[kMaxRows][CPR];
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r)
+    if (r < R)
+#pragma unroll
+      for (int j = 0; j < CPR; ++j) v[r][j] = ld4(xn + r * C + 4 * (lane + 32 * j));
+  float s0 = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPR; ++j) s0 += (v[0][j].x + v[0][j].y) + (v[0][j].z + v[0][j].w);
+  const float mean0 = e2a_warp_sum(s0) / C;
+#pragma unroll
+  for (int j = 0; j < CPR; ++j) {
+    v[0][j].x -= mean0; v[0][j].y -= mean0; v[0][j].z -= mean0; v[0][j].w -= mean0;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r >= R) continue;
+    const float bw = 1.f / ((2 * degree_of_row(r) + 1) * (lmax + 1));
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPR; ++j)
+      q += (v[r][j].x * v[r][j].x + v[r][j].y * v[r][j].y) + (v[r][j].z * v[r][j].z + v[r][j].w * v[r][j].w);
+    ss += bw * q;
+  }
+  const float rstd = rsqrtf(e2a_warp_sum(ss) / C + eps);
+  float* yn = y + node * R * C;
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r >= R) continue;
+    const float* wl = w + degree_of_row(r) * C;
+#pragma unroll
+    for (int j = 0; j < CPR; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      const float4 ww = ld4(wl + c);
+      float4 o = make_float4(v[r][j].x * rstd * ww.x, v[r][j].y * rstd * ww.y, v[r][j].z * rstd * ww.z,
+                             v[r][j].w * rstd * ww.w);
+      if (r == 0) {
+        const float4 bb = ld4(b + c);
+        o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+      }
+      st4(yn + r * C + c, o);
+    }
+  }
+  if (lane == 0) {
+    stats[2 * node] = mean0;
+    stats[2 * node + 1] = rstd;
+  }
+}
+
+// dx from dy: df = g w rstd - rstd^3 bw_r f S / C with S = sum g w f; the centred row subtracts its mean.
+template <int CPR>
+__global__ void __launch_bounds__(kNodeThreads)
+k_rms_norm_bwd(const float* __restrict__ x, const float* __restrict__ dy, int64_t n, int R, int lmax,
+               const float* __restrict__ w, const float* __restrict__ stats, float* __restrict__ dx) {
+  constexpr int C = 128 * CPR;
+  const int lane = threadIdx.x & 31;
+  const int64_t node = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (node >= n) return;
+  const float mean0 = stats[2 * node], rstd = stats[2 * node + 1];
+  const float* xn = x + node * R * C;
+  const float* gn = dy + node * R * C;
+  float4 f[kMaxRows][CPR], gw[kMaxRows][CPR];
+  float S = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r >= R) continue;
+    const float* wl = w + degree_of_row(r) * C;
+#pragma unroll
+    for (int j = 0; j < CPR; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      float4 xv = ld4(xn + r * C + c);
+      if (r == 0) { xv.x -= mean0; xv.y -= mean0; xv.z -= mean0; xv.w -= mean0; }
+      const float4 g = ld4(gn + r * C + c), ww = ld4(wl + c);
+      f[r][j] = xv;
+      gw[r][j] = make_float4(g.x * ww.x, g.y * ww.y, g.z * ww.z, g.w * ww.w);
+      S += (gw[r][j].x * xv.x + gw[r][j].y * xv.y) + (gw[r][j].z * xv.z + gw[r][j].w * xv.w);
+    }
+  }
+  S = e2a_warp_sum(S);
+  const float k3 = rstd * rstd * rstd * S / C;
+  float* dn = dx + node * R * C;
+  float4 d0[CPR];
+  float s0 = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r >= R) continue;
+    const float bw = 1.f / ((2 * degree_of_row(r) + 1) * (lmax + 1));
+#pragma unroll
+    for (int j = 0; j < CPR; ++j) {
+      const float4 d = make_float4(gw[r][j].x * rstd - k3 * bw * f[r][j].x, gw[r][j].y * rstd - k3 * bw * f[r][j].y,
+                                   gw[r][j].z * rstd - k3 * bw * f[r][j].z, gw[r][j].w * rstd - k3 * bw * f[r][j].w);
+      if (r == 0) {
+        d0[j] = d;
+        s0 += (d.x + d.y) + (d.z + d.w);
+      } else {
+        st4(dn + r * C + 4 * (lane + 32 * j), d);
+      }
+    }
+  }
+  const float m = e2a_warp_sum(s0) / C;
+#pragma unroll
+  for (int j = 0; j < CPR; ++j)
+    st4(dn + 4 * (lane + 32 * j), make_float4(d0[j].x - m, d0[j].y - m, d0[j].z - m, d0[j].w - m));
+}
+
+__device__ __forceinline__ float sigm(float t) { return 1.f / (1.f + expf(-t)); }
+
+// Gate forward: grid-stride over (node, float4 channel group).
+__global__ void k_gate_fwd(const float* __restrict__ s, const float* __restrict__ h, int64_t n, int R, int C,
+                           float cs, float cv, float* __restrict__ y) {
+  const int C4 = C / 4;
+  const int64_t total = n * C4;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t node = t / C4;
+    const int c = 4 * (int)(t - node * C4);
+    const float* sn = s + node * 3 * C;
+    const float* hn = h + node * R * C;
+    float* yn = y + node * R * C;
+    const float4 s0 = ld4(sn + c);
+    st4(yn + c, make_float4(cs * s0.x * sigm(s0.x), cs * s0.y * sigm(s0.y), cs * s0.z * sigm(s0.z),
+                            cs * s0.w * sigm(s0.w)));
+    for (int l = 1; l <= 2; ++l) {
+      const float4 sl = ld4(sn + l * C + c);
+      const float4 g = make_float4(cv * sigm(sl.x), cv * sigm(sl.y), cv * sigm(sl.z), cv * sigm(sl.w));
+      for (int r = l * l; r < (l + 1) * (l + 1) && r < R; ++r) {
+        const float4 hv = ld4(hn + r * C + c);
+        st4(yn + r * C + c, make_float4(g.x * hv.x, g.y * hv.y, g.z * hv.z, g.w * hv.w));
+      }
+    }
+  }
+}
+
+// Gate backward: ds and dh (dh row 0 is zero: that row reaches the output through s only).
+__global__ void k_gate_bwd(const float* __restrict__ s, const float* __restrict__ h, const float* __restrict__ dy,
+                           int64_t n, int R, int C, float cs, float cv, float* __restrict__ ds, float* __restrict__ dh) {
+  const int C4 = C / 4;
+  const int64_t total = n * C4;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t node = t / C4;
+    const int c = 4 * (int)(t - node * C4);
+    const float* sn = s + node * 3 * C;
+    const float* hn = h + node * R * C;
+    const float* gn = dy + node * R * C;
+    float* dsn = ds + node * 3 * C;
+    float* dhn = dh + node * R * C;
+    {
+      const float4 s0 = ld4(sn + c), g0 = ld4(gn + c);
+      const float sx[4] = {s0.x, s0.y, s0.z, s0.w}, gx[4] = {g0.x, g0.y, g0.z, g0.w};
+      float o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float sg = sigm(sx[u]);
+        o[u] = gx[u] * cs * sg * (1.f + sx[u] * (1.f - sg));
+      }
+      st4(dsn + c, make_float4(o[0], o[1], o[2], o[3]));
+      st4(dhn + c, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    for (int l = 1; l <= 2; ++l) {
+      const float4 sl = ld4(sn + l * C + c);
+      const float sx[4] = {sl.x, sl.y, sl.z, sl.w};
+      float sg[4], acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sg[u] = sigm(sx[u]);
+      for (int r = l * l; r < (l + 1) * (l + 1) && r < R; ++r) {
+        const float4 hv = ld4(hn + r * C + c), gv = ld4(gn + r * C + c);
+        const float hx[4] = {hv.x, hv.y, hv.z, hv.w}, gx[4] = {gv.x, gv.y, gv.z, gv.w};
+        float o[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[u] += gx[u] * hx[u];
+          o[u] = gx[u] * cv * sg[u];
+        }
+        st4(dhn + r * C + c, make_float4(o[0], o[1], o[2], o[3]));
+      }
+      float o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[u] = acc[u] * cv * sg[u] * (1.f - sg[u]);
+      st4(dsn + l * C + c, make_float4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+unsigned grid_nodes(int64_t n) {
+  const int64_t b = (n * 32 + kNodeThreads - 1) / kNodeThreads;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+unsigned grid_flat(int64_t total) {
+  const int64_t b = (total + 255) / 256;
+  return (unsigned)(b < 1 ? 1 : (b > 148 * 64 ? 148 * 64 : b));
+}
+
+}  // namespace
+
+extern "C" {
+
+int e2a_rms_norm_fwd(const float* x, int64_t n_nodes, int rows, int C, const float* weight, const float* bias,
+                     float eps, float* y, float* stats, void* stream) {
+  if (n_nodes < 0 || rows < 1 || rows > kMaxRows || (rows != 1 && rows != 4 && rows != 9)) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!x || !weight || !bias || !y || !stats) return E2A_ERR_ARG;
+  if (C % 128 || C > 256 || !aligned16(x) || !aligned16(y) || !aligned16(weight) || !aligned16(bias))
+    return E2A_ERR_UNSUPPORTED;
+  const int lmax = rows == 1 ? 0 : (rows == 4 ? 1 : 2);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (C / 128) {
+    case 1: k_rms_norm_fwd<1><<<grid_nodes(n_nodes), kNodeThreads, 0, st>>>(x, n_nodes, rows, lmax, weight, bias, eps, y, stats); break;
+    default: k_rms_norm_fwd<2><<<grid_nodes(n_nodes), kNodeThreads, 0, st>>>(x, n_nodes, rows, lmax, weight, bias, eps, y, stats); break;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_rms_norm_bwd(const float* x, const float* dy, int64_t n_nodes, int rows, int C, const float* weight,
+                     const float* stats, float* dx, void* stream) {
+  if (n_nodes < 0 || rows < 1 || rows > kMaxRows || (rows != 1 && rows != 4 && rows != 9)) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!x || !dy || !weight || !stats || !dx) return E2A_ERR_ARG;
+  if (C % 128 || C > 256 || !aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(weight))
+    return E2A_ERR_UNSUPPORTED;
+  const int lmax = rows == 1 ? 0 : (rows == 4 ? 1 : 2);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (C / 128) {
+    case 1: k_rms_norm_bwd<1><<<grid_nodes(n_nodes), kNodeThreads, 0, st>>>(x, dy, n_nodes, rows, lmax, weight, stats, dx); break;
+    default: k_rms_norm_bwd<2><<<grid_nodes(n_nodes), kNodeThreads, 0, st>>>(x, dy, n_nodes, rows, lmax, weight, stats, dx); break;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_gate_fwd(const float* s, const float* h, int64_t n_nodes, int rows, int C, float c_scalar, float c_vector,
+                 float* y, void* stream) {
+  if (n_nodes < 0 || rows != 9 || C <= 0) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!s || !h || !y) return E2A_ERR_ARG;
+  if (C % 4 || !aligned16(s) || !aligned16(h) || !aligned16(y)) return E2A_ERR_UNSUPPORTED;
+  k_gate_fwd<<<grid_flat(n_nodes * (C / 4)), 256, 0, (cudaStream_t)stream>>>(s, h, n_nodes, rows, C, c_scalar,
+                                                                            c_vector, y);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_gate_bwd(const float* s, const float* h, const float* dy, int64_t n_nodes, int rows, int C, float c_scalar,
+                 float c_vector, float* ds, float* dh, void* stream) {
+  if (n_nodes < 0 || rows != 9 || C <= 0) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!s || !h || !dy || !ds || !dh) return E2A_ERR_ARG;
+  if (C % 4 || !aligned16(s) || !aligned16(h) || !aligned16(dy) || !aligned16(ds) || !aligned16(dh))
+    return E2A_ERR_UNSUPPORTED;
+  k_gate_bwd<<<grid_flat(n_nodes * (C / 4)), 256, 0, (cudaStream_t)stream>>>(s, h, dy, n_nodes, rows, C, c_scalar,
+                                                                            c_vector, ds, dh);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // extern "C"

@@ -391,3 +391,77 @@ def rowblock_linear(x, tasks, weights, bias, out_rows):
     weights_t = [w.t().contiguous() for w in weights]
     b = bias.detach().float().contiguous() if bias is not None else None
     return _RowBlockLinearFn.apply(x.float(), tuple(tasks), weights, weights_t, b, out_rows)
+
+
+# ------------------------------------------------------------------------------------------------
+# Node-wise block kernels: equivariant RMS norm and the gated activation (inference path)
+# ------------------------------------------------------------------------------------------------
+def rms_norm_supported(x):
+    return x.is_cuda and x.dim() == 3 and x.shape[1] in (1, 4, 9) and x.shape[2] in (128, 256)
+
+
+class _RmsNormFn(torch.autograd.Function):
+    """EquivariantRMSNormArraySphericalHarmonicsV2_BL with constant affine parameters."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        lib = _lib.load()
+        x = x.contiguous()
+        n, R, C = x.shape
+        y = torch.empty_like(x)
+        stats = torch.empty((n, 2), device=x.device, dtype=torch.float32)
+        check(lib.e2a_rms_norm_fwd(ptr(x), n, R, C, ptr(w), ptr(b), float(eps), ptr(y), ptr(stats),
+                                   stream_of(x.device)), "e2a_rms_norm_fwd")
+        ctx.save_for_backward(x, w, stats)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        x, w, stats = ctx.saved_tensors
+        g = g.contiguous()
+        n, R, C = x.shape
+        dx = torch.empty_like(x)
+        check(lib.e2a_rms_norm_bwd(ptr(x), ptr(g), n, R, C, ptr(w), ptr(stats), ptr(dx), stream_of(x.device)),
+              "e2a_rms_norm_bwd")
+        return dx, None, None, None
+
+
+def rms_norm(x, weight, bias, eps):
+    """Equivariant RMS norm of [n, (lmax+1)^2, C] irreps (CUDA; constant weight [lmax+1, C], bias [C])."""
+    return _RmsNormFn.apply(x.float(), weight.detach().float().contiguous(), bias.detach().float().contiguous(),
+                            float(eps))
+
+
+class _GateFn(torch.autograd.Function):
+    """Gate_s3: y[0] = cs silu(s[0]), y[r] = cv sigmoid(s[l(r)]) h[r]."""
+
+    @staticmethod
+    def forward(ctx, s, h, cs, cv):
+        lib = _lib.load()
+        s = s.contiguous()
+        h = h.contiguous()
+        n, R, C = h.shape
+        y = torch.empty_like(h)
+        check(lib.e2a_gate_fwd(ptr(s), ptr(h), n, R, C, float(cs), float(cv), ptr(y), stream_of(h.device)),
+              "e2a_gate_fwd")
+        ctx.save_for_backward(s, h)
+        ctx.c = (float(cs), float(cv))
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        s, h = ctx.saved_tensors
+        g = g.contiguous()
+        n, R, C = h.shape
+        ds = torch.empty_like(s)
+        dh = torch.empty_like(h)
+        check(lib.e2a_gate_bwd(ptr(s), ptr(h), ptr(g), n, R, C, ctx.c[0], ctx.c[1], ptr(ds), ptr(dh),
+                               stream_of(h.device)), "e2a_gate_bwd")
+        return ds, dh, None, None
+
+
+def gate(s, h, c_scalar, c_vector):
+    """Gated activation of irreps rows ``h`` [n, 9, C] by gate pre-activations ``s`` [n, 3 C] (CUDA)."""
+    return _GateFn.apply(s.float(), h.float(), c_scalar, c_vector)

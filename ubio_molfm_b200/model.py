@@ -21,6 +21,7 @@ import numpy as np
 import torch
 from torch import nn
 
+from . import linear as tc
 from . import ops
 from .attention import E2AttentionArbOrder_sparse
 from .graph import expand_pbc, radius_graph
@@ -52,6 +53,8 @@ class EquivariantRMSNormArraySphericalHarmonicsV2_BL(nn.Module):
     def forward(self, x, batch=None):
         shape = x.shape
         f = x.reshape(-1, (self.lmax + 1) ** 2, self.num_channels)
+        if not self.training and tc.rms_norm_supported(f):
+            return tc.rms_norm(f, self.affine_weight, self.affine_bias, self.eps).reshape(shape)
         f0 = f[:, :1] - f[:, :1].mean(dim=2, keepdim=True)
         f = torch.cat([f0, f[:, 1:]], dim=1)
         ms = (f.pow(2) * self.balance_degree_weight.reshape(1, -1, 1)).sum(dim=1, keepdim=True)
@@ -104,6 +107,8 @@ class Gate_s3(nn.Module):
         x = x.reshape(-1, shape[-2], shape[-1])
         C = self.sphere_channels
         s = lin(x[:, 0], self.gates.weight, self.gates.bias, not self.training)       # [n, C (lmax+1)]
+        if x.is_cuda and not self.training and self.lmax == 2 and C % 4 == 0:
+            return tc.gate(s, x, self.c_silu, self.c_sigmoid).reshape(shape)
         out = [(torch.nn.functional.silu(s[:, :C]) * self.c_silu).unsqueeze(1)]
         start = 1
         for l in range(1, self.lmax + 1):
