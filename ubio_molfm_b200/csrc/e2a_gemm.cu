@@ -256,14 +256,14 @@ k_gemm_tf32x3(const float* __restrict__ A, int64_t lda, const float* __restrict_
 //  * warp 0 (one lane): TMA producer -- per k-slab one 2-D tensor copy each of raw fp32 A and of B
 //    (or of B_hi and B_lo when the caller pre-split the weight operand) into a stage ring, already
 //    in the swizzled K-major layout the tensor core reads;
-//  * warps 2-3 (and 8-9 for 32-wide slabs): splitters -- turn each raw slab into hi = tf32(x) (in
+//  * warps 2-3 (and 12-13 for 32-wide slabs): splitters -- turn each raw slab into hi = tf32(x) (in
 //    place) and lo = tf32(x - hi)
 //    (A only when B arrives pre-split, which measured faster: shared-memory traffic per slab is the
 //    tighter resource);
 //  * warp 1 (one lane): MMA issuer -- tcgen05.mma kind::tf32 hi*hi + hi*lo + lo*hi into one of four
 //    128-column TMEM chain buffers (a chain = 32 k, 12 MMAs), then tcgen05.commit frees the
 //    stage and, at a chain end, hands the buffer to the drain warps;
-//  * warps 4-7: drain every chain into fp32 registers with round-to-nearest adds (the tensor core's
+//  * warps 4-11: drain every chain into fp32 registers with round-to-nearest adds (the tensor core's
 //    own accumulation truncates, so chains are kept short), then run the tile's epilogue (bias /
 //    accumulate / pair product) through a per-warp staging area with coalesced row stores.
 // The roles meet only at mbarriers; there is no block-wide barrier in the loop.  Every wait is
@@ -284,8 +284,8 @@ struct WsCfg {
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
   static constexpr int STAGE = 4 * TILE;                 // A (raw, then hi in place), A_lo, B (same), B_lo
   static constexpr int NBARS = 3 * STAGES + 8;           // + 2 x WS_CHAINS
-  static constexpr int SPLIT = BK == 16 ? 64 : 128;      // splitter threads (warps 2-3, and 8-9 for BK 32)
-  static constexpr int THREADS = 256 + (SPLIT - 64);
+  static constexpr int SPLIT = BK == 16 ? 64 : 128;      // splitter threads (warps 2-3, and 12-13 for BK 32)
+  static constexpr int THREADS = 384 + (SPLIT - 64);      // + 8 drain warps (4-11)
   static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
     // K-major; LBO unused (1); SBO = 8 rows x row bytes; version 1; swizzle 64 B (4) or 128 B (2)
     return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(BK * 4 * 8 / 16) << 32) | (1ull << 46) |
@@ -293,9 +293,11 @@ struct WsCfg {
   }
 };
 constexpr int WS_CHAINS = 4;                     // TMEM chain buffers of BN columns (512 columns)
-constexpr int WS_EH = BN / 4;                    // epilogue staged in four column quarters
+constexpr int WS_DRAIN = 8;                      // drain warps: 4 TMEM lane quarters x 2 column halves
+constexpr int WS_DCOLS = BN / 2;                 // accumulator columns per drain warp
+constexpr int WS_EH = 16;                        // epilogue staged 16 columns at a time
 constexpr int WS_LD = WS_EH + 4;                 // staging row stride (floats)
-constexpr int WS_EPI = 4 * 32 * WS_LD * 4;       // four drain warps x 32 rows x one quarter
+constexpr int WS_EPI = WS_DRAIN * 32 * WS_LD * 4;
 constexpr uint32_t kWsTmemCols = WS_CHAINS * BN;
 template <int BK>
 constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024; }
@@ -387,7 +389,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     }
     for (int c = 0; c < WS_CHAINS; ++c) {
       e2a_mbar_init(&tfull[c], 1);
-      e2a_mbar_init(&tempty[c], 128);
+      e2a_mbar_init(&tempty[c], 32 * WS_DRAIN);
     }
     *abort_flag = 0;
     e2a_fence_mbar_init();
@@ -460,9 +462,9 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       if (!run && last >= 0)  // let the committed MMAs finish before the tensor memory is freed
         e2a_mbar_wait_bounded(&empty[last % Cfg::STAGES], (uint32_t)((last / Cfg::STAGES) & 1), &g_e2a_gemm_status);
     }
-  } else if (warp < 4 || warp >= 8) {
+  } else if (warp < 4 || warp >= 12) {
     // ------------------------------------------------------------------ splitters (128 threads)
-    const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 192;
+    const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 320;
     uint32_t n = 0;
     bool run = true;
     for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
@@ -492,41 +494,43 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       }
     }
   } else {
-    // ------------------------------------------------------------------ drain + epilogue (128 threads)
-    const int q = warp & 3;
+    // ------------------------------------------------------------------ drain + epilogue (8 warps)
+    const int q = warp & 3;                        // TMEM lane quarter this warp may read
+    const int half = (warp - 4) >> 2;              // column half of the tile
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    float* stg = epi + q * 32 * WS_LD;
+    float* stg = epi + (warp - 4) * 32 * WS_LD;
     uint32_t c = 0;
     bool run = true;
     const int nch = (nk + Cfg::SPC - 1) / Cfg::SPC;
     for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-      float acc[BN];
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN + WS_DCOLS * half;
+      float acc[WS_DCOLS];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) acc[i] = 0.f;
+      for (int i = 0; i < WS_DCOLS; ++i) acc[i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++c) {
         const uint32_t cb = c % WS_CHAINS;
         if (!ws_wait(&tfull[cb], (c / WS_CHAINS) & 1, abort_flag)) { run = false; break; }
         if (threadIdx.x == 128) WS_TRACE(4, c);
         tc_fence_after();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float v[64];
+        for (int h = 0; h < WS_DCOLS / 32; ++h) {
+          float v[32];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) tmem_ld16_nowait(tmem + lane_base + cb * BN + h * 64 + 16 * j, v + 16 * j);
+          for (int j = 0; j < 2; ++j)
+            tmem_ld16_nowait(tmem + lane_base + cb * BN + WS_DCOLS * half + 32 * h + 16 * j, v + 16 * j);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int i = 0; i < 64; ++i) acc[h * 64 + i] += v[i];
+          for (int i = 0; i < 32; ++i) acc[32 * h + i] += v[i];
         }
         tc_fence_before();
         mbar_arrive(&tempty[cb]);
         if (threadIdx.x == 128) WS_TRACE(5, c);
       }
       if (!run) break;
-      // epilogue: stage this warp's 32 rows one column quarter at a time, then write them row by row
-      // (lanes across columns)
+      // epilogue: stage this warp's 32 rows x 64 columns 16 columns at a time, then write them row by
+      // row (4 lanes per row, 8 rows per step)
 #pragma unroll
-      for (int hh = 0; hh < BN / WS_EH; ++hh) {
+      for (int hh = 0; hh < WS_DCOLS / WS_EH; ++hh) {
 #pragma unroll
         for (int i = 0; i < WS_EH; i += 4)
           *reinterpret_cast<float4*>(stg + lane * WS_LD + i) =
