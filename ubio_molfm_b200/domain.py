@@ -1,0 +1,160 @@
+"""Spatial domain decomposition of one periodic system over ranks, with a per-layer halo exchange.
+
+Each rank owns the atoms of one slab of the cell along its first lattice vector (fractional
+coordinate 0) and evaluates the energy of its own atoms.  Its graph has queries only for owned atoms;
+the keys are every atom (any periodic image) within the cutoff of an owned atom: owned atoms plus
+*ghosts* owned by other ranks.  Node features of the ghosts change every layer, so before every block
+the ghost rows of the residual stream are refreshed from their owners (``all_to_all`` over NCCL):
+the per-layer halo exchange.  The exchange is an autograd
+function whose backward sends the ghosts' gradients back to their owners and adds them there, so
+``E_rank.backward()`` on every rank gives exact forces on the owned atoms for the total energy
+(positions go through the same exchange).  Nothing else is communicated except the final energy sum.
+
+The result equals the single-GPU evaluation up to fp32 summation order
+(``tests/test_domain.py``; the host-side logic is tested on CPU ``gloo`` ranks).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .graph import _DistFn, expand_pbc, morton_row_order, pbc_image_offsets, radius_graph
+from .nn import polynomial
+
+
+def slab_owner(pos, cell, world):
+    """Owner rank of each atom: the slab of its fractional coordinate along the first lattice vector."""
+    cell = torch.as_tensor(cell, dtype=torch.float64, device=pos.device)
+    frac = pos.detach().to(torch.float64) @ torch.linalg.inv(cell)
+    f0 = torch.remainder(frac[:, 0], 1.0)
+    return torch.clamp((f0 * world).floor().to(torch.int64), 0, world - 1)
+
+
+class HaloPlan:
+    """Who sends which owned rows to whom.  ``local`` rows = owned atoms (ascending global id), then
+    ghosts grouped by owner rank (ascending global id within an owner)."""
+
+    def __init__(self, own_gid, ghost_gid, ghost_owner, world, rank, group=None):
+        self.world, self.rank, self.group = world, rank, group
+        self.n_own = own_gid.numel()
+        dev = own_gid.device
+        order = torch.argsort(ghost_owner * (int(ghost_gid.max()) + 1 if ghost_gid.numel() else 1) + ghost_gid)
+        self.ghost_gid = ghost_gid[order]
+        self.ghost_owner = ghost_owner[order]
+        self.recv_counts = torch.bincount(self.ghost_owner, minlength=world).cpu()
+        # requests: tell each owner how many and which of its atoms this rank needs
+        cdev = dev if dist.get_backend(group) == "nccl" else torch.device("cpu")
+        counts_out = torch.empty(world, dtype=torch.int64, device=cdev)
+        dist.all_to_all_single(counts_out, self.recv_counts.to(cdev), group=group)
+        self.send_counts = counts_out.cpu()
+        req = torch.empty(int(self.send_counts.sum()), dtype=torch.int64, device=cdev)
+        dist.all_to_all_single(req, self.ghost_gid.to(cdev).contiguous(), output_split_sizes=self.send_counts.tolist(),
+                               input_split_sizes=self.recv_counts.tolist(), group=group)
+        req = req.to(dev)
+        # requested global ids -> rows of this rank's owned block
+        pos_in_own = torch.searchsorted(own_gid, req)
+        if req.numel() and not bool((own_gid[pos_in_own.clamp(max=max(self.n_own - 1, 0))] == req).all()):
+            raise RuntimeError("halo plan: a rank requested an atom it does not own here")
+        self.send_idx = pos_in_own
+
+    def exchange(self, x_own):
+        """Rows [n_own + n_ghost, ...]: owned rows, then the ghosts' current rows from their owners."""
+        return _HaloFn.apply(x_own, self)
+
+
+class _HaloFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_own, plan):
+        send = x_own[plan.send_idx].contiguous()
+        tail = tuple(x_own.shape[1:])
+        recv = x_own.new_empty((int(plan.recv_counts.sum()),) + tail)
+        dist.all_to_all_single(recv, send, output_split_sizes=plan.recv_counts.tolist(),
+                               input_split_sizes=plan.send_counts.tolist(), group=plan.group)
+        ctx.plan = plan
+        return torch.cat([x_own, recv], dim=0)
+
+    @staticmethod
+    def backward(ctx, g):
+        plan = ctx.plan
+        g = g.contiguous()
+        g_own = g[:plan.n_own].clone()
+        g_ghost = g[plan.n_own:].contiguous()
+        back = g.new_empty((int(plan.send_counts.sum()),) + tuple(g.shape[1:]))
+        dist.all_to_all_single(back, g_ghost, output_split_sizes=plan.send_counts.tolist(),
+                               input_split_sizes=plan.recv_counts.tolist(), group=plan.group)
+        if back.shape[0]:
+            g_own.index_add_(0, plan.send_idx, back)
+        return g_own, None
+
+
+def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=None):
+    """Graph of this rank's owned atoms over the owned + ghost atoms, and the halo plan.
+
+    Returns ``(plan, own_gid, local_gid, geometry)``; ``geometry`` holds the local expanded nodes
+    (``outcell`` into local rows, image ``offsets``), the edge list (queries = owned local rows,
+    neighbours = local expanded nodes) and the kernel's bit-exact distances."""
+    dev = pos_all.device
+    owner = slab_owner(pos_all, cell, world)
+    own_gid = torch.nonzero(owner == rank).flatten()
+    n_own = own_gid.numel()
+    p = pos_all.detach().to(torch.float32)
+    exp_pos, outcell_g, image_g = expand_pbc(p, torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff)
+    g = radius_graph(p[own_gid], exp_pos, torch.tensor([0, n_own]), torch.tensor([0, exp_pos.shape[0]]), cutoff,
+                     1e-4, max_neighbors, with_key_csr=False)
+    used = torch.unique(g["neighbor_idx"])                                   # global expanded nodes (sorted)
+    atoms_needed = torch.unique(outcell_g[used])
+    is_own = torch.zeros(pos_all.shape[0], dtype=torch.bool, device=dev)
+    is_own[own_gid] = True
+    ghost_gid = atoms_needed[~is_own[atoms_needed]]
+    plan = HaloPlan(own_gid, ghost_gid, owner[ghost_gid], world, rank, group)
+    local_gid = torch.cat([own_gid, plan.ghost_gid])
+    g2l = torch.full((pos_all.shape[0],), -1, dtype=torch.int64, device=dev)
+    g2l[local_gid] = torch.arange(local_gid.numel(), device=dev)
+    e2l = torch.full((exp_pos.shape[0],), -1, dtype=torch.int64, device=dev)
+    e2l[used] = torch.arange(used.numel(), device=dev)
+    offsets = pbc_image_offsets(torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff).to(dev)
+    geometry = {
+        "outcell": g2l[outcell_g[used]],
+        "offsets": offsets[image_g[used]],
+        "query_idx": g["query_idx"],
+        "neighbor_idx": e2l[g["neighbor_idx"]],
+        "dist": g["f_dist"].detach(),
+    }
+    return plan, own_gid, local_gid, geometry
+
+
+def local_graph(pos_local, geometry, n_local, cutoff):
+    """The decoder's neighbour dict on the local rows, differentiable in ``pos_local``."""
+    outcell, qi, ni = geometry["outcell"], geometry["query_idx"], geometry["neighbor_idx"]
+    exp_pos = pos_local[outcell] + geometry["offsets"]
+    vec = pos_local[qi] - exp_pos[ni]
+    dist_ = _DistFn.apply(vec, geometry["dist"])
+    md = ops.prepare_sparse_qk_edge_index_metadata(qi, ni, n_local, exp_pos.shape[0])
+    return {
+        "query_idx": qi, "neighbor_idx": ni, "metadata": md, "f_edge_vec": vec, "f_dist": dist_,
+        "f_poly_dist": polynomial(dist_, float(cutoff)), "f_outcell_index": outcell, "f_exp_node_pos": exp_pos,
+        "row_order": morton_row_order(pos_local, max(float(cutoff), 1e-3)),
+        "key_order": morton_row_order(exp_pos, max(float(cutoff), 1e-3)), "query_sorted": True,
+    }
+
+
+def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), group=None):
+    """Energy of the whole system and forces on this rank's owned atoms under slab decomposition.
+
+    ``pos_all`` / ``Z_all``: every atom's position and type (replicated on every rank).  Returns
+    ``(energy_total [1], own_gid, forces_own [n_own, 3])``; every rank must call it (collectives)."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    dec = model.decoder
+    plan, own_gid, local_gid, geom = domain_graph(pos_all, cell, pbc, dec.max_radius, dec.max_neighbors, world,
+                                                  rank, group)
+    with torch.enable_grad():
+        pos_own = pos_all.detach()[own_gid].to(torch.float32).requires_grad_(True)
+        pos_local = plan.exchange(pos_own)
+        graph = local_graph(pos_local, geom, local_gid.numel(), dec.max_radius)
+        x = dec(pos_local, Z_all[local_gid], graph, True, halo=lambda t: plan.exchange(t[:plan.n_own]))
+        e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1).sum()
+        (grad,) = torch.autograd.grad(e_own, pos_own)
+    energy = e_own.detach().reshape(1).clone()
+    dist.all_reduce(energy, group=group)
+    return energy, own_gid, -grad

@@ -287,10 +287,12 @@ class E2former(nn.Module):
             elif rest == "edge_deg_embed_dense.sph.W":
                 del state_dict[k]
 
-    def forward(self, node_pos, atomic_numbers, graph, pbc_any):
+    def forward(self, node_pos, atomic_numbers, graph, pbc_any, halo=None):
         """``graph``: the flattened neighbour dict (``query_idx``, ``neighbor_idx``, ``metadata``,
         ``f_edge_vec``, ``f_dist``, ``f_poly_dist``, ``f_outcell_index``, ``f_exp_node_pos`` and the
-        optional ``row_order`` / ``key_order``).  Returns the node irreps [N, (lmax+1)^2, C]."""
+        optional ``row_order`` / ``key_order``).  Returns the node irreps [N, (lmax+1)^2, C].
+        ``halo`` (domain decomposition): called on the node irreps before every block to refresh the
+        rows of atoms owned by other ranks."""
         jd = [j.to(torch.float64) for j in self.Jd_list]
         W, Wi = node_wigner(node_pos, self.lmax, self.l3_sequential, dtype=node_pos.dtype, jd=jd)
         if pbc_any:
@@ -305,6 +307,8 @@ class E2former(nn.Module):
                                       atomic_numbers=atomic_numbers, edge_vec=graph["f_edge_vec"], batched_data=bd,
                                       attn_mask=None, poly_dist=graph["f_poly_dist"], edge_scalars=f_dist_embedding)
         for blk in self.blocks:
+            if halo is not None:
+                x = halo(x)
             x, f_dist_embedding = blk(node_pos=node_pos, node_irreps=x, sys_node_embedding=None,
                                       edge_dis=graph["f_dist"], edge_vec=graph["f_edge_vec"],
                                       attn_weight=f_dist_embedding, atomic_numbers=atomic_numbers, attn_mask=None,
