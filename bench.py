@@ -17,7 +17,9 @@ attention-layer microbenchmark (one layer forward + backward on a uniform box).
   its launch stream inside the timed region, against its compulsory (algorithmic) bytes.
 * ``cpu_baseline``: the CPU oracle (the reference algorithm restated) on a bounded sample.
 
-Multi-GPU: ``--gpus N`` under torchrun runs one independent system per rank (``scaling: weak``).
+Multi-GPU: ``--gpus N`` under torchrun splits the one ~1e5-atom system into N slabs (spatial domain
+decomposition with a per-layer halo exchange of boundary-atom features over NCCL; ``scaling:
+strong``); ``--replicas`` (and the layer workload) runs one independent system per rank (``weak``).
 ``--impl reference`` times the CPU restatement of the reference path (the reference itself is pure
 Python and is not installed on the GPU box).
 """
@@ -56,6 +58,9 @@ def parse():
                     help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="model workload with N > 1: independent systems per rank instead of one system "
+                         "split into slabs (domain decomposition)")
     return ap.parse_args()
 
 
@@ -546,7 +551,7 @@ def run_model(args, ws, rank, local):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     model = make_model(dev)
-    pos_np, Z_np, cell_np = blob_in_water(seed=100 + rank)
+    pos_np, Z_np, cell_np = blob_in_water(seed=100 if (ws > 1 and not args.replicas) else 100 + rank)
     pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
     Z = torch.tensor(Z_np, device=dev)
     cell = torch.tensor(cell_np, dtype=torch.float32)
@@ -556,8 +561,15 @@ def run_model(args, ws, rank, local):
     E, N2 = g["query_idx"].numel(), g["f_exp_node_pos"].shape[0]
     del g
 
-    def step():
-        return model(pos, Z, cell, pbc)
+    domain = ws > 1 and not args.replicas
+    if domain:
+        from ubio_molfm_b200.domain import domain_energy_forces
+
+        def step():
+            return domain_energy_forces(model, pos, Z, cell, pbc)
+    else:
+        def step():
+            return model(pos, Z, cell, pbc)
 
     for _ in range(args.warmup):
         step()
@@ -583,19 +595,25 @@ def run_model(args, ws, rank, local):
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, ws, dev)
     kern = ops.TIMER.summary()
     name, (nl, tot) = max(kern.items(), key=lambda kv: kv[1][1])
+    if domain:   # this rank's share of the span: its owned rows, their edges, their expanded keys
+        from ubio_molfm_b200.domain import domain_graph
+        _, _, local_gid, geom = domain_graph(pos, cell, pbc, CUTOFF, 32, ws, rank)
+        N_r, E_r, N2_r = local_gid.numel(), geom["query_idx"].numel(), geom["outcell"].numel()
+    else:
+        N_r, E_r, N2_r = N, E, N2
     alg = {"e2a_attn_fwd": fwd_algorithmic_bytes, "e2a_attn_bwd_query": bwdq_algorithmic_bytes,
            "e2a_attn_bwd_key": bwdk_algorithmic_bytes, "e2a_attn_bwd_value": bwdv_algorithmic_bytes,
-           "e2a_attn_bwd_softmax": bwds_algorithmic_bytes, "e2a_attn_bwd_dk": bwddk_algorithmic_bytes}[name](N, N2, E)
+           "e2a_attn_bwd_softmax": bwds_algorithmic_bytes, "e2a_attn_bwd_dk": bwddk_algorithmic_bytes}[name](N_r, N2_r, E_r)
     per_launch_ms = tot / nl
     peak, peak_kind = measured_peaks()
     achieved = alg / (per_launch_ms * 1e-3) / 1e9
     roof = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-            "traffic": MEASURED_TRAFFIC_MODEL.get(name),
+            "traffic": None if domain else MEASURED_TRAFFIC_MODEL.get(name),
             "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
             "kernels_ms_per_launch": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
             "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
-    value = ws * N * 1e3 / ms
+    value = (1 if domain else ws) * N * 1e3 / ms
 
     e2e = None
     if not args.no_e2e:
@@ -607,9 +625,14 @@ def run_model(args, ws, rank, local):
         def e2e_step():
             p = h_pos.to(dev, non_blocking=True)
             z = h_Z.to(dev, non_blocking=True)
-            e, f = model(p, z, cell, pbc)
-            h_e.copy_(e, non_blocking=True)
-            h_f.copy_(f, non_blocking=True)
+            if domain:
+                e, _, f = domain_energy_forces(model, p, z, cell, pbc)
+                h_e.copy_(e, non_blocking=True)
+                h_f[: f.shape[0]].copy_(f, non_blocking=True)
+            else:
+                e, f = model(p, z, cell, pbc)
+                h_e.copy_(e, non_blocking=True)
+                h_f.copy_(f, non_blocking=True)
 
         for _ in range(max(1, min(args.warmup, 2))):
             e2e_step()
@@ -624,7 +647,7 @@ def run_model(args, ws, rank, local):
         torch.cuda.synchronize()
         barrier(ws)
         ems = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
-        e2e = {"value": ws * N * 1e3 / ems, "unit": "atom-steps/s",
+        e2e = {"value": (1 if domain else ws) * N * 1e3 / ems, "unit": "atom-steps/s",
                "h2d_bytes_per_step": h_pos.numel() * 4 + h_Z.numel() * 8,
                "d2h_bytes_per_step": h_e.numel() * 4 + h_f.numel() * 4, "ms_per_step": round(ems, 3),
                "includes": "H2D positions + atomic numbers, PBC images, radius graph + CSR, Wigner, backbone, "
@@ -635,11 +658,18 @@ def run_model(args, ws, rank, local):
         cpu = run_cpu_model(args.cpu_atoms or 500, 1, 0)
 
     if rank == 0:
+        cfgd = model_config_dict(args, N, E, N2)
+        if domain:
+            cfgd["parallelism"] = f"slab domain decomposition x{ws}, per-layer halo exchange (NCCL all_to_all)"
+            cfgd.update({"atoms_total": N, "edges_total": E, "atoms_per_rank": round(N / ws),
+                         "rank0_local_atoms_incl_ghosts": N_r, "rank0_edges": E_r, "rank0_expanded_nodes": N2_r})
+            for k in ("edges_per_rank", "expanded_nodes_per_rank"):
+                cfgd.pop(k, None)
         line = {"metric": "atom-steps/s", "value": round(value, 1), "unit": "atom-steps/s", "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "scaling": "strong" if domain else "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded blob-in-water periodic system, seeded random weights)",
-                "config": model_config_dict(args, N, E, N2), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "config": cfgd, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_timed, "clocks": clk}
         print(json.dumps(line))
 
