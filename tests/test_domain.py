@@ -84,3 +84,41 @@ def test_domain_decomposition_equals_single_gpu():
                          env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "DOMAIN_OK" in res.stdout, res.stdout[-3000:]
+
+
+def test_shard_molecules_balances_and_partitions():
+    from ubio_molfm_b200.domain import shard_molecules
+
+    g = torch.Generator().manual_seed(9)
+    sizes = torch.randint(10, 61, (4096,), generator=g).tolist()
+    for world in (1, 2, 4, 8):
+        parts = shard_molecules(sizes, world)
+        flat = sorted(i for p in parts for i in p)
+        assert flat == list(range(len(sizes)))
+        loads = [sum(sizes[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= 60
+
+
+def _gather_worker(rank, world, port, out):
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from ubio_molfm_b200.domain import gather_molecule_results, shard_molecules
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sizes = [5, 9, 2, 7, 7, 3, 11]
+    parts = shard_molecules(sizes, world)
+    mine = parts[rank]
+    energies = torch.tensor([float(10 * i + 1) for i in mine])
+    allE = gather_molecule_results(energies, mine, len(sizes))
+    out[rank] = allE.tolist() == [float(10 * i + 1) for i in range(len(sizes))]
+    dist.destroy_process_group()
+
+
+def test_gather_molecule_results_gloo():
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_gather_worker, args=(3, _free_port(), out), nprocs=3, join=True)
+    assert all(out[r] for r in range(3)), dict(out)

@@ -158,3 +158,62 @@ def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), gr
     energy = e_own.detach().reshape(1).clone()
     dist.all_reduce(energy, group=group)
     return energy, own_gid, -grad
+
+
+# ------------------------------------------------------------------------------------------------
+# Config 4: independent molecules, data parallel
+# ------------------------------------------------------------------------------------------------
+def shard_molecules(sizes, world):
+    """Balanced assignment of molecules to ranks: largest first, each to the rank with the fewest atoms
+    so far (ties to the lower rank).  Returns one sorted index list per rank."""
+    order = sorted(range(len(sizes)), key=lambda i: (-int(sizes[i]), i))
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        out[r].append(i)
+        load[r] += int(sizes[i])
+    return [sorted(v) for v in out]
+
+
+def molecules_energy_forces(model, mols, device, max_atoms_per_call=60000):
+    """Energies [M] and forces (list of [n_i, 3]) of non-periodic molecules ``mols`` = [(pos, Z), ...],
+    evaluated in batches of at most ``max_atoms_per_call`` atoms (systems never see each other)."""
+    energies, forces = [], []
+    i = 0
+    while i < len(mols):
+        j, n = i, 0
+        while j < len(mols) and (j == i or n + len(mols[j][1]) <= max_atoms_per_call):
+            n += len(mols[j][1])
+            j += 1
+        pos = torch.cat([torch.as_tensor(m[0], dtype=torch.float32) for m in mols[i:j]]).to(device)
+        Z = torch.cat([torch.as_tensor(m[1], dtype=torch.int64) for m in mols[i:j]]).to(device)
+        batch = torch.cat([torch.full((len(m[1]),), k, dtype=torch.int64) for k, m in enumerate(mols[i:j])]).to(device)
+        e, f = model(pos, Z, None, (False, False, False), batch)
+        energies.append(e)
+        forces.extend(torch.split(f, [len(m[1]) for m in mols[i:j]]))
+        i = j
+    return torch.cat(energies), forces
+
+
+def gather_molecule_results(energies, idx, n_total, group=None):
+    """All ranks' energies into one [n_total] tensor (ordered by molecule index) on every rank."""
+    world = dist.get_world_size(group)
+    dev = energies.device
+    counts = torch.tensor([len(idx)], device=dev)
+    all_counts = [torch.zeros_like(counts) for _ in range(world)]
+    dist.all_gather(all_counts, counts, group=group)
+    m = int(max(int(c) for c in all_counts))
+    buf_e = torch.zeros(m, device=dev, dtype=energies.dtype)
+    buf_i = torch.full((m,), -1, device=dev, dtype=torch.int64)
+    buf_e[: len(idx)] = energies
+    buf_i[: len(idx)] = torch.as_tensor(idx, device=dev)
+    ge = [torch.zeros_like(buf_e) for _ in range(world)]
+    gi = [torch.zeros_like(buf_i) for _ in range(world)]
+    dist.all_gather(ge, buf_e, group=group)
+    dist.all_gather(gi, buf_i, group=group)
+    out = torch.zeros(n_total, device=dev, dtype=energies.dtype)
+    for e_r, i_r in zip(ge, gi):
+        keep = i_r >= 0
+        out[i_r[keep]] = e_r[keep]
+    return out
