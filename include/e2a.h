@@ -291,6 +291,13 @@ int e2a_gate_fwd(const float* s, const float* h, int64_t n_nodes, int rows, int 
 int e2a_gate_bwd(const float* s, const float* h, const float* dy, int64_t n_nodes, int rows, int C, float c_scalar,
                  float c_vector, float* ds, float* dh, void* stream);
 
+/* Gaussian radial basis formed by its consumer (GaussianSmearing, module_utils.py:1853-1870):     */
+/* out[e,k] = exp(coeff (d_e - mu_k)^2); backward d_dist[e] = sum_k grad[e,k] out[e,k] 2 coeff (d_e - mu_k) */
+/* with the basis recomputed (nothing stored).                                                      */
+int e2a_rbf_fwd(const float* dist, int64_t n_edges, const float* mu, int nb, float coeff, float* out, void* stream);
+int e2a_rbf_bwd(const float* dist, const float* grad, int64_t n_edges, const float* mu, int nb, float coeff,
+                float* d_dist, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -511,3 +511,25 @@ def test_three_stage_backward_equals_two_entry_backward():
     # d(beta) is summed in a different order on the two paths (fp32 rounding only)
     for a, b in zip(grads, [dq, dk, dv, dg, dp, dd]):
         assert (a - b).abs().max().item() <= 1e-4 * max(b.abs().max().item(), 1.0)
+
+
+@pytest.mark.parametrize("L,F", [(1, 256), (3, 128), (5, 256)])
+def test_edge_outer_vectorised_backward(L, F):
+    """The float4 edge-outer backward (F in {128, 256}, L in {1, 3, 5}) against the torch oracle."""
+    from ubio_molfm_b200 import ops
+
+    N, M, E = 60, 60, 2000
+    q, _ = _random_graph(N, M, E, 3, True)
+    g = torch.Generator().manual_seed(L * F)
+    SH = torch.randn(E, L, generator=g)
+    FE = torch.randn(E, F, generator=g)
+    qt = _t(q)
+    ag = [SH.to(DEV).requires_grad_(True), FE.to(DEV).requires_grad_(True)]
+    ar = [SH.clone().requires_grad_(True), FE.clone().requires_grad_(True)]
+    og = ops.edge_degree_outer_triton(ag[0], ag[1], qt, N, None)
+    orf = R.edge_outer(ar[0], ar[1], torch.tensor(q), N)
+    w = torch.randn(orf.shape, generator=g)
+    gg = torch.autograd.grad(og, ag, w.to(DEV))
+    gr = torch.autograd.grad(orf, ar, w)
+    for a, b in zip(gg, gr):
+        torch.testing.assert_close(a.cpu(), b, atol=1e-4, rtol=1e-5)

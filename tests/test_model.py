@@ -145,3 +145,25 @@ def test_nve_velocity_verlet_conserves_energy():
     assert abs(e1 - e0) < 0.02 * ke0, (e0, e1, ke0)
     assert (md._com(md.x) - com0).abs().max().item() < 1e-4
     assert md.nsteps == 20
+
+
+def test_rbf_linear_matches_materialised_basis():
+    """rbf_linear (basis formed inside the product, distance gradient reduced per edge) against the
+    GaussianSmearing module followed by a linear map, fp64 reference."""
+    from ubio_molfm_b200.linear import rbf_linear
+    from ubio_molfm_b200.nn import GaussianSmearing
+
+    g = torch.Generator().manual_seed(2)
+    E, nb, h = 3000, 256, 128
+    rbf = GaussianSmearing(nb, cutoff=6.0)
+    d = (torch.rand(E, generator=g, dtype=torch.float64) * 6.0).requires_grad_(True)
+    w = torch.randn(h, nb, generator=g, dtype=torch.float64) / 16
+    b = torch.randn(h, generator=g, dtype=torch.float64)
+    ref = rbf.double()(d) @ w.t() + b
+    dg = d.detach().float().to(DEV).requires_grad_(True)
+    out = rbf_linear(dg, rbf.offset.float().to(DEV), rbf.coeff, w.float().to(DEV), b.float().to(DEV))
+    assert (out.double().cpu() - ref).abs().max().item() < 1e-5 * ref.abs().max().item()
+    wo = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    (gr,) = torch.autograd.grad(ref, d, wo)
+    (gg,) = torch.autograd.grad(out, dg, wo.float().to(DEV))
+    assert (gg.double().cpu() - gr).abs().max().item() < 1e-4 * gr.abs().max().item()

@@ -19,7 +19,7 @@ import math
 import torch
 from torch import nn
 
-from .nn import (E2TensorProductSO2_FirstOrder, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
+from .nn import (E2TensorProductSO2_FirstOrder, RbfSpec, RadialProfile, SO3_Linear2Scalar_e2former, SO3_Linear_e2former,
                  irreps_channels_lmax, lin, parse_irreps, run_mlp)
 from . import linear as tc
 from .ops import attention_span
@@ -99,7 +99,10 @@ class E2AttentionArbOrder_sparse(nn.Module):
             s_tab = (self.source_embedding.weight @ w[:, nb + e:].t()).contiguous()     # [types, h]
         z_q = atomic_numbers[query_idx]
         z_k = atomic_numbers[f_outcell_index][neighbor_idx]
-        h = lin(attn_weight, w[:, :nb], lin0.bias, cw)
+        if isinstance(attn_weight, RbfSpec):
+            h = attn_weight.linear(w[:, :nb], lin0.bias, cw)
+        else:
+            h = lin(attn_weight, w[:, :nb], lin0.bias, cw)
         h = run_mlp(list(net)[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
         return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
 

@@ -291,3 +291,64 @@ int e2a_gate_bwd(const float* s, const float* h, const float* dy, int64_t n_node
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Gaussian radial basis (GaussianSmearing, module_utils.py:1853-1870) formed where it is consumed:
+//   rbf[e, k] = exp(coeff (d_e - mu_k)^2)
+// and the distance gradient of a consumer's d(rbf), reduced over k without storing rbf:
+//   d_d[e] = sum_k g[e, k] rbf[e, k] 2 coeff (d_e - mu_k)
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+__global__ void k_rbf_fwd(const float* __restrict__ d, int64_t E, const float* __restrict__ mu, int nb, float coeff,
+                          float* __restrict__ out) {
+  const int64_t total = E * (int64_t)nb;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / nb;
+    const int k = (int)(t - e * nb);
+    const float x = d[e] - mu[k];
+    out[t] = expf(coeff * (x * x));
+  }
+}
+
+__global__ void k_rbf_bwd(const float* __restrict__ d, const float* __restrict__ g, int64_t E,
+                          const float* __restrict__ mu, int nb, float coeff, float* __restrict__ dd) {
+  const int lane = threadIdx.x & 31;
+  int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (; e < E; e += nw) {
+    const float de = d[e];
+    float acc = 0.f;
+    for (int k = lane; k < nb; k += 32) {
+      const float x = de - mu[k];
+      acc += g[e * nb + k] * expf(coeff * (x * x)) * (2.f * coeff * x);
+    }
+    acc = e2a_warp_sum(acc);
+    if (lane == 0) dd[e] = acc;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int e2a_rbf_fwd(const float* dist, int64_t n_edges, const float* mu, int nb, float coeff, float* out, void* stream) {
+  if (n_edges < 0 || nb <= 0) return E2A_ERR_ARG;
+  if (n_edges == 0) return E2A_OK;
+  if (!dist || !mu || !out) return E2A_ERR_ARG;
+  k_rbf_fwd<<<grid_flat(n_edges * nb), 256, 0, (cudaStream_t)stream>>>(dist, n_edges, mu, nb, coeff, out);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_rbf_bwd(const float* dist, const float* grad, int64_t n_edges, const float* mu, int nb, float coeff,
+                float* d_dist, void* stream) {
+  if (n_edges < 0 || nb <= 0) return E2A_ERR_ARG;
+  if (n_edges == 0) return E2A_OK;
+  if (!dist || !grad || !mu || !d_dist) return E2A_ERR_ARG;
+  k_rbf_bwd<<<grid_flat(n_edges * 32), 256, 0, (cudaStream_t)stream>>>(dist, grad, n_edges, mu, nb, coeff, d_dist);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // extern "C"

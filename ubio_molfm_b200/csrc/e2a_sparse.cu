@@ -156,6 +156,57 @@ __global__ void k_edge_outer_bwd(const float* __restrict__ go, const float* __re
   }
 }
 
+// Same products, vectorised: one warp per edge, float4 lanes over the F channels (F = 128 FV), the
+// destination's L gradient rows read once for both outputs (L, FV compile-time).
+template <int L, int FV>
+__global__ void __launch_bounds__(256)
+k_edge_outer_bwd_v(const float* __restrict__ go, const float* __restrict__ sh, const float* __restrict__ fea,
+                   const int32_t* __restrict__ qidx, int64_t E, float* __restrict__ d_sh, float* __restrict__ d_fea) {
+  constexpr int F = 128 * FV;
+  const int lane = threadIdx.x & 31;
+  int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (; e < E; e += nw) {
+    const float* g = go + (int64_t)qidx[e] * L * F;
+    float s[L], ps[L];
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+      s[l] = d_fea ? __ldg(sh + e * L + l) : 0.f;
+      ps[l] = 0.f;
+    }
+    float4 fv[FV], dv[FV];
+#pragma unroll
+    for (int j = 0; j < FV; ++j) {
+      fv[j] = d_sh ? __ldg(reinterpret_cast<const float4*>(fea + e * F) + lane + 32 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      dv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+#pragma unroll
+      for (int j = 0; j < FV; ++j) {
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(g + l * F) + lane + 32 * j);
+        dv[j].x = fmaf(s[l], gv.x, dv[j].x); dv[j].y = fmaf(s[l], gv.y, dv[j].y);
+        dv[j].z = fmaf(s[l], gv.z, dv[j].z); dv[j].w = fmaf(s[l], gv.w, dv[j].w);
+        ps[l] += (gv.x * fv[j].x + gv.y * fv[j].y) + (gv.z * fv[j].z + gv.w * fv[j].w);
+      }
+    }
+    if (d_fea) {
+#pragma unroll
+      for (int j = 0; j < FV; ++j) reinterpret_cast<float4*>(d_fea + e * F)[lane + 32 * j] = dv[j];
+    }
+    if (d_sh) {
+#pragma unroll
+      for (int l = 0; l < L; ++l) ps[l] = e2a_warp_sum(ps[l]);
+      if (lane < L) {
+        float v = 0.f;
+#pragma unroll
+        for (int l = 0; l < L; ++l) v = lane == l ? ps[l] : v;
+        d_sh[e * L + lane] = v;
+      }
+    }
+  }
+}
+
 int rows_grid(int64_t n) { return (int)(n < (1 << 30) ? (n > 0 ? n : 1) : (1 << 30)); }
 int flat_grid(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
@@ -252,8 +303,20 @@ int e2a_edge_outer_bwd(const float* grad_out, const float* sh, const float* fea,
   if (n_edges < 0 || L <= 0 || F <= 0) return E2A_ERR_ARG;
   if (n_edges == 0) return E2A_OK;
   if (!grad_out || !query_idx || (d_sh && !fea) || (d_fea && !sh)) return E2A_ERR_ARG;
-  k_edge_outer_bwd<<<flat_grid(n_edges * 32, 256), 256, 0, (cudaStream_t)stream>>>(grad_out, sh, fea, query_idx,
-                                                                                  n_edges, L, F, d_sh, d_fea);
+  const bool al = ((reinterpret_cast<uintptr_t>(grad_out) | reinterpret_cast<uintptr_t>(fea) |
+                    reinterpret_cast<uintptr_t>(d_fea)) & 15u) == 0;
+  const int grid = flat_grid(n_edges * 32, 256);
+  cudaStream_t st = (cudaStream_t)stream;
+#define E2A_EO_BWD(LL, FVV) k_edge_outer_bwd_v<LL, FVV><<<grid, 256, 0, st>>>(grad_out, sh, fea, query_idx, n_edges, d_sh, d_fea)
+  if (al && (F == 128 || F == 256) && (L == 1 || L == 3 || L == 5)) {
+    const int fv = F / 128;
+    if (L == 1) { if (fv == 1) E2A_EO_BWD(1, 1); else E2A_EO_BWD(1, 2); }
+    else if (L == 3) { if (fv == 1) E2A_EO_BWD(3, 1); else E2A_EO_BWD(3, 2); }
+    else { if (fv == 1) E2A_EO_BWD(5, 1); else E2A_EO_BWD(5, 2); }
+  } else {
+    k_edge_outer_bwd<<<grid, 256, 0, st>>>(grad_out, sh, fea, query_idx, n_edges, L, F, d_sh, d_fea);
+  }
+#undef E2A_EO_BWD
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }

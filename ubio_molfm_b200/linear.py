@@ -465,3 +465,42 @@ class _GateFn(torch.autograd.Function):
 def gate(s, h, c_scalar, c_vector):
     """Gated activation of irreps rows ``h`` [n, 9, C] by gate pre-activations ``s`` [n, 3 C] (CUDA)."""
     return _GateFn.apply(s.float(), h.float(), c_scalar, c_vector)
+
+
+# ------------------------------------------------------------------------------------------------
+# Gaussian radial basis consumed by a linear map, formed on the fly (inference path)
+# ------------------------------------------------------------------------------------------------
+class _RbfLinearFn(torch.autograd.Function):
+    """``h = rbf(d) W^T (+ b)`` with rbf[e,k] = exp(coeff (d_e - mu_k)^2): the basis is formed for the
+    product and dropped; the backward forms d(rbf) = g W and reduces it to d(d) per edge with the basis
+    recomputed, so only [E] vectors reach the distance's other consumers."""
+
+    @staticmethod
+    def forward(ctx, dist, mu, coeff, w, b):
+        lib = _lib.load()
+        d = dist.contiguous()
+        E, nb = d.shape[0], mu.shape[0]
+        rbf = torch.empty((E, nb), device=d.device, dtype=torch.float32)
+        check(lib.e2a_rbf_fwd(ptr(d), E, ptr(mu), nb, float(coeff), ptr(rbf), stream_of(d.device)), "e2a_rbf_fwd")
+        h = gemm(rbf, w, b)
+        ctx.save_for_backward(d, mu, w)
+        ctx.coeff = float(coeff)
+        return h
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        d, mu, w = ctx.saved_tensors
+        g = g.contiguous()
+        d_rbf = gemm(g, w.t().contiguous())
+        dd = torch.empty_like(d)
+        check(lib.e2a_rbf_bwd(ptr(d), ptr(d_rbf), d.shape[0], ptr(mu), mu.shape[0], ctx.coeff, ptr(dd),
+                              stream_of(d.device)), "e2a_rbf_bwd")
+        return dd, None, None, None, None
+
+
+def rbf_linear(dist, mu, coeff, w, b=None):
+    """``GaussianSmearing(dist) @ w.T (+ b)`` without materialising the basis for autograd (CUDA,
+    constant weights)."""
+    return _RbfLinearFn.apply(dist.float(), mu.float().contiguous(), float(coeff), w.detach().float().contiguous(),
+                              None if b is None else b.detach().float().contiguous())

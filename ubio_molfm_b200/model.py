@@ -25,7 +25,7 @@ from . import linear as tc
 from . import ops
 from .attention import E2AttentionArbOrder_sparse
 from .graph import expand_pbc, radius_graph
-from .nn import GaussianSmearing, RadialProfile, SO3_Linear_e2former, irreps_channels_lmax, lin, run_mlp
+from .nn import GaussianSmearing, RadialProfile, RbfSpec, SO3_Linear_e2former, irreps_channels_lmax, lin, run_mlp
 from .wigner import jd_matrices, node_wigner
 
 
@@ -224,12 +224,17 @@ class EdgeDegreeEmbeddingNetwork_higherorder(nn.Module):
                     s_tab = (self.source_embedding.weight @ w[:, 2 * nb:].t()).contiguous()
                 z_q = atomic_numbers[qi]
                 z_k = atomic_numbers[batched_data["f_outcell_index"]][ni]
-                h = lin(edge_scalars, w[:, :nb], lin0.bias, cw)
+                if isinstance(edge_scalars, RbfSpec):
+                    h = edge_scalars.linear(w[:, :nb], lin0.bias, cw)
+                else:
+                    h = lin(edge_scalars, w[:, :nb], lin0.bias, cw)
                 h = run_mlp(layers[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
             else:
-                h = prof(edge_scalars)
-            h = h * poly_dist.reshape(-1, 1)
-            feats.append(ops.edge_degree_outer_triton(sh[:, l * l:(l + 1) ** 2].contiguous(), h.contiguous(), qi, n,
+                h = prof(edge_scalars.materialize() if isinstance(edge_scalars, RbfSpec) else edge_scalars)
+            # the envelope scales each edge's product: applied to the [E, 2l+1] harmonics rather than the
+            # [E, C] features (the same sum, a fraction of the elementwise work)
+            sh_l = sh[:, l * l:(l + 1) ** 2] * poly_dist.reshape(-1, 1)
+            feats.append(ops.edge_degree_outer_triton(sh_l.contiguous(), h.contiguous(), qi, n,
                                                       batched_data["metadata"]))
         return torch.cat(feats, dim=1) / self.avg_aggregate_num
 
@@ -302,7 +307,11 @@ class E2former(nn.Module):
             We, Wie = W, Wi
         bd = dict(graph)
         bd.update({"wigner": W, "wigner_inv": Wi, "wigner_exp": We, "wigner_inv_exp": Wie})
-        f_dist_embedding = self.rbf(graph["f_dist"])
+        if node_pos.is_cuda and not self.training:
+            # the basis is formed inside each consumer's first product (see linear.rbf_linear)
+            f_dist_embedding = RbfSpec(graph["f_dist"], self.rbf.offset, self.rbf.coeff)
+        else:
+            f_dist_embedding = self.rbf(graph["f_dist"])
         x = self.edge_deg_embed_dense(node_input=None, node_pos=node_pos, edge_dis=graph["f_dist"],
                                       atomic_numbers=atomic_numbers, edge_vec=graph["f_edge_vec"], batched_data=bd,
                                       attn_mask=None, poly_dist=graph["f_poly_dist"], edge_scalars=f_dist_embedding)

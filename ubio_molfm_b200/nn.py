@@ -206,6 +206,23 @@ class GaussianSmearing(nn.Module):
         return torch.exp(self.coeff * torch.pow(d, 2)).reshape(*shape, -1)
 
 
+class RbfSpec:
+    """A Gaussian radial basis not yet formed: ``(dist [E], offsets [nb], coeff)``.  Consumers that start
+    with a linear map of the basis use :func:`linear.rbf_linear`; others call :meth:`materialize`."""
+
+    def __init__(self, dist, offset, coeff):
+        self.dist, self.offset, self.coeff = dist, offset, coeff
+
+    def materialize(self):
+        d = self.dist.view(-1, 1) - self.offset.view(1, -1)
+        return torch.exp(self.coeff * torch.pow(d, 2))
+
+    def linear(self, w, b, const_weights):
+        if self.dist.is_cuda and const_weights:
+            return tc.rbf_linear(self.dist, self.offset, self.coeff, w, b)
+        return lin(self.materialize(), w, b, const_weights)
+
+
 def polynomial(dist, cutoff, exponent=5):
     """Smooth envelope 1 + r^p (a + r (b + c r)), zero for r >= 1 (module_utils.py:1946-1954)."""
     a = -(exponent + 1) * (exponent + 2) / 2
