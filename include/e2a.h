@@ -298,6 +298,18 @@ int e2a_rbf_fwd(const float* dist, int64_t n_edges, const float* mu, int nb, flo
 int e2a_rbf_bwd(const float* dist, const float* grad, int64_t n_edges, const float* mu, int nb, float coeff,
                 float* d_dist, void* stream);
 
+/* Per-node map of the first-order SO(2) product from the node position (fp64 inside):            */
+/* A[n,k,s] = |p| sum_j Wi^T[k,j] W[sel[j],s] cg[j] with W = blockdiag(D^0, D^1, D^2),                */
+/* D^l = J_l Y_l(-beta) J_l Y_l(-alpha) of the position's Euler angles (module_utils.py:182-337),     */
+/* Wi = the l3_sequential ((0,1),(1,3),(2,2)) repetition of the blocks (so2_tensor_product.py:341-389); */
+/* rows written in row_perm order (NULL = identity).  j1 [3x3], j2 [5x5], sel [20], cg [20],          */
+/* row_perm [20] are HOST arrays.  Backward: dpos from dA (angles held constant at the poles and near */
+/* the origin, as the reference detaches them).                                                       */
+int e2a_node_map_fwd(const float* pos, int64_t n_nodes, const double* j1, const double* j2, const int32_t* sel,
+                     const double* cg, const int32_t* row_perm, float* A, void* stream);
+int e2a_node_map_bwd(const float* pos, const float* dA, int64_t n_nodes, const double* j1, const double* j2,
+                     const int32_t* sel, const double* cg, const int32_t* row_perm, float* dpos, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

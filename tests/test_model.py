@@ -167,3 +167,29 @@ def test_rbf_linear_matches_materialised_basis():
     (gr,) = torch.autograd.grad(ref, d, wo)
     (gg,) = torch.autograd.grad(out, dg, wo.float().to(DEV))
     assert (gg.double().cpu() - gr).abs().max().item() < 1e-4 * gr.abs().max().item()
+
+
+def test_node_map_from_positions_matches_wigner_path():
+    """The fused per-node SO(2) map (fp64 inside the kernel) against node_wigner + node_map in fp64,
+    values and position gradients, including nodes on the y axis and at the origin (angles held)."""
+    from ubio_molfm_b200.nn import E2TensorProductSO2_FirstOrder
+    from ubio_molfm_b200.wigner import jd_matrices, node_wigner
+
+    g = torch.Generator().manual_seed(8)
+    tp = E2TensorProductSO2_FirstOrder(16, 16, 2, 4)
+    perm, _ = tp.so2_tp.mc_row_order()
+    pos = torch.randn(500, 3, generator=g, dtype=torch.float64) * 7
+    pos[0] = torch.tensor([0.0, 3.0, 0.0], dtype=torch.float64)     # pole
+    pos[1] = torch.tensor([0.0, -2.0, 0.0], dtype=torch.float64)    # pole
+    pos[2] = 0.0                                                    # origin
+    jd = jd_matrices(2)
+    pr = pos.clone().requires_grad_(True)
+    W, Wi = node_wigner(pr, dtype=torch.float64, jd=jd)
+    ref = tp.double().node_map(W, Wi, pr, perm)
+    pg = pos.float().to(DEV).requires_grad_(True)
+    out = tp.float().node_map_from_pos(pg, [j.float() for j in jd], perm)
+    assert (out.double().cpu() - ref).abs().max().item() < 1e-5 * max(1.0, ref.abs().max().item())
+    w = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    (gr,) = torch.autograd.grad(ref, pr, w)
+    (gg,) = torch.autograd.grad(out, pg, w.float().to(DEV))
+    assert (gg.double().cpu() - gr).abs().max().item() < 1e-4 * max(1.0, gr.abs().max().item())

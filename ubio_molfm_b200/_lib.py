@@ -58,6 +58,8 @@ SIGNATURES = {
     "e2a_node_apply_bwd": (I32, [P, P, I64, P, I64, P, I64, I64, I32, I32, I32, P, I64, P, I64, P, P]),
     "e2a_rbf_fwd": (I32, [P, I64, P, I32, ctypes.c_float, P, P]),
     "e2a_rbf_bwd": (I32, [P, P, I64, P, I32, ctypes.c_float, P, P]),
+    "e2a_node_map_fwd": (I32, [P, I64, P, P, P, P, P, P, P]),
+    "e2a_node_map_bwd": (I32, [P, P, I64, P, P, P, P, P, P, P]),
     "e2a_rms_norm_fwd": (I32, [P, I64, I32, I32, P, P, ctypes.c_float, P, P, P]),
     "e2a_rms_norm_bwd": (I32, [P, P, I64, I32, I32, P, P, P, P]),
     "e2a_gate_fwd": (I32, [P, P, I64, I32, I32, ctypes.c_float, ctypes.c_float, P, P]),

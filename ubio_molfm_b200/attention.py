@@ -132,7 +132,11 @@ class E2AttentionArbOrder_sparse(nn.Module):
         if fused:
             # rows of both halves in the (m, c) order of the output linear; [A_b v ; v] in one kernel
             row_perm, tasks = self._fused_rows()
-            A_b = tp.node_map(bd["wigner_exp"], bd["wigner_inv_exp"], bd["f_exp_node_pos"], row_perm)
+            jd = bd.get("node_map_jd")
+            if jd is not None:   # maps straight from positions (the caller did not form Wigner matrices)
+                A_b = tp.node_map_from_pos(bd["f_exp_node_pos"], jd, row_perm)
+            else:
+                A_b = tp.node_map(bd["wigner_exp"], bd["wigner_inv_exp"], bd["f_exp_node_pos"], row_perm)
             merged = tc.node_apply(A_b, value, "merge")                               # [N2, 29, C]
             n_b = A_b.shape[1]
         else:
@@ -158,7 +162,10 @@ class E2AttentionArbOrder_sparse(nn.Module):
         agg = agg.reshape(N1, -1, C)
         if fused:
             # A_a agg_v - agg_b, then output linear and proj_first as one GEMM per output row
-            A_a = tp.node_map(bd["wigner"], bd["wigner_inv"], node_pos, row_perm)
+            if jd is not None:
+                A_a = tp.node_map_from_pos(node_pos, jd, row_perm)
+            else:
+                A_a = tp.node_map(bd["wigner"], bd["wigner_inv"], node_pos, row_perm)
             diff = tc.node_apply(A_a, agg, "sub")                                          # [N1, 20, C]
             out = tc.rowblock_linear(diff, tasks, self._fused_out_weights(), self.proj_first.bias,
                                      (self.lmax + 1) ** 2)

@@ -352,3 +352,272 @@ int e2a_rbf_bwd(const float* dist, const float* grad, int64_t n_edges, const flo
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Per-node map of the first-order SO(2) product, straight from the node's position (fp64 inside):
+//   (alpha, beta) = the Euler angles of the position (module_utils.py:182-226, eval: gamma = 0; the
+//                   angles are held constant at the poles / near the origin, as the reference
+//                   detaches them there),
+//   D^l = J_l Y_l(-beta) J_l Y_l(-alpha)  (module_utils.py:266-337; Y_l = rotation about y),
+//   W   = blockdiag(D^0, D^1, D^2),  Wi^T = blockdiag over l3_sequential of (D^l3)^T,
+//   A[k, s] = |pos| sum_j Wi^T[k, j] W[sel[j], s] cg[j]       (so2_tensor_product.py:341-389),
+// rows written in the order row_perm (new row k <- old row row_perm[k]).  The backward is the
+// analytic derivative of A with respect to the position (through |pos| and the two angles).
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+struct NodeMapTables {
+  double J1[9], J2[25];
+  double cg[20];
+  int sel[20];
+  int perm[20];
+};
+
+// (row0, l) of the six Wi blocks for l3_sequential = ((0,1), (1,3), (2,2))
+__device__ __forceinline__ void wi_block(int k, int& r0, int& l) {
+  if (k == 0) { r0 = 0; l = 0; }
+  else if (k < 10) { r0 = 1 + 3 * ((k - 1) / 3); l = 1; }
+  else { r0 = 10 + 5 * ((k - 10) / 5); l = 2; }
+}
+
+template <int L>
+__device__ __forceinline__ void yrot(double th, double (&Y)[2 * L + 1][2 * L + 1], double (&dY)[2 * L + 1][2 * L + 1]) {
+  constexpr int M = 2 * L + 1;
+#pragma unroll
+  for (int i = 0; i < M; ++i)
+#pragma unroll
+    for (int j = 0; j < M; ++j) { Y[i][j] = 0.0; dY[i][j] = 0.0; }
+#pragma unroll
+  for (int i = 0; i < M; ++i) {
+    const double f = (double)(L - i);
+    double s, c;
+    sincos(f * th, &s, &c);
+    Y[i][2 * L - i] = s;
+    dY[i][2 * L - i] = f * c;
+    Y[i][i] = c;                  // overwrites the centre entry (f = 0): cos 0 = 1
+    dY[i][i] = -f * s;
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void matmul(const double (&A)[M][M], const double (&B)[M][M], double (&C)[M][M]) {
+#pragma unroll
+  for (int i = 0; i < M; ++i)
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+      double acc = 0.0;
+#pragma unroll
+      for (int k = 0; k < M; ++k) acc += A[i][k] * B[k][j];
+      C[i][j] = acc;
+    }
+}
+
+template <int L>
+__device__ __forceinline__ void load_j(const double* src, double (&J)[2 * L + 1][2 * L + 1]) {
+#pragma unroll
+  for (int i = 0; i < 2 * L + 1; ++i)
+#pragma unroll
+    for (int j = 0; j < 2 * L + 1; ++j) J[i][j] = src[i * (2 * L + 1) + j];
+}
+
+// D = J Yb J Yc and (optionally) the pieces of its angle derivatives
+template <int L>
+struct DBlock {
+  static constexpr int M = 2 * L + 1;
+  double D[M][M], JYbJ[M][M], Yc[M][M], dYc[M][M], Yb[M][M], dYb[M][M], J[M][M];
+  __device__ __forceinline__ void build(const double* jsrc, double b, double c) {
+    load_j<L>(jsrc, J);
+    yrot<L>(b, Yb, dYb);
+    yrot<L>(c, Yc, dYc);
+    double T[M][M];
+    matmul<M>(J, Yb, T);
+    matmul<M>(T, J, JYbJ);
+    matmul<M>(JYbJ, Yc, D);
+  }
+};
+
+struct Geo {
+  double p[3], d, xn, yn, zn;
+  bool mask;
+  double beta, alpha;
+};
+
+__device__ __forceinline__ Geo geometry(const float* pos, int64_t n) {
+  Geo g;
+  g.p[0] = pos[3 * n]; g.p[1] = pos[3 * n + 1]; g.p[2] = pos[3 * n + 2];
+  g.d = sqrt(g.p[0] * g.p[0] + g.p[1] * g.p[1] + g.p[2] * g.p[2]);
+  const bool small = g.d < 1e-5;
+  const double dd = small ? 1.0 : g.d;
+  g.xn = g.p[0] / dd; g.yn = g.p[1] / dd; g.zn = g.p[2] / dd;
+  g.mask = small || fabs(fabs(g.yn) - 1.0) <= 1e-8 + 1e-5;
+  g.beta = acos(fmin(1.0, fmax(-1.0, g.yn)));
+  g.alpha = atan2(g.xn, g.zn);
+  return g;
+}
+
+// W[row][s] for row, s in 0..8 from the blocks
+__device__ __forceinline__ double wget(const DBlock<1>& b1, const DBlock<2>& b2, int r, int s) {
+  if (r == 0) return s == 0 ? 1.0 : 0.0;
+  if (r < 4) return (s >= 1 && s < 4) ? b1.D[r - 1][s - 1] : 0.0;
+  return s >= 4 ? b2.D[r - 4][s - 4] : 0.0;
+}
+
+__device__ __forceinline__ double dget(const DBlock<1>& b1, const DBlock<2>& b2, int l, int i, int j) {
+  return l == 0 ? 1.0 : (l == 1 ? b1.D[i][j] : b2.D[i][j]);
+}
+
+__global__ void __launch_bounds__(128)
+k_node_map_fwd(const float* __restrict__ pos, int64_t n_nodes, NodeMapTables t, float* __restrict__ A) {
+  const int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (n >= n_nodes) return;
+  const Geo g = geometry(pos, n);
+  DBlock<1> b1;
+  DBlock<2> b2;
+  b1.build(t.J1, -g.beta, -g.alpha);
+  b2.build(t.J2, -g.beta, -g.alpha);
+  float* out = A + n * 180;
+  for (int kn = 0; kn < 20; ++kn) {
+    const int k = t.perm[kn];
+    int r0, l;
+    wi_block(k, r0, l);
+    const int kk = k - r0;
+    for (int s = 0; s < 9; ++s) {
+      double acc = 0.0;
+      for (int jj = 0; jj < 2 * l + 1; ++jj) {
+        const int j = r0 + jj;
+        acc += dget(b1, b2, l, jj, kk) * wget(b1, b2, t.sel[j], s) * t.cg[j];
+      }
+      out[kn * 9 + s] = (float)(g.d * acc);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128)
+k_node_map_bwd(const float* __restrict__ pos, const float* __restrict__ dA, int64_t n_nodes, NodeMapTables t,
+               float* __restrict__ dpos) {
+  const int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (n >= n_nodes) return;
+  const Geo g = geometry(pos, n);
+  DBlock<1> b1;
+  DBlock<2> b2;
+  b1.build(t.J1, -g.beta, -g.alpha);
+  b2.build(t.J2, -g.beta, -g.alpha);
+  double dD1[3][3] = {}, dD2[5][5] = {};
+  double dW[9][9] = {};
+  double dscale = 0.0;
+  const float* gA = dA + n * 180;
+  for (int kn = 0; kn < 20; ++kn) {
+    const int k = t.perm[kn];
+    int r0, l;
+    wi_block(k, r0, l);
+    const int kk = k - r0;
+    for (int s = 0; s < 9; ++s) {
+      const double ga = gA[kn * 9 + s];
+      if (ga == 0.0) continue;
+      double tks = 0.0;
+      for (int jj = 0; jj < 2 * l + 1; ++jj) {
+        const int j = r0 + jj;
+        const double m = wget(b1, b2, t.sel[j], s) * t.cg[j];
+        const double wi = dget(b1, b2, l, jj, kk);
+        tks += wi * m;
+        // A = d * sum_j Wi^T[k][j] M[j][s]:  d(D^l[jj][kk]) += ga d M[j][s];  dM[j][s] += ga d Wi^T[k][j]
+        if (l == 1) dD1[jj][kk] += ga * g.d * m;
+        else if (l == 2) dD2[jj][kk] += ga * g.d * m;
+        dW[t.sel[j]][s] += ga * g.d * wi * t.cg[j];
+      }
+      dscale += ga * tks;
+    }
+  }
+  // W blocks -> D blocks
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) dD1[i][j] += dW[1 + i][1 + j];
+  for (int i = 0; i < 5; ++i)
+    for (int j = 0; j < 5; ++j) dD2[i][j] += dW[4 + i][4 + j];
+  double gp[3] = {0.0, 0.0, 0.0};
+  if (g.d > 0.0) {
+    gp[0] = dscale * g.p[0] / g.d; gp[1] = dscale * g.p[1] / g.d; gp[2] = dscale * g.p[2] / g.d;
+  }
+  if (!g.mask) {
+    // D = (J Yb J) Yc:  dL/dc = <dD, JYbJ Yc'>;  dL/db = <dD, J Yb' J Yc>
+    double dLdb = 0.0, dLdc = 0.0;
+    {
+      double T[3][3], U[3][3], V[3][3], X[3][3];
+      matmul<3>(b1.JYbJ, b1.dYc, T);
+      matmul<3>(b1.J, b1.dYb, U);
+      matmul<3>(U, b1.J, V);
+      matmul<3>(V, b1.Yc, X);
+      for (int i = 0; i < 3; ++i)
+        for (int j = 0; j < 3; ++j) { dLdc += dD1[i][j] * T[i][j]; dLdb += dD1[i][j] * X[i][j]; }
+    }
+    {
+      double T[5][5], U[5][5], V[5][5], X[5][5];
+      matmul<5>(b2.JYbJ, b2.dYc, T);
+      matmul<5>(b2.J, b2.dYb, U);
+      matmul<5>(U, b2.J, V);
+      matmul<5>(V, b2.Yc, X);
+      for (int i = 0; i < 5; ++i)
+        for (int j = 0; j < 5; ++j) { dLdc += dD2[i][j] * T[i][j]; dLdb += dD2[i][j] * X[i][j]; }
+    }
+    const double dbeta = -dLdb, dalpha = -dLdc;     // b = -beta, c = -alpha
+    const double pn[3] = {g.xn, g.yn, g.zn};
+    const double dbdy = -1.0 / sqrt(fmax(1e-300, 1.0 - g.yn * g.yn));
+    const double rxz = g.xn * g.xn + g.zn * g.zn;
+    const double dadx = g.zn / rxz, dadz = -g.xn / rxz;
+    for (int i = 0; i < 3; ++i) {
+      const double dyn = ((i == 1 ? 1.0 : 0.0) - g.yn * pn[i]) / g.d;
+      const double dxn = ((i == 0 ? 1.0 : 0.0) - g.xn * pn[i]) / g.d;
+      const double dzn = ((i == 2 ? 1.0 : 0.0) - g.zn * pn[i]) / g.d;
+      gp[i] += dbeta * dbdy * dyn + dalpha * (dadx * dxn + dadz * dzn);
+    }
+  }
+  dpos[3 * n] = (float)gp[0];
+  dpos[3 * n + 1] = (float)gp[1];
+  dpos[3 * n + 2] = (float)gp[2];
+}
+
+int fill_tables(NodeMapTables& t, const double* j1, const double* j2, const int32_t* sel, const double* cg,
+                const int32_t* row_perm) {
+  if (!j1 || !j2 || !sel || !cg) return E2A_ERR_ARG;
+  for (int i = 0; i < 9; ++i) t.J1[i] = j1[i];
+  for (int i = 0; i < 25; ++i) t.J2[i] = j2[i];
+  for (int i = 0; i < 20; ++i) {
+    if (sel[i] < 0 || sel[i] > 8) return E2A_ERR_ARG;
+    t.sel[i] = sel[i];
+    t.cg[i] = cg[i];
+    t.perm[i] = row_perm ? row_perm[i] : i;
+    if (t.perm[i] < 0 || t.perm[i] >= 20) return E2A_ERR_ARG;
+  }
+  return E2A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int e2a_node_map_fwd(const float* pos, int64_t n_nodes, const double* j1, const double* j2, const int32_t* sel,
+                     const double* cg, const int32_t* row_perm, float* A, void* stream) {
+  if (n_nodes < 0) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!pos || !A) return E2A_ERR_ARG;
+  NodeMapTables t;
+  const int rc = fill_tables(t, j1, j2, sel, cg, row_perm);
+  if (rc) return rc;
+  k_node_map_fwd<<<(unsigned)((n_nodes + 127) / 128), 128, 0, (cudaStream_t)stream>>>(pos, n_nodes, t, A);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int e2a_node_map_bwd(const float* pos, const float* dA, int64_t n_nodes, const double* j1, const double* j2,
+                     const int32_t* sel, const double* cg, const int32_t* row_perm, float* dpos, void* stream) {
+  if (n_nodes < 0) return E2A_ERR_ARG;
+  if (n_nodes == 0) return E2A_OK;
+  if (!pos || !dA || !dpos) return E2A_ERR_ARG;
+  NodeMapTables t;
+  const int rc = fill_tables(t, j1, j2, sel, cg, row_perm);
+  if (rc) return rc;
+  k_node_map_bwd<<<(unsigned)((n_nodes + 127) / 128), 128, 0, (cudaStream_t)stream>>>(pos, dA, n_nodes, t, dpos);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // extern "C"

@@ -504,3 +504,55 @@ def rbf_linear(dist, mu, coeff, w, b=None):
     constant weights)."""
     return _RbfLinearFn.apply(dist.float(), mu.float().contiguous(), float(coeff), w.detach().float().contiguous(),
                               None if b is None else b.detach().float().contiguous())
+
+
+# ------------------------------------------------------------------------------------------------
+# Per-node SO(2) map straight from positions (inference path)
+# ------------------------------------------------------------------------------------------------
+class NodeMapTables:
+    """Host tables of the node map: J_1, J_2 (fp64), selection, CG weights, row order."""
+
+    def __init__(self, jd, selected_idx, cg_weight, row_perm=None):
+        import numpy as np
+
+        self.j1 = np.ascontiguousarray(jd[1].detach().cpu().numpy(), dtype=np.float64)
+        self.j2 = np.ascontiguousarray(jd[2].detach().cpu().numpy(), dtype=np.float64)
+        self.sel = np.ascontiguousarray(np.asarray(selected_idx.detach().cpu() if hasattr(selected_idx, "cpu")
+                                                   else selected_idx), dtype=np.int32)
+        self.cg = np.ascontiguousarray(np.asarray(cg_weight.detach().cpu() if hasattr(cg_weight, "cpu")
+                                                  else cg_weight), dtype=np.float64)
+        self.perm = None if row_perm is None else np.ascontiguousarray(np.asarray(row_perm), dtype=np.int32)
+
+    def args(self):
+        import ctypes
+
+        f = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+        return f(self.j1), f(self.j2), f(self.sel), f(self.cg), f(self.perm)
+
+
+class _NodeMapFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pos, tables):
+        lib = _lib.load()
+        p = pos.contiguous()
+        n = p.shape[0]
+        A = torch.empty((n, 20, 9), device=p.device, dtype=torch.float32)
+        check(lib.e2a_node_map_fwd(ptr(p), n, *tables.args(), ptr(A), stream_of(p.device)), "e2a_node_map_fwd")
+        ctx.save_for_backward(p)
+        ctx.tables = tables
+        return A
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        (p,) = ctx.saved_tensors
+        g = g.contiguous()
+        dp = torch.empty_like(p)
+        check(lib.e2a_node_map_bwd(ptr(p), ptr(g), p.shape[0], *ctx.tables.args(), ptr(dp), stream_of(p.device)),
+              "e2a_node_map_bwd")
+        return dp, None
+
+
+def node_map_from_pos(pos, tables):
+    """[n, 20, 9] per-node SO(2) maps from positions [n, 3] (CUDA; differentiable in ``pos``)."""
+    return _NodeMapFn.apply(pos.float(), tables)

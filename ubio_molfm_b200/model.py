@@ -299,14 +299,19 @@ class E2former(nn.Module):
         ``halo`` (domain decomposition): called on the node irreps before every block to refresh the
         rows of atoms owned by other ranks."""
         jd = [j.to(torch.float64) for j in self.Jd_list]
-        W, Wi = node_wigner(node_pos, self.lmax, self.l3_sequential, dtype=node_pos.dtype, jd=jd)
-        if pbc_any:
-            We, Wie = node_wigner(graph["f_exp_node_pos"], self.lmax, self.l3_sequential, dtype=node_pos.dtype,
-                                  jd=jd)
-        else:
-            We, Wie = W, Wi
         bd = dict(graph)
-        bd.update({"wigner": W, "wigner_inv": Wi, "wigner_exp": We, "wigner_inv_exp": Wie})
+        if node_pos.is_cuda and not self.training and self.lmax == 2:
+            # the attention layers form their per-node SO(2) maps from the positions directly
+            bd.update({"wigner": None, "wigner_inv": None, "wigner_exp": None, "wigner_inv_exp": None,
+                       "node_map_jd": list(self.Jd_list)})
+        else:
+            W, Wi = node_wigner(node_pos, self.lmax, self.l3_sequential, dtype=node_pos.dtype, jd=jd)
+            if pbc_any:
+                We, Wie = node_wigner(graph["f_exp_node_pos"], self.lmax, self.l3_sequential,
+                                      dtype=node_pos.dtype, jd=jd)
+            else:
+                We, Wie = W, Wi
+            bd.update({"wigner": W, "wigner_inv": Wi, "wigner_exp": We, "wigner_inv_exp": Wie})
         if node_pos.is_cuda and not self.training:
             # the basis is formed inside each consumer's first product (see linear.rbf_linear)
             f_dist_embedding = RbfSpec(graph["f_dist"], self.rbf.offset, self.rbf.coeff)

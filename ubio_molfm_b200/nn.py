@@ -304,6 +304,16 @@ class E2TensorProductSO2_FirstOrder(nn.Module):
         A = torch.bmm(wigner_inv, wigner[:, tp.selected_idx, :] * scale)
         return A if row_perm is None else A[:, row_perm]
 
+    def node_map_from_pos(self, pos, jd, row_perm=None):
+        """The same maps as :meth:`node_map`, formed by one kernel from the positions (``jd``: the
+        J matrices of degrees 0..2); the Wigner matrices are never materialised."""
+        key = (id(jd[1]), id(jd[2]), None if row_perm is None else tuple(row_perm))
+        cache = getattr(self, "_map_tables", None)
+        if cache is None or cache[0] != key:
+            tp = self.so2_tp
+            self._map_tables = (key, tc.NodeMapTables(jd, tp.selected_idx, tp.CG_weight, row_perm))
+        return tc.node_map_from_pos(pos, self._map_tables[1])
+
     def node_half(self, wigner, wigner_inv, h, pos):
         """W_inv @ (CG-select(W @ h) * |pos|): the per-node half of h (x) r.
 
