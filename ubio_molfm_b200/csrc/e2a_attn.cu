@@ -125,19 +125,20 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
 // once and serves both products:
 //   d_value[k] += beta[e,h] dout[i]                       (the value aggregation's transpose)
 //   d_beta[e,h] = sum_c dout[i,c,h] value[k,c,h]          (the aggregation's weight gradient)
-// The key's own value row stays in registers (each thread owns KS float4 slots, all of the same four
-// heads); d_beta partials of a batch of kVB edges are combined across the warps in shared memory.
+// The key's own value row sits in shared memory (each thread owns KS float4 slots, all of the same four
+// heads, and reads back only what it wrote), which keeps registers for 3 resident CTAs; d_beta partials of a batch of kVB edges are combined across the warps in shared memory.
 // Requires H dividing 1024 and H <= 128 (a thread's slots share heads, every warp covers all head
 // quads, one batch is one float4 per thread) and the [C,H] channel layout.
 // ------------------------------------------------------------------------------------------------
 template <int KS>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 k_value_bwd(const float* __restrict__ value, const float* __restrict__ dout, const float* __restrict__ beta, int H,
             int row_f4, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col,
             const int32_t* __restrict__ perm, const int32_t* __restrict__ order, int64_t n_rows,
             float* __restrict__ d_value, float* __restrict__ d_beta) {
   extern __shared__ float4 smem4[];
   float4* part = smem4;                       // [kWarps][kVB = 1024 / H][H / 4]
+  float4* vv = smem4 + kThreads * kWarps;     // the key's value row [row_f4]
   const int H4 = H / 4, vb = kThreads / H4;   // edges per batch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int hq = threadIdx.x % H4;            // this thread's head quad (heads 4 hq .. 4 hq + 3)
@@ -145,11 +146,11 @@ k_value_bwd(const float* __restrict__ value, const float* __restrict__ dout, con
     const int kk = row_of(order, r);
     const int rs = row_ptr[kk], re = row_ptr[kk + 1];
     const float4* vr = reinterpret_cast<const float4*>(value + (int64_t)kk * row_f4 * 4);
-    float4 vv[KS], acc[KS];
+    float4 acc[KS];
 #pragma unroll
-    for (int s = 0; s < KS; ++s) {
+    for (int s = 0; s < KS; ++s) {   // each thread reads back only the slots it wrote: no barrier
       const int f = threadIdx.x + s * kThreads;
-      vv[s] = f < row_f4 ? __ldg(vr + f) : f4_zero();
+      if (f < row_f4) vv[f] = __ldg(vr + f);
       acc[s] = f4_zero();
     }
     for (int p0 = rs; p0 < re; p0 += vb) {
@@ -166,7 +167,7 @@ k_value_bwd(const float* __restrict__ value, const float* __restrict__ dout, con
           if (f < row_f4) {
             const float4 x = __ldg(xr + f);
             acc[s] = f4_fma4(bw, x, acc[s]);
-            pt = f4_fma4(x, vv[s], pt);
+            pt = f4_fma4(x, vv[f], pt);
           }
         }
         // lanes of one warp cover head quads (32 * warp + lane) % H4; fold the warp's duplicates
@@ -768,7 +769,8 @@ int value_bwd_launch(const float* value, const float* dout, const float* beta, c
                      const int32_t* k_row_ptr, const int32_t* k_col, const int32_t* k_perm, const int32_t* key_order,
                      int64_t n_keys, float* d_value, float* d_beta, cudaStream_t st) {
   if (1024 % dm.H != 0 || dm.H > 128) return E2A_ERR_UNSUPPORTED;  // every warp covers all head quads
-  const size_t sm = (size_t)kWarps * kThreads * 16;  // kWarps x (1024 / H edges x H / 4 quads) float4
+  // kWarps x (1024 / H edges x H / 4 quads) float4 partials + the key's value row
+  const size_t sm = (size_t)kWarps * kThreads * 16 + (size_t)dm.CH4 * 16;
   E2A_DISPATCH_KS(ks, k_value_bwd, {
     E2A_CUDA(prep_smem(kf, sm));
     kf<<<grid_for(n_keys), kThreads, sm, st>>>(value, dout, beta, dm.H, dm.CH4, k_row_ptr, k_col, k_perm, key_order,
