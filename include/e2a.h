@@ -298,6 +298,20 @@ int e2a_rbf_fwd(const float* dist, int64_t n_edges, const float* mu, int nb, flo
 int e2a_rbf_bwd(const float* dist, const float* grad, int64_t n_edges, const float* mu, int nb, float coeff,
                 float* d_dist, void* stream);
 
+/* The radial basis fused into its consumers (GaussianSmearing, module_utils.py:1853-1870; the first   */
+/* layer of fc_easy / gbf_projs, e2former.py:134-138, 701-712):                                       */
+/* C[M,N] = rbf(dist)[M,K] B[N,K]^T (+ bias), rbf[m,k] = exp(coeff (dist[m] - mu[k])^2) formed on chip */
+/* (K <= 256; B / B_lo as in e2a_gemm_tf32x3).                                                        */
+int e2a_gemm_tf32x3_rbf(const float* dist, const float* mu, float coeff, const float* B, const float* B_lo,
+                        int64_t ldb, float* C, int64_t ldc, const float* bias, int64_t M, int64_t N, int64_t K,
+                        int passes, void* stream);
+/* The matching distance gradient without the [M, N] basis gradient: G = A[M,K] B[N,K]^T contracted in */
+/* the epilogue, partial[m, j] = sum_{n in [64 j, 64 j + 64)} G[m,n] rbf[m,n] 2 coeff (dist[m] - mu[n]); */
+/* d(dist)[m] = sum_j partial[m, j] (ld_partial >= ceil(N / 64)).                                     */
+int e2a_gemm_tf32x3_rbf_dist_grad(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb,
+                                  const float* dist, const float* mu, float coeff, float* partial, int64_t ld_partial,
+                                  int64_t M, int64_t N, int64_t K, int passes, void* stream);
+
 /* Per-node map of the first-order SO(2) product from the node position (fp64 inside):            */
 /* A[n,k,s] = |p| sum_j Wi^T[k,j] W[sel[j],s] cg[j] with W = blockdiag(D^0, D^1, D^2),                */
 /* D^l = J_l Y_l(-beta) J_l Y_l(-alpha) of the position's Euler angles (module_utils.py:182-337),     */

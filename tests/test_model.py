@@ -147,17 +147,19 @@ def test_nve_velocity_verlet_conserves_energy():
     assert md.nsteps == 20
 
 
-def test_rbf_linear_matches_materialised_basis():
-    """rbf_linear (basis formed inside the product, distance gradient reduced per edge) against the
-    GaussianSmearing module followed by a linear map, fp64 reference."""
+@pytest.mark.parametrize("E,nb,h", [(3000, 256, 128), (3001, 32, 16), (517, 36, 132), (700, 300, 64)])
+def test_rbf_linear_matches_materialised_basis(E, nb, h):
+    """rbf_linear (basis formed inside the GEMM's A tiles, distance gradient contracted in its
+    epilogue; the materialised fallback for nb > 256) against the GaussianSmearing module followed by
+    a linear map, fp64 reference.  Ragged edge counts, a basis narrower than one 64-column block and a
+    K that is not a multiple of the 16-wide slab."""
     from ubio_molfm_b200.linear import rbf_linear
     from ubio_molfm_b200.nn import GaussianSmearing
 
     g = torch.Generator().manual_seed(2)
-    E, nb, h = 3000, 256, 128
     rbf = GaussianSmearing(nb, cutoff=6.0)
     d = (torch.rand(E, generator=g, dtype=torch.float64) * 6.0).requires_grad_(True)
-    w = torch.randn(h, nb, generator=g, dtype=torch.float64) / 16
+    w = torch.randn(h, nb, generator=g, dtype=torch.float64) / (nb ** 0.5)
     b = torch.randn(h, generator=g, dtype=torch.float64)
     ref = rbf.double()(d) @ w.t() + b
     dg = d.detach().float().to(DEV).requires_grad_(True)

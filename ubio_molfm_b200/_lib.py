@@ -57,6 +57,8 @@ SIGNATURES = {
     "e2a_node_apply_fwd": (I32, [P, P, I64, P, I64, I64, I32, I32, I32, P, I64, I32, P]),
     "e2a_node_apply_bwd": (I32, [P, P, I64, P, I64, P, I64, I64, I32, I32, I32, P, I64, P, I64, P, P]),
     "e2a_rbf_fwd": (I32, [P, I64, P, I32, ctypes.c_float, P, P]),
+    "e2a_gemm_tf32x3_rbf": (I32, [P, P, ctypes.c_float, P, P, I64, P, I64, P, I64, I64, I64, I32, P]),
+    "e2a_gemm_tf32x3_rbf_dist_grad": (I32, [P, I64, P, P, I64, P, P, ctypes.c_float, P, I64, I64, I64, I64, I32, P]),
     "e2a_rbf_bwd": (I32, [P, P, I64, P, I32, ctypes.c_float, P, P]),
     "e2a_node_map_fwd": (I32, [P, I64, P, P, P, P, P, P, P]),
     "e2a_node_map_bwd": (I32, [P, P, I64, P, P, P, P, P, P, P]),

@@ -80,8 +80,8 @@ __device__ __forceinline__ void combine_stripes(float* red, float* out_s, int H,
 //   HEAD_INNER = false: rows are [H, D] (head = f / D, one head per float4, D % 4 == 0)
 // e_p = perm[p] (or p).  One CTA per output row, launched over the rows in `order`.
 // ------------------------------------------------------------------------------------------------
-template <int KS, bool HEAD_INNER>
-__global__ void __launch_bounds__(kThreads, 3)
+template <int KS, bool HEAD_INNER, int MINB = 3>
+__global__ void __launch_bounds__(kThreads, MINB)
 k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D, int row_f4,
           const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const int32_t* __restrict__ perm,
           const int32_t* __restrict__ order, int64_t n_rows, float* __restrict__ out) {
@@ -467,8 +467,8 @@ k_softmax_bwd(const float* __restrict__ q, const float* __restrict__ k, const fl
 // lane l owns heads [l*HPL, (l+1)*HPL), so every per-head row statistic is lane-local and the q.k
 // dot needs only the lane's own HPL*D-float slice of each k row (coalesced across the warp).
 // ------------------------------------------------------------------------------------------------
-template <int HPL, int D>
-__global__ void __launch_bounds__(kThreads)
+template <int HPL, int D, int MINB = 1>
+__global__ void __launch_bounds__(kThreads, MINB)
 k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
                    const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
                    const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
@@ -529,8 +529,8 @@ k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   *reinterpret_cast<float4*>(row_sum + (int64_t)i * H + lane * HPL) = make_float4(S[0], S[1], S[2], S[3]);
 }
 
-template <int HPL, int D>
-__global__ void __launch_bounds__(kThreads)
+template <int HPL, int D, int MINB = 1>
+__global__ void __launch_bounds__(kThreads, MINB)
 k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
                    const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
                    const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
@@ -697,7 +697,7 @@ cudaError_t prep_smem(Kern kern, size_t smem) {
 template <int KS>
 void agg_ch(const float* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
             const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
-  k_row_agg<KS, true><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
+  k_row_agg<KS, true, 4><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
                                                              n_rows, out);
 }
 
@@ -749,7 +749,7 @@ int bwd_query_launch(const float* q, const float* k, const float* value, const f
   }
   E2A_CHECK_LAUNCH();
   if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
-    k_softmax_bwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+    k_softmax_bwd_warp<4, 8, 3><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
         q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
         d_inputhead, ld_dgi, d_poly, d_dist, d_logit, bufA, bufB);
   } else {
@@ -788,7 +788,7 @@ int softmax_bwd_dq_launch(const float* q, const float* k, const float* gate, con
                           float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
                           float* bufB, cudaStream_t st) {
   if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
-    k_softmax_bwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+    k_softmax_bwd_warp<4, 8, 3><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
         q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
         d_inputhead, ld_dgi, d_poly, d_dist, d_logit, d_beta, bufB);
   } else {
@@ -820,7 +820,8 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value, const float
   if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   if (warp_softmax_ok(dm, ld_gi)) {
-    k_softmax_fwd_warp<4, 8><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+    // 64 registers: 4 CTAs (32 warps) per SM keep more k-row gathers in flight
+    k_softmax_fwd_warp<4, 8, 4><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
         q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum);
   } else {
     const size_t ssm = softmax_smem(dm, 2);

@@ -300,7 +300,7 @@ constexpr int WS_LD = WS_EH + 4;                 // staging row stride (floats)
 constexpr int WS_EPI = WS_DRAIN * 32 * WS_LD * 4;
 constexpr uint32_t kWsTmemCols = WS_CHAINS * BN;
 template <int BK>
-constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024; }
+constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024 + 1024; }
 
 __device__ __forceinline__ float tf32_lo(float a, float h) { return tf32_hi(a - h); }
 
@@ -354,12 +354,26 @@ __device__ unsigned long long g_ws_trace[8][512];
 #define WS_TRACE(k, i) do { } while (0)
 #endif
 
+// Gaussian radial basis rbf[m, k] = exp(coeff (d[m] - mu[k])^2) (module_utils.py:1853-1870) as a GEMM
+// operand or epilogue factor:
+//  * gen (d set, rdot null): A is not read; the splitter warps form A's tile from d and mu on chip;
+//  * rdot (rdot set): the epilogue writes no C but, per row and 64-column block of the tile,
+//    rdot[m, n / 64] = sum_n acc[m, n] * rbf[m, n] * 2 coeff (d[m] - mu[n])   (d rbf / d d, contracted).
+struct RbfArgs {
+  const float* d;
+  const float* mu;
+  float coeff;
+  float* rdot;
+  int64_t ld_rdot;
+};
+
 template <int BK_>
 __global__ void __launch_bounds__(WsCfg<BK_>::THREADS, 1)
 k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
           const __grid_constant__ CUtensorMap tmBl, int b_split, float* C, int64_t ldc, const float* __restrict__ bias, float* P,
-          int64_t ldp, int M, int N, int K, int accumulate, int passes) {
+          int64_t ldp, int M, int N, int K, int accumulate, int passes, const RbfArgs rb) {
   using Cfg = WsCfg<BK_>;
+  const bool gen = BK_ == 16 && rb.d != nullptr && rb.rdot == nullptr;   // A formed on chip
   extern __shared__ uint8_t ws_raw[];
   uint8_t* smem = ws_raw + ((1024u - (e2a_smem_u32(ws_raw) & 1023u)) & 1023u);
   uint8_t* stages = smem;
@@ -372,6 +386,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   uint64_t* tempty = tfull + WS_CHAINS;           // chain buffer drained  (128 arrives)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* mu_s = reinterpret_cast<float*>(tmem_slot + 4);   // gen: the basis offsets (K <= 256)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = (N + BN - 1) / BN;
   const int tiles = ((M + BM - 1) / BM) * tiles_n;
@@ -394,6 +409,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     *abort_flag = 0;
     e2a_fence_mbar_init();
   }
+  if (gen)
+    for (int k = threadIdx.x; k < 256; k += blockDim.x) mu_s[k] = k < K ? __ldg(rb.mu + k) : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -405,7 +422,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
       if (b_split) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmBl)) : "memory");
-      const uint32_t bytes = (b_split ? 3 : 2) * Cfg::TILE;
+      const uint32_t bytes = (b_split ? 2 : 1) * Cfg::TILE + (gen ? 0 : Cfg::TILE);
       uint32_t n = 0;
       bool run = true;
       for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
@@ -416,7 +433,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           WS_TRACE(0, n);
           uint8_t* st = stages + s * Cfg::STAGE;
           mbar_expect_tx(&full[s], bytes);
-          tma_load_2d(st, &tmA, kb * Cfg::BK, m0, &full[s]);
+          if (!gen) tma_load_2d(st, &tmA, kb * Cfg::BK, m0, &full[s]);
           tma_load_2d(st + 2 * Cfg::TILE, &tmB, kb * Cfg::BK, n0, &full[s]);
           if (b_split) tma_load_2d(st + 3 * Cfg::TILE, &tmBl, kb * Cfg::BK, n0, &full[s]);
         }
@@ -467,6 +484,15 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 320;
     uint32_t n = 0;
     bool run = true;
+    float dreg[8], dnext[8];   // gen: the distances of this thread's 8 rows in this / the next tile
+    if (gen) {
+      const int m0 = ((int)blockIdx.x / tiles_n) * BM;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int row = m0 + (t >> 2) + 16 * j;
+        dnext[j] = (int)blockIdx.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
+      }
+    }
     for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
       for (int kb = 0; kb < nk; ++kb, ++n) {
         const uint32_t s = n % Cfg::STAGES;
@@ -486,7 +512,57 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             *reinterpret_cast<float4*>(st + Cfg::TILE + off) = l;
           }
         };
-        if (b_split) split(IntC<Cfg::TILE / 16 / Cfg::SPLIT>{});
+        if (gen) {
+          if constexpr (BK_ == 16) {
+            // A's tile from the basis.  Float4 slot idx = t + SPLIT j of the 64-byte-swizzled [BM][16] tile
+            // holds row r = idx / 4 = t / 4 + 16 j and logical 16-byte chunk (idx % 4) ^ ((r / 2) % 4),
+            // which is (t % 4) ^ ((t / 8) % 4) for every j: one mu float4 per slab, the rows' distances
+            // loaded once per tile.
+            static_assert(Cfg::SPLIT == 64 && Cfg::TILE / 16 / Cfg::SPLIT == 8, "BK 16 slot map");
+            const int c = (t & 3) ^ ((t >> 3) & 3);
+            const int k0 = kb * Cfg::BK + 4 * c;
+            if (kb == 0) {   // this tile's distances (prefetched a tile ahead), then the next tile's
+              const int m1 = ((tile + (int)gridDim.x) / tiles_n) * BM;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                dreg[j] = dnext[j];
+                const int row = m1 + (t >> 2) + 16 * j;
+                dnext[j] = tile + (int)gridDim.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
+              }
+            }
+            float mu[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) mu[u] = mu_s[(k0 + u) & 255];
+            const float c2 = rb.coeff * 1.44269504088896341f;   // exp(a) = 2^(a log2 e)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int idx = t + j * Cfg::SPLIT;
+              float v[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float x = dreg[j] - mu[u];
+                v[u] = k0 + u < K ? exp2f(c2 * (x * x)) : 0.f;
+              }
+              float4 h, l;
+              h.x = tf32_hi(v[0]); h.y = tf32_hi(v[1]); h.z = tf32_hi(v[2]); h.w = tf32_hi(v[3]);
+              l.x = tf32_lo(v[0], h.x); l.y = tf32_lo(v[1], h.y); l.z = tf32_lo(v[2], h.z); l.w = tf32_lo(v[3], h.w);
+              *reinterpret_cast<float4*>(st + idx * 16) = h;
+              *reinterpret_cast<float4*>(st + Cfg::TILE + idx * 16) = l;
+            }
+            if (!b_split) {   // B's tile still needs its split
+#pragma unroll
+              for (int j = 0; j < Cfg::TILE / 16 / Cfg::SPLIT; ++j) {
+                const int off = 2 * Cfg::TILE + (t + j * Cfg::SPLIT) * 16;
+                const float4 v = *reinterpret_cast<const float4*>(st + off);
+                float4 h, l;
+                h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
+                l.x = tf32_lo(v.x, h.x); l.y = tf32_lo(v.y, h.y); l.z = tf32_lo(v.z, h.z); l.w = tf32_lo(v.w, h.w);
+                *reinterpret_cast<float4*>(st + off) = h;
+                *reinterpret_cast<float4*>(st + Cfg::TILE + off) = l;
+              }
+            }
+          }
+        } else if (b_split) split(IntC<Cfg::TILE / 16 / Cfg::SPLIT>{});
         else split(IntC<2 * Cfg::TILE / 16 / Cfg::SPLIT>{});
         e2a_fence_proxy_async();
         mbar_arrive(&split_done[s]);
@@ -527,6 +603,22 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         if (threadIdx.x == 128) WS_TRACE(5, c);
       }
       if (!run) break;
+      if (rb.rdot) {   // contract this warp's 64 columns with d rbf / d d; no C
+        const int row = m0 + 32 * q + lane;
+        if (row < M && n0 < N) {
+          const float dv = __ldg(rb.d + row);
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < WS_DCOLS; ++j) {   // fully unrolled: acc stays in registers
+            if (n0 + j < N) {
+              const float x = dv - __ldg(rb.mu + n0 + j);
+              sum += acc[j] * expf(rb.coeff * (x * x)) * (2.f * rb.coeff * x);
+            }
+          }
+          rb.rdot[(int64_t)row * rb.ld_rdot + n0 / WS_DCOLS] = sum;
+        }
+        continue;
+      }
       // epilogue: stage this warp's 32 rows x 64 columns 16 columns at a time, then write them row by
       // row (4 lanes per row, 8 rows per step)
 #pragma unroll
@@ -647,15 +739,18 @@ __global__ void k_tf32_split(const float* __restrict__ B, int64_t ldb, int64_t N
 // Launches the warp-specialised kernel; E2A_ERR_UNSUPPORTED when the operands do not suit it.
 static int launch_ws(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
                      int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
-                     int accumulate, int passes, cudaStream_t st) {
+                     int accumulate, int passes, cudaStream_t st, RbfArgs rb = RbfArgs{nullptr, nullptr, 0.f, nullptr, 0}) {
+  const bool gen = rb.d != nullptr && rb.rdot == nullptr;
+  if (gen) { A = B; lda = ldb; }   // the A map is never read
   const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
                    ((reinterpret_cast<uintptr_t>(B) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(B_lo) & 15u) == 0);
   if (!vec || K == 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return E2A_ERR_UNSUPPORTED;
   EncodeTiledFn enc = tensor_map_encoder();
   if (!enc) return E2A_ERR_UNSUPPORTED;
   const int bk = K <= 256 ? 16 : 32;
+  if (gen && bk != 16) return E2A_ERR_UNSUPPORTED;
   CUtensorMap ta, tb, tbl;
-  if (!make_map_2d(enc, &ta, A, M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
+  if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
       !make_map_2d(enc, &tbl, B_lo ? B_lo : B, N, K, ldb, bk))
     return E2A_ERR_UNSUPPORTED;
   int dev = 0, sms = 0;
@@ -667,11 +762,11 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
   if (bk == 16) {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<16>()));
     k_gemm_ws<16><<<grid, WsCfg<16>::THREADS, ws_smem<16>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
-                                                            (int)N, (int)K, accumulate, passes);
+                                                            (int)N, (int)K, accumulate, passes, rb);
   } else {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32>()));
     k_gemm_ws<32><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
-                                                            (int)N, (int)K, accumulate, passes);
+                                                            (int)N, (int)K, accumulate, passes, rb);
   }
   E2A_CHECK_LAUNCH();
   return E2A_OK;
@@ -706,6 +801,28 @@ int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const 
   if (M == 0 || N == 0) return E2A_OK;
   if (!P || (K > 0 && (!A || !B)) || lda < K || ldb < K || (C && ldc < N) || ldp < N / 2) return E2A_ERR_ARG;
   return launch_ws(A, lda, B, B_lo, ldb, C, ldc, bias, P, ldp, M, N, K, accumulate, passes, (cudaStream_t)stream);
+}
+
+int e2a_gemm_tf32x3_rbf(const float* dist, const float* mu, float coeff, const float* B, const float* B_lo,
+                        int64_t ldb, float* C, int64_t ldc, const float* bias, int64_t M, int64_t N, int64_t K,
+                        int passes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!C || !dist || !mu || !B || K == 0 || ldb < K || ldc < N) return E2A_ERR_ARG;
+  if (K > 256) return E2A_ERR_UNSUPPORTED;
+  return launch_ws(nullptr, 0, B, B_lo, ldb, C, ldc, bias, nullptr, 0, M, N, K, 0, passes, (cudaStream_t)stream,
+                   RbfArgs{dist, mu, coeff, nullptr, 0});
+}
+
+int e2a_gemm_tf32x3_rbf_dist_grad(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb,
+                                  const float* dist, const float* mu, float coeff, float* partial, int64_t ld_partial,
+                                  int64_t M, int64_t N, int64_t K, int passes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!A || !B || !dist || !mu || !partial || K == 0 || lda < K || ldb < K || ld_partial < (N + 63) / 64)
+    return E2A_ERR_ARG;
+  return launch_ws(A, lda, B, B_lo, ldb, nullptr, 0, nullptr, nullptr, 0, M, N, K, 0, passes, (cudaStream_t)stream,
+                   RbfArgs{dist, mu, coeff, partial, ld_partial});
 }
 
 int e2a_tf32_split(const float* B, int64_t ldb, int64_t N, int64_t K, float* B_hi, float* B_lo, int64_t ldo,

@@ -471,20 +471,33 @@ def gate(s, h, c_scalar, c_vector):
 # Gaussian radial basis consumed by a linear map, formed on the fly (inference path)
 # ------------------------------------------------------------------------------------------------
 class _RbfLinearFn(torch.autograd.Function):
-    """``h = rbf(d) W^T (+ b)`` with rbf[e,k] = exp(coeff (d_e - mu_k)^2): the basis is formed for the
-    product and dropped; the backward forms d(rbf) = g W and reduces it to d(d) per edge with the basis
-    recomputed, so only [E] vectors reach the distance's other consumers."""
+    """``h = rbf(d) W^T (+ b)`` with rbf[e,k] = exp(coeff (d_e - mu_k)^2) formed inside the GEMM (its
+    splitter warps build each A tile from d and mu; the basis never reaches HBM).  The backward forms
+    d(rbf) = g W tile by tile and contracts it with d rbf / d d in the GEMM's epilogue, so only [E]
+    vectors reach the distance's other consumers."""
+
+    @staticmethod
+    def fused_ok(nb, n_out):
+        return PRESPLIT_WEIGHTS and 0 < nb <= 256 and nb % 4 == 0 and n_out % 4 == 0
 
     @staticmethod
     def forward(ctx, dist, mu, coeff, w, b):
         lib = _lib.load()
         d = dist.contiguous()
         E, nb = d.shape[0], mu.shape[0]
-        rbf = torch.empty((E, nb), device=d.device, dtype=torch.float32)
-        check(lib.e2a_rbf_fwd(ptr(d), E, ptr(mu), nb, float(coeff), ptr(rbf), stream_of(d.device)), "e2a_rbf_fwd")
-        h = gemm(rbf, w, b)
+        N = w.shape[0]
         ctx.save_for_backward(d, mu, w)
         ctx.coeff = float(coeff)
+        ctx.fused = _RbfLinearFn.fused_ok(nb, N)
+        if not ctx.fused:   # basis materialised for the product, then dropped
+            rbf = torch.empty((E, nb), device=d.device, dtype=torch.float32)
+            check(lib.e2a_rbf_fwd(ptr(d), E, ptr(mu), nb, float(coeff), ptr(rbf), stream_of(d.device)),
+                  "e2a_rbf_fwd")
+            return gemm(rbf, w, b)
+        h = torch.empty((E, N), device=d.device, dtype=torch.float32)
+        hi, lo = split_tf32(w)
+        check(lib.e2a_gemm_tf32x3_rbf(ptr(d), ptr(mu), float(coeff), ptr(hi), ptr(lo), nb, ptr(h), N, ptr(b), E, N,
+                                      nb, PASSES, stream_of(d.device)), "e2a_gemm_tf32x3_rbf")
         return h
 
     @staticmethod
@@ -492,11 +505,21 @@ class _RbfLinearFn(torch.autograd.Function):
         lib = _lib.load()
         d, mu, w = ctx.saved_tensors
         g = g.contiguous()
-        d_rbf = gemm(g, w.t().contiguous())
-        dd = torch.empty_like(d)
-        check(lib.e2a_rbf_bwd(ptr(d), ptr(d_rbf), d.shape[0], ptr(mu), mu.shape[0], ctx.coeff, ptr(dd),
-                              stream_of(d.device)), "e2a_rbf_bwd")
-        return dd, None, None, None, None
+        E, nb, Kh = d.shape[0], mu.shape[0], w.shape[0]
+        if not ctx.fused:
+            d_rbf = gemm(g, w.t().contiguous())
+            dd = torch.empty_like(d)
+            check(lib.e2a_rbf_bwd(ptr(d), ptr(d_rbf), E, ptr(mu), nb, ctx.coeff, ptr(dd), stream_of(d.device)),
+                  "e2a_rbf_bwd")
+            return dd, None, None, None, None
+        wt = w.t().contiguous()           # [nb, Kh]: d(rbf) = g @ w
+        hi, lo = split_tf32(wt)
+        nblk = (nb + 63) // 64
+        part = torch.empty((E, nblk), device=d.device, dtype=torch.float32)
+        check(lib.e2a_gemm_tf32x3_rbf_dist_grad(ptr(g), Kh, ptr(hi), ptr(lo), Kh, ptr(d), ptr(mu), ctx.coeff,
+                                                ptr(part), nblk, E, nb, Kh, PASSES, stream_of(d.device)),
+              "e2a_gemm_tf32x3_rbf_dist_grad")
+        return part.sum(1), None, None, None, None
 
 
 def rbf_linear(dist, mu, coeff, w, b=None):
