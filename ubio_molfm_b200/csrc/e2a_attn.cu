@@ -92,7 +92,28 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
 #pragma unroll
     for (int s = 0; s < KS; ++s) acc[s] = f4_zero();
     const int h0 = HEAD_INNER ? (4 * threadIdx.x) % H : 0;
-    for (int p = rs; p < re; ++p) {
+    int p = rs;
+    if constexpr (!HEAD_INNER && KS == 1) {
+      // one float4 per thread and edge: gather four edges at a time (more loads in flight), then
+      // accumulate them in CSR order (the same sum, term by term)
+      const int f = threadIdx.x;
+      if (f < row_f4) {
+        const int hcol = (4 * f) / D;
+        for (; p + 4 <= re; p += 4) {
+          float4 x[4];
+          float wv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t e = perm ? perm[p + u] : p + u;
+            x[u] = ldg4(X + (int64_t)col[p + u] * row_f4 * 4 + 4 * f);
+            wv[u] = __ldg(w + e * H + hcol);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) acc[0] = f4_fma(wv[u], x[u], acc[0]);
+        }
+      }
+    }
+    for (; p < re; ++p) {
       const int64_t e = perm ? perm[p] : p;
       const float* xr = X + (int64_t)col[p] * row_f4 * 4;
       if (HEAD_INNER) {
@@ -697,7 +718,7 @@ cudaError_t prep_smem(Kern kern, size_t smem) {
 template <int KS>
 void agg_ch(const float* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
             const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
-  k_row_agg<KS, true, 4><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
+  k_row_agg<KS, true, (KS >= 16 ? 2 : 4)><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
                                                              n_rows, out);
 }
 
