@@ -209,12 +209,13 @@ def bwdk_algorithmic_bytes(N, N2, E):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of each span entry point (sum over its kernels),
-# one ncu capture of the default workload (1e5 atoms, k = 32); summary in profiles/attn_kernels_dram_100k.txt.
-MEASURED_TRAFFIC_DEFAULT = {"e2a_attn_fwd": 20.52e9, "e2a_attn_bwd_value": 16.78e9,
-                            "e2a_attn_bwd_softmax": 25.52e9, "e2a_attn_bwd_dk": 2.74e9}
-# the same per-launch figures for the default model workload (blob in water, 97,862 atoms); filled from
-# one ncu capture of that workload (profiles/model_100k_launches.md), empty until captured
-MEASURED_TRAFFIC_MODEL = {}
+# one ncu capture of the layer workload (1e5 atoms, k = 32); summary in profiles/attn_kernels_dram_100k.txt.
+MEASURED_TRAFFIC_DEFAULT = {"e2a_attn_fwd": 22.89e9, "e2a_attn_bwd_value": 17.01e9,
+                            "e2a_attn_bwd_softmax": 26.97e9, "e2a_attn_bwd_dk": 2.74e9}
+# the same per-launch figures for the default model workload (blob in water, 97,865 atoms, mean over its
+# four layers), from one ncu capture of that workload (profiles/attn_kernels_dram_100k.txt)
+MEASURED_TRAFFIC_MODEL = {"e2a_attn_fwd": 23.77e9, "e2a_attn_bwd_value": 16.88e9,
+                          "e2a_attn_bwd_softmax": 26.51e9, "e2a_attn_bwd_dk": 2.74e9}
 
 
 def bwdv_algorithmic_bytes(N, N2, E):
