@@ -294,6 +294,64 @@ def test_attention_span_row_order_and_determinism():
         assert torch.equal(x, y)  # independent of the processing order
 
 
+def test_attention_span_full_size_sampled_rows():
+    """Full-size span (1e5 rows, 1.2e5 keys, ~3.2M edges, H = 128, D = 8, C = 58): the CUDA forward and
+    backward over the whole graph, checked on seeded samples against the fp64 oracle run on the
+    sub-problem those samples depend on -- sampled rows (with all their edges) for out, d_q and the
+    per-edge gradients, and sampled keys (with every row that reaches them, complete) for d_value and
+    d_k, which are then exact full-graph sums."""
+    from ubio_molfm_b200 import ops
+
+    N, M, H, D, C = 100_000, 120_000, 128, 8, 58
+    rng = np.random.default_rng(21)
+    deg = rng.integers(20, 45, N)
+    deg[rng.choice(N, 50, replace=False)] = 0                      # some isolated rows
+    q = np.repeat(np.arange(N), deg)
+    n = rng.integers(0, M, len(q))
+    E = len(q)
+    g = torch.Generator(device=DEV).manual_seed(22)
+    Q = torch.randn(N, H, D, generator=g, device=DEV) / D ** 0.5
+    K = torch.randn(M, H, D, generator=g, device=DEV)
+    V = torch.randn(M, C, H, generator=g, device=DEV)
+    G = torch.randn(E, 2 * H, generator=g, device=DEV)
+    P = torch.rand(E, generator=g, device=DEV)
+    Dd = 1.0 + 4 * torch.rand(E, generator=g, device=DEV)
+    W = torch.randn(N, C, H, generator=g, device=DEV)
+    md = ops.prepare_sparse_qk_edge_index_metadata(_t(q), _t(n), N, M)
+    ins = [Q, K, V, G, P, Dd]
+    ag = [a.clone().requires_grad_(True) for a in ins]
+    out = ops.attention_span(*ag, md)
+    grads = torch.autograd.grad(out, ag, W)
+    del ag
+
+    row_ptr = np.concatenate([[0], np.cumsum(deg)])
+    keys = rng.choice(np.unique(n), 4, replace=False)
+    rows = np.union1d(rng.choice(np.nonzero(deg)[0], 24, replace=False), np.unique(q[np.isin(n, keys)]))
+    rows = np.union1d(rows, np.nonzero(deg == 0)[0][:2])
+    eidx = np.concatenate([np.arange(row_ptr[r], row_ptr[r + 1]) for r in rows])
+    ukeys, nsub = np.unique(n[eidx], return_inverse=True)
+    qsub = np.repeat(np.arange(len(rows)), deg[rows])
+    et, rt, kt = (torch.as_tensor(x, device=DEV) for x in (eidx, rows, ukeys))
+    sub = [Q[rt], K[kt], V[kt], G[et], P[et], Dd[et]]
+    ar = [a.cpu().double().requires_grad_(True) for a in sub]
+    ref = R.attention_span(*ar, torch.as_tensor(qsub), torch.as_tensor(nsub), len(rows))
+    gref = torch.autograd.grad(ref, ar, W[rt].cpu().double())
+
+    def close(a, b, rel, what):
+        tol = rel * max(b.abs().max().item(), 1.0)
+        assert (a.cpu().double() - b).abs().max().item() <= tol, what
+
+    close(out[rt], ref, 2e-5, "out")
+    assert torch.all(out[torch.as_tensor(np.nonzero(deg == 0)[0], device=DEV)] == 0)
+    close(grads[0][rt], gref[0], 5e-5, "d_q")
+    for name, i in (("d_gate", 3), ("d_poly", 4), ("d_dist", 5)):
+        close(grads[i][et], gref[i], 5e-5, name)
+    kpos = torch.as_tensor(np.searchsorted(ukeys, keys))
+    kt_s = torch.as_tensor(keys, device=DEV)
+    close(grads[1][kt_s], gref[1][kpos], 5e-5, "d_k")
+    close(grads[2][kt_s], gref[2][kpos], 5e-5, "d_value")
+
+
 # ------------------------------------------------------------------------------------------------
 # full layer against the reference's golden vectors
 # ------------------------------------------------------------------------------------------------

@@ -41,20 +41,28 @@ __device__ __forceinline__ float e2a_warp_sum(float v) {
   return v;
 }
 
+// Two independent round-to-nearest fp32 fmas in one instruction (Blackwell's packed f32x2 pipe):
+// the same results as two fmaf calls, half the issue slots.
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+
 __device__ __forceinline__ float4 f4_fma(float s, float4 v, float4 acc) {
-  acc.x = fmaf(s, v.x, acc.x);
-  acc.y = fmaf(s, v.y, acc.y);
-  acc.z = fmaf(s, v.z, acc.z);
-  acc.w = fmaf(s, v.w, acc.w);
-  return acc;
+  const float2 ss = make_float2(s, s);
+  const float2 lo = f2_fma(ss, make_float2(v.x, v.y), make_float2(acc.x, acc.y));
+  const float2 hi = f2_fma(ss, make_float2(v.z, v.w), make_float2(acc.z, acc.w));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
 __device__ __forceinline__ float4 f4_fma4(float4 s, float4 v, float4 acc) {
-  acc.x = fmaf(s.x, v.x, acc.x);
-  acc.y = fmaf(s.y, v.y, acc.y);
-  acc.z = fmaf(s.z, v.z, acc.z);
-  acc.w = fmaf(s.w, v.w, acc.w);
-  return acc;
+  const float2 lo = f2_fma(make_float2(s.x, s.y), make_float2(v.x, v.y), make_float2(acc.x, acc.y));
+  const float2 hi = f2_fma(make_float2(s.z, s.w), make_float2(v.z, v.w), make_float2(acc.z, acc.w));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
