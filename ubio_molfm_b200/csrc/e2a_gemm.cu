@@ -284,7 +284,10 @@ struct WsCfg {
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
   static constexpr int STAGE = 4 * TILE;                 // A (raw, then hi in place), A_lo, B (same), B_lo
   static constexpr int NBARS = 3 * STAGES + 8;           // + 2 x WS_CHAINS
-  static constexpr int SPLIT = BK == 16 ? 64 : 128;      // splitter threads (warps 2-3, and 12-13 for BK 32)
+#ifndef E2A_WS_SPLIT16
+#define E2A_WS_SPLIT16 128
+#endif
+  static constexpr int SPLIT = BK == 16 ? E2A_WS_SPLIT16 : 128;   // splitter threads (warps 2-3, + 12-13)
   static constexpr int THREADS = 384 + (SPLIT - 64);      // + 8 drain warps (4-11)
   static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
     // K-major; LBO unused (1); SBO = 8 rows x row bytes; version 1; swizzle 64 B (4) or 128 B (2)
@@ -488,8 +491,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     if (gen) {
       const int m0 = ((int)blockIdx.x / tiles_n) * BM;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int row = m0 + (t >> 2) + 16 * j;
+      for (int j = 0; j < Cfg::TILE / 16 / Cfg::SPLIT && j < 8; ++j) {
+        const int row = m0 + (t >> 2) + (Cfg::SPLIT / 4) * j;
         dnext[j] = (int)blockIdx.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
       }
     }
@@ -515,18 +518,19 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         if (gen) {
           if constexpr (BK_ == 16) {
             // A's tile from the basis.  Float4 slot idx = t + SPLIT j of the 64-byte-swizzled [BM][16] tile
-            // holds row r = idx / 4 = t / 4 + 16 j and logical 16-byte chunk (idx % 4) ^ ((r / 2) % 4),
+            // holds row r = idx / 4 = t / 4 + (SPLIT / 4) j and logical 16-byte chunk (idx % 4) ^ ((r / 2) % 4),
             // which is (t % 4) ^ ((t / 8) % 4) for every j: one mu float4 per slab, the rows' distances
             // loaded once per tile.
-            static_assert(Cfg::SPLIT == 64 && Cfg::TILE / 16 / Cfg::SPLIT == 8, "BK 16 slot map");
+            constexpr int NJ = Cfg::TILE / 16 / Cfg::SPLIT, RS = Cfg::SPLIT / 4;   // slots, row stride
+            static_assert(NJ * Cfg::SPLIT * 16 == Cfg::TILE && NJ <= 8, "BK 16 slot map");
             const int c = (t & 3) ^ ((t >> 3) & 3);
             const int k0 = kb * Cfg::BK + 4 * c;
             if (kb == 0) {   // this tile's distances (prefetched a tile ahead), then the next tile's
               const int m1 = ((tile + (int)gridDim.x) / tiles_n) * BM;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < NJ; ++j) {
                 dreg[j] = dnext[j];
-                const int row = m1 + (t >> 2) + 16 * j;
+                const int row = m1 + (t >> 2) + RS * j;
                 dnext[j] = tile + (int)gridDim.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
               }
             }
@@ -535,7 +539,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             for (int u = 0; u < 4; ++u) mu[u] = mu_s[(k0 + u) & 255];
             const float c2 = rb.coeff * 1.44269504088896341f;   // exp(a) = 2^(a log2 e)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < NJ; ++j) {
               const int idx = t + j * Cfg::SPLIT;
               float v[4];
 #pragma unroll
