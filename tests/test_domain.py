@@ -86,6 +86,70 @@ def test_domain_decomposition_equals_single_gpu():
     assert "DOMAIN_OK" in res.stdout, res.stdout[-3000:]
 
 
+class _LocalPlan:
+    """HaloPlan stand-in without collectives: the same ordering of the ghost rows."""
+
+    def __init__(self, own_gid, ghost_gid, ghost_owner, world, rank, group=None):
+        self.n_own = own_gid.numel()
+        order = torch.argsort(ghost_owner * (int(ghost_gid.max()) + 1 if ghost_gid.numel() else 1) + ghost_gid)
+        self.ghost_gid = ghost_gid[order]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("restrict", [True, False])
+def test_domain_slab_on_one_gpu_matches_full_system(restrict, monkeypatch):
+    """One rank's slab of a 2-rank decomposition, on one GPU, with the halo exchange replaced by the
+    full system's own block inputs for the ghost rows: the owned atoms' per-atom energies equal the
+    full-system ones, with the ghosts as keys only (``n_query`` = owned rows: no query-side, output or
+    FFN work on them) and with every row computed."""
+    from ubio_molfm_b200 import domain
+    from ubio_molfm_b200.model import E2FormerPotential
+    from ubio_molfm_b200.synthetic import bio_box, seeded_params_
+
+    cfg = dict(irreps_node_embedding="128x0e+128x1e+128x2e", num_layers=2, max_neighbors=32, max_radius=4.5,
+               number_of_basis=32, num_attn_heads=64, attn_scalar_head=8, irreps_head="2x0e+2x1e+2x2e",
+               norm_layer="rms_norm_sh", alpha_drop=0.0, atom_type_cnt=256, avg_degree=23.0)
+    model = E2FormerPotential(**cfg)
+    seeded_params_(model.decoder, 21)
+    seeded_params_(model.energy_head, 22)
+    model = model.cuda().eval()
+    dec = model.decoder
+    pos, Z, cell = bio_box(n_atoms=900, seed=5)
+    pos = torch.tensor(pos, dtype=torch.float32, device="cuda")
+    Z = torch.tensor(Z, device="cuda")
+    pbc = (True, True, True)
+
+    inputs = []
+    hooks = [b.register_forward_pre_hook(lambda m, a, kw: inputs.append(kw["node_irreps"].detach()),
+                                         with_kwargs=True) for b in dec.blocks]
+    with torch.no_grad():
+        g, pbc_any = model.build_graph(pos, torch.tensor(cell, dtype=torch.float32), pbc, None)
+        x_full = dec(pos, Z, g, pbc_any)
+        e_full = model.energy_head(x_full[:, 0]).squeeze(-1)
+    for h in hooks:
+        h.remove()
+    assert len(inputs) == cfg["num_layers"]
+
+    monkeypatch.setattr(domain, "HaloPlan", _LocalPlan)
+    plan, own_gid, local_gid, geom = domain.domain_graph(pos, cell, pbc, dec.max_radius, dec.max_neighbors, 2, 0)
+    assert 0 < plan.n_own < pos.shape[0] and plan.ghost_gid.numel() > 0
+    step = iter(range(cfg["num_layers"]))
+
+    def halo(t):
+        return torch.cat([t[:plan.n_own], inputs[next(step)][plan.ghost_gid]], dim=0)
+
+    with torch.no_grad():
+        pos_local = pos[local_gid]
+        graph = domain.local_graph(pos_local, geom, local_gid.numel(), dec.max_radius,
+                                   n_query=plan.n_own if restrict else None)
+        x = dec(pos_local, Z[local_gid], graph, True, halo=halo)
+        e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1)
+    if restrict:
+        assert x.shape[0] == plan.n_own   # the blocks returned the query rows only
+    ref = e_full[own_gid]
+    assert (e_own - ref).abs().max().item() <= 1e-5 * ref.abs().max().item() + 1e-6
+
+
 def test_shard_molecules_balances_and_partitions():
     from ubio_molfm_b200.domain import shard_molecules
 

@@ -110,10 +110,12 @@ class E2AttentionArbOrder_sparse(nn.Module):
                 poly_dist=None, attn_mask=None, batch=None, batched_data=None, **kwargs):
         if self.training and self.alpha_drop > 0:
             raise NotImplementedError("attention dropout (training) is not part of the inference path")
-        N1 = node_irreps_input.shape[0]
+        bd = batched_data
+        n_all = node_irreps_input.shape[0]
+        # rows [0, N1) are queries (all rows unless the graph says otherwise: domain ghosts are keys only)
+        N1 = int(bd.get("n_query", n_all))
         H = self.num_attn_heads
         C = self.scalar_dim
-        bd = batched_data
         outcell = bd["f_outcell_index"]
         N2 = outcell.shape[0]
         query_idx = bd["query_idx"].to(torch.long)
@@ -121,7 +123,7 @@ class E2AttentionArbOrder_sparse(nn.Module):
         metadata = bd["metadata"]
         x = node_irreps_input
 
-        query = self.query_linear(x).reshape(N1, H, -1)
+        query = self.query_linear(x if N1 == n_all else x[:N1]).reshape(N1, H, -1)
         key = self.key_linear(x)[outcell].reshape(N2, H, -1)
         q_scaled = query / math.sqrt(query.shape[-1])
         gate = self.edge_gate(attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx)
@@ -163,14 +165,14 @@ class E2AttentionArbOrder_sparse(nn.Module):
         if fused:
             # A_a agg_v - agg_b, then output linear and proj_first as one GEMM per output row
             if jd is not None:
-                A_a = tp.node_map_from_pos(node_pos, jd, row_perm)
+                A_a = tp.node_map_from_pos(node_pos[:N1], jd, row_perm)
             else:
-                A_a = tp.node_map(bd["wigner"], bd["wigner_inv"], node_pos, row_perm)
+                A_a = tp.node_map(bd["wigner"][:N1], bd["wigner_inv"][:N1], node_pos[:N1], row_perm)
             diff = tc.node_apply(A_a, agg, "sub")                                          # [N1, 20, C]
             out = tc.rowblock_linear(diff, tasks, self._fused_out_weights(), self.proj_first.bias,
                                      (self.lmax + 1) ** 2)
             return out, attn_weight
         h_b_agg, h_a = agg[:, :n_b], agg[:, n_b:]
-        h_a = tp.node_half(bd["wigner"], bd["wigner_inv"], h_a, node_pos)
+        h_a = tp.node_half(bd["wigner"][:N1], bd["wigner_inv"][:N1], h_a, node_pos[:N1])
         out = tp.so2_tp.forward_linear(h_a - h_b_agg)
         return self.proj_first(out), attn_weight

@@ -124,19 +124,25 @@ def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=N
     return plan, own_gid, local_gid, geometry
 
 
-def local_graph(pos_local, geometry, n_local, cutoff):
-    """The decoder's neighbour dict on the local rows, differentiable in ``pos_local``."""
+def local_graph(pos_local, geometry, n_local, cutoff, n_query=None):
+    """The decoder's neighbour dict on the local rows, differentiable in ``pos_local``.  With ``n_query``
+    (the owned atoms, the leading rows) only those rows are queries: the ghosts that follow them serve
+    as keys and values only, and the decoder computes nothing else for them."""
+    nq = n_local if n_query is None else int(n_query)
     outcell, qi, ni = geometry["outcell"], geometry["query_idx"], geometry["neighbor_idx"]
     exp_pos = pos_local[outcell] + geometry["offsets"]
     vec = pos_local[qi] - exp_pos[ni]
     dist_ = _DistFn.apply(vec, geometry["dist"])
-    md = ops.prepare_sparse_qk_edge_index_metadata(qi, ni, n_local, exp_pos.shape[0])
-    return {
+    md = ops.prepare_sparse_qk_edge_index_metadata(qi, ni, nq, exp_pos.shape[0])
+    g = {
         "query_idx": qi, "neighbor_idx": ni, "metadata": md, "f_edge_vec": vec, "f_dist": dist_,
         "f_poly_dist": polynomial(dist_, float(cutoff)), "f_outcell_index": outcell, "f_exp_node_pos": exp_pos,
-        "row_order": morton_row_order(pos_local, max(float(cutoff), 1e-3)),
+        "row_order": morton_row_order(pos_local[:nq], max(float(cutoff), 1e-3)),
         "key_order": morton_row_order(exp_pos, max(float(cutoff), 1e-3)), "query_sorted": True,
     }
+    if nq != n_local:
+        g["n_query"] = nq
+    return g
 
 
 def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), group=None):
@@ -151,7 +157,7 @@ def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), gr
     with torch.enable_grad():
         pos_own = pos_all.detach()[own_gid].to(torch.float32).requires_grad_(True)
         pos_local = plan.exchange(pos_own)
-        graph = local_graph(pos_local, geom, local_gid.numel(), dec.max_radius)
+        graph = local_graph(pos_local, geom, local_gid.numel(), dec.max_radius, n_query=plan.n_own)
         x = dec(pos_local, Z_all[local_gid], graph, True, halo=lambda t: plan.exchange(t[:plan.n_own]))
         e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1).sum()
         (grad,) = torch.autograd.grad(e_own, pos_own)

@@ -154,7 +154,9 @@ class TransBlock(nn.Module):
     def forward(self, node_pos, node_irreps, sys_node_embedding, edge_dis, edge_vec, attn_weight, atomic_numbers,
                 attn_mask, poly_dist=None, batch=None, batched_data=None, **kwargs):
         node_irreps = node_irreps[:, :(self.lmax + 1) ** 2]
-        res = node_irreps
+        # rows past n_query (domain ghosts) only serve as keys / values: the block returns the query rows
+        nq = int(batched_data.get("n_query", node_irreps.shape[0])) if batched_data is not None else node_irreps.shape[0]
+        res = node_irreps[:nq]
         h = self.norm_1(node_irreps)
         if sys_node_embedding is not None:
             h = torch.cat([h[:, :1] + sys_node_embedding.unsqueeze(1), h[:, 1:]], dim=1)
@@ -209,7 +211,7 @@ class EdgeDegreeEmbeddingNetwork_higherorder(nn.Module):
                 edge_scalars, **kwargs):
         qi = batched_data["query_idx"].to(torch.long)
         ni = batched_data["neighbor_idx"].to(torch.long)
-        n = node_pos.shape[0]
+        n = int(batched_data.get("n_query", node_pos.shape[0]))   # output rows: the query rows
         nb = self.number_of_basis
         cw = not self.training
         sh = spherical_harmonics_l2(torch.nn.functional.normalize(edge_vec, dim=-1))
@@ -297,7 +299,11 @@ class E2former(nn.Module):
         ``f_edge_vec``, ``f_dist``, ``f_poly_dist``, ``f_outcell_index``, ``f_exp_node_pos`` and the
         optional ``row_order`` / ``key_order``).  Returns the node irreps [N, (lmax+1)^2, C].
         ``halo`` (domain decomposition): called on the node irreps before every block to refresh the
-        rows of atoms owned by other ranks."""
+        rows of atoms owned by other ranks.  With ``graph["n_query"]`` = n, only rows [0, n) are queries:
+        the embedding and every block return those rows, and ``halo`` appends the others before each
+        block (it receives the n query rows)."""
+        if int(graph.get("n_query", node_pos.shape[0])) != node_pos.shape[0] and halo is None:
+            raise ValueError("n_query < number of nodes needs a halo to refresh the other rows")
         jd = [j.to(torch.float64) for j in self.Jd_list]
         bd = dict(graph)
         if node_pos.is_cuda and not self.training and self.lmax == 2:
