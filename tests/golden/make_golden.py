@@ -16,6 +16,8 @@ packages) and records, as compressed ``.npz`` files:
   ``tp_type="QK_alpha"`` / ``attn_type="so2-first-order"`` on seeded inputs and seeded weights
   (:func:`ubio_molfm_b200.synthetic.seeded_params_`), plus the gradients of ``<out, dOut>`` with
   respect to every floating-point input, for a seeded ``dOut``.
+* ``jd_reference.npz`` -- the reference's ``Jd.pt`` (the J matrices of its Wigner construction,
+  module_utils.py:266-337), degrees 0..2, as stored.
 * ``so2_pin.json`` -- the reference's own identity check ``test_so2_o1`` (so2_tensor_product.py:
   392-478), restated with the current ``eulers_to_wigner`` return convention: the node-decomposed
   first-order TP equals the per-edge rotated TP.
@@ -339,6 +341,13 @@ def so2_pin(mods):
 
 def main(only=None):
     """Write every fixture, or only those whose name starts with ``only``."""
+    if only in (None, "jd"):
+        jd = torch.load(os.path.join(refshim.REF_ROOT, "src", "molfm", "models", "e2former", "Jd.pt"))
+        np.savez_compressed(os.path.join(HERE, "jd_reference.npz"),
+                            **{f"J{l}": jd[l].double().numpy() for l in range(3)})
+        print("jd_reference", [tuple(jd[l].shape) for l in range(3)])
+        if only == "jd":
+            return
     mods = refshim.load_reference()
     if only is None:
         pin = so2_pin(mods)

@@ -30,12 +30,11 @@ def test_wigner_gradient_finite_at_origin_and_pole():
 
 
 def test_jd_matches_reference_constants():
-    import os
-    path = "/root/reference/src/molfm/models/e2former/Jd.pt"
-    if not os.path.exists(path):
-        pytest.skip("reference data not mounted")
+    """The computed J matrices against the reference's ``Jd.pt`` (fixture written by
+    ``tests/golden/make_golden.py jd``)."""
+    from golden_io import load
     from ubio_molfm_b200.wigner import jd_matrices
 
-    ref = torch.load(path)
+    ref = load("jd_reference")
     for l, J in enumerate(jd_matrices(2)):
-        np.testing.assert_allclose(J.numpy(), ref[l].numpy(), atol=1e-12)
+        np.testing.assert_allclose(J.numpy(), ref[f"J{l}"], atol=1e-12)
