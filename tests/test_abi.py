@@ -39,6 +39,38 @@ def test_host_only_entry_points():
                             None, None, None, None, None) == 1  # NULL pointers -> invalid argument
 
 
+def test_argument_validation_of_fused_entries():
+    """The radial-basis GEMMs and the node-map kernels reject bad arguments on the host, before any
+    device work (the device pointers below are never dereferenced)."""
+    import numpy as np
+
+    lib = _lib.load()
+    dev = ctypes.c_void_p(4096)   # stands in for a device address
+    f = ctypes.c_float
+    # C = rbf(d) B^T: empty is a no-op, negative sizes / missing operands are invalid
+    assert lib.e2a_gemm_tf32x3_rbf(dev, dev, f(-1.0), dev, None, 256, dev, 128, None, 0, 128, 256, 3, None) == 0
+    assert lib.e2a_gemm_tf32x3_rbf(dev, dev, f(-1.0), dev, None, 256, dev, 128, None, -5, 128, 256, 3, None) == 1
+    assert lib.e2a_gemm_tf32x3_rbf(None, dev, f(-1.0), dev, None, 256, dev, 128, None, 10, 128, 256, 3, None) == 1
+    assert lib.e2a_gemm_tf32x3_rbf(dev, dev, f(-1.0), dev, None, 256, dev, 128, None, 10, 128, 256, 2, None) == 1
+    # the distance gradient needs ceil(N / 64) partial columns per row
+    assert lib.e2a_gemm_tf32x3_rbf_dist_grad(dev, 128, dev, None, 128, dev, dev, f(-1.0), dev, 3, 10, 256, 128, 3,
+                                             None) == 1
+    j1, j2 = np.eye(3), np.eye(5)
+    sel = np.zeros(20, dtype=np.int32)
+    cg = np.ones(20)
+    P = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    assert lib.e2a_node_map_fwd(dev, -1, P(j1), P(j2), P(sel), P(cg), None, dev, None) == 1
+    assert lib.e2a_node_map_fwd(dev, 0, None, None, None, None, None, dev, None) == 0
+    assert lib.e2a_node_map_fwd(dev, 4, None, P(j2), P(sel), P(cg), None, dev, None) == 1
+    bad_sel = sel.copy()
+    bad_sel[3] = 9
+    assert lib.e2a_node_map_fwd(dev, 4, P(j1), P(j2), P(bad_sel), P(cg), None, dev, None) == 1
+    dup = np.arange(20, dtype=np.int32)
+    dup[5] = 4
+    assert lib.e2a_node_map_fwd(dev, 4, P(j1), P(j2), P(sel), P(cg), P(dup), dev, None) == 1
+    assert lib.e2a_node_map_bwd(dev, dev, 4, P(j1), P(j2), P(sel), P(cg), P(dup), dev, None) == 1
+
+
 def test_ops_refuse_cpu_tensors():
     import pytest
     import torch

@@ -580,12 +580,14 @@ int fill_tables(NodeMapTables& t, const double* j1, const double* j2, const int3
   if (!j1 || !j2 || !sel || !cg) return E2A_ERR_ARG;
   for (int i = 0; i < 9; ++i) t.J1[i] = j1[i];
   for (int i = 0; i < 25; ++i) t.J2[i] = j2[i];
+  uint32_t seen = 0;
   for (int i = 0; i < 20; ++i) {
     if (sel[i] < 0 || sel[i] > 8) return E2A_ERR_ARG;
     t.sel[i] = sel[i];
     t.cg[i] = cg[i];
     t.perm[i] = row_perm ? row_perm[i] : i;
-    if (t.perm[i] < 0 || t.perm[i] >= 20) return E2A_ERR_ARG;
+    if (t.perm[i] < 0 || t.perm[i] >= 20 || (seen >> t.perm[i]) & 1u) return E2A_ERR_ARG;   // a permutation
+    seen |= 1u << t.perm[i];
   }
   return E2A_OK;
 }
