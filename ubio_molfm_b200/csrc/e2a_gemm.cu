@@ -50,6 +50,27 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
 }
 
+// D (+)= A B^T with A read from tensor memory (row m in lane m, k in consecutive columns)
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+// this warp's 32 lanes x 16 consecutive columns of tensor memory from registers
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
+        "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                ::"r"(e2a_smem_u32(bar)) : "memory");
@@ -280,14 +301,12 @@ template <int BK_>
 struct WsCfg {
   static constexpr int BK = BK_;
   static constexpr int SPC = 32 / BK;                    // slabs per TMEM chain (32 k = 12 MMAs)
-  static constexpr int STAGES = BK == 16 ? 6 : 3;
+  static constexpr int STAGES = BK == 16 ? 6 : 4;
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
-  static constexpr int STAGE = 4 * TILE;                 // A (raw, then hi in place), A_lo, B (same), B_lo
-  static constexpr int NBARS = 3 * STAGES + 8;           // + 2 x WS_CHAINS
-#ifndef E2A_WS_SPLIT16
-#define E2A_WS_SPLIT16 128
-#endif
-  static constexpr int SPLIT = BK == 16 ? E2A_WS_SPLIT16 : 128;   // splitter threads (warps 2-3, + 12-13)
+  static constexpr int STAGE = 3 * TILE;                 // A (raw), B (split in place when not pre-split), B_lo
+  static constexpr int ATS = BK == 16 ? 4 : 2;           // A hi / lo slots in tensor memory (2 BK columns each)
+  static constexpr int NBARS = 3 * STAGES + 6 + ATS;     // + 2 x WS_CHAINS + the A slots
+  static constexpr int SPLIT = 128;                      // splitter threads (warps 2-3 and 12-13)
   static constexpr int THREADS = 384 + (SPLIT - 64);      // + 8 drain warps (4-11)
   static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
     // K-major; LBO unused (1); SBO = 8 rows x row bytes; version 1; swizzle 64 B (4) or 128 B (2)
@@ -295,13 +314,14 @@ struct WsCfg {
            ((BK == 16 ? 4ull : 2ull) << 61);
   }
 };
-constexpr int WS_CHAINS = 4;                     // TMEM chain buffers of BN columns (512 columns)
+constexpr int WS_CHAINS = 3;                     // TMEM chain buffers of BN columns (columns 0 .. 383)
+constexpr uint32_t WS_ACOL = WS_CHAINS * BN;      // A hi / lo slots: columns 384 .. 511
 constexpr int WS_DRAIN = 8;                      // drain warps: 4 TMEM lane quarters x 2 column halves
 constexpr int WS_DCOLS = BN / 2;                 // accumulator columns per drain warp
 constexpr int WS_EH = 16;                        // epilogue staged 16 columns at a time
 constexpr int WS_LD = WS_EH + 4;                 // staging row stride (floats)
 constexpr int WS_EPI = WS_DRAIN * 32 * WS_LD * 4;
-constexpr uint32_t kWsTmemCols = WS_CHAINS * BN;
+constexpr uint32_t kWsTmemCols = 512;
 template <int BK>
 constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024 + 1024; }
 
@@ -386,7 +406,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   uint64_t* split_done = bars + Cfg::STAGES;        // A hi / lo written     (one per splitter)
   uint64_t* empty = bars + 2 * Cfg::STAGES;         // MMAs of the slab done (tcgen05.commit)
   uint64_t* tfull = bars + 3 * Cfg::STAGES;         // chain buffer ready    (tcgen05.commit)
-  uint64_t* tempty = tfull + WS_CHAINS;           // chain buffer drained  (128 arrives)
+  uint64_t* tempty = tfull + WS_CHAINS;           // chain buffer drained  (256 arrives)
+  uint64_t* a_empty = tempty + WS_CHAINS;         // A slot read by the slab's MMAs (tcgen05.commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* mu_s = reinterpret_cast<float*>(tmem_slot + 4);   // gen: the basis offsets (K <= 256)
@@ -409,6 +430,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       e2a_mbar_init(&tfull[c], 1);
       e2a_mbar_init(&tempty[c], 32 * WS_DRAIN);
     }
+    for (int a = 0; a < Cfg::ATS; ++a) e2a_mbar_init(&a_empty[a], 1);
     *abort_flag = 0;
     e2a_fence_mbar_init();
   }
@@ -437,8 +459,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           uint8_t* st = stages + s * Cfg::STAGE;
           mbar_expect_tx(&full[s], bytes);
           if (!gen) tma_load_2d(st, &tmA, kb * Cfg::BK, m0, &full[s]);
-          tma_load_2d(st + 2 * Cfg::TILE, &tmB, kb * Cfg::BK, n0, &full[s]);
-          if (b_split) tma_load_2d(st + 3 * Cfg::TILE, &tmBl, kb * Cfg::BK, n0, &full[s]);
+          tma_load_2d(st + Cfg::TILE, &tmB, kb * Cfg::BK, n0, &full[s]);
+          if (b_split) tma_load_2d(st + 2 * Cfg::TILE, &tmBl, kb * Cfg::BK, n0, &full[s]);
         }
       }
       if (!run) {  // copies still in flight must land before the CTA exits
@@ -460,18 +482,19 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           WS_TRACE(3, n);
           tc_fence_after();
           const uint32_t d = tmem + cb * BN;
-          const uint32_t a_hi = e2a_smem_u32(stages + s * Cfg::STAGE), a_lo = a_hi + Cfg::TILE;
-          const uint32_t b_hi = a_hi + 2 * Cfg::TILE, b_lo = a_hi + 3 * Cfg::TILE;
+          const uint32_t a_hi = tmem + WS_ACOL + (n % Cfg::ATS) * 2 * Cfg::BK, a_lo = a_hi + Cfg::BK;
+          const uint32_t b_hi = e2a_smem_u32(stages + s * Cfg::STAGE) + Cfg::TILE, b_lo = b_hi + Cfg::TILE;
 #pragma unroll
           for (int kk = 0; kk < Cfg::BK / 8; ++kk) {
             const uint32_t koff = kk * 32;
-            mma_tf32(d, Cfg::desc(a_hi + koff), Cfg::desc(b_hi + koff), ((kb % Cfg::SPC) == 0 && kk == 0) ? 0u : 1u);
+            mma_tf32_ta(d, a_hi + 8 * kk, Cfg::desc(b_hi + koff), ((kb % Cfg::SPC) == 0 && kk == 0) ? 0u : 1u);
             if (passes == 3) {
-              mma_tf32(d, Cfg::desc(a_hi + koff), Cfg::desc(b_lo + koff), 1u);
-              mma_tf32(d, Cfg::desc(a_lo + koff), Cfg::desc(b_hi + koff), 1u);
+              mma_tf32_ta(d, a_hi + 8 * kk, Cfg::desc(b_lo + koff), 1u);
+              mma_tf32_ta(d, a_lo + 8 * kk, Cfg::desc(b_hi + koff), 1u);
             }
           }
           mma_commit(&empty[s]);
+          mma_commit(&a_empty[n % Cfg::ATS]);
           last = n;
           if ((kb % Cfg::SPC) == Cfg::SPC - 1 || kb == nk - 1) {
             mma_commit(&tfull[cb]);
@@ -483,92 +506,83 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         e2a_mbar_wait_bounded(&empty[last % Cfg::STAGES], (uint32_t)((last / Cfg::STAGES) & 1), &g_e2a_gemm_status);
     }
   } else if (warp < 4 || warp >= 12) {
-    // ------------------------------------------------------------------ splitters (128 threads)
-    const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 320;
+    // ------------------------------------------------------------------ splitters (4 warps)
+    // Warp w owns tensor-memory lane quarter w % 4 (warps 2, 3, 12, 13: quarters 2, 3, 0, 1), so lane l of
+    // it owns tile row 32 (w % 4) + l: it reads that row of the raw A slab from its swizzled stage (or forms
+    // it from the radial basis), splits it into tf32 hi / lo in registers and stores both into this slab's
+    // A slot in tensor memory, where the MMAs read it.  Shared memory then carries only the TMA writes and
+    // the MMAs' B reads.
+    static_assert(Cfg::SPLIT == 128, "four splitter warps cover the four lane quarters");
+    const int q = warp & 3;
+    const int r = 32 * q + lane;                              // tile row of this thread
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    const int t = warp < 4 ? threadIdx.x - 64 : threadIdx.x - 320;   // 0 .. 127 (B split)
+    const float c2 = rb.coeff * 1.44269504088896341f;         // gen: exp(a) = 2^(a log2 e)
     uint32_t n = 0;
     bool run = true;
-    float dreg[8], dnext[8];   // gen: the distances of this thread's 8 rows in this / the next tile
+    float dcur = 0.f, dnext = 0.f;                            // gen: this row's distance, this / next tile
     if (gen) {
-      const int m0 = ((int)blockIdx.x / tiles_n) * BM;
-#pragma unroll
-      for (int j = 0; j < Cfg::TILE / 16 / Cfg::SPLIT && j < 8; ++j) {
-        const int row = m0 + (t >> 2) + (Cfg::SPLIT / 4) * j;
-        dnext[j] = (int)blockIdx.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
-      }
+      const int row = ((int)blockIdx.x / tiles_n) * BM + r;
+      dnext = (int)blockIdx.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
     }
     for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
       for (int kb = 0; kb < nk; ++kb, ++n) {
         const uint32_t s = n % Cfg::STAGES;
         if (!ws_wait(&full[s], (n / Cfg::STAGES) & 1, abort_flag)) { run = false; break; }
+        // the A slot must have been read by the MMAs of slab n - ATS
+        if (!ws_wait(&a_empty[n % Cfg::ATS], ((n / Cfg::ATS) & 1) ^ 1, abort_flag)) { run = false; break; }
         if (t == 0) WS_TRACE(1, n);
         uint8_t* st = stages + s * Cfg::STAGE;
-        auto split = [&](auto count) {
+        if (gen && kb == 0) {   // this tile's distance (prefetched a tile ahead), then the next tile's
+          dcur = dnext;
+          const int row = ((tile + (int)gridDim.x) / tiles_n) * BM + r;
+          dnext = tile + (int)gridDim.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
+        }
+        const uint32_t acol = tmem + lane_addr + WS_ACOL + (n % Cfg::ATS) * 2 * Cfg::BK;
 #pragma unroll
-          for (int j = 0; j < decltype(count)::value; ++j) {      // float4 index over A then B
-            const int idx = t + j * Cfg::SPLIT;
-            const int off = (idx & (Cfg::TILE / 16 - 1)) * 16 + (idx >= Cfg::TILE / 16 ? 2 * Cfg::TILE : 0);
-            const float4 v = *reinterpret_cast<const float4*>(st + off);
-            float4 h, l;
-            h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
-            l.x = tf32_lo(v.x, h.x); l.y = tf32_lo(v.y, h.y); l.z = tf32_lo(v.z, h.z); l.w = tf32_lo(v.w, h.w);
-            *reinterpret_cast<float4*>(st + off) = h;
-            *reinterpret_cast<float4*>(st + Cfg::TILE + off) = l;
-          }
-        };
-        if (gen) {
-          if constexpr (BK_ == 16) {
-            // A's tile from the basis.  Float4 slot idx = t + SPLIT j of the 64-byte-swizzled [BM][16] tile
-            // holds row r = idx / 4 = t / 4 + (SPLIT / 4) j and logical 16-byte chunk (idx % 4) ^ ((r / 2) % 4),
-            // which is (t % 4) ^ ((t / 8) % 4) for every j: one mu float4 per slab, the rows' distances
-            // loaded once per tile.
-            constexpr int NJ = Cfg::TILE / 16 / Cfg::SPLIT, RS = Cfg::SPLIT / 4;   // slots, row stride
-            static_assert(NJ * Cfg::SPLIT * 16 == Cfg::TILE && NJ <= 8, "BK 16 slot map");
-            const int c = (t & 3) ^ ((t >> 3) & 3);
-            const int k0 = kb * Cfg::BK + 4 * c;
-            if (kb == 0) {   // this tile's distances (prefetched a tile ahead), then the next tile's
-              const int m1 = ((tile + (int)gridDim.x) / tiles_n) * BM;
+        for (int h = 0; h < Cfg::BK / 16; ++h) {   // 16 columns at a time
+          float v[16], hi[16], lo[16];
+          if (gen) {
 #pragma unroll
-              for (int j = 0; j < NJ; ++j) {
-                dreg[j] = dnext[j];
-                const int row = m1 + (t >> 2) + RS * j;
-                dnext[j] = tile + (int)gridDim.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
-              }
+            for (int u = 0; u < 16; ++u) {
+              const int k = kb * Cfg::BK + 16 * h + u;
+              const float x = dcur - mu_s[k & 255];
+              v[u] = k < K ? exp2f(c2 * (x * x)) : 0.f;
             }
-            float mu[4];
+          } else {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) mu[u] = mu_s[(k0 + u) & 255];
-            const float c2 = rb.coeff * 1.44269504088896341f;   // exp(a) = 2^(a log2 e)
-#pragma unroll
-            for (int j = 0; j < NJ; ++j) {
-              const int idx = t + j * Cfg::SPLIT;
-              float v[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const float x = dreg[j] - mu[u];
-                v[u] = k0 + u < K ? exp2f(c2 * (x * x)) : 0.f;
-              }
-              float4 h, l;
-              h.x = tf32_hi(v[0]); h.y = tf32_hi(v[1]); h.z = tf32_hi(v[2]); h.w = tf32_hi(v[3]);
-              l.x = tf32_lo(v[0], h.x); l.y = tf32_lo(v[1], h.y); l.z = tf32_lo(v[2], h.z); l.w = tf32_lo(v[3], h.w);
-              *reinterpret_cast<float4*>(st + idx * 16) = h;
-              *reinterpret_cast<float4*>(st + Cfg::TILE + idx * 16) = l;
-            }
-            if (!b_split) {   // B's tile still needs its split
-#pragma unroll
-              for (int j = 0; j < Cfg::TILE / 16 / Cfg::SPLIT; ++j) {
-                const int off = 2 * Cfg::TILE + (t + j * Cfg::SPLIT) * 16;
-                const float4 v = *reinterpret_cast<const float4*>(st + off);
-                float4 h, l;
-                h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
-                l.x = tf32_lo(v.x, h.x); l.y = tf32_lo(v.y, h.y); l.z = tf32_lo(v.z, h.z); l.w = tf32_lo(v.w, h.w);
-                *reinterpret_cast<float4*>(st + off) = h;
-                *reinterpret_cast<float4*>(st + Cfg::TILE + off) = l;
-              }
+            for (int c4 = 0; c4 < 4; ++c4) {
+              // logical 16-byte chunk c of the row sits at chunk c ^ ((r / 2) % 4) (64-byte swizzle, 16-wide
+              // slabs) or c ^ (r % 8) (128-byte swizzle, 32-wide slabs)
+              const int c = 4 * h + c4;
+              const int pc = Cfg::BK == 16 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
+              const float4 x = *reinterpret_cast<const float4*>(st + r * (Cfg::BK * 4) + 16 * pc);
+              v[4 * c4] = x.x; v[4 * c4 + 1] = x.y; v[4 * c4 + 2] = x.z; v[4 * c4 + 3] = x.w;
             }
           }
-        } else if (b_split) split(IntC<Cfg::TILE / 16 / Cfg::SPLIT>{});
-        else split(IntC<2 * Cfg::TILE / 16 / Cfg::SPLIT>{});
-        e2a_fence_proxy_async();
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            hi[u] = tf32_hi(v[u]);
+            lo[u] = tf32_lo(v[u], hi[u]);
+          }
+          tmem_st16(acol + 16 * h, hi);
+          tmem_st16(acol + Cfg::BK + 16 * h, lo);
+        }
+        if (!b_split) {   // B's tile split in place (hi) and into the B_lo part
+#pragma unroll
+          for (int j = 0; j < Cfg::TILE / 16 / Cfg::SPLIT; ++j) {
+            const int off = Cfg::TILE + (t + j * Cfg::SPLIT) * 16;
+            const float4 x = *reinterpret_cast<const float4*>(st + off);
+            float4 hh, ll;
+            hh.x = tf32_hi(x.x); hh.y = tf32_hi(x.y); hh.z = tf32_hi(x.z); hh.w = tf32_hi(x.w);
+            ll.x = tf32_lo(x.x, hh.x); ll.y = tf32_lo(x.y, hh.y); ll.z = tf32_lo(x.z, hh.z); ll.w = tf32_lo(x.w, hh.w);
+            *reinterpret_cast<float4*>(st + off) = hh;
+            *reinterpret_cast<float4*>(st + Cfg::TILE + off) = ll;
+          }
+          e2a_fence_proxy_async();
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
         mbar_arrive(&split_done[s]);
         if (t == 0) WS_TRACE(2, n);
       }
