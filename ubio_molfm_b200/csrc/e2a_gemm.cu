@@ -765,7 +765,8 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
   if (!vec || K == 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return E2A_ERR_UNSUPPORTED;
   EncodeTiledFn enc = tensor_map_encoder();
   if (!enc) return E2A_ERR_UNSUPPORTED;
-  const int bk = K <= 256 ? 16 : 32;
+  // 32-wide slabs (four stages) from K = 256 up; 16-wide for shorter K and for the on-chip basis
+  const int bk = (gen || K < 256) ? 16 : 32;
   if (gen && bk != 16) return E2A_ERR_UNSUPPORTED;
   CUtensorMap ta, tb, tbl;
   if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
