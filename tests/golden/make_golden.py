@@ -16,6 +16,9 @@ packages) and records, as compressed ``.npz`` files:
   ``tp_type="QK_alpha"`` / ``attn_type="so2-first-order"`` on seeded inputs and seeded weights
   (:func:`ubio_molfm_b200.synthetic.seeded_params_`), plus the gradients of ``<out, dOut>`` with
   respect to every floating-point input, for a seeded ``dOut``.
+* ``faiss_expand_*.npz`` -- ``distributed_cell_expand`` (sp/dist_ner.py:27-84), the image expansion of
+  the reference's FAISS neighbour path, with the atoms' bounding box as the wrapper passes it
+  (e2former_wrapper.py:179-191): expanded positions and the image -> atom map.
 * ``jd_reference.npz`` -- the reference's ``Jd.pt`` (the J matrices of its Wigner construction,
   module_utils.py:266-337), degrees 0..2, as stored.
 * ``so2_pin.json`` -- the reference's own identity check ``test_so2_o1`` (so2_tensor_product.py:
@@ -339,6 +342,30 @@ def so2_pin(mods):
     }
 
 
+def faiss_cases(mods):
+    """The FAISS path's image expansion on three periodic systems (CPU, fp32)."""
+    import importlib
+
+    dn = importlib.import_module("molfm.models.e2former.sp.dist_ner")
+    rng = np.random.default_rng(31)
+    systems = {}
+    pos, _, cell = synthetic.water_box(n_side=6, box=18.64, jitter=0.3, seed=1)
+    systems["faiss_expand_water648"] = (pos, cell, [True, True, True], 5.0)
+    tri = np.array([[8.0, 0.0, 0.0], [2.0, 7.0, 0.0], [1.0, 1.5, 9.0]])
+    systems["faiss_expand_triclinic60"] = (rng.random((60, 3)) @ tri, tri, [True, True, False], 4.5)
+    systems["faiss_expand_small40"] = (rng.random((40, 3)) * 7.0, np.eye(3) * 7.0, [True, True, True], 5.0)
+    out = {}
+    for name, (p, c, pbc, cutoff) in systems.items():
+        pt = torch.tensor(p, dtype=torch.float32).unsqueeze(0)
+        ct = torch.tensor(c, dtype=torch.float32)
+        bmin, bmax = pt[0].min(dim=0)[0], pt[0].max(dim=0)[0]
+        r = dn.distributed_cell_expand(pt, ct, cutoff, bmin, bmax, 1, torch.tensor([pbc]))
+        out[name] = {"pos": pt[0].numpy(), "cell": ct.numpy(), "pbc": np.array(pbc), "cutoff": np.array(cutoff),
+                     "expand_node_pos": r["expand_node_pos"][0].numpy(),
+                     "outcell_index": r["outcell_index"][0].numpy(), "n_edges": np.array(0)}
+    return out
+
+
 def main(only=None):
     """Write every fixture, or only those whose name starts with ``only``."""
     if only in (None, "jd"):
@@ -355,7 +382,7 @@ def main(only=None):
         with open(os.path.join(HERE, "so2_pin.json"), "w") as f:
             json.dump(pin, f, indent=1)
         print("so2 pin", pin["max_abs_diff"])
-    makers = {"graph": graph_cases, "layer": layer_cases, "backbone": backbone_cases}
+    makers = {"graph": graph_cases, "layer": layer_cases, "backbone": backbone_cases, "faiss": faiss_cases}
     for prefix, make in makers.items():
         if only is not None and prefix != only:
             continue

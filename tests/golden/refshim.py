@@ -338,7 +338,9 @@ def install():
     tgd = _mod("torch_geometric.data", Data=dict, Batch=dict)
     tg.data = tgd
     _mod("opt_einsum_fx", optimize_einsums_full=None)
-    _mod("faiss")
+    fa = _mod("faiss")
+    fa.contrib = _mod("faiss.contrib")
+    fa.contrib.torch_utils = _mod("faiss.contrib.torch_utils")
 
     if REF_SRC not in sys.path:
         sys.path.insert(0, REF_SRC)
@@ -349,6 +351,7 @@ def install():
         ("molfm.models.e2former", E2F_DIR),
         ("molfm.models.e2former.wigner6j", os.path.join(E2F_DIR, "wigner6j")),
         ("molfm.models.e2former.triton_dr", os.path.join(E2F_DIR, "triton_dr")),
+        ("molfm.models.e2former.sp", os.path.join(E2F_DIR, "sp")),
     ]:
         p = types.ModuleType(name)
         p.__path__ = [path]

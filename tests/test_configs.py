@@ -106,3 +106,26 @@ def test_config3_bio1500_full_model_energy_forces():
     energy, forces = model(pos_t.to(DEV), Z_t.to(DEV), cell_t, (True, True, True))
     e_ref, f_ref = _oracle_potential(p, ph, FULL, cell)(pos_t, Z_t)
     _check_energy_forces(energy, forces, e_ref, f_ref, len(Z))
+
+
+def test_use_faiss_order_equals_default():
+    """``use_faiss=True`` (the expanded-node order of the reference's FAISS path) changes only the index
+    space of the expanded nodes: energy and forces equal the default expansion's on the config-1 box."""
+    from ubio_molfm_b200.model import E2FormerPotential
+    from ubio_molfm_b200.synthetic import seeded_params_, water_box
+
+    pos, Z, cell = water_box(n_side=6, box=18.64, jitter=0.3, seed=1)
+    pos_t, Z_t = torch.tensor(pos, dtype=torch.float32, device=DEV), torch.tensor(Z, device=DEV)
+    cell_t = torch.tensor(cell, dtype=torch.float32)
+    out = []
+    for faiss_order in (False, True):
+        m = E2FormerPotential(use_faiss=faiss_order, **SMALL)
+        seeded_params_(m.decoder, 11)
+        seeded_params_(m.energy_head, 12)
+        m = m.to(DEV).eval()
+        out.append(m(pos_t, Z_t, cell_t, (True, True, True)))
+        g, _ = m.build_graph(pos_t, cell_t, (True, True, True), None)
+        out[-1] = out[-1] + (g["query_idx"].numel(),)
+    (e0, f0, n0), (e1, f1, n1) = out
+    assert n0 == n1
+    _check_energy_forces(e1, f1, e0.detach().cpu(), f0.detach().cpu(), len(Z))

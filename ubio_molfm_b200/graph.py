@@ -4,6 +4,9 @@
   computed on the host with the same fp32 torch operations.
 * :func:`expand_pbc` -- ``CellExpander.expand_includeself`` (module_utils.py:1065-1275) for one
   periodic system: cell-list existence test per image on the GPU.
+* :func:`distributed_cell_expand` -- the image expansion of the reference's FAISS neighbour path
+  (sp/dist_ner.py:27-84): its expanded-node order (candidate cells in i-j-k order, atoms ascending,
+  kept by their box distance to the atoms' bounding box).
 * :func:`radius_graph` -- the flattened (pyG-style) radius graph: cell-list neighbour search,
   (distance, index)-ordered rows, ``max_neighbors`` truncation, CSR metadata and a spatial row order.
 * :func:`construct_radius_neighbor` -- the reference's padded ``[B, L]`` API (module_utils.py:3119).
@@ -94,6 +97,45 @@ def expand_pbc(pos, cell, pbc, cutoff, num_cell_per_direction=4):
     image = img_atom // n
     exp_pos = pos.to(torch.float32)[outcell] + offsets[image]
     return exp_pos, outcell, image
+
+
+def distributed_cell_expand(pos, cell_size, cutoff, cell_boundMIN, cell_boundMAX, num_cell_perdirection=1,
+                            pbc=None):
+    """Image expansion of the reference's FAISS neighbour path (``distributed_cell_expand``,
+    sp/dist_ner.py:27-84, called from e2former_wrapper.py:179-191 with the atoms' bounding box).
+
+    ``pos`` [1, N, 3] (one system).  The candidate cells are i, j, k in [-n, n] (only 0 along a
+    non-periodic direction), i slowest; every cell contributes all atoms in order, translated by
+    ``[i, j, k] @ cell_size``; an image is kept when its distance to the box [``cell_boundMIN``,
+    ``cell_boundMAX``] is below ``cutoff``.  The home cell is not first (it sits in the middle of the
+    candidate order), unlike ``CellExpander``.  Same fp32 operations as the reference, so the kept
+    set and the positions are bit-identical on the same device; differentiable in ``pos``.  Returns the
+    reference's dict of ``expand_node_pos`` [1, M, 3], ``outcell_index`` [1, M], ``expand_node_mask``."""
+    if pos.dim() != 3:
+        raise ValueError("please check your pos shape: 1*N*3")
+    if pos.shape[0] != 1:
+        raise ValueError("sorry, we did not support pos batch size >1 in distributed version")
+    p = pos[0]
+    n_atoms, dev = p.shape[0], p.device
+    if pbc is None:
+        return {"expand_node_pos": p.unsqueeze(0),
+                "outcell_index": torch.arange(n_atoms, dtype=torch.long, device=dev).unsqueeze(0),
+                "expand_node_mask": torch.ones(1, n_atoms, dtype=torch.bool, device=dev)}
+    periodic = [bool(v) for v in torch.as_tensor(pbc).reshape(-1)[:3]]
+    steps = [range(-num_cell_perdirection, num_cell_perdirection + 1) if periodic[d] else range(0, 1)
+             for d in range(3)]
+    cand = torch.tensor([[i, j, k] for i in steps[0] for j in steps[1] for k in steps[2]], dtype=torch.float32,
+                        device=dev)
+    shift = cand @ torch.as_tensor(cell_size, dtype=torch.float32, device=dev)       # [C, 3]
+    images = (p.unsqueeze(0) + shift.unsqueeze(1)).reshape(-1, 3)                   # cell-major
+    lo = torch.as_tensor(cell_boundMIN, dtype=images.dtype, device=dev).reshape(1, 3)
+    hi = torch.as_tensor(cell_boundMAX, dtype=images.dtype, device=dev).reshape(1, 3)
+    outside = torch.clamp(torch.maximum(lo - images.detach(), images.detach() - hi), min=0.0)
+    keep = torch.sqrt(torch.sum(outside ** 2, dim=-1)) < cutoff
+    atom = torch.arange(n_atoms, dtype=torch.long, device=dev).repeat(cand.shape[0])
+    kept = images[keep]
+    return {"expand_node_pos": kept.unsqueeze(0), "outcell_index": atom[keep].unsqueeze(0),
+            "expand_node_mask": torch.ones(1, kept.shape[0], dtype=torch.bool, device=dev)}
 
 
 # ------------------------------------------------------------------------------------------------

@@ -24,7 +24,7 @@ from torch import nn
 from . import linear as tc
 from . import ops
 from .attention import E2AttentionArbOrder_sparse
-from .graph import expand_pbc, radius_graph
+from .graph import distributed_cell_expand, expand_pbc, radius_graph
 from .nn import GaussianSmearing, RadialProfile, RbfSpec, SO3_Linear_e2former, irreps_channels_lmax, lin, run_mlp
 from .wigner import jd_matrices, node_wigner
 
@@ -360,8 +360,12 @@ class E2FormerPotential(nn.Module):
     ``(energy [B], forces [N,3])``.  Periodic systems are one per call; non-periodic molecules may be
     batched (``batch`` sorted, systems do not see each other)."""
 
-    def __init__(self, memory_saving=True, **backbone_kwargs):
+    def __init__(self, memory_saving=True, use_faiss=False, **backbone_kwargs):
         super().__init__()
+        # use_faiss: expanded nodes in the order of the reference's FAISS neighbour path
+        # (distributed_cell_expand, one image cell per direction) instead of CellExpander's; the edges
+        # are the same physical neighbours, found by the same exact search (FAISS itself is not used)
+        self.use_faiss = use_faiss
         self.decoder = E2former(**backbone_kwargs)
         self.energy_head = MLP_energy_head(self.decoder.scalar_dim, self.decoder.lmax)
         # large systems: the Q / K projections are formed again in the backward (saves 2 x 4 x hidden
@@ -378,8 +382,15 @@ class E2FormerPotential(nn.Module):
         if pbc_any:
             if batch is not None and int(batch.max()) > 0:
                 raise NotImplementedError("periodic systems are evaluated one per call")
-            exp_pos, outcell, _ = expand_pbc(pos, torch.as_tensor(cell, dtype=torch.float32), list(pbc),
-                                             dec.max_radius)
+            if self.use_faiss:
+                pd = pos.detach()
+                ex = distributed_cell_expand(pos.unsqueeze(0), torch.as_tensor(cell, dtype=torch.float32),
+                                             dec.max_radius, pd.min(dim=0).values, pd.max(dim=0).values, 1,
+                                             torch.as_tensor([bool(v) for v in pbc]))
+                exp_pos, outcell = ex["expand_node_pos"][0], ex["outcell_index"][0]
+            else:
+                exp_pos, outcell, _ = expand_pbc(pos, torch.as_tensor(cell, dtype=torch.float32), list(pbc),
+                                                 dec.max_radius)
             q_ptr = torch.tensor([0, n])
             p_ptr = torch.tensor([0, exp_pos.shape[0]])
         else:
