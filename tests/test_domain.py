@@ -52,6 +52,56 @@ def _halo_worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
+def _halo_fault_worker(rank, world, port, out):
+    """Rank ``world - 1`` leaves after the plan is built (a rank that died between steps); the others
+    must get an error from their next exchange within the process group's timeout instead of waiting."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from ubio_molfm_b200.domain import HaloPlan
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    n = 12
+    owner = torch.arange(n) % world
+    own = torch.nonzero(owner == rank).flatten()
+    ghost = torch.nonzero(owner != rank).flatten()        # every other atom is a ghost
+    plan = HaloPlan(own, ghost, owner[ghost], world, rank)
+    if rank == world - 1:
+        out[rank] = "left"
+        return                                            # leaves without exchanging (no teardown)
+    t0 = time.monotonic()
+    try:
+        plan.exchange(torch.ones(own.numel(), 2))
+        out[rank] = "no error"
+    except RuntimeError:
+        out[rank] = "error after %.1f s" % (time.monotonic() - t0)
+
+
+def test_halo_exchange_reports_a_missing_rank_gloo():
+    mgr = mp.Manager()
+    out = mgr.dict()
+    world = 3
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_halo_fault_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(60)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert out.get(world - 1) == "left", dict(out)
+    for r in range(world - 1):
+        assert str(out.get(r, "")).startswith("error after"), dict(out)
+        assert float(str(out[r]).split()[2]) < 30.0, dict(out)
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_halo_exchange_forward_and_adjoint_gloo(world):
     mgr = mp.Manager()
