@@ -301,7 +301,13 @@ template <int BK_>
 struct WsCfg {
   static constexpr int BK = BK_;
   static constexpr int SPC = 32 / BK;                    // slabs per TMEM chain (32 k = 12 MMAs)
-  static constexpr int STAGES = BK == 16 ? 6 : 4;
+#ifndef E2A_WS_STAGES16
+#define E2A_WS_STAGES16 6   // shared memory allows up to 8 (24 KB stages)
+#endif
+#ifndef E2A_WS_STAGES32
+#define E2A_WS_STAGES32 4   // 48 KB stages
+#endif
+  static constexpr int STAGES = BK == 16 ? E2A_WS_STAGES16 : E2A_WS_STAGES32;
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
   static constexpr int STAGE = 3 * TILE;                 // A (raw), B (split in place when not pre-split), B_lo
   static constexpr int ATS = BK == 16 ? 4 : 2;           // A hi / lo slots in tensor memory (2 BK columns each)
