@@ -76,6 +76,15 @@ class E2AttentionArbOrder_sparse(nn.Module):
         The SO(2) output linear and proj_first are consecutive linear maps (no bias or activation
         between them), so one product per output row replaces the two."""
         so2 = self.first_order_tp.so2_tp
+        # formed once and reused while the source tensors are unchanged (their version counters move with
+        # every in-place update, e.g. an optimiser step or load_state_dict, and .to() gives them new
+        # storage); this also keeps the path_norm check, a host read, out of every forward
+        srcs = [self.proj_first.weight, so2.path_norm] + [so2.out_linear[i].weight
+                                                           for i in range(len(so2.l3_sequential))]
+        key = tuple((id(t), t._version, t.data_ptr(), t.dtype, t.device) for t in srcs)   # .to() swaps .data
+        cache = getattr(self, "_fused_out_cache", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
         pw = self.proj_first.weight.detach()
         norm = so2.path_norm.detach().reshape(-1)
         ws = []
@@ -84,6 +93,7 @@ class E2AttentionArbOrder_sparse(nn.Module):
             if not bool((nl == nl[0]).all()):
                 raise NotImplementedError("path_norm must be constant within an l3 block")
             ws.append(pw[l3] @ (so2.out_linear[idx].weight.detach() * nl[0]))
+        self._fused_out_cache = (key, ws)
         return ws
 
     # -- edge radial MLP with the first layer split as W_r rbf + (W_t T)[Z_i] + (W_s S)[Z_j] + b --
