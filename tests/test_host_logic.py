@@ -1,6 +1,7 @@
 """Host-side logic of the inference path that needs no GPU."""
 import torch
 
+
 def test_fused_output_weights_cache_follows_the_parameters():
     """The merged output-linear weights of the inference path are formed once and re-formed whenever a
     source tensor changes: in place, through load_state_dict, or by a dtype conversion."""
