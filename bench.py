@@ -677,9 +677,9 @@ def run_model(args, ws, rank, local):
 
 
 def run_molecules(args, ws, rank, local):
-    """Config 4: a batch of non-periodic molecules (10-60 atoms) sharded across ranks by size; each rank
-    evaluates its molecules' energies and forces (batched, systems independent); one all-gather of the
-    energies.  The full-size backbone at the reference's small-molecule cutoff (4.5 A, <= 32 neighbours)."""
+    """Config 4: a batch of non-periodic molecules (10-60 atoms, charges in [-1, 1], multiplicity 1)
+    sharded across ranks by size; each rank evaluates its molecules' energies and forces (batched,
+    systems independent, each with its charge embedding); energies and forces gathered to rank 0.  The full-size backbone at the reference's small-molecule cutoff (4.5 A, <= 32 neighbours)."""
     from ubio_molfm_b200 import _lib
     from ubio_molfm_b200.domain import gather_molecule_results, molecules_energy_forces, shard_molecules
     from ubio_molfm_b200.model import E2FormerPotential
@@ -694,13 +694,13 @@ def run_molecules(args, ws, rank, local):
     mols = molecule_batch(args.molecules, 10, 60, seed=11)
     parts = shard_molecules([len(z) for _, z, _, _ in mols], ws)
     mine = parts[rank]
-    my = [(mols[i][0], mols[i][1]) for i in mine]
+    my = [mols[i] for i in mine]           # (pos, Z, charge, multiplicity)
     n_atoms_total = sum(len(z) for _, z, _, _ in mols)
 
     def step():
-        e, _ = molecules_energy_forces(m, my, dev)
+        e, f = molecules_energy_forces(m, my, dev)
         if ws > 1:
-            gather_molecule_results(e, mine, len(mols))
+            e, f = gather_molecule_results(e, f, mine, len(mols))
         return e
 
     for _ in range(args.warmup):
@@ -730,7 +730,7 @@ def run_molecules(args, ws, rank, local):
                                        f"H/C/N/O/F/S/Cl), full-size backbone, cutoff 4.5 A, <= 32 neighbours",
                            "molecules": len(mols), "atoms_total": n_atoms_total,
                            "molecules_per_s": round(len(mols) * 1e3 / ms, 1),
-                           "parallelism": f"molecules sharded by size over {ws} ranks, one all-gather",
+                           "parallelism": f"molecules sharded by size over {ws} ranks; energies and forces gathered to rank 0",
                            "l2": "inputs larger than L2"},
                 "e2e": {"value": round(n_atoms_total * 1e3 / ms, 1), "unit": "atom-steps/s",
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * len(mols),

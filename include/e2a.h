@@ -241,6 +241,9 @@ int e2a_node_apply_bwd(const float* A, const float* h, int64_t h_node_stride, co
                        float* dA, void* stream);
 /* Status bits of the GEMM's bounded waits (1 = a wait timed out); copies and optionally clears. */
 int e2a_gemm_status(unsigned int* status, int reset, void* stream);
+/* Test hook (no reference counterpart): one bounded mbarrier wait on a barrier nothing arrives at,   */
+/* giving up after limit_ns (1e3..1e8 ns) and setting the timeout bit that e2a_gemm_status reports.   */
+int e2a_gemm_wait_selftest(long long limit_ns, void* stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Fused row-wise LayerNorm + SiLU of the radial MLP (RadialProfile, module_utils.py:2151-2178), */

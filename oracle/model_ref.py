@@ -152,8 +152,18 @@ def polynomial(dist, cutoff, p=5):
     return torch.where(r < 1, 1 + r ** p * (a + r * (b + c * r)), torch.zeros_like(r))
 
 
-def backbone(p, cfg, pos, Z, qi, ni, outcell, exp_pos, pbc_any):
-    """e2f/e2former.py:944-1145 (no cluster blocks) -> node irreps [N, 9, C]."""
+def system_embedding(p, charge, multiplicity):
+    """e2f/e2former_wrapper.py:249-255: SiLU(Linear([emb_q(clip(q,-10,10)+10), emb_s(clip(s,0,20))]))
+    per system, [B, C]; ``p`` holds the backbone-level parameters (``embedding_charge.weight`` ...)."""
+    q = torch.clamp(torch.as_tensor(charge).reshape(-1).long(), -10, 10) + 10
+    s = torch.clamp(torch.as_tensor(multiplicity).reshape(-1).long(), 0, 20)
+    h = torch.cat([p["embedding_charge.weight"][q], p["embedding_multiplicity.weight"][s]], dim=-1)
+    return F.silu(F.linear(h, p["mix_cm.0.weight"], p["mix_cm.0.bias"]))
+
+
+def backbone(p, cfg, pos, Z, qi, ni, outcell, exp_pos, pbc_any, sys_node=None):
+    """e2f/e2former.py:944-1145 (no cluster blocks) -> node irreps [N, 9, C].  ``sys_node`` [N, C]: the
+    system embedding of each atom's system, added to the normed l=0 row of every block (582-583)."""
     lmax, nb, cutoff = 2, cfg["number_of_basis"], cfg["max_radius"]
     H, D = cfg["num_attn_heads"], cfg["attn_scalar_head"]
     l3 = R.L3_SEQUENTIAL
@@ -172,19 +182,27 @@ def backbone(p, cfg, pos, Z, qi, ni, outcell, exp_pos, pbc_any):
         pre = f"blocks.{i}."
         res = x
         h = rms_norm(p, pre + "norm_1.", x, lmax)
+        if sys_node is not None:
+            h = torch.cat([h[:, :1] + sys_node.unsqueeze(1), h[:, 1:]], dim=1)
         h = R.attention_layer(_sub(p, pre + "ga."), H, D, pos, h, dist, rbf, Z, poly, bd)
         x = h + res
         x = x + ffn(p, pre + "ffn.", rms_norm(p, pre + "norm_ffn.", x, lmax), lmax)
     return rms_norm(p, "norm_final.", x, lmax)
 
 
-def energy_forces(p_backbone, p_head, cfg, pos, Z, graph, batch=None):
+def energy_forces(p_backbone, p_head, cfg, pos, Z, graph, batch=None, p_system=None, charge=None,
+                  multiplicity=None):
     """Energies per system and forces -dE/dpos.  ``graph`` = (qi, ni, outcell, image offsets [N2,3]
-    or None, pbc_any): expanded positions are pos[outcell] + offset, so forces include the images."""
+    or None, pbc_any): expanded positions are pos[outcell] + offset, so forces include the images.
+    With ``charge`` given, ``p_system`` holds the backbone-level parameters of :func:`system_embedding`."""
     qi, ni, outcell, offsets, pbc_any = graph
     pos = pos.detach().clone().requires_grad_(True)
     exp_pos = pos[outcell] + offsets if offsets is not None else pos[outcell]
-    x = backbone(p_backbone, cfg, pos, Z, qi, ni, outcell, exp_pos, pbc_any)
+    sys_node = None
+    if charge is not None:
+        se = system_embedding(p_system, charge, multiplicity)
+        sys_node = se[batch] if batch is not None else se[:1].expand(pos.shape[0], -1)
+    x = backbone(p_backbone, cfg, pos, Z, qi, ni, outcell, exp_pos, pbc_any, sys_node)
     h = F.silu(F.linear(x[:, 0], p_head["mlp.0.weight"], p_head["mlp.0.bias"]))
     h = F.silu(F.linear(h, p_head["mlp.2.weight"], p_head["mlp.2.bias"]))
     e_atom = F.linear(h, p_head["mlp.4.weight"], p_head["mlp.4.bias"]).squeeze(-1)

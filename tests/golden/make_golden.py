@@ -1,9 +1,9 @@
 """Generate the golden fixtures under ``tests/golden/`` by running the REFERENCE code on CPU.
 
 TEST INFRASTRUCTURE ONLY.  Run in a container where the reference sources are mounted
-(default ``/root/reference``; override with ``E2A_REFERENCE_ROOT``)::
+(``E2A_REFERENCE_ROOT`` = the reference checkout, the directory holding ``src/molfm``)::
 
-    python tests/golden/make_golden.py
+    E2A_REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py [graph|layer|backbone|faiss|system]
 
 It imports the reference's own modules through ``refshim`` (stand-ins for the missing third-party
 packages) and records, as compressed ``.npz`` files:
@@ -304,6 +304,64 @@ def backbone_cases(mods):
     return cases
 
 
+def system_case(mods, P, ZZ, cell, pbc, charge, mult, seed, max_neighbors=None):
+    """The reference's ``E2FormerBackbone`` (e2former_wrapper.py:140-339) -- PBC expansion, radius
+    graph, the charge / multiplicity system embedding (``mix_cm``, e2former_wrapper.py:249-259) added to
+    the normed l=0 row of every block (e2former.py:582-583) -- plus ``MLP_energy_head`` summed over the
+    atoms (pipeline/head.py:552-580) and forces = -dE/dpos (GradientHead, head.py:305-328), on the
+    collated input layout of ``dict_to_model_input`` (interface/data_utils.py:37-80: ``pos [B,L,3]``,
+    ``atom_masks``, ``charge [B,1]``, ``multiplicity [B,1]``, ``cell [B,3,3]``, ``pbc [B,3]``).  All
+    weights of the backbone are seeded by their names in the backbone (``decoder.blocks...``)."""
+    import importlib
+
+    wrapper = importlib.import_module("molfm.models.e2former.e2former_wrapper")
+    cfg = dict(BACKBONE_CFG, max_neighbors=max_neighbors, encoder="default")
+    bb = wrapper.E2FormerBackbone(use_faiss=False, **cfg).eval()
+    synthetic.seeded_params_(bb, seed, gains=synthetic.SYSTEM_EMBED_GAINS)
+    C = int(cfg["irreps_node_embedding"].split("x")[0])
+    head, head_kind = _energy_head(C)
+    synthetic.seeded_params_(head, seed + 1)
+    P = torch.tensor(P, dtype=torch.float32)
+    Z = torch.tensor(ZZ, dtype=torch.long)
+    B, L = Z.shape
+    node_mask = Z != 0
+    pos = P.clone().requires_grad_(True)
+    bd = {"pos": pos, "atom_masks": node_mask, "atomic_numbers": Z,
+          "pbc": torch.tensor(pbc, dtype=torch.int32).reshape(1, 3).repeat(B, 1),
+          "cell": torch.tensor(cell, dtype=torch.float32).reshape(1, 3, 3).repeat(B, 1, 1),
+          "charge": torch.tensor(charge, dtype=torch.int32).reshape(B, 1),
+          "multiplicity": torch.tensor(mult, dtype=torch.int32).reshape(B, 1)}
+    out = bb(bd)
+    e_atom = head(out["node_featuresBxN"], out["node_irrepsBxN"]).squeeze(-1).masked_fill(~node_mask, 0.0)
+    energy = e_atom.sum(dim=-1)
+    (grad,) = torch.autograd.grad(energy.sum(), pos)
+    return {
+        "cfg": np.array(json.dumps(dict(cfg, seed=seed, head=head_kind))),
+        "pos": _np(P[node_mask]), "Z": _np(Z[node_mask]),
+        "batch": _np(torch.arange(B).unsqueeze(1).repeat(1, L)[node_mask]),
+        "cell": np.asarray(cell, np.float32), "pbc": np.asarray(pbc, bool),
+        "charge": np.asarray(charge, np.int64), "multiplicity": np.asarray(mult, np.int64),
+        "energy": _np(energy), "forces": _np(-grad[node_mask]),
+        "node_irreps": _np(out["node_irrepsBxN"][node_mask]),
+        "n_edges": np.array(int(out["neighbor_info"]["query_idx"].numel())),
+        "state_dict_shapes": np.array(json.dumps({k: list(v.shape) for k, v in bb.state_dict().items()})),
+    }
+
+
+def system_cases(mods):
+    cases = {}
+    rng = np.random.default_rng(8)
+    pos = rng.uniform(0, 8.0, size=(40, 3)).astype(np.float32)
+    Z = rng.choice([1, 6, 7, 8], size=40)
+    cases["system_pbc40"] = system_case(mods, pos[None], Z[None], np.eye(3, dtype=np.float32) * 8.0,
+                                        [True, True, True], [1], [2], seed=41)
+    mols = synthetic.molecule_batch(4, 8, 20, seed=10)
+    P, ZZ = pad_systems([(m[0], m[1]) for m in mols])
+    cases["system_mol4"] = system_case(mods, P, ZZ, np.zeros((3, 3), np.float32), [False] * 3,
+                                       [-1, 0, 1, 0], [1, 2, 1, 1], seed=42, max_neighbors=12)
+    return cases
+
+
 def so2_pin(mods):
     mu, so2tp = mods["mu"], mods["so2tp"]
     torch.manual_seed(0)
@@ -382,7 +440,8 @@ def main(only=None):
         with open(os.path.join(HERE, "so2_pin.json"), "w") as f:
             json.dump(pin, f, indent=1)
         print("so2 pin", pin["max_abs_diff"])
-    makers = {"graph": graph_cases, "layer": layer_cases, "backbone": backbone_cases, "faiss": faiss_cases}
+    makers = {"graph": graph_cases, "layer": layer_cases, "backbone": backbone_cases, "faiss": faiss_cases,
+              "system": system_cases}
     for prefix, make in makers.items():
         if only is not None and prefix != only:
             continue

@@ -37,7 +37,8 @@ from collections import namedtuple
 import numpy as np
 import torch
 
-REF_ROOT = os.environ.get("E2A_REFERENCE_ROOT", "/root/reference")
+# the reference checkout: set E2A_REFERENCE_ROOT to its top directory (the one holding ``src/molfm``)
+REF_ROOT = os.environ.get("E2A_REFERENCE_ROOT", "")
 REF_SRC = os.path.join(REF_ROOT, "src")
 E2F_DIR = os.path.join(REF_SRC, "molfm", "models", "e2former")
 
@@ -308,7 +309,8 @@ def install():
     if _INSTALLED:
         return E2F_DIR
     if not os.path.isdir(E2F_DIR):
-        raise RuntimeError(f"reference sources not found at {E2F_DIR}")
+        raise RuntimeError(f"reference sources not found at {E2F_DIR!r}: set E2A_REFERENCE_ROOT to the "
+                           "reference checkout (the directory holding src/molfm)")
 
     e3nn = _mod("e3nn")
     o3 = _mod("e3nn.o3", Irreps=Irreps, Irrep=Irrep, spherical_harmonics=spherical_harmonics,

@@ -226,12 +226,21 @@ def _gather_worker(rank, world, port, out):
     parts = shard_molecules(sizes, world)
     mine = parts[rank]
     energies = torch.tensor([float(10 * i + 1) for i in mine])
-    allE = gather_molecule_results(energies, mine, len(sizes))
-    out[rank] = allE.tolist() == [float(10 * i + 1) for i in range(len(sizes))]
+    forces = [torch.arange(3 * sizes[i], dtype=torch.float32).reshape(-1, 3) + 100 * i for i in mine]
+    allE, allF = gather_molecule_results(energies, forces, mine, len(sizes))
+    if rank == 0:
+        ok = allE.tolist() == [float(10 * i + 1) for i in range(len(sizes))]
+        ok &= all(torch.equal(allF[i], torch.arange(3 * sizes[i], dtype=torch.float32).reshape(-1, 3) + 100 * i)
+                  for i in range(len(sizes)))
+    else:
+        ok = allE is None and allF is None
+    out[rank] = ok
     dist.destroy_process_group()
 
 
 def test_gather_molecule_results_gloo():
+    """Energies and forces of every rank's molecules end up on rank 0 in molecule order (3 ranks; one
+    rank holds fewer molecules, so the padded buffers differ in fill)."""
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_gather_worker, args=(3, _free_port(), out), nprocs=3, join=True)

@@ -117,3 +117,33 @@ def test_pair_product_recompute_matches_saved():
     (d1,) = torch.autograd.grad(p1, x, G)
     assert torch.equal(p0, p1)
     assert torch.equal(d0, d1)
+
+
+def test_bounded_wait_timeout_is_reported_and_raised():
+    """A bounded mbarrier wait that nothing completes (a test hook on the GEMM's own wait routine, with
+    a 1 ms limit) gives up and sets the status word; the host reads it once, the potential raises after
+    an evaluation that saw it, and the context stays usable."""
+    from ubio_molfm_b200 import _lib
+    from ubio_molfm_b200.model import E2FormerPotential
+    from ubio_molfm_b200.synthetic import seeded_params_
+
+    assert _lib.device_status_gemm(reset=True) == 0
+    _lib.gemm_wait_selftest(1_000_000)
+    assert _lib.device_status_gemm(reset=True) == 1
+    assert _lib.device_status_gemm(reset=True) == 0
+    with pytest.raises(_lib.E2AError):
+        _lib.gemm_wait_selftest(10)           # limits outside [1 us, 100 ms] are refused
+    m = E2FormerPotential(irreps_node_embedding="32x0e+32x1e+32x2e", num_layers=1, max_neighbors=None,
+                          max_radius=4.0, number_of_basis=32, num_attn_heads=8, attn_scalar_head=8,
+                          irreps_head="4x0e+4x1e+4x2e", norm_layer="rms_norm_sh", alpha_drop=0.0)
+    seeded_params_(m, 1)
+    m = m.cuda().eval()
+    g = torch.Generator().manual_seed(0)
+    pos = (torch.rand(30, 3, generator=g) * 6.0).cuda()
+    Z = torch.randint(1, 9, (30,), generator=g).cuda()
+    e0, f0 = m(pos, Z)
+    _lib.gemm_wait_selftest(1_000_000)
+    with pytest.raises(_lib.E2AError, match="timed out"):
+        m(pos, Z)
+    e1, f1 = m(pos, Z)                    # the word was cleared; the next evaluation is clean
+    assert torch.equal(e0, e1) and torch.equal(f0, f1)

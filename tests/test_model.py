@@ -195,3 +195,69 @@ def test_node_map_from_positions_matches_wigner_path():
     (gr,) = torch.autograd.grad(ref, pr, w)
     (gg,) = torch.autograd.grad(out, pg, w.float().to(DEV))
     assert (gg.double().cpu() - gr).abs().max().item() < 1e-4 * max(1.0, gr.abs().max().item())
+
+
+def _system_interface(rec, use_tf32=False):
+    from ubio_molfm_b200.interface import E2FormerModelInterface
+    from ubio_molfm_b200.model import E2FormerPotential
+    from ubio_molfm_b200.synthetic import SYSTEM_EMBED_GAINS, seeded_params_
+
+    cfg = json.loads(str(rec["cfg"]))
+    seed = cfg.pop("seed")
+    cfg.pop("head")
+    m = E2FormerPotential(**cfg)
+    seeded_params_(m.backbone, seed, gains=SYSTEM_EMBED_GAINS)
+    seeded_params_(m.energy_head, seed + 1)
+    return E2FormerModelInterface(model=m, device=DEV, use_tf32=use_tf32)
+
+
+def _system_input(rec):
+    from ubio_molfm_b200.interface import collate_systems
+
+    systems = []
+    for b in range(int(rec["batch"].max()) + 1):
+        sel = rec["batch"] == b
+        systems.append({"atoms": rec["Z"][sel], "coords": rec["pos"][sel], "charge": int(rec["charge"][b]),
+                        "multiplicity": int(rec["multiplicity"][b]),
+                        "cell": rec["cell"] if rec["pbc"].any() else None, "pbc": rec["pbc"]})
+    return collate_systems(systems, device=DEV)
+
+
+@pytest.mark.parametrize("name", ["system_pbc40", "system_mol4"])
+def test_predict_with_charge_matches_reference_backbone(name):
+    """``E2FormerModelInterface.predict`` on the collated input of the reference interface (charge and
+    multiplicity included) against the reference's own ``E2FormerBackbone`` + energy head: per-atom
+    energy within 1e-6 relative, forces within 1e-4 eV/A."""
+    rec = load(name)
+    out = _system_interface(rec).predict(_system_input(rec))
+    mask = _system_input(rec)["atom_masks"]
+    n_atoms = mask.sum(-1).double().cpu()
+    e_ref = torch.tensor(rec["energy"], dtype=torch.float64)
+    de = ((out["pred_energy"].double().cpu() - e_ref) / n_atoms).abs()
+    assert bool((de <= 1e-6 * (e_ref / n_atoms).abs() + 1e-7).all()), (out["pred_energy"], e_ref)
+    f = out["pred_forces"][mask].double().cpu()
+    assert (f - torch.tensor(rec["forces"], dtype=torch.float64)).abs().max().item() <= 1e-4
+    assert float(out["pred_forces"][~mask].abs().max()) == 0.0 if (~mask).any() else True
+    torch.testing.assert_close(out["pred_energy_per_atom"].cpu(), out["pred_energy"].cpu() / n_atoms.float())
+
+
+# Measured tolerance of the single-pass TF32 projection mode (``use_tf32=True``) against the
+# reference's fp32 results on the golden fixtures: relative to the largest |force| of the system.
+TF32_FORCE_REL_TOL = 2e-2
+TF32_ENERGY_REL_TOL = 2e-3
+
+
+@pytest.mark.parametrize("name", ["system_pbc40", "system_mol4"])
+def test_predict_tf32_mode_within_stated_tolerance(name):
+    rec = load(name)
+    out = _system_interface(rec, use_tf32=True).predict(_system_input(rec))
+    mask = _system_input(rec)["atom_masks"]
+    f_ref = torch.tensor(rec["forces"], dtype=torch.float64)
+    e_ref = torch.tensor(rec["energy"], dtype=torch.float64)
+    ferr = (out["pred_forces"][mask].double().cpu() - f_ref).abs().max().item() / f_ref.abs().max().item()
+    eerr = ((out["pred_energy"].double().cpu() - e_ref).abs() / e_ref.abs()).max().item()
+    print(f"tf32 mode {name}: force err {ferr:.2e} of max |F|, energy err {eerr:.2e} relative")
+    assert ferr <= TF32_FORCE_REL_TOL and eerr <= TF32_ENERGY_REL_TOL
+    # and the mode is really different from the fp32 parity mode
+    out32 = _system_interface(rec).predict(_system_input(rec))
+    assert not torch.equal(out32["pred_forces"], out["pred_forces"])

@@ -90,3 +90,33 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
                                         9000, 128, 8, 58, None, None, None, None, None, None, None, 256, None, None,
                                         None, None)
     assert rc == 3
+
+
+def test_noalloc_backward_matches_oracle_gradients():
+    """The allocation-free entry point's gradients directly against the CPU oracle of the reference's
+    attention span (float64 autograd), with the span parity tolerances (5e-5 of the largest gradient);
+    every output starts filled with 7.0 so an element the kernel leaves unwritten shows."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from oracle import attention_ref as R
+    from ubio_molfm_b200._lib import check, stream_of
+
+    dev = torch.device("cuda")
+    for seed in (2, 3):
+        lib, md, t, beta, rmax, rsum, shape = _setup(seed=seed)
+        N, M, E, H, D, C = shape
+        got = _outputs(shape)
+        check(lib.e2a_attn_bwd_query_noalloc(*_args(md, t, beta, rmax, rsum, shape, got), stream_of(dev)),
+              "e2a_attn_bwd_query_noalloc")
+        torch.cuda.synchronize()
+        ins = [t[k].detach().cpu().double().requires_grad_(True) for k in ("q", "k", "v", "gi", "poly", "dist")]
+        q_idx = torch.repeat_interleave(torch.arange(N), torch.diff(md[0].cpu().long()))
+        n_idx = md[1].cpu().long()
+        ref = R.attention_span(*ins, q_idx, n_idx, N)
+        gq, _, _, ggi, gp, gd = torch.autograd.grad(ref, ins, t["dout"].cpu().double())
+        for name, a, b in [("d_q", got["dq"], gq), ("d_gate/d_inputhead", got["dg"], ggi), ("d_poly", got["dp"], gp),
+                           ("d_dist", got["dd"], gd)]:
+            tol = 5e-5 * max(b.abs().max().item(), 1.0)
+            assert (a.cpu().double() - b).abs().max().item() <= tol, name

@@ -52,6 +52,7 @@ SIGNATURES = {
     "e2a_gemm_tf32x3": (I32, [P, I64, P, P, I64, P, I64, P, I64, I64, I64, I32, I32, P]),
     "e2a_tf32_split": (I32, [P, I64, I64, I64, P, P, I64, P]),
     "e2a_gemm_status": (I32, [P, I32, P]),
+    "e2a_gemm_wait_selftest": (I32, [I64, P]),
     "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
     "e2a_pair_grad": (I32, [P, P, I64, I32, I32, I32, P, P]),
     "e2a_node_apply_fwd": (I32, [P, P, I64, P, I64, I64, I32, I32, I32, P, I64, I32, P]),
@@ -121,6 +122,22 @@ def device_status_gemm(device=None, reset=True):
     v = ctypes.c_uint(0)
     check(lib.e2a_gemm_status(ctypes.byref(v), 1 if reset else 0, stream_of(device)), "e2a_gemm_status")
     return int(v.value)
+
+
+def raise_on_device_status(device=None):
+    """Read and clear the GEMM's wait-status word; raise if a bounded wait gave up since the last check
+    (the GEMM then left part of its output unwritten, so the results of that evaluation are invalid).
+    One stream synchronisation."""
+    st = device_status_gemm(device, reset=True)
+    if st:
+        raise E2AError(f"a tensor-core GEMM wait timed out on the device (status bits {st:#x}): the results "
+                       "computed since the last check are invalid")
+
+
+def gemm_wait_selftest(limit_ns=1_000_000, device=None):
+    """Run one bounded wait that nothing completes (test hook): it gives up after ``limit_ns`` and sets
+    the timeout bit that :func:`device_status_gemm` reports."""
+    check(load().e2a_gemm_wait_selftest(int(limit_ns), stream_of(device)), "e2a_gemm_wait_selftest")
 
 
 def ptr(t):

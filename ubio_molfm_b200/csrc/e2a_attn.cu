@@ -16,6 +16,8 @@
 //    the gathers in flight.  Rows run in a spatially coherent (Morton) order so that concurrently
 //    running CTAs share their gathered rows in L2.
 // Every sum over edges runs in CSR order inside one CTA: deterministic, no atomics.
+#include <mutex>
+
 #include "e2a_common.cuh"
 
 namespace {
@@ -980,7 +982,10 @@ int e2a_attn_bwd_dk(const float* q, const float* d_logit, const int32_t* k_row_p
 //    n_edges * H > 2^20 are rejected with E2A_ERR_WORKSPACE;
 //  * every GPU that loads the library holds the 8 MiB array until the process exits;
 //  * the first call on a device looks up the array's device address (cudaGetSymbolAddress) with
-//    that device current; make that first call before any stream capture;
+//    that device current; make that first call before any stream capture.  The address is kept per
+//    device together with the id of the CUDA context it was looked up in: when that context is
+//    destroyed and a new one made (cudaDeviceReset, a framework tearing its context down), the next
+//    call looks the address up again (the array's contents do not survive);
 //  * all calls share the one array: calls whose execution overlaps on the GPU (different streams,
 //    or different host threads on one device) race and corrupt each other's results.  Nothing in the
 //    array needs to start at zero: every scratch element is written before it is read in a call.
@@ -989,7 +994,37 @@ namespace {
 constexpr size_t kNoAllocScratchFloats = (size_t)2 << 20;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 constexpr int kMaxDevices = 64;
-float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+struct NoAllocSlot {
+  unsigned long long ctx_id = 0;  // id of the context the address belongs to (0: none yet)
+  float* ptr = nullptr;
+};
+NoAllocSlot g_noalloc_slot[kMaxDevices];
+std::mutex g_noalloc_mutex;  // set-up may race between host threads
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetCurrent + cuCtxGetId, reached through
+// the runtime's driver entry points, so the library needs no link against libcuda); 0 if unavailable.
+unsigned long long current_context_id() {
+  typedef int (*GetCurrentFn)(void**);
+  typedef int (*GetIdFn)(void*, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(f);
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
 }  // namespace
 
 extern "C" int e2a_attn_bwd_query_noalloc(
@@ -1012,12 +1047,19 @@ extern "C" int e2a_attn_bwd_query_noalloc(
   int dev = 0;
   E2A_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return E2A_ERR_UNSUPPORTED;
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    E2A_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  const unsigned long long ctx = current_context_id();
+  float* bufA = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (slot.ptr == nullptr || ctx == 0 || slot.ctx_id != ctx) {  // ctx 0: no id available, look up again
+      void* p = nullptr;
+      E2A_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      slot.ptr = static_cast<float*>(p);
+      slot.ctx_id = ctx;
+    }
+    bufA = slot.ptr;
   }
-  float* bufA = g_noalloc_ptr[dev];
   float* bufB = bufA + kNoAllocScratchFloats / 2;
   return bwd_query_launch(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm, ks,
                           beta, row_max, row_sum, dout, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,

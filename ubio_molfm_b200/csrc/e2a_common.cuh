@@ -118,14 +118,15 @@ __device__ __forceinline__ uint64_t e2a_globaltimer() {
 
 #define E2A_DEV_WAIT_TIMEOUT 1u
 
-// Wait for phase `parity` of `bar`, giving up after ~2 s (then sets E2A_DEV_WAIT_TIMEOUT in
-// *status); returns false on timeout.
-__device__ __forceinline__ bool e2a_mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* status) {
+// Wait for phase `parity` of `bar`, giving up after `limit_ns` (~2 s by default; then sets
+// E2A_DEV_WAIT_TIMEOUT in *status); returns false on timeout.
+__device__ __forceinline__ bool e2a_mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* status,
+                                                      uint64_t limit_ns = 2000000000ull) {
   if (e2a_mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = e2a_globaltimer();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     if (e2a_mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && e2a_globaltimer() - t0 > 2000000000ull) break;
+    if ((it & 255u) == 0u && e2a_globaltimer() - t0 > limit_ns) break;
   }
   atomicOr(status, E2A_DEV_WAIT_TIMEOUT);
   return false;

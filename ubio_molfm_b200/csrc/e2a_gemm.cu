@@ -340,7 +340,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(e2a_smem_u32(bar)) : "memory");
 }
-// 2-D tensor copy global -> this CTA's shared memory (no multicast), completion on `bar`
+// 2-D tensor copy global -> this CTA's shared memory (this CTA only), completion on `bar`
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -868,6 +868,24 @@ int e2a_gemm_trace(unsigned long long* out) {
   return E2A_OK;
 }
 #endif
+
+// One thread waits, through the same bounded wait the GEMM roles use, on an mbarrier that nothing
+// arrives at: the wait gives up after `limit_ns` and records E2A_DEV_WAIT_TIMEOUT in the GEMM's status
+// word, so the host-side reporting path can be exercised without a stuck kernel.
+__global__ void k_gemm_wait_selftest(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  e2a_mbar_init(&bar, 1);
+  e2a_fence_mbar_init();
+  e2a_mbar_wait_bounded(&bar, 0, &g_e2a_gemm_status, limit_ns);
+}
+
+int e2a_gemm_wait_selftest(long long limit_ns, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 100000000LL) return E2A_ERR_ARG;
+  k_gemm_wait_selftest<<<1, 32, 0, (cudaStream_t)stream>>>((uint64_t)limit_ns);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
 
 int e2a_gemm_status(unsigned int* status, int reset, void* stream) {
   if (!status) return E2A_ERR_ARG;

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 from .graph import _DistFn, expand_pbc, morton_row_order, pbc_image_offsets, radius_graph
 from .nn import polynomial
 
@@ -145,11 +145,14 @@ def local_graph(pos_local, geometry, n_local, cutoff, n_query=None):
     return g
 
 
-def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), group=None):
+def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), group=None, charge=None,
+                         multiplicity=None):
     """Energy of the whole system and forces on this rank's owned atoms under slab decomposition.
 
-    ``pos_all`` / ``Z_all``: every atom's position and type (replicated on every rank).  Returns
-    ``(energy_total [1], own_gid, forces_own [n_own, 3])``; every rank must call it (collectives)."""
+    ``pos_all`` / ``Z_all``: every atom's position and type (replicated on every rank).  ``charge`` /
+    ``multiplicity``: the system's (one value each, or None), whose embedding every row takes, ghosts
+    included.  Returns ``(energy_total [1], own_gid, forces_own [n_own, 3])``; every rank must call it
+    (collectives)."""
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     dec = model.decoder
     plan, own_gid, local_gid, geom = domain_graph(pos_all, cell, pbc, dec.max_radius, dec.max_neighbors, world,
@@ -158,9 +161,16 @@ def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), gr
         pos_own = pos_all.detach()[own_gid].to(torch.float32).requires_grad_(True)
         pos_local = plan.exchange(pos_own)
         graph = local_graph(pos_local, geom, local_gid.numel(), dec.max_radius, n_query=plan.n_own)
-        x = dec(pos_local, Z_all[local_gid], graph, True, halo=lambda t: plan.exchange(t[:plan.n_own]))
+        sys_emb = None
+        if charge is not None:
+            mult = torch.ones(1, dtype=torch.long) if multiplicity is None else multiplicity
+            sys_emb = model.backbone.system_embedding(charge, mult)[:1]
+        x = dec(pos_local, Z_all[local_gid], graph, True, halo=lambda t: plan.exchange(t[:plan.n_own]),
+                sys_embedding=sys_emb)
         e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1).sum()
         (grad,) = torch.autograd.grad(e_own, pos_own)
+    if pos_own.is_cuda and model.check_device_status:
+        _lib.raise_on_device_status(pos_own.device)
     energy = e_own.detach().reshape(1).clone()
     dist.all_reduce(energy, group=group)
     return energy, own_gid, -grad
@@ -183,43 +193,70 @@ def shard_molecules(sizes, world):
 
 
 def molecules_energy_forces(model, mols, device, max_atoms_per_call=60000):
-    """Energies [M] and forces (list of [n_i, 3]) of non-periodic molecules ``mols`` = [(pos, Z), ...],
-    evaluated in batches of at most ``max_atoms_per_call`` atoms (systems never see each other)."""
+    """Energies [M] and forces (list of [n_i, 3]) of non-periodic molecules ``mols`` = [(pos, Z) or
+    (pos, Z, charge, multiplicity), ...], evaluated in batches of at most ``max_atoms_per_call`` atoms
+    (systems never see each other).  With charges given, each molecule's charge / multiplicity system
+    embedding enters its evaluation (e2former_wrapper.py:249-259)."""
     energies, forces = [], []
+    with_charge = len(mols) > 0 and len(mols[0]) >= 4
     i = 0
     while i < len(mols):
         j, n = i, 0
         while j < len(mols) and (j == i or n + len(mols[j][1]) <= max_atoms_per_call):
             n += len(mols[j][1])
             j += 1
-        pos = torch.cat([torch.as_tensor(m[0], dtype=torch.float32) for m in mols[i:j]]).to(device)
-        Z = torch.cat([torch.as_tensor(m[1], dtype=torch.int64) for m in mols[i:j]]).to(device)
-        batch = torch.cat([torch.full((len(m[1]),), k, dtype=torch.int64) for k, m in enumerate(mols[i:j])]).to(device)
-        e, f = model(pos, Z, None, (False, False, False), batch)
+        part = mols[i:j]
+        pos = torch.cat([torch.as_tensor(m[0], dtype=torch.float32) for m in part]).to(device)
+        Z = torch.cat([torch.as_tensor(m[1], dtype=torch.int64) for m in part]).to(device)
+        batch = torch.cat([torch.full((len(m[1]),), k, dtype=torch.int64) for k, m in enumerate(part)]).to(device)
+        kw = {}
+        if with_charge:
+            kw = {"charge": torch.tensor([int(m[2]) for m in part]), "multiplicity": torch.tensor([int(m[3]) for m in part])}
+        e, f = model(pos, Z, None, (False, False, False), batch, **kw)
         energies.append(e)
-        forces.extend(torch.split(f, [len(m[1]) for m in mols[i:j]]))
+        forces.extend(torch.split(f, [len(m[1]) for m in part]))
         i = j
     return torch.cat(energies), forces
 
 
-def gather_molecule_results(energies, idx, n_total, group=None):
-    """All ranks' energies into one [n_total] tensor (ordered by molecule index) on every rank."""
-    world = dist.get_world_size(group)
+def gather_molecule_results(energies, forces, idx, n_total, group=None, dst=0):
+    """Every rank's molecule energies and forces on rank ``dst``, ordered by molecule index.
+
+    ``energies`` [m_r], ``forces`` a list of [n_i, 3] in the order of ``idx`` (this rank's molecule
+    indices).  One size exchange, then one gather of a padded buffer per rank holding, per molecule,
+    its index, atom count and energy, followed by all its forces.  Returns ``(energies [n_total],
+    [forces of molecule 0, 1, ...])`` on ``dst`` and ``(None, None)`` elsewhere."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
     dev = energies.device
-    counts = torch.tensor([len(idx)], device=dev)
-    all_counts = [torch.zeros_like(counts) for _ in range(world)]
-    dist.all_gather(all_counts, counts, group=group)
-    m = int(max(int(c) for c in all_counts))
-    buf_e = torch.zeros(m, device=dev, dtype=energies.dtype)
-    buf_i = torch.full((m,), -1, device=dev, dtype=torch.int64)
-    buf_e[: len(idx)] = energies
-    buf_i[: len(idx)] = torch.as_tensor(idx, device=dev)
-    ge = [torch.zeros_like(buf_e) for _ in range(world)]
-    gi = [torch.zeros_like(buf_i) for _ in range(world)]
-    dist.all_gather(ge, buf_e, group=group)
-    dist.all_gather(gi, buf_i, group=group)
-    out = torch.zeros(n_total, device=dev, dtype=energies.dtype)
-    for e_r, i_r in zip(ge, gi):
-        keep = i_r >= 0
-        out[i_r[keep]] = e_r[keep]
-    return out
+    m = len(idx)
+    sizes = [int(f.shape[0]) for f in forces]
+    n_words = 3 * m + 3 * sum(sizes)
+    cnt = torch.tensor([n_words, m], device=dev, dtype=torch.int64)
+    all_cnt = [torch.zeros_like(cnt) for _ in range(world)]
+    dist.all_gather(all_cnt, cnt, group=group)
+    all_cnt = [c.tolist() for c in all_cnt]
+    width = max(c[0] for c in all_cnt)
+    buf = torch.zeros(max(width, 1), device=dev, dtype=torch.float64)
+    if m:
+        head = torch.stack([torch.as_tensor(idx, dtype=torch.float64, device=dev),
+                            torch.tensor(sizes, dtype=torch.float64, device=dev), energies.to(torch.float64)], 1)
+        buf[:3 * m] = head.reshape(-1)
+        if sum(sizes):
+            buf[3 * m:n_words] = torch.cat([f.reshape(-1) for f in forces]).to(torch.float64)
+    bufs = [torch.zeros_like(buf) for _ in range(world)] if rank == dst else None
+    dist.gather(buf, bufs, dst=dst, group=group)
+    if rank != dst:
+        return None, None
+    out_e = torch.zeros(n_total, device=dev, dtype=energies.dtype)
+    out_f = [None] * n_total
+    for b, (words, k) in zip(bufs, all_cnt):
+        if k == 0:
+            continue
+        hd = b[:3 * k].reshape(k, 3)
+        mol = hd[:, 0].long()
+        nat = hd[:, 1].long().tolist()
+        out_e[mol] = hd[:, 2].to(energies.dtype)
+        fl = b[3 * k:words].reshape(-1, 3).to(energies.dtype)
+        for j, part in zip(mol.tolist(), torch.split(fl, nat)):
+            out_f[j] = part
+    return out_e, out_f

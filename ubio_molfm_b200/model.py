@@ -21,6 +21,7 @@ import numpy as np
 import torch
 from torch import nn
 
+from . import _lib
 from . import linear as tc
 from . import ops
 from .attention import E2AttentionArbOrder_sparse
@@ -294,14 +295,16 @@ class E2former(nn.Module):
             elif rest == "edge_deg_embed_dense.sph.W":
                 del state_dict[k]
 
-    def forward(self, node_pos, atomic_numbers, graph, pbc_any, halo=None):
+    def forward(self, node_pos, atomic_numbers, graph, pbc_any, halo=None, sys_embedding=None):
         """``graph``: the flattened neighbour dict (``query_idx``, ``neighbor_idx``, ``metadata``,
         ``f_edge_vec``, ``f_dist``, ``f_poly_dist``, ``f_outcell_index``, ``f_exp_node_pos`` and the
         optional ``row_order`` / ``key_order``).  Returns the node irreps [N, (lmax+1)^2, C].
         ``halo`` (domain decomposition): called on the node irreps before every block to refresh the
         rows of atoms owned by other ranks.  With ``graph["n_query"]`` = n, only rows [0, n) are queries:
         the embedding and every block return those rows, and ``halo`` appends the others before each
-        block (it receives the n query rows)."""
+        block (it receives the n query rows).  ``sys_embedding`` ([rows, C] or [1, C], or None): the
+        charge / multiplicity embedding of each row's system, added to the normed l=0 row of every
+        block (e2former.py:1074-1077, 582-583); with a halo it must cover the appended rows too."""
         if int(graph.get("n_query", node_pos.shape[0])) != node_pos.shape[0] and halo is None:
             raise ValueError("n_query < number of nodes needs a halo to refresh the other rows")
         jd = [j.to(torch.float64) for j in self.Jd_list]
@@ -329,11 +332,52 @@ class E2former(nn.Module):
         for blk in self.blocks:
             if halo is not None:
                 x = halo(x)
-            x, f_dist_embedding = blk(node_pos=node_pos, node_irreps=x, sys_node_embedding=None,
+            x, f_dist_embedding = blk(node_pos=node_pos, node_irreps=x, sys_node_embedding=sys_embedding,
                                       edge_dis=graph["f_dist"], edge_vec=graph["f_edge_vec"],
                                       attn_weight=f_dist_embedding, atomic_numbers=atomic_numbers, attn_mask=None,
                                       poly_dist=graph["f_poly_dist"], batched_data=bd)
         return self.norm_final(x)
+
+
+class E2FormerBackbone(nn.Module):
+    """The wrapper around :class:`E2former` with the reference's parameters and names
+    (e2former_wrapper.py:36-339): the atom-type table ``embedding``, the system embedding of the total
+    charge and spin multiplicity (``embedding_charge``, ``embedding_multiplicity``, ``mix_cm``),
+    ``unifiedtokentoembedding`` and, with ``encoder != "default"``, ``embed_proj``; the decoder is
+    ``self.decoder``.  A strict ``load_state_dict`` of the reference backbone's state dict works.
+
+    Of these only the system embedding reaches the output: the decoder never reads the per-atom token
+    embedding (e2former.py:1032-1043 passes it to the edge-degree embedding, which uses only its row
+    count), so ``embedding`` / ``unifiedtokentoembedding`` / ``embed_proj`` are kept for checkpoints."""
+
+    def __init__(self, use_faiss=False, **kwargs):
+        super().__init__()
+        self.use_faiss = use_faiss
+        C, _ = irreps_channels_lmax(kwargs["irreps_node_embedding"])
+        encoder = kwargs.get("encoder", "default")
+        dim = C if encoder == "default" else kwargs["encoder_embed_dim"]
+        self.embedding = nn.Embedding(256, dim)
+        self.embedding_charge = nn.Embedding(30, dim)
+        self.embedding_multiplicity = nn.Embedding(30, dim)
+        self.mix_cm = nn.Sequential(nn.Linear(2 * dim, dim), nn.SiLU())
+        self.unifiedtokentoembedding = nn.Linear(dim, dim)
+        if encoder != "default":
+            self.embed_proj = nn.Sequential(nn.Linear(kwargs["encoder_embed_dim"], C), nn.SiLU(),
+                                            nn.LayerNorm(C, eps=1e-6))
+        if kwargs.get("max_neighbors", None) == "None":
+            kwargs["max_neighbors"] = None
+        self.decoder = E2former(**kwargs)
+
+    def system_embedding(self, charge, multiplicity):
+        """[B, C] from the per-system total charge and spin multiplicity (integers, any shape holding
+        B values): ``mix_cm([embedding_charge(clip(q, -10, 10) + 10), embedding_multiplicity(clip(m, 0,
+        20))])`` (e2former_wrapper.py:249-255)."""
+        q = torch.clamp(torch.as_tensor(charge).reshape(-1).to(torch.long), -10, 10) + 10
+        s = torch.clamp(torch.as_tensor(multiplicity).reshape(-1).to(torch.long), 0, 20)
+        dev = self.embedding_charge.weight.device
+        h = torch.cat([self.embedding_charge(q.to(dev)), self.embedding_multiplicity(s.to(dev))], dim=-1)
+        lin0 = self.mix_cm[0]
+        return torch.nn.functional.silu(lin(h, lin0.weight, lin0.bias, not self.training))
 
 
 class MLP_energy_head(nn.Module):
@@ -366,13 +410,41 @@ class E2FormerPotential(nn.Module):
         # (distributed_cell_expand, one image cell per direction) instead of CellExpander's; the edges
         # are the same physical neighbours, found by the same exact search (FAISS itself is not used)
         self.use_faiss = use_faiss
-        self.decoder = E2former(**backbone_kwargs)
+        # after every evaluation, read (one stream sync) and clear the status word of the GEMM's bounded
+        # waits, raising if one gave up: an aborted projection leaves its output partly unwritten
+        self.check_device_status = True
+        self.backbone = E2FormerBackbone(use_faiss=use_faiss, **backbone_kwargs)
         self.energy_head = MLP_energy_head(self.decoder.scalar_dim, self.decoder.lmax)
         # large systems: the Q / K projections are formed again in the backward (saves 2 x 4 x hidden
         # floats per irreps row per layer; ~29 GB at 1e5 atoms with the full-size model)
         for blk in self.decoder.blocks:
             blk.ga.query_linear.recompute_pair_product = memory_saving
             blk.ga.key_linear.recompute_pair_product = memory_saving
+
+    @property
+    def decoder(self):
+        """The :class:`E2former` inside the backbone."""
+        return self.backbone.decoder
+
+    def load_reference_state_dict(self, state_dict, head_name=None, strict=True):
+        """Load a reference ``MolfmAtomic`` state dict (tasks/pretrain_smallmol.py:170-210): ``decoder.*``
+        is the backbone, ``head.energy_heads.<head_name>.mlp.*`` the energy MLP.  With ``head_name``
+        None the state dict must hold exactly one energy head."""
+        sd = {}
+        heads = sorted({k.split(".")[2] for k in state_dict if k.startswith("head.energy_heads.")})
+        if head_name is None:
+            if len(heads) != 1:
+                raise ValueError(f"state dict holds energy heads {heads}: pass head_name")
+            head_name = heads[0]
+        elif head_name not in heads:
+            raise KeyError(f"no energy head {head_name!r} in the state dict (has {heads})")
+        pre = f"head.energy_heads.{head_name}."
+        for k, v in state_dict.items():
+            if k.startswith("decoder."):
+                sd["backbone." + k[len("decoder."):]] = v
+            elif k.startswith(pre):
+                sd["energy_head." + k[len(pre):]] = v
+        return self.load_state_dict(sd, strict=strict)
 
     def build_graph(self, pos, cell, pbc, batch):
         dec = self.decoder
@@ -407,11 +479,22 @@ class E2FormerPotential(nn.Module):
         g["f_exp_node_pos"] = exp_pos
         return g, pbc_any
 
-    def forward(self, pos, atomic_numbers, cell=None, pbc=(False, False, False), batch=None, need_forces=True):
+    def forward(self, pos, atomic_numbers, cell=None, pbc=(False, False, False), batch=None, need_forces=True,
+                charge=None, multiplicity=None):
+        """``charge`` / ``multiplicity``: per-system integers ([B] or None).  Given (as the reference's
+        interface always does, interface/data_utils.py:53-65), their system embedding is added to the
+        normed l=0 row of every block; None evaluates the decoder without it (e2former_wrapper.py:249-250
+        with no ``charge`` key).  ``multiplicity`` defaults to 1 when only ``charge`` is given."""
         pos = pos.detach().to(torch.float32).requires_grad_(need_forces)
         with torch.enable_grad() if need_forces else torch.no_grad():
             g, pbc_any = self.build_graph(pos, cell, pbc, batch)
-            x = self.decoder(pos, atomic_numbers, g, pbc_any)
+            sys_emb = None
+            if charge is not None:
+                if multiplicity is None:
+                    multiplicity = torch.ones_like(torch.as_tensor(charge))
+                sys_emb = self.backbone.system_embedding(charge, multiplicity)
+                sys_emb = sys_emb[batch] if batch is not None else sys_emb[:1]
+            x = self.decoder(pos, atomic_numbers, g, pbc_any, sys_embedding=sys_emb)
             e_atom = self.energy_head(x[:, 0]).squeeze(-1)
             if batch is None:
                 energy = e_atom.sum().reshape(1)
@@ -422,4 +505,6 @@ class E2FormerPotential(nn.Module):
             if need_forces:
                 (grad,) = torch.autograd.grad(energy.sum(), pos)
                 forces = -grad
+        if pos.is_cuda and self.check_device_status:
+            _lib.raise_on_device_status(pos.device)
         return energy.detach(), forces

@@ -307,7 +307,12 @@ class E2TensorProductSO2_FirstOrder(nn.Module):
     def node_map_from_pos(self, pos, jd, row_perm=None):
         """The same maps as :meth:`node_map`, formed by one kernel from the positions (``jd``: the
         J matrices of degrees 0..2); the Wigner matrices are never materialised."""
-        key = (id(jd[1]), id(jd[2]), None if row_perm is None else tuple(row_perm))
+        # the tables are rebuilt when any source changes: the J matrices, and the selection table and CG
+        # weights (state-dict entries: load_state_dict / .to() move their version counter or storage)
+        tp = self.so2_tp
+        srcs = [jd[1], jd[2], tp.selected_idx, tp.CG_weight]
+        key = (tuple((id(t), t._version, t.data_ptr(), t.dtype, t.device) for t in srcs),
+               None if row_perm is None else tuple(row_perm))
         cache = getattr(self, "_map_tables", None)
         if cache is None or cache[0] != key:
             tp = self.so2_tp

@@ -222,8 +222,15 @@ def seeded_tensor(seed, name, shape, kind="weight"):
     return (u / math.sqrt(fan_in)).float()
 
 
-def seeded_params_(module: torch.nn.Module, seed: int = 0):
-    """Overwrite trainable float parameters of ``module`` in place (frozen tables are kept)."""
+# fixtures with a charge / multiplicity: the system embedding tables drawn 300x larger and its linear 3x, so that the
+# embedding moves energies and forces well beyond the parity tolerances
+SYSTEM_EMBED_GAINS = {"embedding_charge.": 300.0, "embedding_multiplicity.": 300.0, "mix_cm.": 3.0}
+
+
+def seeded_params_(module: torch.nn.Module, seed: int = 0, gains=None):
+    """Overwrite trainable float parameters of ``module`` in place (frozen tables are kept).
+    ``gains``: {parameter-name prefix: factor} applied after the draw (e.g. to make a small term of
+    the model large enough for a test to see)."""
     with torch.no_grad():
         for name, p in module.named_parameters():
             if not p.is_floating_point() or name.endswith(_FROZEN_SUFFIXES) or not p.requires_grad:
@@ -239,5 +246,9 @@ def seeded_params_(module: torch.nn.Module, seed: int = 0):
                 kind = "bias"
             else:
                 kind = "weight"
-            p.copy_(seeded_tensor(seed, name, tuple(p.shape), kind).to(p.device))
+            t = seeded_tensor(seed, name, tuple(p.shape), kind)
+            for pre, f in (gains or {}).items():
+                if name.startswith(pre):
+                    t = t * f
+            p.copy_(t.to(p.device))
     return module
