@@ -51,13 +51,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules"])
+    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules", "span"])
     ap.add_argument("--molecules", type=int, default=4096, help="molecules workload: batch size")
     ap.add_argument("--atoms", type=int, default=100_000, help="layer workload: atoms")
     ap.add_argument("--k", type=int, default=32)
     ap.add_argument("--cpu-atoms", type=int, default=None,
                     help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fused-fwd", type=int, default=1, choices=[0, 1, 2],
+                    help="forward span kernels: 0 softmax + aggregation, 1 / 2 fused at 3 / 2 CTAs per SM")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="model workload with N > 1: independent systems per rank instead of one system "
@@ -739,15 +741,159 @@ def run_molecules(args, ws, rank, local):
         print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------
+# Same-box kernel bar: this package's attention span against the reference's own Triton kernels
+# ------------------------------------------------------------------------------------------------
+def _load_reference_triton():
+    """The reference's Triton modules (triton_dr/*.py) from the offline install under baseline/_ref,
+    loaded without executing the parent packages' __init__ (they import e3nn / torch_geometric)."""
+    import importlib
+    import types
+
+    base = os.path.join(ROOT, "baseline", "_ref", "molfm", "models", "e2former")
+    if not os.path.isdir(os.path.join(base, "triton_dr")):
+        return None, "the reference is not installed under baseline/_ref"
+    for name, path in [("molfm", os.path.join(ROOT, "baseline", "_ref", "molfm")),
+                       ("molfm.models", os.path.join(ROOT, "baseline", "_ref", "molfm", "models")),
+                       ("molfm.models.e2former", base)]:
+        if name not in sys.modules:
+            m = types.ModuleType(name)
+            m.__path__ = [path]
+            sys.modules[name] = m
+    try:
+        mods = {s: importlib.import_module(f"molfm.models.e2former.triton_dr.{s}") for s in
+                ("triton_sparse_qk_autograd", "sparse_alpha_sum_edge_index_autograd",
+                 "sparse_v_agg_edge_index_cblocked_bench")}
+    except Exception as exc:  # noqa: BLE001
+        return None, f"reference Triton kernels failed to import: {exc!r}"[:300]
+    return mods, None
+
+
+def reference_span(mods, q, k, v, gi, poly, dist, q_idx, n_idx, md, N):
+    """The reference's attention span on its Triton path, composed as E2AttentionArbOrder_sparse
+    does (e2former.py:311-364 and 393-422; so2_tensor_product.py:341-389 aggregates the merged value
+    with one call): Triton q.k, torch segmented max / exp, Triton row sum, alpha / r, Triton V
+    aggregation."""
+    H = q.shape[1]
+    qk = mods["triton_sparse_qk_autograd"].sparse_qk_edge_index_triton(q, k, q_idx, n_idx, metadata=md)
+    gate, inputhead = gi[:, :H], gi[:, H:]
+    alpha = gate * qk
+    qil = q_idx.long()
+    idx = qil.unsqueeze(-1).expand(-1, H)
+    amax = torch.full((N, H), -torch.inf, device=q.device, dtype=alpha.dtype)
+    amax.scatter_reduce_(0, idx, alpha, reduce="amax", include_self=True)
+    alpha = torch.exp(alpha - amax[qil]) * poly.unsqueeze(-1)
+    asum = mods["sparse_alpha_sum_edge_index_autograd"].sparse_alpha_sum_edge_index_triton(
+        alpha, q_idx, N, metadata=(md[0], md[2]))
+    alpha = alpha * inputhead / (asum[qil] + 1e-3)
+    alpha_r = alpha / dist.unsqueeze(-1).clamp_min(1e-6)
+    return mods["sparse_v_agg_edge_index_cblocked_bench"].sparse_v_agg_edge_index_triton_cblocked(
+        value=v.contiguous(), alpha=alpha_r, query_index=q_idx, value_index=n_idx, num_queries=N, metadata=md)
+
+
+def run_span(args, ws, rank, local):
+    """The attention span alone (q.k, segmented softmax, alpha / r, value aggregation; forward and the
+    first-order backward) on the config-2 graph (uniform periodic box, ~k neighbours within 6 A,
+    H = 128 heads of 8, C = 58 value rows), this package's kernels against the reference's Triton
+    kernels from baseline/_ref on the same inputs, CUDA events, median of ``--steps`` repeats."""
+    from ubio_molfm_b200 import _lib, ops
+    from ubio_molfm_b200.graph import expand_pbc, radius_graph
+    from ubio_molfm_b200.synthetic import uniform_box
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pos_np, _, cell = uniform_box(args.atoms, args.k, CUTOFF, seed=100)
+    pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
+    exp_pos, _, _ = expand_pbc(pos, cell, [True, True, True], CUTOFF)
+    N, N2 = pos.shape[0], exp_pos.shape[0]
+    g = radius_graph(pos, exp_pos, torch.tensor([0, N]), torch.tensor([0, N2]), CUTOFF, 1e-4, None)
+    q_idx, n_idx = g["query_idx"], g["neighbor_idx"]
+    E = q_idx.numel()
+    H, D, C = HEADS, DHEAD, 58
+    gen = torch.Generator(device=dev).manual_seed(0)
+    ins = [torch.randn(N, H, D, device=dev, generator=gen) / D ** 0.5, torch.randn(N2, H, D, device=dev, generator=gen),
+           torch.randn(N2, C, H, device=dev, generator=gen), torch.randn(E, 2 * H, device=dev, generator=gen),
+           g["f_poly_dist"].detach(), g["f_dist"].detach()]
+    dout = torch.randn(N, C, H, device=dev, generator=gen)
+    leaves = [t.detach().clone().requires_grad_(True) for t in ins]
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return round(statistics.median(ts), 3)
+
+    def ours_fwd():
+        with torch.no_grad():
+            return ops.attention_span(*ins, g["metadata"], g["row_order"])
+
+    def ours_fb():
+        out = ops.attention_span(*leaves, g["metadata"], g["row_order"])
+        return torch.autograd.grad(out, leaves, dout)
+
+    clocks = ClockSampler(local)
+    res = {"ours_fwd_ms": timed(ours_fwd), "ours_fwd_bwd_ms": timed(ours_fb)}
+    mods, why = _load_reference_triton()
+    if mods is None:
+        res["reference"] = {"unavailable": why}
+    else:
+        md_ref = mods["triton_sparse_qk_autograd"].prepare_sparse_qk_edge_index_metadata(
+            q_idx.to(torch.int32), n_idx.to(torch.int32), N, N2)
+        qi32, ni32 = q_idx.to(torch.int32), n_idx.to(torch.int32)
+        rleaves = [t.detach().clone().requires_grad_(True) for t in ins]
+
+        def ref_fwd():
+            with torch.no_grad():
+                return reference_span(mods, *ins, qi32, ni32, md_ref, N)
+
+        def ref_fb():
+            out = reference_span(mods, *rleaves, qi32, ni32, md_ref, N)
+            return torch.autograd.grad(out, rleaves, dout, allow_unused=True)
+
+        try:
+            o_ref = ref_fwd()
+            o_us = ours_fwd()
+            err = float((o_ref - o_us).abs().max()) / max(1.0, float(o_us.abs().max()))
+            res["reference"] = {"fwd_ms": timed(ref_fwd), "fwd_bwd_ms": timed(ref_fb), "max_rel_diff_vs_ours": err}
+            res["speedup_fwd"] = round(res["reference"]["fwd_ms"] / res["ours_fwd_ms"], 2)
+            res["speedup_fwd_bwd"] = round(res["reference"]["fwd_bwd_ms"] / res["ours_fwd_bwd_ms"], 2)
+        except Exception as exc:  # noqa: BLE001
+            res["reference"] = {"unavailable": f"reference Triton kernels failed on this box: {exc!r}"[:300]}
+    clk = clocks.stop()
+    if rank == 0:
+        line = {"metric": "attention span ms (forward; forward+backward)", "unit": "ms", "n_gpus": 1,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
+                "data": "synthetic (seeded uniform box, seeded N(0,1) features)",
+                "config": {"workload": f"attention span, uniform periodic box {N} atoms, ~{args.k} neighbours "
+                                       f"within {CUTOFF} A", "edges": E, "expanded_nodes": N2, "heads": H,
+                           "head_dim": D, "value_rows": C},
+                "results": res, "gpu_launches": None, "clocks": clk}
+        print(json.dumps(line))
+
+
 def main():
     args = parse()
     ws, rank, local = dist_init(args)
+    if args.impl == "ours":
+        from ubio_molfm_b200 import _lib
+
+        _lib.load().e2a_attn_set_fused_fwd(args.fused_fwd)
     if args.workload == "molecules":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the molecules workload has no CPU reference "
                                                                   "arm; use the default workload"}))
         else:
             run_molecules(args, ws, rank, local)
+    elif args.workload == "span":
+        run_span(args, ws, rank, local)
     elif args.workload == "model":
         if args.impl == "reference":
             run_reference_model(args, ws, rank)

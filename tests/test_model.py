@@ -242,9 +242,10 @@ def test_predict_with_charge_matches_reference_backbone(name):
 
 
 # Measured tolerance of the single-pass TF32 projection mode (``use_tf32=True``) against the
-# reference's fp32 results on the golden fixtures: relative to the largest |force| of the system.
-TF32_FORCE_REL_TOL = 2e-2
-TF32_ENERGY_REL_TOL = 2e-3
+# reference's fp32 results on the golden fixtures, relative to the largest |force| of the system (measured
+# on B200: 5.4e-4 and 6.7e-4 for forces, 5.1e-5 and 5.5e-5 for energies; bounds set 3x above that).
+TF32_FORCE_REL_TOL = 2e-3
+TF32_ENERGY_REL_TOL = 2e-4
 
 
 @pytest.mark.parametrize("name", ["system_pbc40", "system_mol4"])
