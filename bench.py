@@ -296,7 +296,7 @@ def run_cpu_baseline(n_atoms, k, steps=1, warmup=0):
         run()
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": kind,
             "sample": f"{desc}; median of {steps} steps, {t:.2f} s/step", "cpu_model": _cpu_model()}
 
 
@@ -517,8 +517,61 @@ def cpu_model_setup(n_atoms):
     return run, desc
 
 
+def cpu_model_setup_reference(n_atoms):
+    """The reference's own CPU path on the same bounded sample: its unmodified ``E2FormerBackbone``
+    (PBC expansion, dense radius graph, E2former, charge / multiplicity embedding) and
+    ``MLP_energy_head`` from the offline install under baseline/_ref, imported through the test-only
+    shim that stands in for its missing third-party packages (e3nn, torch_geometric, faiss), energy
+    and forces = -dE/dpos by autograd.  Returns (closure, description) or (None, why)."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "molfm")):
+        return None, "the reference is not installed under baseline/_ref"
+    os.environ["E2A_REFERENCE_ROOT"] = ref
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    try:
+        import importlib
+
+        import refshim
+
+        from ubio_molfm_b200.synthetic import bio_box, seeded_params_
+
+        refshim.load_reference()
+        wrapper = importlib.import_module("molfm.models.e2former.e2former_wrapper")
+        head_mod = importlib.import_module("molfm.pipeline.head")
+    except Exception as exc:  # noqa: BLE001
+        return None, f"the reference did not import: {exc!r}"[:300]
+    torch.set_num_threads(os.cpu_count() or 1)
+    bb = wrapper.E2FormerBackbone(use_faiss=False, encoder="default", tp_type="QK_alpha", attn_type="so2-first-order",
+                                  **MODEL_CFG).eval()
+    seeded_params_(bb, 0)
+    head = head_mod.MLP_energy_head(C_CH, 2)
+    seeded_params_(head, 1)
+    pos, Z, cell = bio_box(n_atoms, seed=3)
+    P = torch.tensor(pos, dtype=torch.float32).unsqueeze(0)
+    Zt = torch.tensor(Z, dtype=torch.long).unsqueeze(0)
+
+    def run():
+        p = P.clone().requires_grad_(True)
+        bd = {"pos": p, "atom_masks": torch.ones_like(Zt, dtype=torch.bool), "atomic_numbers": Zt,
+              "pbc": torch.ones((1, 3), dtype=torch.int32), "cell": torch.tensor(cell, dtype=torch.float32)[None],
+              "charge": torch.zeros((1, 1), dtype=torch.int32), "multiplicity": torch.ones((1, 1), dtype=torch.int32)}
+        out = bb(bd)
+        e = head(out["node_featuresBxN"], out["node_irrepsBxN"]).sum()
+        torch.autograd.grad(e, p)
+
+    desc = (f"{n_atoms}-atom biomolecular box: energy+forces of the full-size model by the reference's own "
+            f"E2FormerBackbone + MLP_energy_head on the CPU (pure-PyTorch path, fp32)")
+    return run, desc
+
+
 def run_cpu_model(n_atoms, steps=1, warmup=0):
-    run, desc = cpu_model_setup(n_atoms)
+    run, desc = cpu_model_setup_reference(n_atoms)
+    kind = "reference"
+    if run is None:
+        why = desc
+        run, desc = cpu_model_setup(n_atoms)
+        kind = "port"
+        desc = f"{desc} (the reference itself: {why})"
     for _ in range(warmup):
         run()
     times = []
@@ -527,7 +580,7 @@ def run_cpu_model(n_atoms, steps=1, warmup=0):
         run()
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": n_atoms / t, "unit": "atom-steps/s", "cores": torch.get_num_threads(), "kind": kind,
             "sample": f"{desc}; median of {steps} steps, {t:.2f} s/step", "cpu_model": _cpu_model()}
 
 
@@ -659,7 +712,7 @@ def run_model(args, ws, rank, local):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = run_cpu_model(args.cpu_atoms or 500, 1, 0)
+        cpu = run_cpu_model(args.cpu_atoms or 500, 1, 1)
 
     if rank == 0:
         cfgd = model_config_dict(args, N, E, N2)

@@ -37,9 +37,12 @@ from collections import namedtuple
 import numpy as np
 import torch
 
-# the reference checkout: set E2A_REFERENCE_ROOT to its top directory (the one holding ``src/molfm``)
+# the reference: set E2A_REFERENCE_ROOT to a checkout (the directory holding ``src/molfm``) or to an
+# installed copy (the directory holding ``molfm``)
 REF_ROOT = os.environ.get("E2A_REFERENCE_ROOT", "")
-REF_SRC = os.path.join(REF_ROOT, "src")
+# a checkout holds the package under src/; an installed copy (pip --target) holds it at the top
+REF_SRC = (os.path.join(REF_ROOT, "src") if os.path.isdir(os.path.join(REF_ROOT, "src", "molfm"))
+           else REF_ROOT)
 E2F_DIR = os.path.join(REF_SRC, "molfm", "models", "e2former")
 
 

@@ -129,3 +129,20 @@ def test_use_faiss_order_equals_default():
     (e0, f0, n0), (e1, f1, n1) = out
     assert n0 == n1
     _check_energy_forces(e1, f1, e0.detach().cpu(), f0.detach().cpu(), len(Z))
+
+
+def test_config5_like_blob_in_water_full_model_cutoff6():
+    """Config 5's composition and cutoff at a size the CPU oracle finishes: a seeded 1,000-atom
+    H/C/N/O/S blob at 1.35 g/cm^3 in rigid water at 1.0 g/cm^3 (40 A periodic cube, ~6k atoms), the
+    full-size model at cutoff 6 A with <= 32 neighbours: energy and forces against the oracle."""
+    from ubio_molfm_b200.synthetic import blob_in_water
+
+    cfg = dict(FULL, max_radius=6.0)
+    model, p, ph = _models(cfg, 17)
+    pos, Z, cell = blob_in_water(box=40.0, n_blob=1000, seed=5)
+    assert 5000 <= len(Z) <= 10000
+    pos_t, Z_t = torch.tensor(pos, dtype=torch.float32), torch.tensor(Z)
+    cell_t = torch.tensor(cell, dtype=torch.float32)
+    energy, forces = model(pos_t.to(DEV), Z_t.to(DEV), cell_t, (True, True, True))
+    e_ref, f_ref = _oracle_potential(p, ph, cfg, cell)(pos_t, Z_t)
+    _check_energy_forces(energy, forces, e_ref, f_ref, len(Z))
