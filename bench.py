@@ -51,15 +51,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules", "span"])
+    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules", "span", "gemm"])
     ap.add_argument("--molecules", type=int, default=4096, help="molecules workload: batch size")
     ap.add_argument("--atoms", type=int, default=100_000, help="layer workload: atoms")
     ap.add_argument("--k", type=int, default=32)
     ap.add_argument("--cpu-atoms", type=int, default=None,
                     help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--fused-fwd", type=int, default=1, choices=[0, 1, 2],
-                    help="forward span kernels: 0 softmax + aggregation, 1 / 2 fused at 3 / 2 CTAs per SM")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="model workload with N > 1: independent systems per rank instead of one system "
@@ -727,7 +725,8 @@ def run_model(args, ws, rank, local):
                 "scaling": "strong" if domain else "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded blob-in-water periodic system, seeded random weights)",
                 "config": cfgd, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches_timed, "clocks": clk}
+                "gpu_launches": launches_timed, "clocks": clk,
+                "peak_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1)}
         print(json.dumps(line))
 
 
@@ -932,13 +931,68 @@ def run_span(args, ws, rank, local):
         print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------
+# The tensor-core projections alone: k_gemm_ws on the model's GEMM shapes
+# ------------------------------------------------------------------------------------------------
+GEMM_SHAPES = [  # (M, N, K, what) at the bench system: 97,865 atoms, 129,287 images, 3.13 M edges
+    (97865 * 9, 1024, 256, "Q / K per-degree projections (pair product), all 9 irreps rows"),
+    (97865, 512, 1536, "Q / K scalar MLP, first linear"),
+    (97865, 1024, 512, "Q / K scalar MLP, second linear"),
+    (97865 * 9, 256, 256, "proj_value / FFN per-degree linears"),
+    (3131680, 128, 256, "edge radial MLP, first layer (radial basis x W)"),
+    (3131680, 128, 128, "edge radial MLP, middle layer"),
+    (3131680, 256, 128, "edge radial MLP, last layer (gate | inputhead)"),
+]
+
+
+def run_gemm(args, ws, rank, local):
+    """Each of the model's GEMM shapes through ``linear.gemm`` (3xTF32 on tcgen05, fp32-accurate),
+    CUDA events over ``--steps`` launches after ``--warmup``; TFLOP/s of fp32-accurate output (2MNK per
+    product) against the 3xTF32 ceiling (a third of the dense tf32 rate, taken as half the measured
+    bf16 rate) and against the measured bf16 peak."""
+    from ubio_molfm_b200 import linear
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16 = float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        bf16 = 1400.0   # the fallback sustained figure
+    ceiling = bf16 / 2 / 3
+    g = torch.Generator(device=dev).manual_seed(0)
+    rows = []
+    clocks = ClockSampler(local)
+    for M, N, K, what in GEMM_SHAPES:
+        a = torch.randn(M, K, device=dev, generator=g)
+        b = torch.randn(N, K, device=dev, generator=g)
+        bs = linear.split_tf32(b)
+        out = torch.empty(M, N, device=dev)
+        for _ in range(max(args.warmup, 1)):
+            linear.gemm(a, b, out=out, b_split=bs)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            linear.gemm(a, b, out=out, b_split=bs)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / args.steps
+        tf = 2.0 * M * N * K / ms / 1e9
+        rows.append({"M": M, "N": N, "K": K, "what": what, "ms": round(ms, 4), "tflops": round(tf, 1),
+                     "frac_of_3xtf32_ceiling": round(tf / ceiling, 3), "frac_of_bf16_peak": round(tf / bf16, 3)})
+        del a, b, bs, out
+    clk = clocks.stop()
+    if rank == 0:
+        print(json.dumps({"metric": "GEMM TFLOP/s of fp32-accurate output", "unit": "TFLOP/s", "n_gpus": 1,
+                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
+                          "data": "synthetic N(0,1) operands", "ceiling_3xtf32_tflops": round(ceiling, 1),
+                          "bf16_peak_tflops": bf16, "shapes": rows, "clocks": clk}))
+
+
 def main():
     args = parse()
     ws, rank, local = dist_init(args)
-    if args.impl == "ours":
-        from ubio_molfm_b200 import _lib
-
-        _lib.load().e2a_attn_set_fused_fwd(args.fused_fwd)
     if args.workload == "molecules":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the molecules workload has no CPU reference "
@@ -947,6 +1001,8 @@ def main():
             run_molecules(args, ws, rank, local)
     elif args.workload == "span":
         run_span(args, ws, rank, local)
+    elif args.workload == "gemm":
+        run_gemm(args, ws, rank, local)
     elif args.workload == "model":
         if args.impl == "reference":
             run_reference_model(args, ws, rank)

@@ -154,10 +154,6 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value,
                  const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
                  int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
                  float* out, float* beta, float* row_max, float* row_sum, void* stream);
-/* Selects the forward span kernels of e2a_attn_fwd (no reference counterpart; a measurement switch):   */
-/* 0 = softmax kernel + aggregation kernel, 1 / 2 = the fused kernel at 3 / 2 resident CTAs per SM      */
-/* (the default is 1).  Returns the previous setting; process-wide, not thread-safe.                    */
-int e2a_attn_set_fused_fwd(int mode);
 /* Query-side backward: given dout [N,C,H] produces d_q [N,H,D] (w.r.t. the scaled q), d_gate and */
 /* d_inputhead ([E,H] views with row stride ld_dgi), d_poly [E], d_dist [E] and d_logit [E,H]     */
 /* (= dL/ds, consumed by e2a_attn_bwd_key).  The gradient of the row max follows PyTorch's        */

@@ -52,7 +52,6 @@ SIGNATURES = {
     "e2a_gemm_tf32x3": (I32, [P, I64, P, P, I64, P, I64, P, I64, I64, I64, I32, I32, P]),
     "e2a_tf32_split": (I32, [P, I64, I64, I64, P, P, I64, P]),
     "e2a_gemm_status": (I32, [P, I32, P]),
-    "e2a_attn_set_fused_fwd": (I32, [I32]),
     "e2a_gemm_wait_selftest": (I32, [I64, P]),
     "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
     "e2a_pair_grad": (I32, [P, P, I64, I32, I32, I32, P, P]),

@@ -677,141 +677,6 @@ k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   }
 }
 
-// ------------------------------------------------------------------------------------------------
-// Fused forward span for 128 heads of width 8: one CTA (256 threads) per destination row computes the
-// row's logits, the segmented softmax and beta (written out for the backward), then aggregates the
-// value rows of its edges with beta read back from shared memory.  Compared with a softmax kernel
-// followed by an aggregation kernel, beta makes no round trip through global memory before it is
-// used, and the latency-bound q.k phase of one CTA overlaps the bandwidth-bound aggregation of the
-// other CTAs resident on the SM.
-//   logits: warp w takes edges rs + w, rs + w + 8, ...; lane l owns heads 4l .. 4l + 3, so it reads
-//           the 128-byte slice of the key row for those heads (coalesced across the warp);
-//   softmax: thread t reduces head t % 128 over half of the chunk's edges (two halves combined in
-//           shared memory), with the same per-edge formula as the two-kernel path;
-//   aggregation: thread t owns the float4 slots f = t + 256 s of the [C, H] row, all in head quad
-//           t % 32, and accumulates beta[e, quad] * value[col[e], f] in CSR order.
-// Rows with more than EC edges are done in chunks of EC: the row max and row sum are formed over all
-// chunks first (logits recomputed per chunk), then each chunk's beta is formed and aggregated.
-// ------------------------------------------------------------------------------------------------
-template <int KS, int EC, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB)
-k_attn_fwd_fused(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ value,
-                 const float* __restrict__ gate, const float* __restrict__ inputhead, int64_t ld_gi,
-                 const float* __restrict__ poly, const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
-                 const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows, int row_f4,
-                 float* __restrict__ out, float* __restrict__ beta, float* __restrict__ row_max,
-                 float* __restrict__ row_sum) {
-  constexpr int H = 128, D = 8, HPL = 4, F4 = HPL * D / 4;
-  __shared__ __align__(16) float lg[EC * H];     // logits, then beta, of the current chunk
-  __shared__ float red[2 * H];
-  __shared__ float m_s[H], s_s[H];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int hh = threadIdx.x % H, half = threadIdx.x / H;
-  const int hq = threadIdx.x & 31;               // head quad of this thread's aggregation slots
-  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
-    const int i = row_of(order, r);
-    const int rs = row_ptr[i], re = row_ptr[i + 1];
-    const int deg = re - rs;
-    // logits of edges [c0, c1) into lg (local index e - c0); the lane's q slice is reloaded per call
-    auto logits = [&](int c0, int c1) {
-      if (c0 + warp >= c1) return;
-      float4 qv[F4];
-      const float* qr = q + (int64_t)i * H * D + lane * HPL * D;
-#pragma unroll
-      for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
-      for (int e = c0 + warp; e < c1; e += kWarps) {
-        const float* kr = k + (int64_t)col[e] * H * D + lane * HPL * D;
-        float sv[HPL];
-#pragma unroll
-        for (int u = 0; u < HPL; ++u) {
-          float acc = 0.f;
-#pragma unroll
-          for (int t = 0; t < D / 4; ++t) {
-            const float4 kv = ldg4(kr + 4 * (u * (D / 4) + t));
-            const float4 qq = qv[u * (D / 4) + t];
-            acc += qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
-          }
-          sv[u] = acc;
-        }
-        const float4 g = ldg4(gate + (int64_t)e * ld_gi + lane * HPL);
-        *reinterpret_cast<float4*>(lg + (e - c0) * H + lane * HPL) =
-            make_float4(g.x * sv[0], g.y * sv[1], g.z * sv[2], g.w * sv[3]);
-      }
-    };
-    // 1. row max over all edges
-    float mx = -INFINITY;
-    for (int c0 = rs; c0 < re; c0 += EC) {
-      const int c1 = min(c0 + EC, re);
-      logits(c0, c1);
-      __syncthreads();
-      for (int e = half; e < c1 - c0; e += 2) mx = fmaxf(mx, lg[e * H + hh]);
-      if (deg > EC) __syncthreads();
-    }
-    red[threadIdx.x] = mx;
-    __syncthreads();
-    if (half == 0) m_s[hh] = fmaxf(red[hh], red[H + hh]);
-    __syncthreads();
-    const float m = m_s[hh];
-    // 2. row sum of exp(a - m) poly (chunks after the first recompute their logits)
-    float sm = 0.f;
-    for (int c0 = rs; c0 < re; c0 += EC) {
-      const int c1 = min(c0 + EC, re);
-      if (deg > EC) {
-        logits(c0, c1);
-        __syncthreads();
-      }
-      for (int e = half; e < c1 - c0; e += 2) sm += expf(lg[e * H + hh] - m) * __ldg(poly + c0 + e);
-      if (deg > EC) __syncthreads();
-    }
-    red[threadIdx.x] = sm;
-    __syncthreads();
-    if (half == 0) s_s[hh] = red[hh] + red[H + hh];
-    __syncthreads();
-    const float S = s_s[hh];
-    const float den = S + kSoftmaxEps;
-    if (half == 0) {
-      row_max[(int64_t)i * H + hh] = m;
-      row_sum[(int64_t)i * H + hh] = S;
-    }
-    // 3. per chunk: beta = exp(a - m) poly ih / (S + eps) / max(d, 1e-6) (to shared memory and out),
-    //    then the chunk's value aggregation
-    float4 acc[KS];
-#pragma unroll
-    for (int s = 0; s < KS; ++s) acc[s] = f4_zero();
-    for (int c0 = rs; c0 < re; c0 += EC) {
-      const int c1 = min(c0 + EC, re);
-      if (deg > EC) {
-        logits(c0, c1);
-        __syncthreads();
-      }
-      for (int e = half; e < c1 - c0; e += 2) {
-        const int ge = c0 + e;
-        const float x = expf(lg[e * H + hh] - m) * __ldg(poly + ge);
-        const float b = x * __ldg(inputhead + (int64_t)ge * ld_gi + hh) / den / fmaxf(__ldg(dist + ge), kMinDist);
-        lg[e * H + hh] = b;
-        beta[(int64_t)ge * H + hh] = b;
-      }
-      __syncthreads();
-      for (int e = 0; e < c1 - c0; ++e) {
-        const float4 bw = *reinterpret_cast<const float4*>(lg + e * H + 4 * hq);
-        const float* vr = value + (int64_t)col[c0 + e] * row_f4 * 4;
-#pragma unroll
-        for (int s = 0; s < KS; ++s) {
-          const int f = threadIdx.x + s * kThreads;
-          if (f < row_f4) acc[s] = f4_fma4(bw, ldg4(vr + 4 * f), acc[s]);
-        }
-      }
-      __syncthreads();
-    }
-    float* orow = out + (int64_t)i * row_f4 * 4;
-#pragma unroll
-    for (int s = 0; s < KS; ++s) {
-      const int f = threadIdx.x + s * kThreads;
-      if (f < row_f4) reinterpret_cast<float4*>(orow)[f] = acc[s];
-    }
-  }
-}
-
 int check_dims(int H, int D, int C, Dims& dm, int& ks) {
   if (H <= 0 || D <= 0 || C <= 0) return E2A_ERR_ARG;
   if (H % 4 || kThreads % H) return E2A_ERR_UNSUPPORTED;
@@ -962,20 +827,7 @@ int softmax_bwd_dq_launch(const float* q, const float* k, const float* gate, con
 
 }  // namespace
 
-namespace {
-// forward span path: 0 softmax + aggregation kernels; 1 / 2 the fused kernel with 3 / 2 resident CTAs per SM
-int g_fused_fwd = 1;
-}
-
 extern "C" {
-
-/* Selects the forward span kernels (0 two-kernel, 1 / 2 fused at 3 / 2 CTAs per SM); returns the previous
-   setting. */
-int e2a_attn_set_fused_fwd(int mode) {
-  const int old = g_fused_fwd;
-  if (mode >= 0 && mode <= 2) g_fused_fwd = mode;
-  return old;
-}
 
 int e2a_attn_fwd(const float* q, const float* k, const float* value, const float* gate, const float* inputhead,
                  int64_t ld_gi, const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
@@ -990,13 +842,6 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value, const float
   if (!q || !row_ptr || !out || !row_max || !row_sum) return E2A_ERR_ARG;
   if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  if (warp_softmax_ok(dm, ld_gi) && ks == 8 && g_fused_fwd) {
-    auto kf = g_fused_fwd == 2 ? k_attn_fwd_fused<8, 32, 2> : k_attn_fwd_fused<8, 32, 3>;
-    kf<<<grid_for(n_rows), kThreads, 0, st>>>(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col,
-                                              row_order, n_rows, dm.CH4, out, beta, row_max, row_sum);
-    E2A_CHECK_LAUNCH();
-    return E2A_OK;
-  }
   if (warp_softmax_ok(dm, ld_gi)) {
     // 64 registers: 4 CTAs (32 warps) per SM keep more k-row gathers in flight
     k_softmax_fwd_warp<4, 8, 4><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
