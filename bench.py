@@ -617,6 +617,8 @@ def run_model(args, ws, rank, local):
     del g
 
     domain = ws > 1 and not args.replicas
+    from ubio_molfm_b200 import linear
+    from ubio_molfm_b200.domain import HALO_STATS
     if domain:
         from ubio_molfm_b200.domain import domain_energy_forces
 
@@ -634,6 +636,11 @@ def run_model(args, ws, rank, local):
     clocks = ClockSampler(local)
     ops.TIMER.enabled = True
     ops.TIMER.events = {}
+    linear.GEMM_TIMER.enabled = True
+    linear.GEMM_TIMER.records = []
+    if domain:
+        HALO_STATS.enabled = True
+        HALO_STATS.records = []
     launches0 = _lib.launch_count()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -645,10 +652,14 @@ def run_model(args, ws, rank, local):
     barrier(ws)
     torch.cuda.synchronize()
     ops.TIMER.enabled = False
+    linear.GEMM_TIMER.enabled = False
+    HALO_STATS.enabled = False
     launches_timed = _lib.launch_count() - launches0
     clk = clocks.stop()
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, ws, dev)
     kern = ops.TIMER.summary()
+    g_n, g_ms, g_flop = linear.GEMM_TIMER.summary()
+    halo = HALO_STATS.summary() if domain else None
     name, (nl, tot) = max(kern.items(), key=lambda kv: kv[1][1])
     if domain:   # this rank's share of the span: its owned rows, their edges, their expanded keys
         from ubio_molfm_b200.domain import domain_graph
@@ -668,6 +679,34 @@ def run_model(args, ws, rank, local):
             "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
             "kernels_ms_per_launch": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
             "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
+    # every span entry point against its algorithmic bytes, and the tensor-core projections of the step
+    entries = {}
+    for k, (nl_k, tot_k) in kern.items():
+        fn = {"e2a_attn_fwd": fwd_algorithmic_bytes, "e2a_attn_bwd_value": bwdv_algorithmic_bytes,
+              "e2a_attn_bwd_softmax": bwds_algorithmic_bytes, "e2a_attn_bwd_dk": bwddk_algorithmic_bytes,
+              "e2a_attn_bwd_query": bwdq_algorithmic_bytes, "e2a_attn_bwd_key": bwdk_algorithmic_bytes}.get(k)
+        if fn is None:
+            continue
+        b_k = fn(N_r, N2_r, E_r)
+        ms_k = tot_k / nl_k
+        entries[k] = {"ms": round(ms_k, 4), "algorithmic_bytes": b_k,
+                      "frac": round(b_k / (ms_k * 1e-3) / 1e9 / peak, 4)}
+    roof["entry_points"] = entries
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16s = float(json.load(f)["bf16_tflops_sustained"])
+        bsrc = "measured"
+    except Exception:
+        bf16s, bsrc = 1400.0, "fallback"
+    if g_n:
+        tfs = g_flop / args.steps / (g_ms / args.steps * 1e-3) / 1e12
+        roof["gemm"] = {"kernel": "k_gemm_ws (tcgen05 3xTF32)", "bound": "tensor", "launches_per_step": g_n // args.steps,
+                        "ms_per_step": round(g_ms / args.steps, 3), "tflop_per_step": round(g_flop / args.steps / 1e12, 3),
+                        "achieved": round(tfs, 1), "unit": "TFLOP/s of fp32-accurate output",
+                        "peak_3xtf32": round(bf16s / 6, 1), "frac_of_3xtf32": round(tfs / (bf16s / 6), 3),
+                        "peak_bf16_sustained": bf16s, "frac_of_bf16_sustained": round(tfs / bf16s, 4),
+                        "peak_source": bsrc, "step_share": round(g_ms / args.steps / ms, 4),
+                        "note": "3xTF32 issues three tf32 MMAs per product; the tf32 rate is half the bf16 rate"}
     value = (1 if domain else ws) * N * 1e3 / ms
 
     e2e = None
@@ -727,6 +766,10 @@ def run_model(args, ws, rank, local):
                 "config": cfgd, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_timed, "clocks": clk,
                 "peak_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1)}
+        if halo is not None:
+            line["halo_exchange"] = {d: {"calls_per_step": v["calls"] // args.steps,
+                                         "ms_per_step": round(v["ms"] / args.steps, 3),
+                                         "bytes_per_step": v["bytes"] // args.steps} for d, v in halo.items()}
         print(json.dumps(line))
 
 

@@ -63,14 +63,52 @@ class HaloPlan:
         return _HaloFn.apply(x_own, self)
 
 
+class HaloStats:
+    """Opt-in timing of the halo exchanges (CUDA events around each ``all_to_all`` on the current
+    stream): ``records`` holds (direction, start, end, bytes sent); :meth:`summary` sums them."""
+
+    def __init__(self):
+        self.enabled = False
+        self.records = []
+
+    def _start(self):
+        if not self.enabled or not torch.cuda.is_available():
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def _stop(self, direction, e0, nbytes):
+        if e0 is None:
+            return
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        self.records.append((direction, e0, e1, nbytes))
+
+    def summary(self):
+        torch.cuda.synchronize()
+        out = {}
+        for d, e0, e1, nb in self.records:
+            o = out.setdefault(d, {"calls": 0, "ms": 0.0, "bytes": 0})
+            o["calls"] += 1
+            o["ms"] += e0.elapsed_time(e1)
+            o["bytes"] += int(nb)
+        return out
+
+
+HALO_STATS = HaloStats()
+
+
 class _HaloFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_own, plan):
         send = x_own[plan.send_idx].contiguous()
         tail = tuple(x_own.shape[1:])
         recv = x_own.new_empty((int(plan.recv_counts.sum()),) + tail)
+        t0 = HALO_STATS._start()
         dist.all_to_all_single(recv, send, output_split_sizes=plan.recv_counts.tolist(),
                                input_split_sizes=plan.send_counts.tolist(), group=plan.group)
+        HALO_STATS._stop("forward", t0, send.numel() * send.element_size())
         ctx.plan = plan
         return torch.cat([x_own, recv], dim=0)
 
@@ -81,8 +119,10 @@ class _HaloFn(torch.autograd.Function):
         g_own = g[:plan.n_own].clone()
         g_ghost = g[plan.n_own:].contiguous()
         back = g.new_empty((int(plan.send_counts.sum()),) + tuple(g.shape[1:]))
+        t0 = HALO_STATS._start()
         dist.all_to_all_single(back, g_ghost, output_split_sizes=plan.send_counts.tolist(),
                                input_split_sizes=plan.recv_counts.tolist(), group=plan.group)
+        HALO_STATS._stop("adjoint", t0, g_ghost.numel() * g_ghost.element_size())
         if back.shape[0]:
             g_own.index_add_(0, plan.send_idx, back)
         return g_own, None

@@ -40,8 +40,47 @@ def _presplit_ok(a_ptr, lda, K):
     return PRESPLIT_WEIGHTS and K > 0 and K % 4 == 0 and a_ptr % 16 == 0 and lda % 4 == 0
 
 
+class GemmTimer:
+    """Opt-in CUDA-event bracketing of every tensor-core GEMM launch with its product count (2MNK):
+    used by the benchmark to report the projections' delivered TFLOP/s inside the model step."""
+
+    def __init__(self):
+        self.enabled = False
+        self.records = []
+
+    def start(self):
+        if not self.enabled:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def stop(self, e0, M, N, K):
+        if e0 is None:
+            return
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        self.records.append((e0, e1, 2.0 * M * N * K))
+
+    def summary(self):
+        """(launches, total ms, total flop); call after synchronising."""
+        return (len(self.records), sum(a.elapsed_time(b) for a, b, _ in self.records),
+                sum(f for _, _, f in self.records))
+
+
+GEMM_TIMER = GemmTimer()
+
+
 def _gemm_ptrs(lib, a, lda, b, b_lo, ldb, c, ldc, bias, M, N, K, accumulate, passes, dev, P=None, ldp=0):
     """Raw-pointer GEMM (pair-product epilogue when ``P`` is given; ``b_lo`` = pre-split low part)."""
+    t0 = GEMM_TIMER.start()
+    try:
+        _gemm_ptrs_launch(lib, a, lda, b, b_lo, ldb, c, ldc, bias, M, N, K, accumulate, passes, dev, P, ldp)
+    finally:
+        GEMM_TIMER.stop(t0, M, N, K)
+
+
+def _gemm_ptrs_launch(lib, a, lda, b, b_lo, ldb, c, ldc, bias, M, N, K, accumulate, passes, dev, P=None, ldp=0):
     st = stream_of(dev)
     if P is not None:
         check(lib.e2a_gemm_tf32x3_pairprod(a, lda, b, b_lo, ldb, c, ldc, bias, P, ldp, M, N, K,
@@ -496,8 +535,10 @@ class _RbfLinearFn(torch.autograd.Function):
             return gemm(rbf, w, b)
         h = torch.empty((E, N), device=d.device, dtype=torch.float32)
         hi, lo = split_tf32(w)
+        t0 = GEMM_TIMER.start()
         check(lib.e2a_gemm_tf32x3_rbf(ptr(d), ptr(mu), float(coeff), ptr(hi), ptr(lo), nb, ptr(h), N, ptr(b), E, N,
                                       nb, PASSES, stream_of(d.device)), "e2a_gemm_tf32x3_rbf")
+        GEMM_TIMER.stop(t0, E, N, nb)
         return h
 
     @staticmethod
@@ -516,9 +557,11 @@ class _RbfLinearFn(torch.autograd.Function):
         hi, lo = split_tf32(wt)
         nblk = (nb + 63) // 64
         part = torch.empty((E, nblk), device=d.device, dtype=torch.float32)
+        t0 = GEMM_TIMER.start()
         check(lib.e2a_gemm_tf32x3_rbf_dist_grad(ptr(g), Kh, ptr(hi), ptr(lo), Kh, ptr(d), ptr(mu), ctx.coeff,
                                                 ptr(part), nblk, E, nb, Kh, PASSES, stream_of(d.device)),
               "e2a_gemm_tf32x3_rbf_dist_grad")
+        GEMM_TIMER.stop(t0, E, nb, Kh)
         return part.sum(1), None, None, None, None
 
 
