@@ -297,10 +297,25 @@ struct IntC { static constexpr int value = V; };
 // Two slab shapes: 16-wide slabs (64-byte rows and swizzle, six stages) suit K <= 256, where tiles
 // turn over quickly; 32-wide slabs (128-byte rows and swizzle, three stages) move more bytes per
 // TMA request and suit long K.
+#ifndef E2A_WS_CHAINS16
+#define E2A_WS_CHAINS16 3
+#endif
+#ifndef E2A_WS_CHAINS32
+#define E2A_WS_CHAINS32 3
+#endif
+#ifndef E2A_WS_ATS16
+#define E2A_WS_ATS16 4
+#endif
+#ifndef E2A_WS_ATS32
+#define E2A_WS_ATS32 2
+#endif
+#ifndef E2A_WS_CHAINK
+#define E2A_WS_CHAINK 32
+#endif
 template <int BK_>
 struct WsCfg {
   static constexpr int BK = BK_;
-  static constexpr int SPC = 32 / BK;                    // slabs per TMEM chain (32 k = 12 MMAs)
+  static constexpr int SPC = E2A_WS_CHAINK / BK;         // slabs per TMEM chain (32 k = 12 MMAs by default)
 #ifndef E2A_WS_STAGES16
 #define E2A_WS_STAGES16 6   // shared memory allows up to 8 (24 KB stages)
 #endif
@@ -310,8 +325,11 @@ struct WsCfg {
   static constexpr int STAGES = BK == 16 ? E2A_WS_STAGES16 : E2A_WS_STAGES32;
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
   static constexpr int STAGE = 3 * TILE;                 // A (raw), B (split in place when not pre-split), B_lo
-  static constexpr int ATS = BK == 16 ? 4 : 2;           // A hi / lo slots in tensor memory (2 BK columns each)
-  static constexpr int NBARS = 3 * STAGES + 6 + ATS;     // + 2 x WS_CHAINS + the A slots
+  static constexpr int CHAINS = BK == 16 ? E2A_WS_CHAINS16 : E2A_WS_CHAINS32;   // TMEM chain buffers (BN columns)
+  static constexpr int ATS = BK == 16 ? E2A_WS_ATS16 : E2A_WS_ATS32;  // A hi / lo slots in TMEM (2 BK columns each)
+  static constexpr uint32_t ACOL = CHAINS * 128;         // first A-slot column
+  static constexpr int NBARS = 3 * STAGES + 2 * CHAINS + ATS;
+  static_assert(CHAINS * 128 + ATS * 2 * BK <= 512, "chain buffers + A slots exceed the 512 TMEM columns");
   static constexpr int SPLIT = 128;                      // splitter threads (warps 2-3 and 12-13)
   static constexpr int THREADS = 384 + (SPLIT - 64);      // + 8 drain warps (4-11)
   static __device__ __forceinline__ uint64_t desc(uint32_t addr) {
@@ -320,8 +338,6 @@ struct WsCfg {
            ((BK == 16 ? 4ull : 2ull) << 61);
   }
 };
-constexpr int WS_CHAINS = 3;                     // TMEM chain buffers of BN columns (columns 0 .. 383)
-constexpr uint32_t WS_ACOL = WS_CHAINS * BN;      // A hi / lo slots: columns 384 .. 511
 constexpr int WS_DRAIN = 8;                      // drain warps: 4 TMEM lane quarters x 2 column halves
 constexpr int WS_DCOLS = BN / 2;                 // accumulator columns per drain warp
 constexpr int WS_EH = 16;                        // epilogue staged 16 columns at a time
@@ -412,8 +428,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   uint64_t* split_done = bars + Cfg::STAGES;        // A hi / lo written     (one per splitter)
   uint64_t* empty = bars + 2 * Cfg::STAGES;         // MMAs of the slab done (tcgen05.commit)
   uint64_t* tfull = bars + 3 * Cfg::STAGES;         // chain buffer ready    (tcgen05.commit)
-  uint64_t* tempty = tfull + WS_CHAINS;           // chain buffer drained  (256 arrives)
-  uint64_t* a_empty = tempty + WS_CHAINS;         // A slot read by the slab's MMAs (tcgen05.commit)
+  uint64_t* tempty = tfull + Cfg::CHAINS;           // chain buffer drained  (256 arrives)
+  uint64_t* a_empty = tempty + Cfg::CHAINS;         // A slot read by the slab's MMAs (tcgen05.commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* mu_s = reinterpret_cast<float*>(tmem_slot + 4);   // gen: the basis offsets (K <= 256)
@@ -432,7 +448,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       e2a_mbar_init(&split_done[s], Cfg::SPLIT);
       e2a_mbar_init(&empty[s], 1);
     }
-    for (int c = 0; c < WS_CHAINS; ++c) {
+    for (int c = 0; c < Cfg::CHAINS; ++c) {
       e2a_mbar_init(&tfull[c], 1);
       e2a_mbar_init(&tempty[c], 32 * WS_DRAIN);
     }
@@ -482,13 +498,13 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       bool run = true;
       for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
         for (int kb = 0; kb < nk; ++kb, ++n) {
-          const uint32_t s = n % Cfg::STAGES, cb = c % WS_CHAINS;
-          if ((kb % Cfg::SPC) == 0 && !ws_wait(&tempty[cb], ((c / WS_CHAINS) & 1) ^ 1, abort_flag)) { run = false; break; }
+          const uint32_t s = n % Cfg::STAGES, cb = c % Cfg::CHAINS;
+          if ((kb % Cfg::SPC) == 0 && !ws_wait(&tempty[cb], ((c / Cfg::CHAINS) & 1) ^ 1, abort_flag)) { run = false; break; }
           if (!ws_wait(&split_done[s], (n / Cfg::STAGES) & 1, abort_flag)) { run = false; break; }
           WS_TRACE(3, n);
           tc_fence_after();
           const uint32_t d = tmem + cb * BN;
-          const uint32_t a_hi = tmem + WS_ACOL + (n % Cfg::ATS) * 2 * Cfg::BK, a_lo = a_hi + Cfg::BK;
+          const uint32_t a_hi = tmem + Cfg::ACOL + (n % Cfg::ATS) * 2 * Cfg::BK, a_lo = a_hi + Cfg::BK;
           const uint32_t b_hi = e2a_smem_u32(stages + s * Cfg::STAGE) + Cfg::TILE, b_lo = b_hi + Cfg::TILE;
 #pragma unroll
           for (int kk = 0; kk < Cfg::BK / 8; ++kk) {
@@ -544,7 +560,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           const int row = ((tile + (int)gridDim.x) / tiles_n) * BM + r;
           dnext = tile + (int)gridDim.x < tiles && row < M ? __ldg(rb.d + row) : 0.f;
         }
-        const uint32_t acol = tmem + lane_addr + WS_ACOL + (n % Cfg::ATS) * 2 * Cfg::BK;
+        const uint32_t acol = tmem + lane_addr + Cfg::ACOL + (n % Cfg::ATS) * 2 * Cfg::BK;
 #pragma unroll
         for (int h = 0; h < Cfg::BK / 16; ++h) {   // 16 columns at a time
           float v[16], hi[16], lo[16];
@@ -608,8 +624,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
 #pragma unroll
       for (int i = 0; i < WS_DCOLS; ++i) acc[i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++c) {
-        const uint32_t cb = c % WS_CHAINS;
-        if (!ws_wait(&tfull[cb], (c / WS_CHAINS) & 1, abort_flag)) { run = false; break; }
+        const uint32_t cb = c % Cfg::CHAINS;
+        if (!ws_wait(&tfull[cb], (c / Cfg::CHAINS) & 1, abort_flag)) { run = false; break; }
         if (threadIdx.x == 128) WS_TRACE(4, c);
         tc_fence_after();
 #pragma unroll
@@ -771,8 +787,11 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
   if (!vec || K == 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return E2A_ERR_UNSUPPORTED;
   EncodeTiledFn enc = tensor_map_encoder();
   if (!enc) return E2A_ERR_UNSUPPORTED;
-  // 32-wide slabs (four stages) from K = 256 up; 16-wide for shorter K and for the on-chip basis
-  const int bk = (gen || K < 256) ? 16 : 32;
+  // 32-wide slabs (four stages) from K = E2A_WS_BK32_MINK up; 16-wide for shorter K and for the on-chip basis
+#ifndef E2A_WS_BK32_MINK
+#define E2A_WS_BK32_MINK 256
+#endif
+  const int bk = (gen || K < E2A_WS_BK32_MINK) ? 16 : 32;
   if (gen && bk != 16) return E2A_ERR_UNSUPPORTED;
   CUtensorMap ta, tb, tbl;
   if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
