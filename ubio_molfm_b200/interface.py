@@ -85,7 +85,7 @@ class E2FormerModelInterface:
     checkpoint: ``torch.load(...)["model"]``, ``head.energy_heads.<head_name>``)."""
 
     def __init__(self, model=None, backbone_config=None, checkpoint_path=None, head_name=None, device="cuda:0",
-                 use_tf32=False, use_faiss=True, use_compile=False, ref_energy=None, memory_saving=True):
+                 use_tf32=False, use_faiss=True, use_compile=False, ref_energy=None, memory_saving="auto"):
         if use_compile:
             raise NotImplementedError("use_compile: this build runs its own CUDA kernels, not torch.compile")
         self.device = torch.device(device)

@@ -404,7 +404,7 @@ class E2FormerPotential(nn.Module):
     ``(energy [B], forces [N,3])``.  Periodic systems are one per call; non-periodic molecules may be
     batched (``batch`` sorted, systems do not see each other)."""
 
-    def __init__(self, memory_saving=True, use_faiss=False, **backbone_kwargs):
+    def __init__(self, memory_saving="auto", use_faiss=False, **backbone_kwargs):
         super().__init__()
         # use_faiss: expanded nodes in the order of the reference's FAISS neighbour path
         # (distributed_cell_expand, one image cell per direction) instead of CellExpander's; the edges
@@ -415,11 +415,28 @@ class E2FormerPotential(nn.Module):
         self.check_device_status = True
         self.backbone = E2FormerBackbone(use_faiss=use_faiss, **backbone_kwargs)
         self.energy_head = MLP_energy_head(self.decoder.scalar_dim, self.decoder.lmax)
-        # large systems: the Q / K projections are formed again in the backward (saves 2 x 4 x hidden
-        # floats per irreps row per layer; ~29 GB at 1e5 atoms with the full-size model)
+        # memory_saving: True = the Q / K per-degree projections are formed again in the backward instead
+        # of kept (2 x heads x head-dim floats per irreps row and layer, ~29 GB at 1e5 atoms with the
+        # full-size model; ~10% of the step's tensor-core work); False = kept; "auto" = kept unless the
+        # evaluation's estimated peak with them kept passes 85% of the device's memory
+        self.memory_saving = memory_saving
+        self._set_recompute(memory_saving is True)
+
+    def _set_recompute(self, on):
         for blk in self.decoder.blocks:
-            blk.ga.query_linear.recompute_pair_product = memory_saving
-            blk.ga.key_linear.recompute_pair_product = memory_saving
+            blk.ga.query_linear.recompute_pair_product = on
+            blk.ga.key_linear.recompute_pair_product = on
+
+    # peak bytes of an evaluation per edge, projections recomputed (measured: 112.6 GB at 3.13 M edges)
+    _PEAK_BYTES_PER_EDGE = 36.0e3
+
+    def _auto_recompute(self, n_rows, n_edges, device):
+        """Whether to recompute the Q / K projections for a graph of this size (``memory_saving="auto"``)."""
+        dec = self.decoder
+        blk = dec.blocks[0].ga
+        kept = 2 * len(dec.blocks) * n_rows * (dec.lmax + 1) ** 2 * blk.num_attn_heads * blk.attn_scalar_head * 4
+        total = torch.cuda.get_device_properties(device).total_memory
+        return self._PEAK_BYTES_PER_EDGE * n_edges + kept > 0.85 * total
 
     @property
     def decoder(self):
@@ -488,6 +505,8 @@ class E2FormerPotential(nn.Module):
         pos = pos.detach().to(torch.float32).requires_grad_(need_forces)
         with torch.enable_grad() if need_forces else torch.no_grad():
             g, pbc_any = self.build_graph(pos, cell, pbc, batch)
+            if self.memory_saving == "auto" and pos.is_cuda:
+                self._set_recompute(self._auto_recompute(pos.shape[0], g["query_idx"].numel(), pos.device))
             sys_emb = None
             if charge is not None:
                 if multiplicity is None:
