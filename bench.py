@@ -706,7 +706,8 @@ def run_model(args, ws, rank, local):
                         "peak_3xtf32": round(bf16s / 6, 1), "frac_of_3xtf32": round(tfs / (bf16s / 6), 3),
                         "peak_bf16_sustained": bf16s, "frac_of_bf16_sustained": round(tfs / bf16s, 4),
                         "peak_source": bsrc, "step_share": round(g_ms / args.steps / ms, 4),
-                        "note": "3xTF32 issues three tf32 MMAs per product; the tf32 rate is half the bf16 rate"}
+                        "note": "3xTF32 issues three tf32 MMAs per product; the tf32 rate is half the bf16 rate",
+                        "by_shape_MNK_launches_ms_tflops": linear.GEMM_TIMER.by_shape()}
     value = (1 if domain else ws) * N * 1e3 / ms
 
     e2e = None
@@ -798,6 +799,9 @@ def run_molecules(args, ws, rank, local):
         e, f = molecules_energy_forces(m, my, dev)
         if ws > 1:
             e, f = gather_molecule_results(e, f, mine, len(mols))
+        if rank == 0:   # the results reach the host on rank 0
+            e = e.cpu()
+            torch.cat(f).cpu()
         return e
 
     for _ in range(args.warmup):
@@ -818,7 +822,7 @@ def run_molecules(args, ws, rank, local):
     launches = _lib.launch_count() - launches0
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, ws, dev)
     if rank == 0:
-        h2d = sum(len(z) * (12 + 8) for _, z in my)
+        h2d = sum(len(m[1]) * (12 + 8) for m in my)
         line = {"metric": "atom-steps/s", "value": round(n_atoms_total * 1e3 / ms, 1), "unit": "atom-steps/s",
                 "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -830,8 +834,8 @@ def run_molecules(args, ws, rank, local):
                            "parallelism": f"molecules sharded by size over {ws} ranks; energies and forces gathered to rank 0",
                            "l2": "inputs larger than L2"},
                 "e2e": {"value": round(n_atoms_total * 1e3 / ms, 1), "unit": "atom-steps/s",
-                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * len(mols),
-                        "includes": "the timed step copies every batch's positions / types from host memory"},
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * len(mols) + 12 * n_atoms_total,
+                        "includes": "the timed step copies every batch's positions / types from host memory and, on rank 0, all energies and forces back"},
                 "gpu_launches": launches, "clocks": clk}
         print(json.dumps(line))
 

@@ -60,12 +60,23 @@ class GemmTimer:
             return
         e1 = torch.cuda.Event(enable_timing=True)
         e1.record()
-        self.records.append((e0, e1, 2.0 * M * N * K))
+        self.records.append((e0, e1, 2.0 * M * N * K, (int(M), int(N), int(K))))
 
     def summary(self):
         """(launches, total ms, total flop); call after synchronising."""
-        return (len(self.records), sum(a.elapsed_time(b) for a, b, _ in self.records),
-                sum(f for _, _, f in self.records))
+        return (len(self.records), sum(r[0].elapsed_time(r[1]) for r in self.records),
+                sum(r[2] for r in self.records))
+
+    def by_shape(self, top=12):
+        """[(M, N, K, launches, ms, TFLOP/s)] of the shapes that took the most time."""
+        agg = {}
+        for a, b, f, shp in self.records:
+            o = agg.setdefault(shp, [0, 0.0, 0.0])
+            o[0] += 1
+            o[1] += a.elapsed_time(b)
+            o[2] += f
+        rows = sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]
+        return [(m, n, k, c, round(ms, 3), round(fl / ms / 1e9, 1)) for (m, n, k), (c, ms, fl) in rows]
 
 
 GEMM_TIMER = GemmTimer()
