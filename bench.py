@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules", "span", "gemm"])
+    ap.add_argument("--workload", default="model", choices=["model", "layer", "molecules", "span", "gemm", "md"])
     ap.add_argument("--molecules", type=int, default=4096, help="molecules workload: batch size")
     ap.add_argument("--atoms", type=int, default=100_000, help="layer workload: atoms")
     ap.add_argument("--k", type=int, default=32)
@@ -1037,6 +1037,58 @@ def run_gemm(args, ws, rank, local):
                           "bf16_peak_tflops": bf16, "shapes": rows, "clocks": clk}))
 
 
+# ------------------------------------------------------------------------------------------------
+# Config 5's workload: NVE molecular dynamics through the MD API
+# ------------------------------------------------------------------------------------------------
+def run_md(args, ws, rank, local):
+    """``--steps`` NVE velocity-Verlet steps at 0.5 fs (``TorchLangevin`` at zero friction with FixCom, on
+    ``TorchAtoms`` with float64 state, forces from ``E2FormerCalculator``) on the bench system, from
+    seeded Maxwell-Boltzmann velocities at 300 K.  Reports atom-steps/s of the MD loop and the drift of
+    the total energy (potential + kinetic) over the run."""
+    from ubio_molfm_b200 import _lib
+    from ubio_molfm_b200.md import FS, E2FormerCalculator, TorchAtoms, TorchLangevin, maxwell_boltzmann
+    from ubio_molfm_b200.synthetic import MASS, blob_in_water
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    model = make_model(dev)
+    pos_np, Z_np, cell_np = blob_in_water(seed=100)
+    masses = [MASS[int(z)] for z in Z_np]
+    atoms = TorchAtoms(Z_np, pos_np, masses, cell_np, (True, True, True), device=dev)
+    atoms.set_velocities(maxwell_boltzmann(masses, 300.0, torch.Generator().manual_seed(0), dev))
+    atoms.calc = E2FormerCalculator(model, use_charge=False)
+    dyn = TorchLangevin(atoms, 0.5 * FS, friction=0.0, fixcm=True)
+    N = len(atoms)
+    for _ in range(args.warmup):
+        dyn.step()
+    e0 = float(atoms.get_potential_energy() + atoms.get_kinetic_energy())
+    ke0 = float(atoms.get_kinetic_energy())
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    launches0 = _lib.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        dyn.step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    e1 = float(atoms.get_potential_energy() + atoms.get_kinetic_energy())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "atom-steps/s (NVE MD, energy+forces per step)", "value": round(N * 1e3 / ms, 1),
+            "unit": "atom-steps/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "dtype": "f32 model, f64 integrator state",
+            "data": "synthetic (seeded blob-in-water periodic system, seeded random weights, MB velocities 300 K)",
+            "config": {"workload": "NVE velocity Verlet, 0.5 fs, FixCom, on the 97,865-atom bench system",
+                       "atoms": N, "dt_fs": 0.5},
+            "energy_drift": {"total_energy_start_eV": e0, "total_energy_end_eV": e1,
+                             "drift_eV": e1 - e0, "drift_per_atom_eV": (e1 - e0) / N,
+                             "drift_over_initial_kinetic": (e1 - e0) / ke0},
+            "gpu_launches": _lib.launch_count() - launches0, "clocks": clk}))
+
+
 def main():
     args = parse()
     ws, rank, local = dist_init(args)
@@ -1050,6 +1102,8 @@ def main():
         run_span(args, ws, rank, local)
     elif args.workload == "gemm":
         run_gemm(args, ws, rank, local)
+    elif args.workload == "md":
+        run_md(args, ws, rank, local)
     elif args.workload == "model":
         if args.impl == "reference":
             run_reference_model(args, ws, rank)

@@ -421,7 +421,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           const __grid_constant__ CUtensorMap tmBl, int b_split, float* C, int64_t ldc, const float* __restrict__ bias, float* P,
           int64_t ldp, int M, int N, int K, int accumulate, int passes, const RbfArgs rb) {
   using Cfg = WsCfg<BK_>;
-  const bool gen = BK_ == 16 && rb.d != nullptr && rb.rdot == nullptr;   // A formed on chip
+  const bool gen = rb.d != nullptr && rb.rdot == nullptr;   // A formed on chip
   extern __shared__ uint8_t ws_raw[];
   uint8_t* smem = ws_raw + ((1024u - (e2a_smem_u32(ws_raw) & 1023u)) & 1023u);
   uint8_t* stages = smem;
@@ -795,8 +795,10 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
 #ifndef E2A_WS_BK32_MINK
 #define E2A_WS_BK32_MINK 128
 #endif
-  const int bk = (gen || K < E2A_WS_BK32_MINK) ? 16 : 32;
-  if (gen && bk != 16) return E2A_ERR_UNSUPPORTED;
+#ifndef E2A_WS_GEN_BK32
+#define E2A_WS_GEN_BK32 0
+#endif
+  const int bk = ((gen && !E2A_WS_GEN_BK32) || K < E2A_WS_BK32_MINK) ? 16 : 32;
   CUtensorMap ta, tb, tbl;
   if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
       !make_map_2d(enc, &tbl, B_lo ? B_lo : B, N, K, ldb, bk))

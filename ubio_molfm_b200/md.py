@@ -50,6 +50,8 @@ class TorchAtoms:
         self._torch_momenta = (torch.zeros_like(self._torch_positions) if momenta is None
                                else torch.as_tensor(momenta).to(self._device, dtype).clone())
         self._torch_cell = None if cell is None else torch.as_tensor(cell).to(self._device, dtype)
+        # the model's graph build takes the cell on the host: kept there too (no device read per step)
+        self._cell_host = None if cell is None else torch.as_tensor(cell).detach().to("cpu", torch.float32)
         self.pbc = tuple(bool(p) for p in pbc)
         self.charge, self.multiplicity = int(charge), int(multiplicity)
         self._torch_forces = None
@@ -127,12 +129,10 @@ class E2FormerCalculator:
         x = atoms.get_positions()
         if self._key is not None and self._key[0] is x and self._key[1] == x._version:
             return
-        cell = atoms.get_cell()
         kw = {}
         if self.use_charge:
             kw = {"charge": torch.tensor([atoms.charge]), "multiplicity": torch.tensor([atoms.multiplicity])}
-        energy, forces = self.potential(x.to(torch.float32), atoms._torch_numbers,
-                                        None if cell is None else cell.to(torch.float32).cpu(), atoms.pbc, **kw)
+        energy, forces = self.potential(x.to(torch.float32), atoms._torch_numbers, atoms._cell_host, atoms.pbc, **kw)
         energy = energy.reshape(-1)[0].to(atoms._dtype)
         if self.add_ref_energy and self.ref_energy is not None:
             energy = energy + torch.as_tensor(self.ref_energy, device=x.device,
