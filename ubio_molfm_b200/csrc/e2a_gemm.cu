@@ -682,16 +682,35 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           if (gc + 3 < N) bv.w = bias[gc + 3];
         }
         const bool cvec = C && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
-        for (int r2 = 0; r2 < 32; r2 += kRowsPerStep) {
-          const int r = r2 + rr;
+        constexpr int kSteps = 32 / kRowsPerStep;
+        // the previous values of a read-modify-write output (P with accumulate, or C with accumulate) are
+        // loaded for all of this warp's row steps first, so their memory latencies overlap instead of
+        // adding up one row step at a time
+        float4 old[kSteps];
+#pragma unroll
+        for (int st2 = 0; st2 < kSteps; ++st2) {
+          old[st2] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const int row = m0 + 32 * q + st2 * kRowsPerStep + rr;
+          if (!accumulate || row >= M) continue;
+          if (P) {
+            const float* pp = P + (int64_t)row * ldp + (gc >> 1);
+            if (gc + 1 < N) old[st2].x = pp[0];
+            if (gc + 3 < N) old[st2].y = pp[1];
+          } else if (cvec) {
+            old[st2] = *reinterpret_cast<const float4*>(C + (int64_t)row * ldc + gc);
+          }
+        }
+#pragma unroll
+        for (int st2 = 0; st2 < kSteps; ++st2) {
+          const int r = st2 * kRowsPerStep + rr;
           const int row = m0 + 32 * q + r;
           if (row >= M) continue;
           float4 x = *reinterpret_cast<const float4*>(stg + r * WS_LD + 4 * sub);
           x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
           if (P) {
             float* pp = P + (int64_t)row * ldp + (gc >> 1);
-            if (gc + 1 < N) pp[0] = (accumulate ? pp[0] : 0.f) + x.x * x.y;
-            if (gc + 3 < N) pp[1] = (accumulate ? pp[1] : 0.f) + x.z * x.w;
+            if (gc + 1 < N) pp[0] = old[st2].x + x.x * x.y;
+            if (gc + 3 < N) pp[1] = old[st2].y + x.z * x.w;
             if (!C) continue;
             float* cp = C + (int64_t)row * ldc + gc;
             if (cvec) {
@@ -706,8 +725,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           float* cp = C + (int64_t)row * ldc + gc;
           if (cvec) {
             if (accumulate) {
-              const float4 o = *reinterpret_cast<const float4*>(cp);
-              x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+              x.x += old[st2].x; x.y += old[st2].y; x.z += old[st2].z; x.w += old[st2].w;
             }
             *reinterpret_cast<float4*>(cp) = x;
           } else {
