@@ -1049,7 +1049,9 @@ def run_gemm(args, ws, rank, local):
             ("Q / K pair product, 9 irreps rows (9 launches, projections kept)",
              lambda: linear.so3_pair_product(x, w1, w2, bias, lidx, recompute=False), 2.0 * N * 9 * 2 * Hd * C),
             ("edge radial MLP first layer, basis formed on chip from 3.13 M edge lengths",
-             lambda: linear.rbf_linear(d, mu, coeff, wr, br), 2.0 * E * 128 * nb)]:
+             lambda: linear.rbf_linear(d, mu, coeff, wr, br, on_chip=True), 2.0 * E * 128 * nb),
+            ("edge radial MLP first layer, basis written by one kernel then the plain GEMM (the default)",
+             lambda: linear.rbf_linear(d, mu, coeff, wr, br, on_chip=False), 2.0 * E * 128 * nb)]:
         for _ in range(max(args.warmup, 1)):
             fn()
         torch.cuda.synchronize()

@@ -147,12 +147,14 @@ def test_nve_velocity_verlet_conserves_energy():
     assert md.nsteps == 20
 
 
+@pytest.mark.parametrize("on_chip", [False, True])
 @pytest.mark.parametrize("E,nb,h", [(3000, 256, 128), (3001, 32, 16), (517, 36, 132), (700, 300, 64)])
-def test_rbf_linear_matches_materialised_basis(E, nb, h):
-    """rbf_linear (basis formed inside the GEMM's A tiles, distance gradient contracted in its
-    epilogue; the materialised fallback for nb > 256) against the GaussianSmearing module followed by
-    a linear map, fp64 reference.  Ragged edge counts, a basis narrower than one 64-column block and a
-    K that is not a multiple of the 16-wide slab."""
+def test_rbf_linear_matches_materialised_basis(E, nb, h, on_chip):
+    """rbf_linear (the basis formed inside the GEMM's A tiles, or written by one kernel and multiplied
+    by the plain GEMM; the distance gradient contracted in the GEMM's epilogue; the materialised path
+    for nb > 256) against the GaussianSmearing module followed by a linear map, fp64 reference.  Ragged
+    edge counts, a basis narrower than one 64-column block and a K that is not a multiple of the
+    16-wide slab."""
     from ubio_molfm_b200.linear import rbf_linear
     from ubio_molfm_b200.nn import GaussianSmearing
 
@@ -163,7 +165,8 @@ def test_rbf_linear_matches_materialised_basis(E, nb, h):
     b = torch.randn(h, generator=g, dtype=torch.float64)
     ref = rbf.double()(d) @ w.t() + b
     dg = d.detach().float().to(DEV).requires_grad_(True)
-    out = rbf_linear(dg, rbf.offset.float().to(DEV), rbf.coeff, w.float().to(DEV), b.float().to(DEV))
+    out = rbf_linear(dg, rbf.offset.float().to(DEV), rbf.coeff, w.float().to(DEV), b.float().to(DEV),
+                     on_chip=on_chip)
     assert (out.double().cpu() - ref).abs().max().item() < 1e-5 * ref.abs().max().item()
     wo = torch.randn(ref.shape, generator=g, dtype=torch.float64)
     (gr,) = torch.autograd.grad(ref, d, wo)

@@ -311,6 +311,25 @@ __global__ void k_rbf_fwd(const float* __restrict__ d, int64_t E, const float* _
   }
 }
 
+// Same basis, four consecutive basis functions per thread (nb % 4 == 0): one 16-byte store each, the
+// offsets staged in shared memory (nb <= 1024).
+__global__ void k_rbf_fwd4(const float* __restrict__ d, int64_t E, const float* __restrict__ mu, int nb, float coeff,
+                           float* __restrict__ out) {
+  __shared__ float mu_s[1024];
+  for (int k = threadIdx.x; k < nb; k += blockDim.x) mu_s[k] = mu[k];
+  __syncthreads();
+  const int nb4 = nb >> 2;
+  const int64_t total = E * (int64_t)nb4;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / nb4;
+    const int k = 4 * (int)(t - e * nb4);
+    const float de = __ldg(d + e);
+    const float x0 = de - mu_s[k], x1 = de - mu_s[k + 1], x2 = de - mu_s[k + 2], x3 = de - mu_s[k + 3];
+    reinterpret_cast<float4*>(out)[t] =
+        make_float4(expf(coeff * (x0 * x0)), expf(coeff * (x1 * x1)), expf(coeff * (x2 * x2)), expf(coeff * (x3 * x3)));
+  }
+}
+
 __global__ void k_rbf_bwd(const float* __restrict__ d, const float* __restrict__ g, int64_t E,
                           const float* __restrict__ mu, int nb, float coeff, float* __restrict__ dd) {
   const int lane = threadIdx.x & 31;
@@ -336,7 +355,10 @@ int e2a_rbf_fwd(const float* dist, int64_t n_edges, const float* mu, int nb, flo
   if (n_edges < 0 || nb <= 0) return E2A_ERR_ARG;
   if (n_edges == 0) return E2A_OK;
   if (!dist || !mu || !out) return E2A_ERR_ARG;
-  k_rbf_fwd<<<grid_flat(n_edges * nb), 256, 0, (cudaStream_t)stream>>>(dist, n_edges, mu, nb, coeff, out);
+  if (nb % 4 == 0 && nb <= 1024 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0)
+    k_rbf_fwd4<<<grid_flat(n_edges * (nb / 4)), 256, 0, (cudaStream_t)stream>>>(dist, n_edges, mu, nb, coeff, out);
+  else
+    k_rbf_fwd<<<grid_flat(n_edges * nb), 256, 0, (cudaStream_t)stream>>>(dist, n_edges, mu, nb, coeff, out);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
 }

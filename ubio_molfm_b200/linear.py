@@ -521,17 +521,18 @@ def gate(s, h, c_scalar, c_vector):
 # Gaussian radial basis consumed by a linear map, formed on the fly (inference path)
 # ------------------------------------------------------------------------------------------------
 class _RbfLinearFn(torch.autograd.Function):
-    """``h = rbf(d) W^T (+ b)`` with rbf[e,k] = exp(coeff (d_e - mu_k)^2) formed inside the GEMM (its
-    splitter warps build each A tile from d and mu; the basis never reaches HBM).  The backward forms
-    d(rbf) = g W tile by tile and contracts it with d rbf / d d in the GEMM's epilogue, so only [E]
-    vectors reach the distance's other consumers."""
+    """``h = rbf(d) W^T (+ b)`` with rbf[e,k] = exp(coeff (d_e - mu_k)^2), either formed inside the GEMM
+    (``on_chip``: its splitter warps build each A tile from d and mu) or written by one elementwise
+    kernel and multiplied by the plain GEMM; the basis is dropped after the product either way.  The
+    backward forms d(rbf) = g W tile by tile and contracts it with d rbf / d d in the GEMM's epilogue,
+    so only [E] vectors reach the distance's other consumers."""
 
     @staticmethod
     def fused_ok(nb, n_out):
         return PRESPLIT_WEIGHTS and 0 < nb <= 256 and nb % 4 == 0 and n_out % 4 == 0
 
     @staticmethod
-    def forward(ctx, dist, mu, coeff, w, b):
+    def forward(ctx, dist, mu, coeff, w, b, on_chip):
         lib = _lib.load()
         d = dist.contiguous()
         E, nb = d.shape[0], mu.shape[0]
@@ -539,7 +540,7 @@ class _RbfLinearFn(torch.autograd.Function):
         ctx.save_for_backward(d, mu, w)
         ctx.coeff = float(coeff)
         ctx.fused = _RbfLinearFn.fused_ok(nb, N)
-        if not ctx.fused:   # basis materialised for the product, then dropped
+        if not ctx.fused or not on_chip:   # basis materialised for the product, then dropped
             rbf = torch.empty((E, nb), device=d.device, dtype=torch.float32)
             check(lib.e2a_rbf_fwd(ptr(d), E, ptr(mu), nb, float(coeff), ptr(rbf), stream_of(d.device)),
                   "e2a_rbf_fwd")
@@ -563,7 +564,7 @@ class _RbfLinearFn(torch.autograd.Function):
             dd = torch.empty_like(d)
             check(lib.e2a_rbf_bwd(ptr(d), ptr(d_rbf), E, ptr(mu), nb, ctx.coeff, ptr(dd), stream_of(d.device)),
                   "e2a_rbf_bwd")
-            return dd, None, None, None, None
+            return dd, None, None, None, None, None
         wt = w.t().contiguous()           # [nb, Kh]: d(rbf) = g @ w
         hi, lo = split_tf32(wt)
         nblk = (nb + 63) // 64
@@ -573,14 +574,22 @@ class _RbfLinearFn(torch.autograd.Function):
                                                 ptr(part), nblk, E, nb, Kh, PASSES, stream_of(d.device)),
               "e2a_gemm_tf32x3_rbf_dist_grad")
         GEMM_TIMER.stop(t0, E, nb, Kh)
-        return part.sum(1), None, None, None, None
+        return part.sum(1), None, None, None, None, None
 
 
-def rbf_linear(dist, mu, coeff, w, b=None):
-    """``GaussianSmearing(dist) @ w.T (+ b)`` without materialising the basis for autograd (CUDA,
-    constant weights)."""
+# Forward of the radial-basis products: False = the basis is written by one elementwise kernel and read
+# by the plain GEMM (measured faster: the on-chip basis makes the GEMM's splitter warps compute one
+# exponential per operand element, which they cannot do at the tensor core's rate); True = formed on
+# chip.  The backward always contracts d(rbf) on chip (only [E] vectors leave the GEMM).
+RBF_FWD_ON_CHIP = False
+
+
+def rbf_linear(dist, mu, coeff, w, b=None, on_chip=None):
+    """``GaussianSmearing(dist) @ w.T (+ b)`` (CUDA, constant weights); the basis is never kept for
+    autograd."""
     return _RbfLinearFn.apply(dist.float(), mu.float().contiguous(), float(coeff), w.detach().float().contiguous(),
-                              None if b is None else b.detach().float().contiguous())
+                              None if b is None else b.detach().float().contiguous(),
+                              RBF_FWD_ON_CHIP if on_chip is None else bool(on_chip))
 
 
 # ------------------------------------------------------------------------------------------------
