@@ -440,6 +440,11 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
   const int tiles_n = (N + BN - 1) / BN;
   const int tiles = ((M + BM - 1) / BM) * tiles_n;
   const int nk = (K + Cfg::BK - 1) / Cfg::BK;
+  // slabs per TMEM chain: the whole K in one chain when K <= E2A_WS_CHAINK_SMALLK, else E2A_WS_CHAINK
+#ifndef E2A_WS_CHAINK_SMALLK
+#define E2A_WS_CHAINK_SMALLK 0
+#endif
+  const int spc = (K <= E2A_WS_CHAINK_SMALLK) ? (nk > 0 ? nk : 1) : Cfg::SPC;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(e2a_smem_u32(tmem_slot)), "r"(kWsTmemCols) : "memory");
@@ -502,7 +507,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
         for (int kb = 0; kb < nk; ++kb, ++n) {
           const uint32_t s = n % Cfg::STAGES, cb = c % Cfg::CHAINS;
-          if ((kb % Cfg::SPC) == 0 && !ws_wait(&tempty[cb], ((c / Cfg::CHAINS) & 1) ^ 1, abort_flag)) { run = false; break; }
+          if ((kb % spc) == 0 && !ws_wait(&tempty[cb], ((c / Cfg::CHAINS) & 1) ^ 1, abort_flag)) { run = false; break; }
           if (!ws_wait(&split_done[s], (n / Cfg::STAGES) & 1, abort_flag)) { run = false; break; }
           WS_TRACE(3, n);
           tc_fence_after();
@@ -512,7 +517,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
 #pragma unroll
           for (int kk = 0; kk < Cfg::BK / 8; ++kk) {
             const uint32_t koff = kk * 32;
-            mma_tf32_ta(d, a_hi + 8 * kk, Cfg::desc(b_hi + koff), ((kb % Cfg::SPC) == 0 && kk == 0) ? 0u : 1u);
+            mma_tf32_ta(d, a_hi + 8 * kk, Cfg::desc(b_hi + koff), ((kb % spc) == 0 && kk == 0) ? 0u : 1u);
             if (passes == 3) {
               mma_tf32_ta(d, a_hi + 8 * kk, Cfg::desc(b_lo + koff), 1u);
               mma_tf32_ta(d, a_lo + 8 * kk, Cfg::desc(b_hi + koff), 1u);
@@ -521,7 +526,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           mma_commit(&empty[s]);
           mma_commit(&a_empty[n % Cfg::ATS]);
           last = n;
-          if ((kb % Cfg::SPC) == Cfg::SPC - 1 || kb == nk - 1) {
+          if ((kb % spc) == spc - 1 || kb == nk - 1) {
             mma_commit(&tfull[cb]);
             ++c;
           }
@@ -620,7 +625,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     float* stg = epi + (warp - 4) * 32 * WS_LD;
     uint32_t c = 0;
     bool run = true;
-    const int nch = (nk + Cfg::SPC - 1) / Cfg::SPC;
+    const int nch = (nk + spc - 1) / spc;
     for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN + WS_DCOLS * half;
       float acc[WS_DCOLS];
