@@ -294,17 +294,19 @@ def test_attention_span_row_order_and_determinism():
         assert torch.equal(x, y)  # independent of the processing order
 
 
-def test_attention_span_full_size_sampled_rows():
-    """Full-size span (1e5 rows, 1.2e5 keys, ~3.2M edges, H = 128, D = 8, C = 58): the CUDA forward and
-    backward over the whole graph, checked on seeded samples against the fp64 oracle run on the
-    sub-problem those samples depend on -- sampled rows (with all their edges) for out, d_q and the
-    per-edge gradients, and sampled keys (with every row that reaches them, complete) for d_value and
-    d_k, which are then exact full-graph sums."""
+@pytest.mark.parametrize("k_avg,n_keys", [(32, 4), (64, 3), (128, 2)])
+def test_attention_span_full_size_sampled_rows(k_avg, n_keys):
+    """Full-size span (1e5 rows, 1.2e5 keys, H = 128, D = 8, C = 58) at the config-2 neighbour counts
+    (~32, 64 and 128 edges per row: 3.2 M, 6.4 M and 12.8 M edges): the CUDA forward and backward over
+    the whole graph, checked on seeded samples against the fp64 oracle run on the sub-problem those
+    samples depend on -- sampled rows (with all their edges) for out, d_q and the per-edge gradients,
+    and sampled keys (with every row that reaches them, complete) for d_value and d_k, which are then
+    exact full-graph sums."""
     from ubio_molfm_b200 import ops
 
     N, M, H, D, C = 100_000, 120_000, 128, 8, 58
     rng = np.random.default_rng(21)
-    deg = rng.integers(20, 45, N)
+    deg = rng.integers(k_avg - 12, k_avg + 13, N)
     deg[rng.choice(N, 50, replace=False)] = 0                      # some isolated rows
     q = np.repeat(np.arange(N), deg)
     n = rng.integers(0, M, len(q))
@@ -325,7 +327,7 @@ def test_attention_span_full_size_sampled_rows():
     del ag
 
     row_ptr = np.concatenate([[0], np.cumsum(deg)])
-    keys = rng.choice(np.unique(n), 4, replace=False)
+    keys = rng.choice(np.unique(n), n_keys, replace=False)
     rows = np.union1d(rng.choice(np.nonzero(deg)[0], 24, replace=False), np.unique(q[np.isin(n, keys)]))
     rows = np.union1d(rows, np.nonzero(deg == 0)[0][:2])
     eidx = np.concatenate([np.arange(row_ptr[r], row_ptr[r + 1]) for r in rows])
