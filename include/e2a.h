@@ -223,6 +223,15 @@ int e2a_tf32_split(const float* B, int64_t ldb, int64_t N, int64_t K, float* B_h
 int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
                              int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
                              int accumulate, int passes, void* stream);
+/* Backward of the pair product fused into the GEMM (no reference counterpart to a fused form; it      */
+/* replaces e2a_pair_grad followed by e2a_gemm_tf32x3 on D, SO3_Linear2Scalar_e2former's backward,      */
+/* module_utils.py:2198-2274): C[M,N] = D[M,K] B[N,K]^T with D[r,2j] = G[r,j] O[r,2j+1] and            */
+/* D[r,2j+1] = G[r,j] O[r,2j], D formed inside the GEMM from the O and G tiles (D never reaches HBM).  */
+/* O rows of K floats (ld ldo), G rows of K/2 floats (ld ldg), B pre-split (B_lo required), K % 32 == 0 */
+/* and 16-byte aligned rows; E2A_ERR_UNSUPPORTED otherwise.                                            */
+int e2a_gemm_tf32x3_pairgrad(const float* O, int64_t ldo, const float* G, int64_t ldg, const float* B,
+                             const float* B_lo, int64_t ldb, float* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                             int passes, void* stream);
 /* Backward of the pair product: D[n,m,2j] = G[n,l(m),j] O[n,m,2j+1], D[n,m,2j+1] = G[n,l(m),j] O[n,m,2j] */
 /* for O, D [n_nodes, R, 2h], G [n_nodes, L1, h], l(m) the degree of row m.                      */
 int e2a_pair_grad(const float* O, const float* G, int64_t n_nodes, int R, int L1, int h, float* D, void* stream);

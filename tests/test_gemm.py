@@ -147,3 +147,31 @@ def test_bounded_wait_timeout_is_reported_and_raised():
         m(pos, Z)
     e1, f1 = m(pos, Z)                    # the word was cleared; the next evaluation is clean
     assert torch.equal(e0, e1) and torch.equal(f0, f1)
+
+
+@pytest.mark.parametrize("N,C,Hd", [(1003, 256, 512), (300, 64, 64)])
+def test_pair_product_backward_fused_equals_two_kernel(N, C, Hd):
+    """The pair-product backward with D = pair_grad(O, G) formed inside the GEMM's A tiles
+    (e2a_gemm_tf32x3_pairgrad) against the pair_grad kernel followed by the plain GEMM: the same fp32
+    products are split the same way, so the input gradients are bitwise equal (ragged M included)."""
+    from ubio_molfm_b200 import linear
+
+    g = torch.Generator(device="cuda").manual_seed(N)
+    x = torch.randn(N, 9, C, device="cuda", generator=g)
+    w1 = torch.randn(3, Hd, C, device="cuda", generator=g) / C ** 0.5
+    w2 = torch.randn(3, Hd, C, device="cuda", generator=g) / C ** 0.5
+    bias = torch.randn(1, 1, Hd, device="cuda", generator=g)
+    lidx = [0, 1, 1, 1, 2, 2, 2, 2, 2]
+    dP = torch.randn(N, 3, Hd, device="cuda", generator=g)
+    out = []
+    old = linear.FUSED_PAIR_GRAD
+    try:
+        for fused in (True, False):
+            linear.FUSED_PAIR_GRAD = fused
+            xx = x.clone().requires_grad_(True)
+            P = linear.so3_pair_product(xx, w1, w2, bias, lidx)
+            (dx,) = torch.autograd.grad(P, xx, dP)
+            out.append(dx)
+    finally:
+        linear.FUSED_PAIR_GRAD = old
+    assert torch.equal(out[0], out[1])

@@ -55,6 +55,7 @@ SIGNATURES = {
     "e2a_gemm_wait_selftest": (I32, [I64, P]),
     "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
     "e2a_pair_grad": (I32, [P, P, I64, I32, I32, I32, P, P]),
+    "e2a_gemm_tf32x3_pairgrad": (I32, [P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I32, P]),
     "e2a_node_apply_fwd": (I32, [P, P, I64, P, I64, I64, I32, I32, I32, P, I64, I32, P]),
     "e2a_node_apply_bwd": (I32, [P, P, I64, P, I64, P, I64, I64, I32, I32, I32, P, I64, P, I64, P, P]),
     "e2a_rbf_fwd": (I32, [P, I64, P, I32, ctypes.c_float, P, P]),

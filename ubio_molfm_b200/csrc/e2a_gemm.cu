@@ -315,9 +315,12 @@ struct IntC { static constexpr int value = V; };
 #ifndef E2A_WS_CHAINK
 #define E2A_WS_CHAINK 64
 #endif
-template <int BK_>
+template <int BK_, bool PG_ = false>
 struct WsCfg {
   static constexpr int BK = BK_;
+  // PG: A is formed on chip from the projections O (loaded as the A slab) and the pair gradient G (one
+  // extra half-width slab per stage): A[r, 2j] = G[r, j] O[r, 2j+1], A[r, 2j+1] = G[r, j] O[r, 2j]
+  static constexpr bool PG = PG_;
   static constexpr int SPC = E2A_WS_CHAINK / BK;         // slabs per TMEM chain (64 k = 24 MMAs by default)
 #ifndef E2A_WS_STAGES16
 #define E2A_WS_STAGES16 6   // shared memory allows up to 8 (24 KB stages)
@@ -325,9 +328,10 @@ struct WsCfg {
 #ifndef E2A_WS_STAGES32
 #define E2A_WS_STAGES32 4   // 48 KB stages
 #endif
-  static constexpr int STAGES = BK == 16 ? E2A_WS_STAGES16 : E2A_WS_STAGES32;
+  static constexpr int STAGES = PG ? 3 : (BK == 16 ? E2A_WS_STAGES16 : E2A_WS_STAGES32);
   static constexpr int TILE = BM * BK * 4;               // bytes per operand part
-  static constexpr int STAGE = 3 * TILE;                 // A (raw), B (split in place when not pre-split), B_lo
+  static constexpr int GSLAB = PG ? BM * (BK / 2) * 4 : 0;   // the G slab (64-byte rows, 64-byte swizzle)
+  static constexpr int STAGE = 3 * TILE + GSLAB;         // A (raw), B (split in place when not pre-split), B_lo, G
   static constexpr int CHAINS = BK == 16 ? E2A_WS_CHAINS16 : E2A_WS_CHAINS32;   // TMEM chain buffers (BN columns)
   static constexpr int ATS = BK == 16 ? E2A_WS_ATS16 : E2A_WS_ATS32;  // A hi / lo slots in TMEM (2 BK columns each)
   static constexpr uint32_t ACOL = CHAINS * 128;         // first A-slot column
@@ -347,8 +351,10 @@ constexpr int WS_EH = 16;                        // epilogue staged 16 columns a
 constexpr int WS_LD = WS_EH + 4;                 // staging row stride (floats)
 constexpr int WS_EPI = WS_DRAIN * 32 * WS_LD * 4;
 constexpr uint32_t kWsTmemCols = 512;
-template <int BK>
-constexpr int ws_smem() { return WsCfg<BK>::STAGES * WsCfg<BK>::STAGE + WS_EPI + WsCfg<BK>::NBARS * 8 + 16 + 1024 + 1024; }
+template <int BK, bool PG = false>
+constexpr int ws_smem() {
+  return WsCfg<BK, PG>::STAGES * WsCfg<BK, PG>::STAGE + WS_EPI + WsCfg<BK, PG>::NBARS * 8 + 16 + 1024 + 1024;
+}
 
 __device__ __forceinline__ float tf32_lo(float a, float h) { return tf32_hi(a - h); }
 
@@ -415,12 +421,13 @@ struct RbfArgs {
   int64_t ld_rdot;
 };
 
-template <int BK_>
-__global__ void __launch_bounds__(WsCfg<BK_>::THREADS, 1)
+template <int BK_, bool PG_ = false>
+__global__ void __launch_bounds__(WsCfg<BK_, PG_>::THREADS, 1)
 k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-          const __grid_constant__ CUtensorMap tmBl, int b_split, float* C, int64_t ldc, const float* __restrict__ bias, float* P,
-          int64_t ldp, int M, int N, int K, int accumulate, int passes, const RbfArgs rb) {
-  using Cfg = WsCfg<BK_>;
+          const __grid_constant__ CUtensorMap tmBl, const __grid_constant__ CUtensorMap tmG, int b_split, float* C,
+          int64_t ldc, const float* __restrict__ bias, float* P, int64_t ldp, int M, int N, int K, int accumulate,
+          int passes, const RbfArgs rb) {
+  using Cfg = WsCfg<BK_, PG_>;
   const bool gen = rb.d != nullptr && rb.rdot == nullptr;   // A formed on chip
   extern __shared__ uint8_t ws_raw[];
   uint8_t* smem = ws_raw + ((1024u - (e2a_smem_u32(ws_raw) & 1023u)) & 1023u);
@@ -477,7 +484,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
       if (b_split) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmBl)) : "memory");
-      const uint32_t bytes = (b_split ? 2 : 1) * Cfg::TILE + (gen ? 0 : Cfg::TILE);
+      if (Cfg::PG) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmG)) : "memory");
+      const uint32_t bytes = (b_split ? 2 : 1) * Cfg::TILE + (gen ? 0 : Cfg::TILE) + Cfg::GSLAB;
       uint32_t n = 0;
       bool run = true;
       for (int tile = blockIdx.x; tile < tiles && run; tile += gridDim.x) {
@@ -491,6 +499,7 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           if (!gen) tma_load_2d(st, &tmA, kb * Cfg::BK, m0, &full[s]);
           tma_load_2d(st + Cfg::TILE, &tmB, kb * Cfg::BK, n0, &full[s]);
           if (b_split) tma_load_2d(st + 2 * Cfg::TILE, &tmBl, kb * Cfg::BK, n0, &full[s]);
+          if (Cfg::PG) tma_load_2d(st + 3 * Cfg::TILE, &tmG, kb * (Cfg::BK / 2), m0, &full[s]);
         }
       }
       if (!run) {  // copies still in flight must land before the CTA exits
@@ -588,6 +597,24 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
               const int pc = Cfg::BK == 16 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
               const float4 x = *reinterpret_cast<const float4*>(st + r * (Cfg::BK * 4) + 16 * pc);
               v[4 * c4] = x.x; v[4 * c4 + 1] = x.y; v[4 * c4 + 2] = x.z; v[4 * c4 + 3] = x.w;
+            }
+            if constexpr (Cfg::PG) {
+              // G columns 8h .. 8h+7 of this row: logical 16-byte chunks 2h, 2h+1 of its 64-byte G row
+              // (64-byte swizzle: chunk c at c ^ ((r / 2) % 4)); A[2i] = G[i] O[2i+1], A[2i+1] = G[i] O[2i]
+              const uint8_t* gs = st + 3 * Cfg::TILE + r * (Cfg::BK / 2) * 4;
+              float g[8];
+#pragma unroll
+              for (int c2 = 0; c2 < 2; ++c2) {
+                const int pc = (2 * h + c2) ^ ((r >> 1) & 3);
+                const float4 x = *reinterpret_cast<const float4*>(gs + 16 * pc);
+                g[4 * c2] = x.x; g[4 * c2 + 1] = x.y; g[4 * c2 + 2] = x.z; g[4 * c2 + 3] = x.w;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float o0 = v[2 * i], o1 = v[2 * i + 1];
+                v[2 * i] = g[i] * o1;
+                v[2 * i + 1] = g[i] * o0;
+              }
             }
           }
 #pragma unroll
@@ -805,7 +832,8 @@ __global__ void k_tf32_split(const float* __restrict__ B, int64_t ldb, int64_t N
 // Launches the warp-specialised kernel; E2A_ERR_UNSUPPORTED when the operands do not suit it.
 static int launch_ws(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
                      int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
-                     int accumulate, int passes, cudaStream_t st, RbfArgs rb = RbfArgs{nullptr, nullptr, 0.f, nullptr, 0}) {
+                     int accumulate, int passes, cudaStream_t st, RbfArgs rb = RbfArgs{nullptr, nullptr, 0.f, nullptr, 0},
+                     const float* G = nullptr, int64_t ldg = 0) {
   const bool gen = rb.d != nullptr && rb.rdot == nullptr;
   if (gen) { A = B; lda = ldb; }   // the A map is never read
   const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
@@ -822,24 +850,33 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
 #define E2A_WS_GEN_BK32 0
 #endif
   const int bk = ((gen && !E2A_WS_GEN_BK32) || K < E2A_WS_BK32_MINK) ? 16 : 32;
-  CUtensorMap ta, tb, tbl;
+  if (G && (bk != 32 || (K % 32) != 0 || !B_lo || (ldg % 4) != 0 || (reinterpret_cast<uintptr_t>(G) & 15u) != 0))
+    return E2A_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb, tbl, tg;
   if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||
       !make_map_2d(enc, &tbl, B_lo ? B_lo : B, N, K, ldb, bk))
     return E2A_ERR_UNSUPPORTED;
+  // the pair-gradient slab: K / 2 columns of G, 16-column boxes with the 64-byte swizzle
+  if (G ? !make_map_2d(enc, &tg, G, M, K / 2, ldg, 16) : false) return E2A_ERR_UNSUPPORTED;
+  if (!G) tg = ta;   // not read
   int dev = 0, sms = 0;
   E2A_CUDA(cudaGetDevice(&dev));
   E2A_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   if (tiles > INT32_MAX) return E2A_ERR_ARG;
   const int grid = (int)(tiles < sms ? tiles : sms);
-  if (bk == 16) {
+  if (G) {
+    E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32, true>()));
+    k_gemm_ws<32, true><<<grid, WsCfg<32, true>::THREADS, ws_smem<32, true>(), st>>>(
+        ta, tb, tbl, tg, 1, C, ldc, bias, P, ldp, (int)M, (int)N, (int)K, accumulate, passes, rb);
+  } else if (bk == 16) {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<16>()));
-    k_gemm_ws<16><<<grid, WsCfg<16>::THREADS, ws_smem<16>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
-                                                            (int)N, (int)K, accumulate, passes, rb);
+    k_gemm_ws<16><<<grid, WsCfg<16>::THREADS, ws_smem<16>(), st>>>(ta, tb, tbl, tg, B_lo ? 1 : 0, C, ldc, bias, P, ldp,
+                                                            (int)M, (int)N, (int)K, accumulate, passes, rb);
   } else {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32>()));
-    k_gemm_ws<32><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(ta, tb, tbl, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M,
-                                                            (int)N, (int)K, accumulate, passes, rb);
+    k_gemm_ws<32><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(ta, tb, tbl, tg, B_lo ? 1 : 0, C, ldc, bias, P, ldp,
+                                                            (int)M, (int)N, (int)K, accumulate, passes, rb);
   }
   E2A_CHECK_LAUNCH();
   return E2A_OK;
@@ -874,6 +911,16 @@ int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const 
   if (M == 0 || N == 0) return E2A_OK;
   if (!P || (K > 0 && (!A || !B)) || lda < K || ldb < K || (C && ldc < N) || ldp < N / 2) return E2A_ERR_ARG;
   return launch_ws(A, lda, B, B_lo, ldb, C, ldc, bias, P, ldp, M, N, K, accumulate, passes, (cudaStream_t)stream);
+}
+
+int e2a_gemm_tf32x3_pairgrad(const float* O, int64_t ldo, const float* G, int64_t ldg, const float* B,
+                             const float* B_lo, int64_t ldb, float* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                             int passes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || (passes != 1 && passes != 3) || (K & 1)) return E2A_ERR_ARG;
+  if (M == 0 || N == 0) return E2A_OK;
+  if (!O || !G || !B || !B_lo || !C || ldo < K || ldg < K / 2 || ldb < K || ldc < N) return E2A_ERR_ARG;
+  return launch_ws(O, ldo, B, B_lo, ldb, C, ldc, nullptr, nullptr, 0, M, N, K, 0, passes, (cudaStream_t)stream,
+                   RbfArgs{nullptr, nullptr, 0.f, nullptr, 0}, G, ldg);
 }
 
 int e2a_gemm_tf32x3_rbf(const float* dist, const float* mu, float coeff, const float* B, const float* B_lo,

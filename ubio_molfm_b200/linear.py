@@ -259,6 +259,11 @@ def ln_silu(h, ln, tables=None):
                            T, zt, S, zs)
 
 
+# Backward of the pair product: True = D = pair_grad(O, G) formed inside the GEMM's A tiles
+# (e2a_gemm_tf32x3_pairgrad; D never reaches HBM), False = pair_grad kernel then the plain GEMM.
+FUSED_PAIR_GRAD = True
+
+
 class _SO3PairProdFn(torch.autograd.Function):
     """``P[n, l, j] = sum_{m in degree l} o1[n,m,j] * o2[n,m,j]`` with ``o1 = x W1[l]^T (+b on m=0)``,
     ``o2 = x W2[l]^T`` (the inner product of SO3_Linear2Scalar_e2former), fused into the GEMM
@@ -316,11 +321,23 @@ class _SO3PairProdFn(torch.autograd.Function):
         N, R, h2 = O.shape
         L1 = w12.shape[0]
         C = w12.shape[2]
-        D = torch.empty_like(O)
-        check(lib.e2a_pair_grad(ptr(O), ptr(G), N, R, L1, h2 // 2, ptr(D), stream_of(O.device)), "e2a_pair_grad")
         wt = w12.transpose(1, 2).contiguous()  # [L+1, C, 2h]
         thi, tlo = _maybe_split(wt)
         dx = torch.empty((N, R, C), device=O.device, dtype=torch.float32)
+        if FUSED_PAIR_GRAD and tlo is not None and h2 % 32 == 0 and O.data_ptr() % 16 == 0 and G.data_ptr() % 16 == 0:
+            # D = pair_grad(O, G) formed inside the GEMM's A tiles, one launch per irreps row
+            st = stream_of(O.device)
+            for m in range(R):
+                l = ctx.lidx[m]
+                t0 = GEMM_TIMER.start()
+                rc = lib.e2a_gemm_tf32x3_pairgrad(O.data_ptr() + 4 * m * h2, R * h2, G.data_ptr() + 4 * l * (h2 // 2),
+                                                  L1 * (h2 // 2), ptr(thi[l]), ptr(tlo[l]), h2,
+                                                  dx.data_ptr() + 4 * m * C, R * C, N, C, h2, PASSES, st)
+                GEMM_TIMER.stop(t0, N, C, h2)
+                check(rc, "e2a_gemm_tf32x3_pairgrad")
+            return dx, None, None, None, None
+        D = torch.empty_like(O)
+        check(lib.e2a_pair_grad(ptr(O), ptr(G), N, R, L1, h2 // 2, ptr(D), stream_of(O.device)), "e2a_pair_grad")
         for m in range(R):
             gemm(D[:, m, :], wt[ctx.lidx[m]], None, out=dx[:, m, :], b_split=(thi[ctx.lidx[m]], tlo[ctx.lidx[m]]))
         return dx, None, None, None, None
