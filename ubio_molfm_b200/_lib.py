@@ -83,6 +83,9 @@ SIGNATURES = {
 _lib = None
 
 
+E2A_ERR_UNSUPPORTED = 4   # status of an entry point that does not take the given operands (include/e2a.h)
+
+
 class E2AError(RuntimeError):
     pass
 

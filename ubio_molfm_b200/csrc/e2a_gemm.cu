@@ -849,8 +849,9 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
 #ifndef E2A_WS_GEN_BK32
 #define E2A_WS_GEN_BK32 0
 #endif
-  const int bk = ((gen && !E2A_WS_GEN_BK32) || K < E2A_WS_BK32_MINK) ? 16 : 32;
-  if (G && (bk != 32 || (K % 32) != 0 || !B_lo || (ldg % 4) != 0 || (reinterpret_cast<uintptr_t>(G) & 15u) != 0))
+  // the pair-gradient mode always runs 32-wide slabs
+  const int bk = G ? 32 : (((gen && !E2A_WS_GEN_BK32) || K < E2A_WS_BK32_MINK) ? 16 : 32);
+  if (G && ((K % 32) != 0 || !B_lo || (ldg % 4) != 0 || (reinterpret_cast<uintptr_t>(G) & 15u) != 0))
     return E2A_ERR_UNSUPPORTED;
   CUtensorMap ta, tb, tbl, tg;
   if (!make_map_2d(enc, &ta, A, gen ? N : M, K, lda, bk) || !make_map_2d(enc, &tb, B, N, K, ldb, bk) ||

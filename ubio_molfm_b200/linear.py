@@ -325,8 +325,11 @@ class _SO3PairProdFn(torch.autograd.Function):
         thi, tlo = _maybe_split(wt)
         dx = torch.empty((N, R, C), device=O.device, dtype=torch.float32)
         if FUSED_PAIR_GRAD and tlo is not None and h2 % 32 == 0 and O.data_ptr() % 16 == 0 and G.data_ptr() % 16 == 0:
-            # D = pair_grad(O, G) formed inside the GEMM's A tiles, one launch per irreps row
+            # D = pair_grad(O, G) formed inside the GEMM's A tiles, one launch per irreps row (rows whose
+            # operands the fused kernel does not take report E2A_ERR_UNSUPPORTED before any launch and
+            # go the two-kernel way below)
             st = stream_of(O.device)
+            done = True
             for m in range(R):
                 l = ctx.lidx[m]
                 t0 = GEMM_TIMER.start()
@@ -334,8 +337,12 @@ class _SO3PairProdFn(torch.autograd.Function):
                                                   L1 * (h2 // 2), ptr(thi[l]), ptr(tlo[l]), h2,
                                                   dx.data_ptr() + 4 * m * C, R * C, N, C, h2, PASSES, st)
                 GEMM_TIMER.stop(t0, N, C, h2)
+                if rc == _lib.E2A_ERR_UNSUPPORTED and m == 0:
+                    done = False
+                    break
                 check(rc, "e2a_gemm_tf32x3_pairgrad")
-            return dx, None, None, None, None
+            if done:
+                return dx, None, None, None, None
         D = torch.empty_like(O)
         check(lib.e2a_pair_grad(ptr(O), ptr(G), N, R, L1, h2 // 2, ptr(D), stream_of(O.device)), "e2a_pair_grad")
         for m in range(R):
