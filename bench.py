@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--cpu-atoms", type=int, default=None,
                     help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--projections", default="fp32", choices=["fp32", "tf32"],
+                    help="model workload: fp32-accurate 3xTF32 projections (parity, the headline) or the "
+                         "single-pass TF32 mode (the reference's use_tf32)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="model workload with N > 1: independent systems per rank instead of one system "
@@ -606,6 +609,9 @@ def run_model(args, ws, rank, local):
     torch.cuda.set_device(dev)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
+    from ubio_molfm_b200 import linear as _linear
+
+    _linear.PASSES = 1 if args.projections == "tf32" else 3
     model = make_model(dev)
     pos_np, Z_np, cell_np = blob_in_water(seed=100 if (ws > 1 and not args.replicas) else 100 + rank)
     pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
@@ -763,7 +769,8 @@ def run_model(args, ws, rank, local):
                 cfgd.pop(k, None)
         line = {"metric": "atom-steps/s", "value": round(value, 1), "unit": "atom-steps/s", "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-                "scaling": "strong" if domain else "weak", "vs_baseline": None, "dtype": "f32",
+                "scaling": "strong" if domain else "weak", "vs_baseline": None,
+                "dtype": "f32" if args.projections == "fp32" else "f32 (tf32 projections)",
                 "data": "synthetic (seeded blob-in-water periodic system, seeded random weights)",
                 "config": cfgd, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_timed, "clocks": clk,
