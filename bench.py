@@ -211,14 +211,15 @@ def bwdk_algorithmic_bytes(N, N2, E):
     return 4 * (reads + writes)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of each span entry point (sum over its kernels),
-# one ncu capture of the layer workload (1e5 atoms, k = 32); summary in profiles/attn_kernels_dram_100k.txt.
-MEASURED_TRAFFIC_DEFAULT = {"e2a_attn_fwd": 22.89e9, "e2a_attn_bwd_value": 17.01e9,
-                            "e2a_attn_bwd_softmax": 26.97e9, "e2a_attn_bwd_dk": 2.74e9}
-# the same per-launch figures for the default model workload (blob in water, 97,865 atoms, mean over its
-# four layers), from one ncu capture of that workload (profiles/attn_kernels_dram_100k.txt)
-MEASURED_TRAFFIC_MODEL = {"e2a_attn_fwd": 23.77e9, "e2a_attn_bwd_value": 16.88e9,
-                          "e2a_attn_bwd_softmax": 26.51e9, "e2a_attn_bwd_dk": 2.74e9}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of a span entry point (sum over its kernels),
+# from one ncu capture of a small case (the 20k-atom layer: 640,210 edges; profiles/attn_kernels_20k_full.md)
+# scaled to a full launch by the edges processed (nodes, keys and edges grow together at a fixed
+# neighbour count): e2a_attn_fwd 4.547 GB and e2a_attn_bwd_value 3.352 GB at 20k atoms.  The softmax
+# backward and d_k entry points were not in that capture (None).
+_TRAFFIC_20K = {"e2a_attn_fwd": 4.547e9, "e2a_attn_bwd_value": 3.352e9}
+_E_20K = 640210
+MEASURED_TRAFFIC_DEFAULT = {k: v * 3197986 / _E_20K for k, v in _TRAFFIC_20K.items()}   # layer workload
+MEASURED_TRAFFIC_MODEL = {k: v * 3131680 / _E_20K for k, v in _TRAFFIC_20K.items()}     # model workload
 
 
 def bwdv_algorithmic_bytes(N, N2, E):
