@@ -336,11 +336,11 @@ class _SO3PairProdFn(torch.autograd.Function):
                 rc = lib.e2a_gemm_tf32x3_pairgrad(O.data_ptr() + 4 * m * h2, R * h2, G.data_ptr() + 4 * l * (h2 // 2),
                                                   L1 * (h2 // 2), ptr(thi[l]), ptr(tlo[l]), h2,
                                                   dx.data_ptr() + 4 * m * C, R * C, N, C, h2, PASSES, st)
-                GEMM_TIMER.stop(t0, N, C, h2)
                 if rc == _lib.E2A_ERR_UNSUPPORTED and m == 0:
                     done = False
                     break
                 check(rc, "e2a_gemm_tf32x3_pairgrad")
+                GEMM_TIMER.stop(t0, N, C, h2)
             if done:
                 return dx, None, None, None, None
         D = torch.empty_like(O)
