@@ -38,6 +38,10 @@ import time
 import numpy as np
 import torch
 
+# growable allocator segments (set before the first device allocation): graph-sized tensors change size
+# every MD step, which fragments fixed segments near the device's capacity
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
