@@ -223,14 +223,6 @@ int e2a_tf32_split(const float* B, int64_t ldb, int64_t N, int64_t K, float* B_h
 int e2a_gemm_tf32x3_pairprod(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
                              int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
                              int accumulate, int passes, void* stream);
-/* A linear layer followed by LayerNorm + SiLU (RadialProfile, module_utils.py:2151-2178) in one GEMM:    */
-/* x = A B^T + bias (+ T[zt[r]] + S[zs[r]]) (written to x_out if not NULL), y = SiLU((x - mean) rstd  */
-/* gamma + beta), mean / rstd per row.  N must be 128 (B_lo required, 16-byte aligned vectors and       */
-/* rows, K >= 128 with 16-byte aligned A rows); E2A_ERR_UNSUPPORTED otherwise.  x_out / y are [M,128]. */
-int e2a_gemm_tf32x3_ln_silu(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb,
-                            const float* bias, const float* T, const int64_t* zt, const float* S, const int64_t* zs,
-                            const float* gamma, const float* beta, float eps, float* x_out, float* y, float* mean,
-                            float* rstd, int64_t M, int64_t N, int64_t K, int passes, void* stream);
 /* Backward of the pair product fused into the GEMM (no reference counterpart to a fused form; it      */
 /* replaces e2a_pair_grad followed by e2a_gemm_tf32x3 on D, SO3_Linear2Scalar_e2former's backward,      */
 /* module_utils.py:2198-2274): C[M,N] = D[M,K] B[N,K]^T with D[r,2j] = G[r,j] O[r,2j+1] and            */

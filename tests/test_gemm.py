@@ -175,84 +175,3 @@ def test_pair_product_backward_fused_equals_two_kernel(N, C, Hd):
     finally:
         linear.FUSED_PAIR_GRAD = old
     assert torch.equal(out[0], out[1])
-
-
-@pytest.mark.parametrize("M,K,tables", [(3001, 128, False), (2048, 256, True), (517, 128, True)])
-def test_linear_ln_silu_epilogue_matches_two_kernels(M, K, tables):
-    """Linear + LayerNorm + SiLU with the LayerNorm in the GEMM's epilogue (the two drain warps of a row
-    exchange their half sums) against the GEMM followed by the LayerNorm+SiLU kernel: outputs and the
-    input gradient agree to float rounding (the row sums are taken in another order); ragged M."""
-    from ubio_molfm_b200 import linear
-
-    g = torch.Generator(device="cuda").manual_seed(M + K)
-    a = torch.randn(M, K, device="cuda", generator=g)
-    w = torch.randn(128, K, device="cuda", generator=g) / K ** 0.5
-    b = torch.randn(128, device="cuda", generator=g)
-    ln = torch.nn.LayerNorm(128).cuda()
-    with torch.no_grad():
-        ln.weight.copy_(1 + 0.1 * torch.randn(128, device="cuda", generator=g))
-        ln.bias.copy_(0.1 * torch.randn(128, device="cuda", generator=g))
-    tab = None
-    if tables:
-        T = torch.randn(9, 128, device="cuda", generator=g)
-        S = torch.randn(9, 128, device="cuda", generator=g)
-        zt = torch.randint(0, 9, (M,), device="cuda", generator=g)
-        zs = torch.randint(0, 9, (M,), device="cuda", generator=g)
-        tab = (T, zt, S, zs)
-    dy = torch.randn(M, 128, device="cuda", generator=g)
-    res = []
-    old = linear.LN_EPILOGUE
-    try:
-        for fused in (True, False):
-            linear.LN_EPILOGUE = fused
-            aa = a.clone().requires_grad_(True)
-            y = linear.linear_ln_silu(aa, w, b, ln, tab)
-            (da,) = torch.autograd.grad(y, aa, dy)
-            res.append((y, da))
-    finally:
-        linear.LN_EPILOGUE = old
-    (y0, d0), (y1, d1) = res
-    assert (y0 - y1).abs().max().item() <= 1e-5 * max(1.0, y1.abs().max().item())
-    assert (d0 - d1).abs().max().item() <= 1e-4 * max(1.0, d1.abs().max().item())
-    # and against float64 math
-    x64 = a.double() @ w.double().t() + b.double()
-    if tables:
-        x64 = x64 + T.double()[zt] + S.double()[zs]
-    y64 = torch.nn.functional.silu(torch.nn.functional.layer_norm(x64, (128,), ln.weight.double(), ln.bias.double(),
-                                                                  ln.eps))
-    assert (y0.double() - y64).abs().max().item() <= 2e-5 * max(1.0, y64.abs().max().item())
-
-
-def test_rbf_linear_ln_silu_matches_two_kernels():
-    """The radial MLP's first layer with its LayerNorm + SiLU in the GEMM's epilogue (the basis written for
-    the product) against the basis product followed by the LayerNorm+SiLU kernel, and the distance
-    gradient through both."""
-    from ubio_molfm_b200 import linear
-
-    g = torch.Generator(device="cuda").manual_seed(5)
-    E, nb = 4099, 256
-    d = (0.5 + 5.0 * torch.rand(E, device="cuda", generator=g))
-    mu = torch.linspace(0, 6.0, nb, device="cuda")
-    coeff = -0.5 / (2.0 * (6.0 / (nb - 1))) ** 2
-    w = torch.randn(128, nb, device="cuda", generator=g) / 16
-    b = torch.randn(128, device="cuda", generator=g)
-    ln = torch.nn.LayerNorm(128).cuda()
-    T = torch.randn(5, 128, device="cuda", generator=g)
-    S = torch.randn(5, 128, device="cuda", generator=g)
-    zt = torch.randint(0, 5, (E,), device="cuda", generator=g)
-    zs = torch.randint(0, 5, (E,), device="cuda", generator=g)
-    dy = torch.randn(E, 128, device="cuda", generator=g)
-    res = []
-    old = linear.LN_EPILOGUE
-    try:
-        for fused in (True, False):
-            linear.LN_EPILOGUE = fused
-            dd = d.clone().requires_grad_(True)
-            y = linear.rbf_linear_ln_silu(dd, mu, coeff, w, b, ln, (T, zt, S, zs))
-            (gd,) = torch.autograd.grad(y, dd, dy)
-            res.append((y, gd))
-    finally:
-        linear.LN_EPILOGUE = old
-    (y0, g0), (y1, g1) = res
-    assert (y0 - y1).abs().max().item() <= 1e-5 * max(1.0, y1.abs().max().item())
-    assert (g0 - g1).abs().max().item() <= 1e-4 * max(1.0, g1.abs().max().item())

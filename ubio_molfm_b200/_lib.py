@@ -56,7 +56,6 @@ SIGNATURES = {
     "e2a_gemm_tf32x3_pairprod": (I32, [P, I64, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I32, I32, P]),
     "e2a_pair_grad": (I32, [P, P, I64, I32, I32, I32, P, P]),
     "e2a_gemm_tf32x3_pairgrad": (I32, [P, I64, P, I64, P, P, I64, P, I64, I64, I64, I64, I32, P]),
-    "e2a_gemm_tf32x3_ln_silu": (I32, [P, I64, P, P, I64, P, P, P, P, P, P, P, F32, P, P, P, P, I64, I64, I64, I32, P]),
     "e2a_node_apply_fwd": (I32, [P, P, I64, P, I64, I64, I32, I32, I32, P, I64, I32, P]),
     "e2a_node_apply_bwd": (I32, [P, P, I64, P, I64, P, I64, I64, I32, I32, I32, P, I64, P, I64, P, P]),
     "e2a_rbf_fwd": (I32, [P, I64, P, I32, ctypes.c_float, P, P]),

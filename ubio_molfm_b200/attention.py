@@ -109,17 +109,11 @@ class E2AttentionArbOrder_sparse(nn.Module):
             s_tab = (self.source_embedding.weight @ w[:, nb + e:].t()).contiguous()     # [types, h]
         z_q = atomic_numbers[query_idx]
         z_k = atomic_numbers[f_outcell_index][neighbor_idx]
-        layers = list(net)
-        if (isinstance(attn_weight, RbfSpec) and cw and attn_weight.dist.is_cuda and len(layers) > 3
-                and isinstance(layers[1], nn.LayerNorm) and isinstance(layers[2], nn.SiLU)):
-            # first Linear + LayerNorm + SiLU as one product (tables added before the norm)
-            h = attn_weight.linear_ln_silu(w[:, :nb], lin0.bias, layers[1], (t_tab, z_q, s_tab, z_k))
-            return run_mlp(layers[3:], h, cw)
         if isinstance(attn_weight, RbfSpec):
             h = attn_weight.linear(w[:, :nb], lin0.bias, cw)
         else:
             h = lin(attn_weight, w[:, :nb], lin0.bias, cw)
-        h = run_mlp(layers[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
+        h = run_mlp(list(net)[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
         return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
 
     def forward(self, node_pos, node_irreps_input, edge_dis, edge_vec, attn_weight, atomic_numbers,

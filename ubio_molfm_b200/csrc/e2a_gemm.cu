@@ -421,34 +421,12 @@ struct RbfArgs {
   int64_t ld_rdot;
 };
 
-// LayerNorm + SiLU epilogue (RadialProfile, module_utils.py:2151-2178) for N == 128 (one column tile;
-// each row's two 64-column halves sit in the two drain warps of one lane quarter, which exchange their
-// row sums through shared memory): x = acc + bias (+ T[zt[r]] + S[zs[r]]), written to x_out when set;
-// y = SiLU((x - mean) rstd gamma + beta) written to C; mean / rstd per row.
-struct LnArgs {
-  const float* T;
-  const int64_t* zt;
-  const float* S;
-  const int64_t* zs;
-  const float* gamma;
-  const float* beta;
-  float eps;
-  float* x_out;
-  float* mean;
-  float* rstd;
-};
-
-__device__ __forceinline__ float silu_f(float z) { return z / (1.f + expf(-z)); }
-
-// named barrier of the two drain warps of one TMEM lane quarter (ids 1..4; 0 is __syncthreads)
-__device__ __forceinline__ void pair_bar(int q) { asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory"); }
-
-template <int BK_, bool PG_ = false, bool LN_ = false>
+template <int BK_, bool PG_ = false>
 __global__ void __launch_bounds__(WsCfg<BK_, PG_>::THREADS, 1)
 k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
           const __grid_constant__ CUtensorMap tmBl, const __grid_constant__ CUtensorMap tmG, int b_split, float* C,
           int64_t ldc, const float* __restrict__ bias, float* P, int64_t ldp, int M, int N, int K, int accumulate,
-          int passes, const RbfArgs rb, const LnArgs ln) {
+          int passes, const RbfArgs rb) {
   using Cfg = WsCfg<BK_, PG_>;
   const bool gen = rb.d != nullptr && rb.rdot == nullptr;   // A formed on chip
   extern __shared__ uint8_t ws_raw[];
@@ -716,79 +694,6 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         }
         continue;
       }
-      const float* ebias = bias;   // the bias the store below adds (already added in the LayerNorm mode)
-      if constexpr (LN_) {
-        // LayerNorm + SiLU of the 128-column row: this warp holds columns n0 .. n0+63 of row `row`, its
-        // partner warp (same lane quarter, other half) the rest
-        const int row = m0 + 32 * q + lane;
-        const bool rv = row < M;
-        const float* tr = (ln.T && rv) ? ln.T + ln.zt[row] * 128 + n0 : nullptr;
-        const float* sr = (ln.S && rv) ? ln.S + ln.zs[row] * 128 + n0 : nullptr;
-        float s1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < WS_DCOLS; j += 4) {
-          float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-          if (bias) {
-            const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias + n0 + j));
-            v.x += b4.x; v.y += b4.y; v.z += b4.z; v.w += b4.w;
-          }
-          if (tr) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(tr + j));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(sr + j));
-            v.x += a.x + b.x; v.y += a.y + b.y; v.z += a.z + b.z; v.w += a.w + b.w;
-          }
-          acc[j] = v.x; acc[j + 1] = v.y; acc[j + 2] = v.z; acc[j + 3] = v.w;
-          s1 += (v.x + v.y) + (v.z + v.w);
-        }
-        float* mine = epi + (warp - 4) * 32 * WS_LD;
-        const float* theirs = epi + (((warp - 4) + 4) & 7) * 32 * WS_LD;
-        mine[lane] = s1;
-        pair_bar(q);
-        const float mean = (half == 0 ? s1 + theirs[lane] : theirs[lane] + s1) * (1.f / 128.f);
-        float s2 = 0.f;
-#pragma unroll
-        for (int j = 0; j < WS_DCOLS; j += 4) {
-          const float a = acc[j] - mean, b = acc[j + 1] - mean, c = acc[j + 2] - mean, d = acc[j + 3] - mean;
-          s2 += (a * a + b * b) + (c * c + d * d);
-        }
-        pair_bar(q);   // both have read the partner's sum
-        mine[lane] = s2;
-        pair_bar(q);
-        const float rstd = rsqrtf((half == 0 ? s2 + theirs[lane] : theirs[lane] + s2) * (1.f / 128.f) + ln.eps);
-        pair_bar(q);   // both have read: the staging area is free again
-        if (half == 0 && rv) {
-          ln.mean[row] = mean;
-          ln.rstd[row] = rstd;
-        }
-        if (ln.x_out) {   // x (the LayerNorm input, kept for the backward), 16 columns at a time
-#pragma unroll
-          for (int hh = 0; hh < WS_DCOLS / WS_EH; ++hh) {
-#pragma unroll
-            for (int i = 0; i < WS_EH; i += 4)
-              *reinterpret_cast<float4*>(mine + lane * WS_LD + i) =
-                  make_float4(acc[hh * WS_EH + i], acc[hh * WS_EH + i + 1], acc[hh * WS_EH + i + 2], acc[hh * WS_EH + i + 3]);
-            __syncwarp();
-            const int sub = lane % (WS_EH / 4), rr = lane / (WS_EH / 4);
-            for (int r2 = 0; r2 < 32; r2 += 32 / (WS_EH / 4)) {
-              const int r = r2 + rr, rw = m0 + 32 * q + r;
-              if (rw < M)
-                *reinterpret_cast<float4*>(ln.x_out + (int64_t)rw * 128 + n0 + hh * WS_EH + 4 * sub) =
-                    *reinterpret_cast<const float4*>(mine + r * WS_LD + 4 * sub);
-            }
-            __syncwarp();
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < WS_DCOLS; j += 4) {
-          const float4 g = __ldg(reinterpret_cast<const float4*>(ln.gamma + n0 + j));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(ln.beta + n0 + j));
-          acc[j] = silu_f((acc[j] - mean) * rstd * g.x + b.x);
-          acc[j + 1] = silu_f((acc[j + 1] - mean) * rstd * g.y + b.y);
-          acc[j + 2] = silu_f((acc[j + 2] - mean) * rstd * g.z + b.z);
-          acc[j + 3] = silu_f((acc[j + 3] - mean) * rstd * g.w + b.w);
-        }
-        ebias = nullptr;
-      }
       // epilogue: stage this warp's 32 rows x 64 columns 16 columns at a time, then write them row by
       // row (4 lanes per row, 8 rows per step)
 #pragma unroll
@@ -802,16 +707,14 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         const int sub = lane % kLanesPerRow, rr = lane / kLanesPerRow;
         const int gc = n0 + hh * WS_EH + 4 * sub;
         float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ebias) {
-          if (gc < N) bv.x = ebias[gc];
-          if (gc + 1 < N) bv.y = ebias[gc + 1];
-          if (gc + 2 < N) bv.z = ebias[gc + 2];
-          if (gc + 3 < N) bv.w = ebias[gc + 3];
+        if (bias) {
+          if (gc < N) bv.x = bias[gc];
+          if (gc + 1 < N) bv.y = bias[gc + 1];
+          if (gc + 2 < N) bv.z = bias[gc + 2];
+          if (gc + 3 < N) bv.w = bias[gc + 3];
         }
         const bool cvec = C && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0) && (gc + 3 < N);
         constexpr int kSteps = 32 / kRowsPerStep;
-        // P's two values of a lane as one 8-byte access when both exist and are aligned
-        const bool pvec = P && ((ldp & 1) == 0) && ((reinterpret_cast<uintptr_t>(P) & 7u) == 0) && (gc + 3 < N);
         // the previous values of a read-modify-write output (P with accumulate, or C with accumulate) are
         // loaded for all of this warp's row steps first, so their memory latencies overlap instead of
         // adding up one row step at a time
@@ -823,14 +726,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           if (!accumulate || row >= M) continue;
           if (P) {
             const float* pp = P + (int64_t)row * ldp + (gc >> 1);
-            if (pvec) {
-              const float2 o2 = *reinterpret_cast<const float2*>(pp);
-              old[st2].x = o2.x;
-              old[st2].y = o2.y;
-            } else {
-              if (gc + 1 < N) old[st2].x = pp[0];
-              if (gc + 3 < N) old[st2].y = pp[1];
-            }
+            if (gc + 1 < N) old[st2].x = pp[0];
+            if (gc + 3 < N) old[st2].y = pp[1];
           } else if (cvec) {
             old[st2] = *reinterpret_cast<const float4*>(C + (int64_t)row * ldc + gc);
           }
@@ -844,12 +741,8 @@ k_gemm_ws(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
           x.x += bv.x; x.y += bv.y; x.z += bv.z; x.w += bv.w;
           if (P) {
             float* pp = P + (int64_t)row * ldp + (gc >> 1);
-            if (pvec) {
-              *reinterpret_cast<float2*>(pp) = make_float2(old[st2].x + x.x * x.y, old[st2].y + x.z * x.w);
-            } else {
-              if (gc + 1 < N) pp[0] = old[st2].x + x.x * x.y;
-              if (gc + 3 < N) pp[1] = old[st2].y + x.z * x.w;
-            }
+            if (gc + 1 < N) pp[0] = old[st2].x + x.x * x.y;
+            if (gc + 3 < N) pp[1] = old[st2].y + x.z * x.w;
             if (!C) continue;
             float* cp = C + (int64_t)row * ldc + gc;
             if (cvec) {
@@ -940,9 +833,7 @@ __global__ void k_tf32_split(const float* __restrict__ B, int64_t ldb, int64_t N
 static int launch_ws(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
                      int64_t ldc, const float* bias, float* P, int64_t ldp, int64_t M, int64_t N, int64_t K,
                      int accumulate, int passes, cudaStream_t st, RbfArgs rb = RbfArgs{nullptr, nullptr, 0.f, nullptr, 0},
-                     const float* G = nullptr, int64_t ldg = 0,
-                     LnArgs ln = LnArgs{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0.f, nullptr, nullptr,
-                                        nullptr}) {
+                     const float* G = nullptr, int64_t ldg = 0) {
   const bool gen = rb.d != nullptr && rb.rdot == nullptr;
   if (gen) { A = B; lda = ldb; }   // the A map is never read
   const bool vec = (lda % 4 == 0) && (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) &&
@@ -975,24 +866,18 @@ static int launch_ws(const float* A, int64_t lda, const float* B, const float* B
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   if (tiles > INT32_MAX) return E2A_ERR_ARG;
   const int grid = (int)(tiles < sms ? tiles : sms);
-  if (ln.gamma) {
-    if (bk != 32 || G || P || gen || rb.rdot) return E2A_ERR_UNSUPPORTED;
-    E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  ws_smem<32>()));
-    k_gemm_ws<32, false, true><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(
-        ta, tb, tbl, tg, B_lo ? 1 : 0, C, ldc, bias, P, ldp, (int)M, (int)N, (int)K, accumulate, passes, rb, ln);
-  } else if (G) {
+  if (G) {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32, true>()));
     k_gemm_ws<32, true><<<grid, WsCfg<32, true>::THREADS, ws_smem<32, true>(), st>>>(
-        ta, tb, tbl, tg, 1, C, ldc, bias, P, ldp, (int)M, (int)N, (int)K, accumulate, passes, rb, ln);
+        ta, tb, tbl, tg, 1, C, ldc, bias, P, ldp, (int)M, (int)N, (int)K, accumulate, passes, rb);
   } else if (bk == 16) {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<16>()));
     k_gemm_ws<16><<<grid, WsCfg<16>::THREADS, ws_smem<16>(), st>>>(ta, tb, tbl, tg, B_lo ? 1 : 0, C, ldc, bias, P, ldp,
-                                                            (int)M, (int)N, (int)K, accumulate, passes, rb, ln);
+                                                            (int)M, (int)N, (int)K, accumulate, passes, rb);
   } else {
     E2A_CUDA(cudaFuncSetAttribute(k_gemm_ws<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ws_smem<32>()));
     k_gemm_ws<32><<<grid, WsCfg<32>::THREADS, ws_smem<32>(), st>>>(ta, tb, tbl, tg, B_lo ? 1 : 0, C, ldc, bias, P, ldp,
-                                                            (int)M, (int)N, (int)K, accumulate, passes, rb, ln);
+                                                            (int)M, (int)N, (int)K, accumulate, passes, rb);
   }
   E2A_CHECK_LAUNCH();
   return E2A_OK;
@@ -1037,24 +922,6 @@ int e2a_gemm_tf32x3_pairgrad(const float* O, int64_t ldo, const float* G, int64_
   if (!O || !G || !B || !B_lo || !C || ldo < K || ldg < K / 2 || ldb < K || ldc < N) return E2A_ERR_ARG;
   return launch_ws(O, ldo, B, B_lo, ldb, C, ldc, nullptr, nullptr, 0, M, N, K, 0, passes, (cudaStream_t)stream,
                    RbfArgs{nullptr, nullptr, 0.f, nullptr, 0}, G, ldg);
-}
-
-int e2a_gemm_tf32x3_ln_silu(const float* A, int64_t lda, const float* B, const float* B_lo, int64_t ldb,
-                            const float* bias, const float* T, const int64_t* zt, const float* S, const int64_t* zs,
-                            const float* gamma, const float* beta, float eps, float* x_out, float* y, float* mean,
-                            float* rstd, int64_t M, int64_t N, int64_t K, int passes, void* stream) {
-  if (M < 0 || K < 0 || (passes != 1 && passes != 3)) return E2A_ERR_ARG;
-  if (N != 128) return E2A_ERR_UNSUPPORTED;   // one 128-column tile per row
-  if (M == 0) return E2A_OK;
-  if (!A || !B || !B_lo || !gamma || !beta || !y || !mean || !rstd || lda < K || ldb < K || K == 0) return E2A_ERR_ARG;
-  if ((T == nullptr) != (S == nullptr) || (T && (!zt || !zs))) return E2A_ERR_ARG;
-  const uintptr_t al = reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta) |
-                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(T) |
-                       reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x_out);
-  if (al & 15u) return E2A_ERR_UNSUPPORTED;
-  return launch_ws(A, lda, B, B_lo, ldb, y, 128, bias, nullptr, 0, M, 128, K, 0, passes, (cudaStream_t)stream,
-                   RbfArgs{nullptr, nullptr, 0.f, nullptr, 0}, nullptr, 0,
-                   LnArgs{T, zt, S, zs, gamma, beta, eps, x_out, mean, rstd});
 }
 
 int e2a_gemm_tf32x3_rbf(const float* dist, const float* mu, float coeff, const float* B, const float* B_lo,

@@ -244,85 +244,6 @@ class _LnSiluFn(torch.autograd.Function):
         return dx, None, None, None, None, None, None, None
 
 
-# Linear + LayerNorm + SiLU of the radial MLPs as one GEMM (the LayerNorm in the GEMM's epilogue) when
-# the output is 128 wide: the pre-norm activations never make a separate round trip through HBM.
-LN_EPILOGUE = True
-
-
-def _ln_silu_bwd(x, dy, gamma, beta, mean, rstd):
-    lib = _lib.load()
-    dy = dy.contiguous()
-    dx = torch.empty_like(dy)
-    rows, W = dy.shape
-    check(lib.e2a_ln_silu_bwd(ptr(x), ptr(dy), ptr(gamma), ptr(beta), ptr(mean), ptr(rstd), rows, W, ptr(dx),
-                              stream_of(dy.device)), "e2a_ln_silu_bwd")
-    return dx
-
-
-def _gemm_ln_silu(a, w_split, bias, gamma, beta, eps, tables):
-    """(y, x, mean, rstd) of SiLU(LayerNorm(a w^T + bias + tables)) from the fused GEMM, or None when it
-    does not take these operands (nothing launched)."""
-    lib = _lib.load()
-    M, K = a.shape
-    hi, lo = w_split
-    dev = a.device
-    T = zt = S = zs = None
-    if tables is not None:
-        T, zt, S, zs = (t.contiguous() for t in tables)
-    y = torch.empty((M, 128), device=dev, dtype=torch.float32)
-    x = torch.empty_like(y)
-    mean = torch.empty(M, device=dev, dtype=torch.float32)
-    rstd = torch.empty_like(mean)
-    t0 = GEMM_TIMER.start()
-    rc = lib.e2a_gemm_tf32x3_ln_silu(ptr(a), a.stride(0), ptr(hi), ptr(lo), K, ptr(bias), ptr(T), ptr(zt), ptr(S),
-                                     ptr(zs), ptr(gamma), ptr(beta), float(eps), ptr(x), ptr(y), ptr(mean),
-                                     ptr(rstd), M, 128, K, PASSES, stream_of(dev))
-    if rc == _lib.E2A_ERR_UNSUPPORTED:
-        return None
-    check(rc, "e2a_gemm_tf32x3_ln_silu")
-    GEMM_TIMER.stop(t0, M, 128, K)
-    return y, x, mean, rstd
-
-
-class _LinearLnSiluFn(torch.autograd.Function):
-    """``SiLU(LayerNorm(a w^T + b (+ T[zt] + S[zs])))`` with constant w / b / LayerNorm / tables: one GEMM
-    with the LayerNorm + SiLU epilogue; the backward is the LayerNorm+SiLU backward kernel then the
-    input-gradient GEMM."""
-
-    @staticmethod
-    def forward(ctx, a, w, b, gamma, beta, eps, T, zt, S, zs):
-        a = a.contiguous()
-        tables = None if T is None else (T, zt, S, zs)
-        r = _gemm_ln_silu(a, split_tf32(w), b, gamma, beta, eps, tables)
-        if r is None:
-            raise _lib.E2AError("e2a_gemm_tf32x3_ln_silu refused operands that linear_ln_silu admitted")
-        y, x, mean, rstd = r
-        ctx.save_for_backward(x, gamma, beta, mean, rstd, w)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        x, gamma, beta, mean, rstd, w = ctx.saved_tensors
-        dh = _ln_silu_bwd(x, dy, gamma, beta, mean, rstd)
-        return gemm(dh, w.t().contiguous()), None, None, None, None, None, None, None, None, None
-
-
-def linear_ln_silu(a, w, b, ln, tables=None):
-    """``SiLU(ln(a w^T + b (+ T[zt] + S[zs])))`` on CUDA with constant weights (eval mode): one fused GEMM
-    when the output is 128 wide, else the GEMM followed by the fused LayerNorm + SiLU kernel."""
-    T = zt = S = zs = None
-    if tables is not None:
-        T, zt, S, zs = tables
-    K = a.shape[-1]
-    # the fused GEMM runs 32-wide slabs (K >= 128) over a 128-wide output with pre-split weights
-    if not (LN_EPILOGUE and PRESPLIT_WEIGHTS and w.shape[0] == 128 and K >= 128 and K % 4 == 0 and a.dim() == 2):
-        return ln_silu(linear(a, w, b), ln, tables)
-    gamma, beta = ln.weight.detach().float().contiguous(), ln.bias.detach().float().contiguous()
-    return _LinearLnSiluFn.apply(a.float().contiguous(), w.detach().float().contiguous(),
-                                 None if b is None else b.detach().float().contiguous(), gamma, beta, float(ln.eps),
-                                 T, zt, S, zs)
-
-
 def ln_silu_supported(W):
     return W % 128 == 0 and W <= 1024
 
@@ -693,62 +614,6 @@ def rbf_linear(dist, mu, coeff, w, b=None, on_chip=None):
     return _RbfLinearFn.apply(dist.float(), mu.float().contiguous(), float(coeff), w.detach().float().contiguous(),
                               None if b is None else b.detach().float().contiguous(),
                               RBF_FWD_ON_CHIP if on_chip is None else bool(on_chip))
-
-
-class _RbfLnSiluFn(torch.autograd.Function):
-    """``SiLU(LayerNorm(rbf(d) w^T + b + T[zt] + S[zs]))``: the basis written for the product (not kept),
-    the LayerNorm + SiLU in the GEMM's epilogue; backward: the LayerNorm+SiLU backward kernel, then
-    d(rbf) = dh w contracted with d rbf / d d in the GEMM's epilogue (only [E] vectors leave it)."""
-
-    @staticmethod
-    def forward(ctx, dist, mu, coeff, w, b, gamma, beta, eps, T, zt, S, zs):
-        lib = _lib.load()
-        d = dist.contiguous()
-        E, nb = d.shape[0], mu.shape[0]
-        rbf = torch.empty((E, nb), device=d.device, dtype=torch.float32)
-        check(lib.e2a_rbf_fwd(ptr(d), E, ptr(mu), nb, float(coeff), ptr(rbf), stream_of(d.device)), "e2a_rbf_fwd")
-        tables = None if T is None else (T, zt, S, zs)
-        r = _gemm_ln_silu(rbf, split_tf32(w), b, gamma, beta, eps, tables)
-        del rbf
-        if r is None:
-            raise _lib.E2AError("e2a_gemm_tf32x3_ln_silu refused operands that rbf_linear_ln_silu admitted")
-        y, x, mean, rstd = r
-        ctx.coeff = float(coeff)
-        ctx.save_for_backward(d, mu, w, x, gamma, beta, mean, rstd)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        lib = _lib.load()
-        d, mu, w, x, gamma, beta, mean, rstd = ctx.saved_tensors
-        g = _ln_silu_bwd(x, dy, gamma, beta, mean, rstd)
-        E, nb, Kh = d.shape[0], mu.shape[0], w.shape[0]
-        wt = w.t().contiguous()
-        hi, lo = split_tf32(wt)
-        nblk = (nb + 63) // 64
-        part = torch.empty((E, nblk), device=d.device, dtype=torch.float32)
-        t0 = GEMM_TIMER.start()
-        check(lib.e2a_gemm_tf32x3_rbf_dist_grad(ptr(g), Kh, ptr(hi), ptr(lo), Kh, ptr(d), ptr(mu), ctx.coeff,
-                                                ptr(part), nblk, E, nb, Kh, PASSES, stream_of(d.device)),
-              "e2a_gemm_tf32x3_rbf_dist_grad")
-        GEMM_TIMER.stop(t0, E, nb, Kh)
-        return part.sum(1), None, None, None, None, None, None, None, None, None, None, None
-
-
-def rbf_linear_ln_silu(dist, mu, coeff, w, b, ln, tables=None):
-    """``SiLU(ln(GaussianSmearing(dist) w^T + b (+ T[zt] + S[zs])))`` (CUDA, constant weights): the first
-    layer of a radial MLP and its LayerNorm + SiLU."""
-    nb = mu.shape[0]
-    if not (LN_EPILOGUE and PRESPLIT_WEIGHTS and not RBF_FWD_ON_CHIP and w.shape[0] == 128 and 128 <= nb <= 256
-            and nb % 4 == 0):
-        return ln_silu(rbf_linear(dist, mu, coeff, w, b), ln, tables)
-    T = zt = S = zs = None
-    if tables is not None:
-        T, zt, S, zs = (t.contiguous() for t in tables)
-    return _RbfLnSiluFn.apply(dist.float(), mu.float().contiguous(), float(coeff), w.detach().float().contiguous(),
-                              None if b is None else b.detach().float().contiguous(),
-                              ln.weight.detach().float().contiguous(), ln.bias.detach().float().contiguous(),
-                              float(ln.eps), T, zt, S, zs)
 
 
 # ------------------------------------------------------------------------------------------------

@@ -227,16 +227,11 @@ class EdgeDegreeEmbeddingNetwork_higherorder(nn.Module):
                     s_tab = (self.source_embedding.weight @ w[:, 2 * nb:].t()).contiguous()
                 z_q = atomic_numbers[qi]
                 z_k = atomic_numbers[batched_data["f_outcell_index"]][ni]
-                if (isinstance(edge_scalars, RbfSpec) and cw and edge_scalars.dist.is_cuda and len(layers) > 3
-                        and isinstance(layers[1], nn.LayerNorm) and isinstance(layers[2], nn.SiLU)):
-                    h = edge_scalars.linear_ln_silu(w[:, :nb], lin0.bias, layers[1], (t_tab, z_q, s_tab, z_k))
-                    h = run_mlp(layers[3:], h, cw)
+                if isinstance(edge_scalars, RbfSpec):
+                    h = edge_scalars.linear(w[:, :nb], lin0.bias, cw)
                 else:
-                    if isinstance(edge_scalars, RbfSpec):
-                        h = edge_scalars.linear(w[:, :nb], lin0.bias, cw)
-                    else:
-                        h = lin(edge_scalars, w[:, :nb], lin0.bias, cw)
-                    h = run_mlp(layers[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
+                    h = lin(edge_scalars, w[:, :nb], lin0.bias, cw)
+                h = run_mlp(layers[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
             else:
                 h = prof(edge_scalars.materialize() if isinstance(edge_scalars, RbfSpec) else edge_scalars)
             # the envelope scales each edge's product: applied to the [E, 2l+1] harmonics rather than the

@@ -165,21 +165,12 @@ class RadialProfile(nn.Module):
 
 
 def run_mlp(layers, h, const_weights, first_tables=None):
-    """Linear / LayerNorm / SiLU stack; on CUDA in eval mode each Linear + LayerNorm + SiLU is one GEMM
-    with the LayerNorm in its epilogue (128-wide outputs) or a GEMM and one fused LayerNorm+SiLU kernel
-    (``first_tables`` are added to the first Linear's output inside that kernel when ``layers`` starts
-    with the LayerNorm)."""
+    """Linear / LayerNorm / SiLU stack; on CUDA in eval mode each LayerNorm+SiLU pair is one fused kernel
+    (``first_tables`` are added to the first Linear's output inside that fused kernel)."""
     i = 0
     pending = first_tables
     while i < len(layers):
         layer = layers[i]
-        if (isinstance(layer, nn.Linear) and i + 2 < len(layers) and isinstance(layers[i + 1], nn.LayerNorm)
-                and isinstance(layers[i + 2], nn.SiLU) and h.is_cuda and const_weights and h.dim() == 2
-                and tc.ln_silu_supported(layer.out_features)):
-            # Linear + LayerNorm + SiLU: one GEMM with the LayerNorm in its epilogue where it applies
-            h = tc.linear_ln_silu(h, layer.weight, layer.bias, layers[i + 1])
-            i += 3
-            continue
         if isinstance(layer, nn.Linear):
             h = lin(h, layer.weight, layer.bias, const_weights)
             i += 1
@@ -230,10 +221,6 @@ class RbfSpec:
         if self.dist.is_cuda and const_weights:
             return tc.rbf_linear(self.dist, self.offset, self.coeff, w, b)
         return lin(self.materialize(), w, b, const_weights)
-
-    def linear_ln_silu(self, w, b, ln, tables):
-        """SiLU(ln(basis w^T + b + T[zt] + S[zs])) for the CUDA inference path (constant weights)."""
-        return tc.rbf_linear_ln_silu(self.dist, self.offset, self.coeff, w, b, ln, tables)
 
 
 def polynomial(dist, cutoff, exponent=5):
