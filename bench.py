@@ -907,6 +907,62 @@ def reference_span(mods, q, k, v, gi, poly, dist, q_idx, n_idx, md, N):
         value=v.contiguous(), alpha=alpha_r, query_index=q_idx, value_index=n_idx, num_queries=N, metadata=md)
 
 
+def compare_kernel_functions(mods, ins, q_idx, n_idx, md_ref, md_ours, N, N2, timed, dev):
+    """Each kernel-level function of the reference (triton_dr/*.py) against this package's function of
+    the same name and signature (``ubio_molfm_b200.ops``) on the same inputs: forward, and forward +
+    backward with a seeded cotangent; ms (median) and the largest relative difference of the outputs."""
+    from ubio_molfm_b200 import ops
+
+    H = ins[0].shape[1]
+    E = q_idx.numel()
+    gen = torch.Generator(device=dev).manual_seed(7)
+    qi32, ni32 = q_idx.to(torch.int32), n_idx.to(torch.int32)
+    alpha = torch.rand(E, H, device=dev, generator=gen)
+    sh = torch.randn(E, 5, device=dev, generator=gen)
+    fea = torch.randn(E, 128, device=dev, generator=gen)
+    ref_qk = mods["triton_sparse_qk_autograd"].sparse_qk_edge_index_triton
+    ref_as = mods["sparse_alpha_sum_edge_index_autograd"].sparse_alpha_sum_edge_index_triton
+    ref_va = mods["sparse_v_agg_edge_index_cblocked_bench"].sparse_v_agg_edge_index_triton_cblocked
+    import importlib
+
+    ref_eo = importlib.import_module("molfm.models.e2former.triton_dr.edge_degree_outer_autograd").edge_degree_outer_triton
+    cases = {
+        "sparse_qk_edge_index_triton": (
+            lambda f, md, a: f(a[0], a[1], qi32, ni32, metadata=md), [ins[0], ins[1]]),
+        "sparse_alpha_sum_edge_index_triton": (
+            lambda f, md, a: f(a[0], qi32, N, metadata=(md[0], md[2])), [alpha]),
+        "sparse_v_agg_edge_index_triton_cblocked": (
+            lambda f, md, a: f(a[0], a[1], qi32, ni32, N, metadata=md), [ins[2], alpha]),
+        "edge_degree_outer_triton": (
+            lambda f, md, a: f(a[0], a[1], qi32, N, metadata=md), [sh, fea]),
+    }
+    impls = {"sparse_qk_edge_index_triton": (ref_qk, ops.sparse_qk_edge_index_triton),
+             "sparse_alpha_sum_edge_index_triton": (ref_as, ops.sparse_alpha_sum_edge_index_triton),
+             "sparse_v_agg_edge_index_triton_cblocked": (ref_va, ops.sparse_v_agg_edge_index_triton_cblocked),
+             "edge_degree_outer_triton": (ref_eo, ops.edge_degree_outer_triton)}
+    out = {}
+    for name, (call, args) in cases.items():
+        row = {}
+        for who, fn, md in (("reference", impls[name][0], md_ref), ("ours", impls[name][1], md_ours)):
+            leaves = [a.detach().clone().requires_grad_(True) for a in args]
+            y = call(fn, md, leaves)
+            w = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(11))
+
+            def fwd(fn=fn, md=md):
+                with torch.no_grad():
+                    return call(fn, md, args)
+
+            def fb(fn=fn, md=md, leaves=leaves, w=w):
+                return torch.autograd.grad(call(fn, md, leaves), leaves, w)
+
+            row[who] = {"fwd_ms": timed(fwd), "fwd_bwd_ms": timed(fb), "y": y.detach()}
+        d = (row["reference"]["y"] - row["ours"]["y"]).abs().max().item()
+        out[name] = {"reference_fwd_ms": row["reference"]["fwd_ms"], "ours_fwd_ms": row["ours"]["fwd_ms"],
+                     "reference_fwd_bwd_ms": row["reference"]["fwd_bwd_ms"], "ours_fwd_bwd_ms": row["ours"]["fwd_bwd_ms"],
+                     "max_rel_diff": d / max(1.0, row["ours"]["y"].abs().max().item())}
+    return out
+
+
 def run_span(args, ws, rank, local):
     """The attention span alone (q.k, segmented softmax, alpha / r, value aggregation; forward and the
     first-order backward) on the config-2 graph (uniform periodic box, ~k neighbours within 6 A,
@@ -981,6 +1037,8 @@ def run_span(args, ws, rank, local):
             res["reference"] = {"fwd_ms": timed(ref_fwd), "fwd_bwd_ms": timed(ref_fb), "max_rel_diff_vs_ours": err}
             res["speedup_fwd"] = round(res["reference"]["fwd_ms"] / res["ours_fwd_ms"], 2)
             res["speedup_fwd_bwd"] = round(res["reference"]["fwd_bwd_ms"] / res["ours_fwd_bwd_ms"], 2)
+            res["by_function"] = compare_kernel_functions(mods, ins, q_idx, n_idx, md_ref, g["metadata"], N, N2,
+                                                          timed, dev)
         except Exception as exc:  # noqa: BLE001
             res["reference"] = {"unavailable": f"reference Triton kernels failed on this box: {exc!r}"[:300]}
     clk = clocks.stop()
