@@ -163,6 +163,17 @@ class ClockSampler:
                                        "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+        # nvidia-smi takes about a second to print its first sample: wait for it (bounded) so that a
+        # short timed region still gets samples, and count only the samples taken after this point
+        self.skip = 0
+        t_end = time.time() + 5.0
+        while self.p is not None and time.time() < t_end:
+            with open(self.f.name) as fh:
+                n = sum(1 for r in fh if r.strip())
+            if n:
+                self.skip = n
+                break
+            time.sleep(0.05)
 
     def stop(self):
         if self.p is None:
@@ -172,6 +183,7 @@ class ClockSampler:
         self.f.seek(0)
         rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
         os.unlink(self.f.name)
+        rows = rows[self.skip:] or rows[-1:]   # at least the last sample before the region ended
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -194,11 +206,18 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+# whether the timed span kept its q.k scores for the backward (the model's and the layer's default at
+# 128 heads of 8): the forward then also writes them and the softmax backward reads them instead of q
+SPAN_LOGITS_KEPT = True
+
+
 def fwd_algorithmic_bytes(N, N2, E):
     """Compulsory bytes of one e2a_attn_fwd launch (fp32): q, k, value rows, gate+inputhead, poly, dist,
-    col, row_ptr read once; out, beta, row stats written once."""
+    col, row_ptr read once; out, beta, row stats (and the kept q.k scores) written once."""
     HD, CH = HEADS * DHEAD, 58 * HEADS
-    return 4 * (N * HD + N2 * HD + N2 * CH + E * 2 * HEADS + E * 3 + (N + 1) + N * CH + E * HEADS + 2 * N * HEADS)
+    kept = E * HEADS if SPAN_LOGITS_KEPT else 0
+    return 4 * (N * HD + N2 * HD + N2 * CH + E * 2 * HEADS + E * 3 + (N + 1) + N * CH + E * HEADS + 2 * N * HEADS
+                + kept)
 
 
 def bwdq_algorithmic_bytes(N, N2, E):
@@ -233,10 +252,11 @@ def bwdv_algorithmic_bytes(N, N2, E):
 
 
 def bwds_algorithmic_bytes(N, N2, E):
-    """e2a_attn_bwd_softmax: q, k rows once, gate + inputhead, poly, dist, col, row_ptr, d_beta, row stats;
-    d_gate + d_inputhead, d_poly, d_dist, ds, d_q."""
+    """e2a_attn_bwd_softmax: q (or the kept q.k scores), k rows once, gate + inputhead, poly, dist, col,
+    row_ptr, d_beta, row stats; d_gate + d_inputhead, d_poly, d_dist, ds, d_q."""
     HD = HEADS * DHEAD
-    reads = N * HD + N2 * HD + E * 2 * HEADS + 3 * E + N + 1 + E * HEADS + 2 * N * HEADS
+    qs = E * HEADS if SPAN_LOGITS_KEPT else N * HD
+    reads = qs + N2 * HD + E * 2 * HEADS + 3 * E + N + 1 + E * HEADS + 2 * N * HEADS
     writes = E * 2 * HEADS + 2 * E + E * HEADS + N * HD
     return 4 * (reads + writes)
 
@@ -642,6 +662,8 @@ def run_model(args, ws, rank, local):
 
     for _ in range(args.warmup):
         step()
+    global SPAN_LOGITS_KEPT
+    SPAN_LOGITS_KEPT = bool(model.decoder.blocks[0].ga.keep_logits)
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
@@ -1007,12 +1029,13 @@ def run_span(args, ws, rank, local):
         with torch.no_grad():
             return ops.attention_span(*ins, g["metadata"], g["row_order"])
 
-    def ours_fb():
-        out = ops.attention_span(*leaves, g["metadata"], g["row_order"])
+    def ours_fb(keep=True):
+        out = ops.attention_span(*leaves, g["metadata"], g["row_order"], keep_logits=keep)
         return torch.autograd.grad(out, leaves, dout)
 
     clocks = ClockSampler(local)
-    res = {"ours_fwd_ms": timed(ours_fwd), "ours_fwd_bwd_ms": timed(ours_fb)}
+    res = {"ours_fwd_ms": timed(ours_fwd), "ours_fwd_bwd_ms": timed(ours_fb),
+           "ours_fwd_bwd_scores_recomputed_ms": timed(lambda: ours_fb(False))}
     mods, why = _load_reference_triton()
     if mods is None:
         res["reference"] = {"unavailable": why}

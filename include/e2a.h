@@ -154,6 +154,17 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value,
                  const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
                  int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
                  float* out, float* beta, float* row_max, float* row_sum, void* stream);
+/* The same forward that also writes the q.k scores s[e,h] (before the gate) to logits [E,H], for   */
+/* e2a_attn_bwd_softmax_logits (no reference counterpart: the reference recomputes them in its     */
+/* backward).  logits = NULL is e2a_attn_fwd.  Only the H = 128, D = 8, ld_gi % 4 == 0 layout keeps  */
+/* them; any other layout with logits != NULL returns E2A_ERR_UNSUPPORTED.                          */
+int e2a_attn_fwd_logits(const float* q, const float* k, const float* value,
+                        const float* gate, const float* inputhead, int64_t ld_gi,
+                        const float* poly, const float* dist,
+                        const int32_t* row_ptr, const int32_t* col, const int32_t* row_order,
+                        int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                        float* out, float* beta, float* row_max, float* row_sum, float* logits,
+                        void* stream);
 /* Query-side backward: given dout [N,C,H] produces d_q [N,H,D] (w.r.t. the scaled q), d_gate and */
 /* d_inputhead ([E,H] views with row stride ld_dgi), d_poly [E], d_dist [E] and d_logit [E,H]     */
 /* (= dL/ds, consumed by e2a_attn_bwd_key).  The gradient of the row max follows PyTorch's        */
@@ -195,6 +206,17 @@ int e2a_attn_bwd_softmax(const float* q, const float* k, const float* gate, cons
                          int C, const float* beta, const float* row_max, const float* row_sum, const float* d_beta,
                          float* d_q, float* d_gate, float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist,
                          float* d_logit, void* workspace, size_t workspace_bytes, void* stream);
+/* 2'. stage 2 from the forward's kept logits (e2a_attn_fwd_logits): reads s[e,h] instead of gathering */
+/*    k rows for q.k; needs no q and no workspace; results equal e2a_attn_bwd_softmax's bit for bit     */
+/*    (same s, same arithmetic).  H = 128, D = 8, ld_gi % 4 == 0, ld_dgi % 4 == 0, else                 */
+/*    E2A_ERR_UNSUPPORTED.                                                                               */
+int e2a_attn_bwd_softmax_logits(const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
+                                const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                                const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H,
+                                int D, int C, const float* beta, const float* row_max, const float* row_sum,
+                                const float* logits, const float* d_beta, float* d_q, float* d_gate,
+                                float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
+                                void* stream);
 /* 3. key side: d_k[k] = sum_e ds[e] q[i_e]. */
 int e2a_attn_bwd_dk(const float* q, const float* d_logit, const int32_t* k_row_ptr, const int32_t* k_col,
                     const int32_t* k_perm, const int32_t* key_order, int64_t n_rows, int64_t n_keys, int64_t n_edges,

@@ -235,7 +235,7 @@ def _span_inputs(N, M, q, n, H, D, C, seed, gate_zero=False):
     return [Q, K, V, G, P, Dd]
 
 
-def _span_parity(N, M, q, n, H, D, C, seed, gate_zero=False, row_order=None):
+def _span_parity(N, M, q, n, H, D, C, seed, gate_zero=False, row_order=None, keep_logits=False):
     from ubio_molfm_b200 import ops
 
     ins = _span_inputs(N, M, q, n, H, D, C, seed, gate_zero)
@@ -243,7 +243,7 @@ def _span_parity(N, M, q, n, H, D, C, seed, gate_zero=False, row_order=None):
     md = ops.prepare_sparse_qk_edge_index_metadata(qt, nt, N, M)
     ag = [a.to(DEV).requires_grad_(True) for a in ins]
     ar = [a.clone().double().requires_grad_(True) for a in ins]
-    og = ops.attention_span(*ag, md, row_order)
+    og = ops.attention_span(*ag, md, row_order, keep_logits=keep_logits)
     orf = R.attention_span(*ar, torch.tensor(q), torch.tensor(n), N)
     scale = orf.abs().max().item()
     assert (og.cpu().double() - orf).abs().max().item() <= 2e-5 * max(scale, 1.0)
@@ -263,14 +263,60 @@ def test_attention_span_random_graphs(H, D, C):
     _span_parity(N, M, q, n, H, D, C, seed=H)
 
 
-@pytest.mark.parametrize("H", [8, 128])
-def test_attention_span_ties_and_empty_rows(H):
+@pytest.mark.parametrize("H,keep", [(8, False), (128, False), (128, True)])
+def test_attention_span_ties_and_empty_rows(H, keep):
     # gate = 0 makes every logit of a row equal: the max gradient is shared among all of them
     N, M = 30, 40
     q = np.sort(np.random.default_rng(4).integers(0, N - 5, 400))  # the last 5 rows have no edges
     n = np.random.default_rng(5).integers(0, M, 400)
-    out = _span_parity(N, M, q, n, H, 8, 16, seed=9, gate_zero=True)
+    out = _span_parity(N, M, q, n, H, 8, 16, seed=9, gate_zero=True, keep_logits=keep)
     assert torch.all(out[N - 5:] == 0)
+
+
+@pytest.mark.parametrize("gate_zero", [False, True])
+def test_attention_span_kept_logits_equal_recomputed(gate_zero):
+    """The backward from the forward's kept q.k scores (e2a_attn_fwd_logits +
+    e2a_attn_bwd_softmax_logits) gives the same output and gradients, bit for bit, as the one that
+    recomputes them from gathered key rows; with row and key orders, ties and empty rows."""
+    from ubio_molfm_b200 import ops
+
+    N, M, E, H, D, C = 400, 500, 9000, 128, 8, 58
+    q, n = _random_graph(N - 7, M, E, 13)   # the last 7 rows have no edges
+    ins = [a.to(DEV) for a in _span_inputs(N, M, q, n, H, D, C, 14, gate_zero)]
+    md = ops.prepare_sparse_qk_edge_index_metadata(_t(q), _t(n), N, M)
+    order = _t(np.random.default_rng(5).permutation(N).astype(np.int32))
+    korder = _t(np.random.default_rng(6).permutation(M).astype(np.int32))
+    res = []
+    for keep in (False, True):
+        a = [x.clone().requires_grad_(True) for x in ins]
+        o = ops.attention_span(*a, md, order, korder, keep_logits=keep)
+        w = torch.randn(o.shape, generator=torch.Generator().manual_seed(15)).to(DEV)
+        res.append([o] + list(torch.autograd.grad(o, a, w)))
+    for name, x, y in zip(["out", "q", "k", "v", "gate", "poly", "dist"], res[0], res[1]):
+        assert torch.equal(x, y), name
+
+
+def test_attention_span_logits_entries_reject_other_layouts():
+    from ubio_molfm_b200 import _lib
+    from ubio_molfm_b200._lib import E2A_ERR_UNSUPPORTED, ptr, stream_of
+
+    lib = _lib.load()
+    N, M, E, H, D, C = 4, 4, 8, 8, 8, 16
+    f = lambda *s: torch.zeros(*s, device=DEV)  # noqa: E731
+    rp = torch.zeros(N + 1, dtype=torch.int32, device=DEV)
+    col = torch.zeros(E, dtype=torch.int32, device=DEV)
+    q, k, v, g = f(N, H, D), f(M, H, D), f(M, C, H), f(E, 2 * H)
+    st = stream_of(q.device)
+    rc = lib.e2a_attn_fwd_logits(ptr(q), ptr(k), ptr(v), ptr(g), ptr(g[:, H:]), 2 * H, ptr(f(E)), ptr(f(E)), ptr(rp),
+                                 ptr(col), None, N, M, E, H, D, C, ptr(f(N, C, H)), ptr(f(E, H)), ptr(f(N, H)),
+                                 ptr(f(N, H)), ptr(f(E, H)), st)
+    assert rc == E2A_ERR_UNSUPPORTED
+    rc = lib.e2a_attn_bwd_softmax_logits(ptr(k), ptr(g), ptr(g[:, H:]), 2 * H, ptr(f(E)), ptr(f(E)), ptr(rp),
+                                         ptr(col), None, N, M, E, H, D, C, ptr(f(E, H)), ptr(f(N, H)), ptr(f(N, H)),
+                                         ptr(f(E, H)), ptr(f(E, H)), ptr(f(N, H, D)), ptr(f(E, 2 * H)),
+                                         ptr(f(E, 2 * H)[:, H:]), 2 * H, ptr(f(E)), ptr(f(E)), ptr(f(E, H)), st)
+    assert rc == E2A_ERR_UNSUPPORTED
+    torch.cuda.synchronize()
 
 
 def test_attention_span_row_order_and_determinism():

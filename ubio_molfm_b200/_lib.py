@@ -46,6 +46,8 @@ SIGNATURES = {
     "e2a_edge_outer_bwd": (I32, [P, P, P, P, I64, I32, I32, P, P, P]),
     "e2a_attn_fwd": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                            P, P, P, P, P]),
+    "e2a_attn_fwd_logits": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
+                                  P, P, P, P, P, P]),
     "e2a_attn_bwd_workspace_bytes": (SZ, [I64, I32]),
     "e2a_attn_bwd_query": (I32, [P, P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32,
                                  P, P, P, P, P, P, P, I64, P, P, P, P, SZ, P]),
@@ -77,6 +79,8 @@ SIGNATURES = {
     "e2a_attn_bwd_softmax_workspace_bytes": (SZ, [I64, I32]),
     "e2a_attn_bwd_softmax": (I32, [P, P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P, P, P, P, P,
                                    I64, P, P, P, P, SZ, P]),
+    "e2a_attn_bwd_softmax_logits": (I32, [P, P, P, I64, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P, P, P, P,
+                                          P, P, P, I64, P, P, P, P]),
     "e2a_attn_bwd_dk": (I32, [P, P, P, P, P, P, I64, I64, I64, I32, I32, I32, P, P]),
 }
 

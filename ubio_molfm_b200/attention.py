@@ -64,6 +64,9 @@ class E2AttentionArbOrder_sparse(nn.Module):
         self.proj_first = SO3_Linear_e2former(num_attn_heads * head_mul, C, lmax=lmax)
         if (29 * C) % num_attn_heads:
             raise NotImplementedError("29*C must be divisible by the number of heads")
+        # keep the span's q.k scores ([E, heads] fp32) from the forward for the backward, which then
+        # gathers no key rows for them (taken where the span kernels support it: 128 heads of 8)
+        self.keep_logits = True
 
     def _fused_rows(self):
         if getattr(self, "_fused_rows_cache", None) is None:
@@ -163,14 +166,14 @@ class E2AttentionArbOrder_sparse(nn.Module):
             bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
         if bd["query_sorted"]:
             agg = attention_span(q_scaled, key, merged, gate, poly, edge_dis, metadata, bd.get("row_order"),
-                                 bd.get("key_order"))
+                                 bd.get("key_order"), keep_logits=self.keep_logits)
         else:
             # permute the edges into query-CSR order (q_perm) so that edge id == CSR slot
             perm = metadata[2].to(torch.long)
             md = (metadata[0], metadata[1], torch.arange(perm.numel(), device=perm.device, dtype=torch.int32),
                   metadata[3], metadata[4], torch.argsort(perm)[metadata[5].to(torch.long)].to(torch.int32))
             agg = attention_span(q_scaled, key, merged, gate[perm], poly[perm], edge_dis[perm], md,
-                                 bd.get("row_order"), bd.get("key_order"))
+                                 bd.get("row_order"), bd.get("key_order"), keep_logits=self.keep_logits)
         agg = agg.reshape(N1, -1, C)
         if fused:
             # A_a agg_v - agg_b, then output linear and proj_first as one GEMM per output row

@@ -490,13 +490,14 @@ k_softmax_bwd(const float* __restrict__ q, const float* __restrict__ k, const fl
 // lane l owns heads [l*HPL, (l+1)*HPL), so every per-head row statistic is lane-local and the q.k
 // dot needs only the lane's own HPL*D-float slice of each k row (coalesced across the warp).
 // ------------------------------------------------------------------------------------------------
-template <int HPL, int D, int MINB = 1>
+template <int HPL, int D, int MINB = 1, bool KEEP_S = false>
 __global__ void __launch_bounds__(kThreads, MINB)
 k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
                    const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
                    const float* __restrict__ dist, const int32_t* __restrict__ row_ptr,
                    const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows,
-                   float* __restrict__ beta, float* __restrict__ row_max, float* __restrict__ row_sum) {
+                   float* __restrict__ beta, float* __restrict__ row_max, float* __restrict__ row_sum,
+                   float* __restrict__ s_out = nullptr) {
   static_assert(HPL == 4, "float4 head groups");
   constexpr int H = 32 * HPL, F4 = HPL * D / 4;  // float4 per lane slice
   const int lane = threadIdx.x & 31;
@@ -528,6 +529,7 @@ k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
     const float4 g = ldg4(gate + (int64_t)e * ld_gi + lane * HPL);
     const float4 a = make_float4(g.x * sv[0], g.y * sv[1], g.z * sv[2], g.w * sv[3]);
     *reinterpret_cast<float4*>(beta + (int64_t)e * H + lane * HPL) = a;
+    if constexpr (KEEP_S) *reinterpret_cast<float4*>(s_out + (int64_t)e * H + lane * HPL) = make_float4(sv[0], sv[1], sv[2], sv[3]);
     m[0] = fmaxf(m[0], a.x); m[1] = fmaxf(m[1], a.y); m[2] = fmaxf(m[2], a.z); m[3] = fmaxf(m[3], a.w);
   }
   float S[HPL] = {0.f, 0.f, 0.f, 0.f};
@@ -552,7 +554,7 @@ k_softmax_fwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   *reinterpret_cast<float4*>(row_sum + (int64_t)i * H + lane * HPL) = make_float4(S[0], S[1], S[2], S[3]);
 }
 
-template <int HPL, int D, int MINB = 1>
+template <int HPL, int D, int MINB = 1, bool HAVE_S = false>
 __global__ void __launch_bounds__(kThreads, MINB)
 k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ gate,
                    const float* __restrict__ inputhead, int64_t ld_gi, const float* __restrict__ poly,
@@ -571,30 +573,37 @@ k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   const int rs = row_ptr[i], re = row_ptr[i + 1];
   if (rs == re) return;
   const int ho = lane * HPL;
-  float4 qv[F4];
-  const float* qr = q + (int64_t)i * H * D + ho * D;
+  float4 qv[HAVE_S ? 1 : F4];
+  if constexpr (!HAVE_S) {
+    const float* qr = q + (int64_t)i * H * D + ho * D;
 #pragma unroll
-  for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
+    for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
+  }
   const float4 mv = ldg4(row_max + (int64_t)i * H + ho), sv4 = ldg4(row_sum + (int64_t)i * H + ho);
   const float m[HPL] = {mv.x, mv.y, mv.z, mv.w};
   const float den[HPL] = {sv4.x + kSoftmaxEps, sv4.y + kSoftmaxEps, sv4.z + kSoftmaxEps, sv4.w + kSoftmaxEps};
   // pass 1: s = q.k -> bufB; T_h = sum_e d_alpha * alpha
   float T[HPL] = {0.f, 0.f, 0.f, 0.f};
   for (int e = rs; e < re; ++e) {
-    const float* kr = k + (int64_t)col[e] * H * D + ho * D;
     float s[HPL];
+    if constexpr (HAVE_S) {   // the forward's q.k scores, kept (no key-row gather)
+      const float4 s4 = ldg4(bufB + (int64_t)e * H + ho);
+      s[0] = s4.x; s[1] = s4.y; s[2] = s4.z; s[3] = s4.w;
+    } else {
+      const float* kr = k + (int64_t)col[e] * H * D + ho * D;
 #pragma unroll
-    for (int u = 0; u < HPL; ++u) {
-      float acc = 0.f;
+      for (int u = 0; u < HPL; ++u) {
+        float acc = 0.f;
 #pragma unroll
-      for (int t = 0; t < D / 4; ++t) {
-        const float4 kv = ldg4(kr + 4 * (u * (D / 4) + t));
-        const float4 qq = qv[u * (D / 4) + t];
-        acc += qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
+        for (int t = 0; t < D / 4; ++t) {
+          const float4 kv = ldg4(kr + 4 * (u * (D / 4) + t));
+          const float4 qq = qv[u * (D / 4) + t];
+          acc += qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
+        }
+        s[u] = acc;
       }
-      s[u] = acc;
+      *reinterpret_cast<float4*>(bufB + (int64_t)e * H + ho) = make_float4(s[0], s[1], s[2], s[3]);
     }
-    *reinterpret_cast<float4*>(bufB + (int64_t)e * H + ho) = make_float4(s[0], s[1], s[2], s[3]);
     const float4 g4 = ldg4(gate + (int64_t)e * ld_gi + ho), ih4 = ldg4(inputhead + (int64_t)e * ld_gi + ho);
     const float4 db4 = *reinterpret_cast<const float4*>(bufA + (int64_t)e * H + ho);
     const float g[HPL] = {g4.x, g4.y, g4.z, g4.w}, ih[HPL] = {ih4.x, ih4.y, ih4.z, ih4.w};
@@ -804,13 +813,19 @@ int value_bwd_launch(const float* value, const float* dout, const float* beta, c
 }
 
 // query-side backward from a given d_beta: softmax backward + d_q; scratch bufB ([E,H])
+// logits != nullptr: bufB holds the forward's q.k scores ([E,H]) and pass 1 reads them instead of
+// gathering k rows (warp layout only; the caller checks)
 int softmax_bwd_dq_launch(const float* q, const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
                           const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
                           const int32_t* row_order, int64_t n_rows, const Dims& dm, const float* beta,
                           const float* row_max, const float* row_sum, const float* d_beta, float* d_q, float* d_gate,
                           float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
-                          float* bufB, cudaStream_t st) {
-  if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
+                          float* bufB, cudaStream_t st, bool have_logits = false) {
+  if (have_logits) {
+    k_softmax_bwd_warp<4, 8, 4, true><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+        q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
+        d_inputhead, ld_dgi, d_poly, d_dist, d_logit, d_beta, bufB);
+  } else if (warp_softmax_ok(dm, ld_gi) && ld_dgi % 4 == 0) {
     k_softmax_bwd_warp<4, 8, 3><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
         q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, d_gate,
         d_inputhead, ld_dgi, d_poly, d_dist, d_logit, d_beta, bufB);
@@ -829,23 +844,29 @@ int softmax_bwd_dq_launch(const float* q, const float* k, const float* gate, con
 
 extern "C" {
 
-int e2a_attn_fwd(const float* q, const float* k, const float* value, const float* gate, const float* inputhead,
-                 int64_t ld_gi, const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
-                 const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
-                 float* out, float* beta, float* row_max, float* row_sum, void* stream) {
+int e2a_attn_fwd_logits(const float* q, const float* k, const float* value, const float* gate,
+                        const float* inputhead, int64_t ld_gi, const float* poly, const float* dist,
+                        const int32_t* row_ptr, const int32_t* col, const int32_t* row_order, int64_t n_rows,
+                        int64_t n_keys, int64_t n_edges, int H, int D, int C, float* out, float* beta, float* row_max,
+                        float* row_sum, float* logits, void* stream) {
   Dims dm;
   int ks;
   int rc = check_dims(H, D, C, dm, ks);
   if (rc) return rc;
   if (n_rows < 0 || n_keys < 0 || n_edges < 0 || ld_gi < H || n_edges > INT32_MAX) return E2A_ERR_ARG;
+  if (logits && !warp_softmax_ok(dm, ld_gi)) return E2A_ERR_UNSUPPORTED;
   if (n_rows == 0) return E2A_OK;
   if (!q || !row_ptr || !out || !row_max || !row_sum) return E2A_ERR_ARG;
   if (n_edges > 0 && (!k || !value || !gate || !inputhead || !poly || !dist || !col || !beta)) return E2A_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   if (warp_softmax_ok(dm, ld_gi)) {
     // 64 registers: 4 CTAs (32 warps) per SM keep more k-row gathers in flight
-    k_softmax_fwd_warp<4, 8, 4><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
-        q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum);
+    if (logits)
+      k_softmax_fwd_warp<4, 8, 4, true><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+          q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum, logits);
+    else
+      k_softmax_fwd_warp<4, 8, 4><<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+          q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, beta, row_max, row_sum);
   } else {
     const size_t ssm = softmax_smem(dm, 2);
     E2A_CUDA(prep_smem(k_softmax_fwd, ssm));
@@ -854,6 +875,14 @@ int e2a_attn_fwd(const float* q, const float* k, const float* value, const float
   }
   E2A_CHECK_LAUNCH();
   return launch_agg_ch(value, beta, dm, ks, row_ptr, col, nullptr, row_order, n_rows, out, st);
+}
+
+int e2a_attn_fwd(const float* q, const float* k, const float* value, const float* gate, const float* inputhead,
+                 int64_t ld_gi, const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                 const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H, int D, int C,
+                 float* out, float* beta, float* row_max, float* row_sum, void* stream) {
+  return e2a_attn_fwd_logits(q, k, value, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, n_keys,
+                             n_edges, H, D, C, out, beta, row_max, row_sum, nullptr, stream);
 }
 
 size_t e2a_attn_bwd_workspace_bytes(int64_t n_edges, int H) {
@@ -950,6 +979,29 @@ int e2a_attn_bwd_softmax(const float* q, const float* k, const float* gate, cons
   return softmax_bwd_dq_launch(q, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm, beta,
                                row_max, row_sum, d_beta, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,
                                bufB, (cudaStream_t)stream);
+}
+
+int e2a_attn_bwd_softmax_logits(const float* k, const float* gate, const float* inputhead, int64_t ld_gi,
+                                const float* poly, const float* dist, const int32_t* row_ptr, const int32_t* col,
+                                const int32_t* row_order, int64_t n_rows, int64_t n_keys, int64_t n_edges, int H,
+                                int D, int C, const float* beta, const float* row_max, const float* row_sum,
+                                const float* logits, const float* d_beta, float* d_q, float* d_gate,
+                                float* d_inputhead, int64_t ld_dgi, float* d_poly, float* d_dist, float* d_logit,
+                                void* stream) {
+  Dims dm;
+  int ks;
+  int rc = check_dims(H, D, C, dm, ks);
+  if (rc) return rc;
+  if (n_rows < 0 || n_keys < 0 || n_edges < 0 || ld_gi < H || ld_dgi < H || n_edges > INT32_MAX) return E2A_ERR_ARG;
+  if (!warp_softmax_ok(dm, ld_gi) || ld_dgi % 4) return E2A_ERR_UNSUPPORTED;
+  if (n_rows == 0) return E2A_OK;
+  if (!row_ptr || !d_q) return E2A_ERR_ARG;
+  if (n_edges > 0 && (!k || !gate || !inputhead || !poly || !dist || !col || !beta || !logits || !d_beta ||
+                      !d_gate || !d_inputhead || !d_poly || !d_dist || !d_logit))
+    return E2A_ERR_ARG;
+  return softmax_bwd_dq_launch(nullptr, k, gate, inputhead, ld_gi, poly, dist, row_ptr, col, row_order, n_rows, dm,
+                               beta, row_max, row_sum, d_beta, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist,
+                               d_logit, const_cast<float*>(logits), (cudaStream_t)stream, true);
 }
 
 int e2a_attn_bwd_dk(const float* q, const float* d_logit, const int32_t* k_row_ptr, const int32_t* k_col,

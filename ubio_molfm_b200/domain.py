@@ -65,7 +65,9 @@ class HaloPlan:
 
 class HaloStats:
     """Opt-in timing of the halo exchanges (CUDA events around each ``all_to_all`` on the current
-    stream): ``records`` holds (direction, start, end, bytes sent); :meth:`summary` sums them."""
+    stream) and of each evaluation's graph build (``"graph_build"``: the slab graph, the halo plan and
+    the local neighbour dict, including the positions' exchange): ``records`` holds (what, start, end,
+    bytes sent); :meth:`summary` sums them."""
 
     def __init__(self):
         self.enabled = False
@@ -195,12 +197,14 @@ def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), gr
     (collectives)."""
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     dec = model.decoder
+    t0 = HALO_STATS._start()
     plan, own_gid, local_gid, geom = domain_graph(pos_all, cell, pbc, dec.max_radius, dec.max_neighbors, world,
                                                   rank, group)
     with torch.enable_grad():
         pos_own = pos_all.detach()[own_gid].to(torch.float32).requires_grad_(True)
         pos_local = plan.exchange(pos_own)
         graph = local_graph(pos_local, geom, local_gid.numel(), dec.max_radius, n_query=plan.n_own)
+        HALO_STATS._stop("graph_build", t0, 0)
         sys_emb = None
         if charge is not None:
             mult = torch.ones(1, dtype=torch.long) if multiplicity is None else multiplicity

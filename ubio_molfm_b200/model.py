@@ -417,26 +417,37 @@ class E2FormerPotential(nn.Module):
         self.energy_head = MLP_energy_head(self.decoder.scalar_dim, self.decoder.lmax)
         # memory_saving: True = the Q / K per-degree projections are formed again in the backward instead
         # of kept (2 x heads x head-dim floats per irreps row and layer, ~29 GB at 1e5 atoms with the
-        # full-size model; ~10% of the step's tensor-core work); False = kept; "auto" = kept unless the
-        # evaluation's estimated peak with them kept passes 85% of the device's memory
+        # full-size model; ~10% of the step's tensor-core work) and the attention span's q.k scores are
+        # not kept (heads floats per edge and layer, ~6.4 GB at 1e5 atoms); False = both kept; "auto" =
+        # both kept unless the evaluation's estimated peak passes 85% of the device's memory, then the
+        # scores are dropped first and the projections second
         self.memory_saving = memory_saving
-        self._set_recompute(memory_saving is True)
+        self._set_memory_mode(memory_saving is True, memory_saving is not True)
 
-    def _set_recompute(self, on):
+    def _set_memory_mode(self, recompute, keep_logits):
         for blk in self.decoder.blocks:
-            blk.ga.query_linear.recompute_pair_product = on
-            blk.ga.key_linear.recompute_pair_product = on
+            blk.ga.query_linear.recompute_pair_product = recompute
+            blk.ga.key_linear.recompute_pair_product = recompute
+            blk.ga.keep_logits = keep_logits
 
-    # peak bytes of an evaluation per edge, projections recomputed (measured: 112.6 GB at 3.13 M edges)
+    # peak bytes of an evaluation per edge, projections recomputed and scores not kept (measured:
+    # 112.6 GB at 3.13 M edges)
     _PEAK_BYTES_PER_EDGE = 36.0e3
 
-    def _auto_recompute(self, n_rows, n_edges, device):
-        """Whether to recompute the Q / K projections for a graph of this size (``memory_saving="auto"``)."""
+    def _auto_memory_mode(self, n_rows, n_edges, device):
+        """(recompute projections, keep scores) for a graph of this size (``memory_saving="auto"``)."""
         dec = self.decoder
         blk = dec.blocks[0].ga
-        kept = 2 * len(dec.blocks) * n_rows * (dec.lmax + 1) ** 2 * blk.num_attn_heads * blk.attn_scalar_head * 4
-        total = torch.cuda.get_device_properties(device).total_memory
-        return self._PEAK_BYTES_PER_EDGE * n_edges + kept > 0.85 * total
+        layers = len(dec.blocks)
+        proj = 2 * layers * n_rows * (dec.lmax + 1) ** 2 * blk.num_attn_heads * blk.attn_scalar_head * 4
+        logits = layers * n_edges * blk.num_attn_heads * 4
+        base = self._PEAK_BYTES_PER_EDGE * n_edges
+        cap = 0.85 * torch.cuda.get_device_properties(device).total_memory
+        if base + proj + logits <= cap:
+            return False, True
+        if base + proj <= cap:
+            return False, False
+        return True, False
 
     @property
     def decoder(self):
@@ -506,7 +517,7 @@ class E2FormerPotential(nn.Module):
         with torch.enable_grad() if need_forces else torch.no_grad():
             g, pbc_any = self.build_graph(pos, cell, pbc, batch)
             if self.memory_saving == "auto" and pos.is_cuda:
-                self._set_recompute(self._auto_recompute(pos.shape[0], g["query_idx"].numel(), pos.device))
+                self._set_memory_mode(*self._auto_memory_mode(pos.shape[0], g["query_idx"].numel(), pos.device))
             sys_emb = None
             if charge is not None:
                 if multiplicity is None:

@@ -298,7 +298,7 @@ class AttnSpanFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order, key_order):
+    def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order, key_order, keep_logits=False):
         lib = _lib.load()
         q, key, value = _f32(q), _f32(key), _f32(value)
         edge_gate, poly, dist = _f32(edge_gate), _f32(poly), _f32(dist)
@@ -312,17 +312,22 @@ class AttnSpanFn(torch.autograd.Function):
         beta = torch.empty((E, H), device=dev, dtype=torch.float32)
         rmax = torch.empty((N, H), device=dev, dtype=torch.float32)
         rsum = torch.empty((N, H), device=dev, dtype=torch.float32)
+        # the q.k scores are kept only where the backward's fused key-side path and the warp layout run
+        keep = bool(keep_logits) and span_keeps_logits(H, D) and any(ctx.needs_input_grad[:6])
+        logits = torch.empty((E, H), device=dev, dtype=torch.float32) if keep else None
         tok = TIMER.start("e2a_attn_fwd")
-        check(lib.e2a_attn_fwd(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
-                               ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
-                               ptr(out), ptr(beta), ptr(rmax), ptr(rsum), stream_of(dev)), "e2a_attn_fwd")
+        check(lib.e2a_attn_fwd_logits(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
+                                      ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D,
+                                      C, ptr(out), ptr(beta), ptr(rmax), ptr(rsum), ptr(logits), stream_of(dev)),
+              "e2a_attn_fwd")
         TIMER.stop(tok)
-        ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, key_order, *md)
+        ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order,
+                              *md)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, row_order, key_order, *md = ctx.saved_tensors
+        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order, *md = ctx.saved_tensors
         lib = _lib.load()
         dout = _f32(dout)
         N, H, D = q.shape
@@ -345,19 +350,27 @@ class AttnSpanFn(torch.autograd.Function):
                                          ptr(key_order), N, M, E, H, D, C, ptr(d_v), ptr(d_beta), st),
                   "e2a_attn_bwd_value")
             TIMER.stop(tok)
-            ws = _workspace(lib.e2a_attn_bwd_softmax_workspace_bytes(E, H), dev)
             tok = TIMER.start("e2a_attn_bwd_softmax")
-            check(lib.e2a_attn_bwd_softmax(ptr(q), ptr(key), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H, ptr(poly),
-                                           ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E, H, D, C,
-                                           ptr(beta), ptr(rmax), ptr(rsum), ptr(d_beta), ptr(d_q), ptr(d_gate),
-                                           ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit), ptr(ws),
-                                           ws.numel(), st), "e2a_attn_bwd_softmax")
+            if logits is not None:
+                check(lib.e2a_attn_bwd_softmax_logits(
+                    ptr(key), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H, ptr(poly), ptr(dist), ptr(md[0]),
+                    ptr(md[1]), ptr(row_order), N, M, E, H, D, C, ptr(beta), ptr(rmax), ptr(rsum), ptr(logits),
+                    ptr(d_beta), ptr(d_q), ptr(d_gate), ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist),
+                    ptr(d_logit), st), "e2a_attn_bwd_softmax_logits")
+            else:
+                ws = _workspace(lib.e2a_attn_bwd_softmax_workspace_bytes(E, H), dev)
+                check(lib.e2a_attn_bwd_softmax(ptr(q), ptr(key), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
+                                               ptr(poly), ptr(dist), ptr(md[0]), ptr(md[1]), ptr(row_order), N, M, E,
+                                               H, D, C,
+                                               ptr(beta), ptr(rmax), ptr(rsum), ptr(d_beta), ptr(d_q), ptr(d_gate),
+                                               ptr(d_gate[:, H:]), 2 * H, ptr(d_poly), ptr(d_dist), ptr(d_logit),
+                                               ptr(ws), ws.numel(), st), "e2a_attn_bwd_softmax")
             TIMER.stop(tok)
             tok = TIMER.start("e2a_attn_bwd_dk")
             check(lib.e2a_attn_bwd_dk(ptr(q), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]), ptr(key_order), N, M,
                                       E, H, D, C, ptr(d_k), st), "e2a_attn_bwd_dk")
             TIMER.stop(tok)
-            return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None
+            return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None, None
         ws = _workspace(lib.e2a_attn_bwd_workspace_bytes(E, H), dev)
         tok = TIMER.start("e2a_attn_bwd_query")
         check(lib.e2a_attn_bwd_query(ptr(q), ptr(key), ptr(value), ptr(edge_gate), ptr(edge_gate[:, H:]), 2 * H,
@@ -370,14 +383,23 @@ class AttnSpanFn(torch.autograd.Function):
         check(lib.e2a_attn_bwd_key(ptr(q), ptr(dout), ptr(beta), ptr(d_logit), ptr(md[3]), ptr(md[4]), ptr(md[5]),
                                    ptr(key_order), N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
         TIMER.stop(tok)
-        return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None
+        return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None, None
 
 
-def attention_span(q_scaled, key, value, edge_gate, poly, dist, metadata, row_order=None, key_order=None):
+def span_keeps_logits(H, D):
+    """Whether :class:`AttnSpanFn` can keep the q.k scores for its backward at this head layout
+    (128 heads of 8: the warp-per-row softmax kernels, with the fused key-side backward)."""
+    return H == 128 and D == 8
+
+
+def attention_span(q_scaled, key, value, edge_gate, poly, dist, metadata, row_order=None, key_order=None,
+                   keep_logits=False):
     """Fused attention span (see :class:`AttnSpanFn`); ``metadata`` is the 6-tuple CSR of a
-    query-sorted edge list (identity query permutation)."""
+    query-sorted edge list (identity query permutation).  ``keep_logits``: keep the q.k scores
+    ([E, H] fp32) for the backward instead of recomputing them from gathered key rows (taken where
+    :func:`span_keeps_logits`; the gradients are the same bit for bit)."""
     require_cuda(q_scaled, key, value, edge_gate, poly, dist)
     md = _check_md(metadata)
     ro = None if row_order is None else _i32(row_order)
     ko = None if key_order is None else _i32(key_order)
-    return AttnSpanFn.apply(q_scaled, key, value, edge_gate, poly, dist, md, ro, ko)
+    return AttnSpanFn.apply(q_scaled, key, value, edge_gate, poly, dist, md, ro, ko, bool(keep_logits))
