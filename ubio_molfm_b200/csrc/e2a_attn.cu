@@ -338,7 +338,7 @@ k_dbeta(const float* __restrict__ value, const float* __restrict__ dout, const i
 __global__ void __launch_bounds__(kThreads)
 k_dbeta_warp(const float* __restrict__ value, const float* __restrict__ dout, const int32_t* __restrict__ row_ptr,
              const int32_t* __restrict__ col, const int32_t* __restrict__ order, int64_t n_rows, Dims dm,
-             float* __restrict__ dbeta) {
+             float* __restrict__ dbeta, const int32_t* __restrict__ perm = nullptr) {
   extern __shared__ float4 smem4[];
   float4* go_s = smem4;  // CH4
   const int H4 = dm.H / 4;
@@ -367,7 +367,7 @@ k_dbeta_warp(const float* __restrict__ value, const float* __restrict__ dout, co
         a0.z += __shfl_xor_sync(0xffffffffu, a0.z, o);
         a0.w += __shfl_xor_sync(0xffffffffu, a0.w, o);
       }
-      if (csub == 0) *reinterpret_cast<float4*>(dbeta + (int64_t)e * dm.H + 4 * hg) = a0;
+      if (csub == 0) *reinterpret_cast<float4*>(dbeta + (int64_t)(perm ? perm[e] : e) * dm.H + 4 * hg) = a0;
     }
     __syncthreads();
   }
@@ -686,6 +686,59 @@ k_softmax_bwd_warp(const float* __restrict__ q, const float* __restrict__ k, con
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Per-edge scores alone (the reference's sparse_qk_edge_index): out[perm[p], h] = <q[i,h,:], k[col[p],h,:]>,
+// one warp per query row, lane l owning heads [4l, 4l+4) (128 heads of 8): the row's q slice stays in
+// registers and each key row is one coalesced 4 KB gather; two edges are gathered per iteration.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 4)
+k_qk_warp(const float* __restrict__ q, const float* __restrict__ k, const int32_t* __restrict__ row_ptr,
+          const int32_t* __restrict__ col, const int32_t* __restrict__ perm, int64_t n_rows,
+          float* __restrict__ out) {
+  constexpr int H = 128, D = 8, F4 = 4 * D / 4;   // 8 float4 per lane slice
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (i >= n_rows) return;
+  const int rs = row_ptr[i], re = row_ptr[i + 1];
+  if (rs == re) return;
+  float4 qv[F4];
+  const float* qr = q + i * H * D + lane * 4 * D;
+#pragma unroll
+  for (int t = 0; t < F4; ++t) qv[t] = ldg4(qr + 4 * t);
+  auto dot4 = [&](const float4* kv) {
+    float sv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < D / 4; ++t) {
+        const float4 a = qv[u * (D / 4) + t], b = kv[u * (D / 4) + t];
+        acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+      }
+      sv[u] = acc;
+    }
+    return make_float4(sv[0], sv[1], sv[2], sv[3]);
+  };
+  int e = rs;
+  for (; e + 2 <= re; e += 2) {
+    float4 k0[F4], k1[F4];
+    const float* kr0 = k + (int64_t)col[e] * H * D + lane * 4 * D;
+    const float* kr1 = k + (int64_t)col[e + 1] * H * D + lane * 4 * D;
+#pragma unroll
+    for (int t = 0; t < F4; ++t) { k0[t] = ldg4(kr0 + 4 * t); k1[t] = ldg4(kr1 + 4 * t); }
+    const int64_t o0 = perm ? perm[e] : e, o1 = perm ? perm[e + 1] : e + 1;
+    *reinterpret_cast<float4*>(out + o0 * H + lane * 4) = dot4(k0);
+    *reinterpret_cast<float4*>(out + o1 * H + lane * 4) = dot4(k1);
+  }
+  if (e < re) {
+    float4 k0[F4];
+    const float* kr0 = k + (int64_t)col[e] * H * D + lane * 4 * D;
+#pragma unroll
+    for (int t = 0; t < F4; ++t) k0[t] = ldg4(kr0 + 4 * t);
+    *reinterpret_cast<float4*>(out + (int64_t)(perm ? perm[e] : e) * H + lane * 4) = dot4(k0);
+  }
+}
+
 int check_dims(int H, int D, int C, Dims& dm, int& ks) {
   if (H <= 0 || D <= 0 || C <= 0) return E2A_ERR_ARG;
   if (H % 4 || kThreads % H) return E2A_ERR_UNSUPPORTED;
@@ -771,7 +824,8 @@ int bwd_query_launch(const float* q, const float* k, const float* value, const f
   if (32 % (dm.H / 4) == 0) {
     const size_t wsm = (size_t)dm.CH4 * 16;
     E2A_CUDA(prep_smem(k_dbeta_warp, wsm));
-    k_dbeta_warp<<<grid_for(n_rows), kThreads, wsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA);
+    k_dbeta_warp<<<grid_for(n_rows), kThreads, wsm, st>>>(value, dout, row_ptr, col, row_order, n_rows, dm, bufA,
+                                                          nullptr);
   } else {
     const size_t dsm = (size_t)kEB * kThreads * 16;
     E2A_DISPATCH_KS(ks, k_dbeta, {
@@ -1117,3 +1171,56 @@ extern "C" int e2a_attn_bwd_query_noalloc(
                           beta, row_max, row_sum, dout, d_q, d_gate, d_inputhead, ld_dgi, d_poly, d_dist, d_logit,
                           bufA, bufB, (cudaStream_t)stream);
 }
+
+// ------------------------------------------------------------------------------------------------
+// Fast paths of the kernel-level functions (e2a_sparse.cu's entry points call these first and use their
+// generic kernels on E2A_ERR_UNSUPPORTED): the span's row-aggregation, d(beta) and score kernels on
+// the layouts they take.
+// ------------------------------------------------------------------------------------------------
+namespace e2a_fast {
+
+static bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int agg_ch(const float* X, const float* w, int H, int C, const int32_t* row_ptr, const int32_t* col,
+           const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st) {
+  if (H <= 0 || C <= 0 || H % 4 || 1024 % H || (C * H) % 4 || (C * H) / 4 > 16 * kThreads) return E2A_ERR_UNSUPPORTED;
+  if (!al16(X) || !al16(w) || !al16(out)) return E2A_ERR_UNSUPPORTED;
+  Dims dm{};
+  dm.H = H; dm.C = C; dm.D = 4; dm.CH4 = C * H / 4; dm.HD4 = H; dm.g = 1;
+  const int need = (dm.CH4 + kThreads - 1) / kThreads;
+  const int ks = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 16;
+  return launch_agg_ch(X, w, dm, ks, row_ptr, col, perm, nullptr, n_rows, out, st);
+}
+
+int agg_hd(const float* X, const float* w, int H, int D, const int32_t* row_ptr, const int32_t* col,
+           const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st) {
+  if (H <= 0 || D <= 0 || D % 4 || H * D / 4 > kThreads) return E2A_ERR_UNSUPPORTED;
+  if (!al16(X) || !al16(out)) return E2A_ERR_UNSUPPORTED;
+  Dims dm{};
+  dm.H = H; dm.D = D; dm.HD4 = H * D / 4; dm.g = D / 4; dm.C = 1; dm.CH4 = 1;
+  return launch_agg_hd(X, w, dm, row_ptr, col, perm, nullptr, n_rows, out, st);
+}
+
+int dbeta(const float* value, const float* dout, int H, int C, const int32_t* row_ptr, const int32_t* col,
+          const int32_t* perm, int64_t n_rows, float* d_w, cudaStream_t st) {
+  if (H <= 0 || C <= 0 || H % 4 || 32 % (H / 4) || (C * H) % 4) return E2A_ERR_UNSUPPORTED;
+  if (!al16(value) || !al16(dout) || !al16(d_w)) return E2A_ERR_UNSUPPORTED;
+  Dims dm{};
+  dm.H = H; dm.C = C; dm.D = 4; dm.CH4 = C * H / 4; dm.HD4 = H; dm.g = 1;
+  const size_t wsm = (size_t)dm.CH4 * 16;
+  if (wsm > 200 * 1024) return E2A_ERR_UNSUPPORTED;
+  E2A_CUDA(prep_smem(k_dbeta_warp, wsm));
+  k_dbeta_warp<<<grid_for(n_rows), kThreads, wsm, st>>>(value, dout, row_ptr, col, nullptr, n_rows, dm, d_w, perm);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+int qk(const float* q, const float* k, int H, int D, const int32_t* row_ptr, const int32_t* col,
+       const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st) {
+  if (H != 128 || D != 8 || !al16(q) || !al16(k) || !al16(out)) return E2A_ERR_UNSUPPORTED;
+  k_qk_warp<<<(int)((n_rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(q, k, row_ptr, col, perm, n_rows, out);
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
+}
+
+}  // namespace e2a_fast

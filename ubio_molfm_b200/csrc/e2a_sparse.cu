@@ -3,7 +3,32 @@
 // row is produced by one warp or CTA from CSR-ordered inputs: deterministic, atomic-free.
 #include "e2a_common.cuh"
 
+// fast paths (e2a_attn.cu): E2A_ERR_UNSUPPORTED outside the layouts they take
+namespace e2a_fast {
+int agg_ch(const float* X, const float* w, int H, int C, const int32_t* row_ptr, const int32_t* col,
+           const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+int agg_hd(const float* X, const float* w, int H, int D, const int32_t* row_ptr, const int32_t* col,
+           const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+int dbeta(const float* value, const float* dout, int H, int C, const int32_t* row_ptr, const int32_t* col,
+          const int32_t* perm, int64_t n_rows, float* d_w, cudaStream_t st);
+int qk(const float* q, const float* k, int H, int D, const int32_t* row_ptr, const int32_t* col,
+       const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+}  // namespace e2a_fast
+
+// head-sliced gathers of [H, D] rows (e2a_sliced.cu) for tables too large to stay in L2 in one piece
+namespace e2a_sliced {
+int agg_hd(const float* X, const float* w, int H, int D, const int32_t* row_ptr, const int32_t* col,
+           const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+int qk(const float* q, const float* k, int H, int D, const int32_t* row_ptr, const int32_t* col,
+       const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+}  // namespace e2a_sliced
+
 namespace {
+
+// A gathered [H, D] table larger than this (estimated from the output row count, the callers' row and
+// table counts being of one size in this model) is gathered in head slices (e2a_sliced.cu).
+constexpr double kSliceAboveBytes = 32.0 * 1048576.0;
+bool sliced(int64_t rows, int64_t row_floats) { return (double)rows * (double)row_floats * 4.0 > kSliceAboveBytes; }
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
@@ -58,6 +83,19 @@ __global__ void k_alpha_sum(const float* __restrict__ alpha, const int32_t* __re
       for (int p = rs; p < re; ++p) acc += alpha[(int64_t)(perm ? perm[p] : p) * H + h];
       out[r * H + h] = acc;
     }
+  }
+}
+
+// ga[e, 4j..4j+4) = go[qidx[e], 4j..4j+4)  (H % 4 == 0, 16-byte aligned rows): one warp per edge row
+// (grid-stride), the lanes over its float4 columns; the output is streamed (evict-first stores).
+__global__ void k_broadcast_rows4(const float4* __restrict__ go, const int32_t* __restrict__ qidx, int64_t E, int H4,
+                                  float4* __restrict__ ga) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; e < E; e += nw) {
+    const float4* src = go + (int64_t)qidx[e] * H4;
+    float4* dst = ga + e * H4;
+    for (int j = lane; j < H4; j += 32) __stcs(dst + j, __ldg(src + j));
   }
 }
 
@@ -223,6 +261,11 @@ int e2a_sparse_qk_fwd(const float* q, const float* k, const int32_t* row_ptr, co
   if (n_rows < 0 || n_edges < 0 || H <= 0 || D <= 0) return E2A_ERR_ARG;
   if (n_rows == 0 || n_edges == 0) return E2A_OK;
   if (!q || !k || !row_ptr || !col || !out) return E2A_ERR_ARG;
+  int rc = sliced(n_rows, (int64_t)H * D)
+               ? e2a_sliced::qk(q, k, H, D, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream)
+               : E2A_ERR_UNSUPPORTED;
+  if (rc == E2A_ERR_UNSUPPORTED) rc = e2a_fast::qk(q, k, H, D, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream);
+  if (rc != E2A_ERR_UNSUPPORTED) return rc;
   k_sparse_qk<<<rows_grid(n_rows), kThreads, 0, (cudaStream_t)stream>>>(q, k, row_ptr, col, perm, n_rows, H, D, out);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
@@ -233,6 +276,12 @@ int e2a_grouped_reduce(const float* alpha, const float* x, const int32_t* row_pt
   if (n_rows < 0 || H <= 0 || D <= 0) return E2A_ERR_ARG;
   if (n_rows == 0) return E2A_OK;
   if (!row_ptr || !out) return E2A_ERR_ARG;
+  int rc = sliced(n_rows, (int64_t)H * D)
+               ? e2a_sliced::agg_hd(x, alpha, H, D, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream)
+               : E2A_ERR_UNSUPPORTED;
+  if (rc == E2A_ERR_UNSUPPORTED)
+    rc = e2a_fast::agg_hd(x, alpha, H, D, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream);
+  if (rc != E2A_ERR_UNSUPPORTED) return rc;
   k_grouped_reduce<<<rows_grid(n_rows), kThreads, 0, (cudaStream_t)stream>>>(alpha, x, row_ptr, col, perm, n_rows,
                                                                               H, D, out);
   E2A_CHECK_LAUNCH();
@@ -254,6 +303,12 @@ int e2a_alpha_sum_bwd(const float* grad_out, const int32_t* query_idx, int64_t n
   if (n_edges < 0 || H <= 0) return E2A_ERR_ARG;
   if (n_edges == 0) return E2A_OK;
   if (!grad_out || !query_idx || !grad_alpha) return E2A_ERR_ARG;
+  if (H % 4 == 0 && ((uintptr_t)grad_out & 15u) == 0 && ((uintptr_t)grad_alpha & 15u) == 0) {
+    k_broadcast_rows4<<<flat_grid(n_edges * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const float4*>(grad_out), query_idx, n_edges, H / 4, reinterpret_cast<float4*>(grad_alpha));
+    E2A_CHECK_LAUNCH();
+    return E2A_OK;
+  }
   k_broadcast_rows<<<flat_grid(n_edges * H, 256), 256, 0, (cudaStream_t)stream>>>(grad_out, query_idx, n_edges, H,
                                                                                  grad_alpha);
   E2A_CHECK_LAUNCH();
@@ -265,6 +320,8 @@ int e2a_v_agg_fwd(const float* value, const float* alpha, const int32_t* row_ptr
   if (n_rows < 0 || C <= 0 || H <= 0) return E2A_ERR_ARG;
   if (n_rows == 0) return E2A_OK;
   if (!row_ptr || !out) return E2A_ERR_ARG;
+  const int rc = e2a_fast::agg_ch(value, alpha, H, C, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream);
+  if (rc != E2A_ERR_UNSUPPORTED) return rc;
   k_v_agg<<<rows_grid(n_rows), kThreads, 0, (cudaStream_t)stream>>>(value, alpha, row_ptr, col, perm, n_rows, C, H,
                                                                      out);
   E2A_CHECK_LAUNCH();
@@ -276,6 +333,8 @@ int e2a_v_agg_bwd_alpha(const float* dout, const float* value, const int32_t* ro
   if (n_rows < 0 || C <= 0 || H <= 0) return E2A_ERR_ARG;
   if (n_rows == 0) return E2A_OK;
   if (!row_ptr || !dout) return E2A_ERR_ARG;
+  const int rc = e2a_fast::dbeta(value, dout, H, C, row_ptr, col, perm, n_rows, d_alpha, (cudaStream_t)stream);
+  if (rc != E2A_ERR_UNSUPPORTED) return rc;
   k_v_agg_dalpha<<<rows_grid(n_rows), kThreads, 0, (cudaStream_t)stream>>>(dout, value, row_ptr, col, perm, n_rows,
                                                                             C, H, d_alpha);
   E2A_CHECK_LAUNCH();
