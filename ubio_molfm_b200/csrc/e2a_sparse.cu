@@ -86,17 +86,14 @@ __global__ void k_alpha_sum(const float* __restrict__ alpha, const int32_t* __re
   }
 }
 
-// ga[e, 4j..4j+4) = go[qidx[e], 4j..4j+4)  (H % 4 == 0, 16-byte aligned rows): one warp per edge row
-// (grid-stride), the lanes over its float4 columns; the output is streamed (evict-first stores).
-__global__ void k_broadcast_rows4(const float4* __restrict__ go, const int32_t* __restrict__ qidx, int64_t E, int H4,
-                                  float4* __restrict__ ga) {
-  const int lane = threadIdx.x & 31;
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; e < E; e += nw) {
-    const float4* src = go + (int64_t)qidx[e] * H4;
-    float4* dst = ga + e * H4;
-    for (int j = lane; j < H4; j += 32) __stcs(dst + j, __ldg(src + j));
-  }
+// ga[e, 4j..4j+4) = go[qidx[e], 4j..4j+4)  (H % 4 == 0, H / 4 a power of two, 16-byte aligned rows):
+// one float4 per thread, the output streamed (evict-first stores).
+__global__ void k_broadcast_rows4(const float4* __restrict__ go, const int32_t* __restrict__ qidx, int64_t n4,
+                                  int sh, float4* __restrict__ ga) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= n4) return;
+  const int64_t e = t >> sh;
+  __stcs(ga + t, __ldg(go + ((int64_t)qidx[e] << sh) + (t - (e << sh))));
 }
 
 __global__ void k_broadcast_rows(const float* __restrict__ go, const int32_t* __restrict__ qidx, int64_t E, int H,
@@ -303,9 +300,14 @@ int e2a_alpha_sum_bwd(const float* grad_out, const int32_t* query_idx, int64_t n
   if (n_edges < 0 || H <= 0) return E2A_ERR_ARG;
   if (n_edges == 0) return E2A_OK;
   if (!grad_out || !query_idx || !grad_alpha) return E2A_ERR_ARG;
-  if (H % 4 == 0 && ((uintptr_t)grad_out & 15u) == 0 && ((uintptr_t)grad_alpha & 15u) == 0) {
-    k_broadcast_rows4<<<flat_grid(n_edges * 32, 256), 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const float4*>(grad_out), query_idx, n_edges, H / 4, reinterpret_cast<float4*>(grad_alpha));
+  const int H4 = H / 4;
+  if (H % 4 == 0 && (H4 & (H4 - 1)) == 0 && ((uintptr_t)grad_out & 15u) == 0 && ((uintptr_t)grad_alpha & 15u) == 0 &&
+      (n_edges * H4 + 255) / 256 <= INT32_MAX) {
+    int sh = 0;
+    while ((1 << sh) < H4) ++sh;
+    const int64_t n4 = n_edges * H4;
+    k_broadcast_rows4<<<(int)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const float4*>(grad_out), query_idx, n4, sh, reinterpret_cast<float4*>(grad_alpha));
     E2A_CHECK_LAUNCH();
     return E2A_OK;
   }
