@@ -121,6 +121,30 @@ def test_slab_owner_partitions_periodic_cell():
     assert torch.equal(own, expect.clamp(0, 3))
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_slab_candidates_cover_every_neighbour(world):
+    """The keys a rank's radius search sees (slab_candidates) include every periodic image within the
+    cutoff of any atom it owns, in a triclinic cell with stored positions outside the home cell."""
+    from ubio_molfm_b200.domain import slab_candidates, slab_owner
+
+    g = torch.Generator().manual_seed(7)
+    cell = torch.tensor([[30.0, 0, 0], [4.0, 25.0, 0], [2.0, 3.0, 28.0]])
+    pos = (torch.rand(400, 3, generator=g) * 3 - 1) @ cell
+    shifts = torch.tensor([[a, b, c] for a in (-1, 0, 1) for b in (-1, 0, 1) for c in (-1, 0, 1)],
+                          dtype=torch.float32) @ cell
+    exp_pos = (pos.unsqueeze(0) + shifts.unsqueeze(1)).reshape(-1, 3)   # every image of every atom
+    cutoff = 5.0
+    owner = slab_owner(pos, cell, world)
+    for rank in range(world):
+        cand = slab_candidates(exp_pos, cell, cutoff, world, rank)
+        own = pos[owner == rank]
+        near = (torch.cdist(own.double(), exp_pos.double()) <= cutoff).any(0)
+        need = torch.nonzero(near).flatten()
+        assert cand is not None and bool(torch.all(cand[1:] > cand[:-1]))
+        assert bool(torch.isin(need, cand).all())
+        assert cand.numel() < exp_pos.shape[0]
+
+
 @pytest.mark.gpu
 def test_domain_decomposition_equals_single_gpu():
     """2 ranks over NCCL (when the box has 2 GPUs): energy and forces of the slab-decomposed model

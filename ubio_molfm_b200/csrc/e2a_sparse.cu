@@ -87,13 +87,24 @@ __global__ void k_alpha_sum(const float* __restrict__ alpha, const int32_t* __re
 }
 
 // ga[e, 4j..4j+4) = go[qidx[e], 4j..4j+4)  (H % 4 == 0, H / 4 a power of two, 16-byte aligned rows):
-// one float4 per thread, the output streamed (evict-first stores).
+// four float4 per thread (index loads, then row loads, then stores: four independent chains in
+// flight), the output streamed (evict-first stores).
 __global__ void k_broadcast_rows4(const float4* __restrict__ go, const int32_t* __restrict__ qidx, int64_t n4,
                                   int sh, float4* __restrict__ ga) {
-  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (t >= n4) return;
-  const int64_t e = t >> sh;
-  __stcs(ga + t, __ldg(go + ((int64_t)qidx[e] << sh) + (t - (e << sh))));
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x * 4 + threadIdx.x;
+  int64_t src[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t t = t0 + (int64_t)u * blockDim.x;
+    const int64_t e = t >> sh;
+    src[u] = t < n4 ? ((int64_t)__ldg(qidx + e) << sh) + (t - (e << sh)) : -1;
+  }
+  float4 v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) v[u] = src[u] >= 0 ? __ldg(go + src[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (src[u] >= 0) __stcs(ga + t0 + (int64_t)u * blockDim.x, v[u]);
 }
 
 __global__ void k_broadcast_rows(const float* __restrict__ go, const int32_t* __restrict__ qidx, int64_t E, int H,
@@ -302,11 +313,11 @@ int e2a_alpha_sum_bwd(const float* grad_out, const int32_t* query_idx, int64_t n
   if (!grad_out || !query_idx || !grad_alpha) return E2A_ERR_ARG;
   const int H4 = H / 4;
   if (H % 4 == 0 && (H4 & (H4 - 1)) == 0 && ((uintptr_t)grad_out & 15u) == 0 && ((uintptr_t)grad_alpha & 15u) == 0 &&
-      (n_edges * H4 + 255) / 256 <= INT32_MAX) {
+      (n_edges * H4 + 1023) / 1024 <= INT32_MAX) {
     int sh = 0;
     while ((1 << sh) < H4) ++sh;
     const int64_t n4 = n_edges * H4;
-    k_broadcast_rows4<<<(int)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+    k_broadcast_rows4<<<(int)((n4 + 1023) / 1024), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<const float4*>(grad_out), query_idx, n4, sh, reinterpret_cast<float4*>(grad_alpha));
     E2A_CHECK_LAUNCH();
     return E2A_OK;

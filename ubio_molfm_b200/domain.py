@@ -130,6 +130,21 @@ class _HaloFn(torch.autograd.Function):
         return g_own, None
 
 
+def slab_candidates(exp_pos, cell, cutoff, world, rank):
+    """Indices (ascending) of the expanded nodes whose fractional coordinate along the first lattice
+    vector lies, modulo 1, within ``cutoff`` (as a perpendicular distance, plus a small margin) of rank
+    ``rank``'s slab [rank / world, (rank + 1) / world): every node that can be within ``cutoff`` of an
+    atom of the slab, whatever image the atom's stored position is in."""
+    inv = torch.linalg.inv(torch.as_tensor(cell, dtype=torch.float64, device=exp_pos.device))
+    f = torch.remainder(exp_pos.detach().to(torch.float64) @ inv[:, 0], 1.0)
+    delta = float(cutoff) * float(torch.linalg.norm(inv[:, 0])) + 1e-6
+    lo, hi = rank / world - delta, (rank + 1) / world + delta
+    if hi - lo >= 1.0:
+        return None
+    keep = ((f >= lo) & (f < hi)) | ((f + 1.0 >= lo) & (f + 1.0 < hi)) | ((f - 1.0 >= lo) & (f - 1.0 < hi))
+    return torch.nonzero(keep).flatten()
+
+
 def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=None):
     """Graph of this rank's owned atoms over the owned + ghost atoms, and the halo plan.
 
@@ -142,8 +157,14 @@ def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=N
     n_own = own_gid.numel()
     p = pos_all.detach().to(torch.float32)
     exp_pos, outcell_g, image_g = expand_pbc(p, torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff)
-    g = radius_graph(p[own_gid], exp_pos, torch.tensor([0, n_own]), torch.tensor([0, exp_pos.shape[0]]), cutoff,
+    # candidate keys: the expanded nodes within the cutoff of this slab (periodically), a superset of every
+    # owned atom's neighbours kept in ascending order, so the search sees the same keys in the same order
+    cand = slab_candidates(exp_pos, cell, cutoff, world, rank) if world > 1 else None
+    keys = exp_pos if cand is None else exp_pos[cand]
+    g = radius_graph(p[own_gid], keys, torch.tensor([0, n_own]), torch.tensor([0, keys.shape[0]]), cutoff,
                      1e-4, max_neighbors, with_key_csr=False)
+    if cand is not None:
+        g["neighbor_idx"] = cand[g["neighbor_idx"]]
     used = torch.unique(g["neighbor_idx"])                                   # global expanded nodes (sorted)
     atoms_needed = torch.unique(outcell_g[used])
     is_own = torch.zeros(pos_all.shape[0], dtype=torch.bool, device=dev)
