@@ -170,12 +170,13 @@ class _LocalPlan:
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("restrict", [True, False])
+@pytest.mark.parametrize("restrict", [True, False, "kv"])
 def test_domain_slab_on_one_gpu_matches_full_system(restrict, monkeypatch):
     """One rank's slab of a 2-rank decomposition, on one GPU, with the halo exchange replaced by the
-    full system's own block inputs for the ghost rows: the owned atoms' per-atom energies equal the
+    full system's own tensors for the ghost rows: the owned atoms' per-atom energies equal the
     full-system ones, with the ghosts as keys only (``n_query`` = owned rows: no query-side, output or
-    FFN work on them) and with every row computed."""
+    FFN work on them), with every row computed, and ("kv", what ``domain_energy_forces`` runs) with the
+    ghosts' key / value projections exchanged instead of their block inputs."""
     from ubio_molfm_b200 import domain
     from ubio_molfm_b200.model import E2FormerPotential
     from ubio_molfm_b200.synthetic import bio_box, seeded_params_
@@ -193,9 +194,12 @@ def test_domain_slab_on_one_gpu_matches_full_system(restrict, monkeypatch):
     Z = torch.tensor(Z, device="cuda")
     pbc = (True, True, True)
 
-    inputs = []
+    inputs, kv = [], {"key": [], "value": []}
     hooks = [b.register_forward_pre_hook(lambda m, a, kw: inputs.append(kw["node_irreps"].detach()),
                                          with_kwargs=True) for b in dec.blocks]
+    for b in dec.blocks:
+        hooks.append(b.ga.key_linear.register_forward_hook(lambda m, a, o: kv["key"].append(o.detach())))
+        hooks.append(b.ga.proj_value.register_forward_hook(lambda m, a, o: kv["value"].append(o.detach())))
     with torch.no_grad():
         g, pbc_any = model.build_graph(pos, torch.tensor(cell, dtype=torch.float32), pbc, None)
         x_full = dec(pos, Z, g, pbc_any)
@@ -212,11 +216,23 @@ def test_domain_slab_on_one_gpu_matches_full_system(restrict, monkeypatch):
     def halo(t):
         return torch.cat([t[:plan.n_own], inputs[next(step)][plan.ghost_gid]], dim=0)
 
+    calls = {"key": 0, "value": 0}
+
+    def kv_halo(t, which):
+        layer = calls[which]
+        calls[which] += 1
+        assert t.shape[0] == plan.n_own
+        return torch.cat([t, kv[which][layer][plan.ghost_gid]], dim=0)
+
     with torch.no_grad():
         pos_local = pos[local_gid]
         graph = domain.local_graph(pos_local, geom, local_gid.numel(), dec.max_radius,
                                    n_query=plan.n_own if restrict else None)
-        x = dec(pos_local, Z[local_gid], graph, True, halo=halo)
+        if restrict == "kv":
+            x = dec(pos_local, Z[local_gid], graph, True, kv_halo=kv_halo)
+            assert calls == {"key": cfg["num_layers"], "value": cfg["num_layers"]}
+        else:
+            x = dec(pos_local, Z[local_gid], graph, True, halo=halo)
         e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1)
     if restrict:
         assert x.shape[0] == plan.n_own   # the blocks returned the query rows only

@@ -137,11 +137,20 @@ class E2AttentionArbOrder_sparse(nn.Module):
         x = node_irreps_input
 
         query = self.query_linear(x if N1 == n_all else x[:N1]).reshape(N1, H, -1)
-        key = self.key_linear(x)[outcell].reshape(N2, H, -1)
+        # kv_halo (domain decomposition): the rows of x are this rank's atoms only; the other atoms'
+        # key / value projections come from their owners, appended after the own rows
+        kv_halo = bd.get("kv_halo")
+        key = self.key_linear(x)
+        if kv_halo is not None:
+            key = kv_halo(key, "key")
+        key = key[outcell].reshape(N2, H, -1)
         q_scaled = query / math.sqrt(query.shape[-1])
         gate = self.edge_gate(attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx)
 
-        value = self.proj_value(x)[outcell]                                          # [N2, 9, C]
+        value = self.proj_value(x)
+        if kv_halo is not None:
+            value = kv_halo(value, "value")
+        value = value[outcell]                                                       # [N2, 9, C]
         tp = self.first_order_tp
         fused = x.is_cuda and not self.training
         if fused:

@@ -230,7 +230,9 @@ def domain_energy_forces(model, pos_all, Z_all, cell, pbc=(True, True, True), gr
         if charge is not None:
             mult = torch.ones(1, dtype=torch.long) if multiplicity is None else multiplicity
             sys_emb = model.backbone.system_embedding(charge, mult)[:1]
-        x = dec(pos_local, Z_all[local_gid], graph, True, halo=lambda t: plan.exchange(t[:plan.n_own]),
+        # the ghosts' key / value projections come from their owners (no norm or projection work here
+        # for atoms owned elsewhere)
+        x = dec(pos_local, Z_all[local_gid], graph, True, kv_halo=lambda t, which: plan.exchange(t),
                 sys_embedding=sys_emb)
         e_own = model.energy_head(x[:plan.n_own, 0]).squeeze(-1).sum()
         (grad,) = torch.autograd.grad(e_own, pos_own)

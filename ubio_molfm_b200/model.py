@@ -295,7 +295,7 @@ class E2former(nn.Module):
             elif rest == "edge_deg_embed_dense.sph.W":
                 del state_dict[k]
 
-    def forward(self, node_pos, atomic_numbers, graph, pbc_any, halo=None, sys_embedding=None):
+    def forward(self, node_pos, atomic_numbers, graph, pbc_any, halo=None, sys_embedding=None, kv_halo=None):
         """``graph``: the flattened neighbour dict (``query_idx``, ``neighbor_idx``, ``metadata``,
         ``f_edge_vec``, ``f_dist``, ``f_poly_dist``, ``f_outcell_index``, ``f_exp_node_pos`` and the
         optional ``row_order`` / ``key_order``).  Returns the node irreps [N, (lmax+1)^2, C].
@@ -304,11 +304,19 @@ class E2former(nn.Module):
         the embedding and every block return those rows, and ``halo`` appends the others before each
         block (it receives the n query rows).  ``sys_embedding`` ([rows, C] or [1, C], or None): the
         charge / multiplicity embedding of each row's system, added to the normed l=0 row of every
-        block (e2former.py:1074-1077, 582-583); with a halo it must cover the appended rows too."""
-        if int(graph.get("n_query", node_pos.shape[0])) != node_pos.shape[0] and halo is None:
+        block (e2former.py:1074-1077, 582-583); with a halo it must cover the appended rows too.
+        ``kv_halo`` (domain decomposition, instead of ``halo``): the node irreps stay at the n query rows
+        through every block, and each attention layer calls ``kv_halo(t, "key")`` / ``kv_halo(t, "value")``
+        on its key / value projections of those rows, which must return them followed by the other
+        atoms' projections (from their owners): no norm or projection work for rows owned elsewhere."""
+        if int(graph.get("n_query", node_pos.shape[0])) != node_pos.shape[0] and halo is None and kv_halo is None:
             raise ValueError("n_query < number of nodes needs a halo to refresh the other rows")
+        if halo is not None and kv_halo is not None:
+            raise ValueError("pass halo or kv_halo, not both")
         jd = [j.to(torch.float64) for j in self.Jd_list]
         bd = dict(graph)
+        if kv_halo is not None:
+            bd["kv_halo"] = kv_halo
         if node_pos.is_cuda and not self.training and self.lmax == 2:
             # the attention layers form their per-node SO(2) maps from the positions directly
             bd.update({"wigner": None, "wigner_inv": None, "wigner_exp": None, "wigner_inv_exp": None,
