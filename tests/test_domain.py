@@ -122,27 +122,54 @@ def test_slab_owner_partitions_periodic_cell():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_slab_candidates_cover_every_neighbour(world):
-    """The keys a rank's radius search sees (slab_candidates) include every periodic image within the
-    cutoff of any atom it owns, in a triclinic cell with stored positions outside the home cell."""
-    from ubio_molfm_b200.domain import slab_candidates, slab_owner
+def test_slab_keys_cover_every_neighbour(world):
+    """The keys a rank's radius search sees (slab_keys) include every periodic image within the cutoff
+    of any atom it owns, in a triclinic cell with stored positions outside the home cell, in the
+    expansion's (cell shift, atom) order."""
+    from ubio_molfm_b200.domain import slab_keys, slab_owner
+    from ubio_molfm_b200.graph import pbc_image_cells
 
     g = torch.Generator().manual_seed(7)
     cell = torch.tensor([[30.0, 0, 0], [4.0, 25.0, 0], [2.0, 3.0, 28.0]])
-    pos = (torch.rand(400, 3, generator=g) * 3 - 1) @ cell
-    shifts = torch.tensor([[a, b, c] for a in (-1, 0, 1) for b in (-1, 0, 1) for c in (-1, 0, 1)],
-                          dtype=torch.float32) @ cell
-    exp_pos = (pos.unsqueeze(0) + shifts.unsqueeze(1)).reshape(-1, 3)   # every image of every atom
+    pos = (torch.rand(400, 3, generator=g) * 1.4 - 0.2) @ cell
     cutoff = 5.0
+    cells, offsets = pbc_image_cells(cell, [True] * 3, cutoff)
+    exp_pos = (pos.unsqueeze(0) + offsets.unsqueeze(1)).reshape(-1, 3)   # every candidate image, k * N + a
     owner = slab_owner(pos, cell, world)
     for rank in range(world):
-        cand = slab_candidates(exp_pos, cell, cutoff, world, rank)
-        own = pos[owner == rank]
-        near = (torch.cdist(own.double(), exp_pos.double()) <= cutoff).any(0)
+        own_gid = torch.nonzero(owner == rank).flatten()
+        index, image, atom, off = slab_keys(pos, own_gid, cell, [True] * 3, cutoff)
+        assert torch.equal(index, image * pos.shape[0] + atom) and bool(torch.all(index[1:] > index[:-1]))
+        assert torch.equal(off, offsets)
+        near = (torch.cdist(pos[own_gid].double(), exp_pos.double()) <= cutoff).any(0)
         need = torch.nonzero(near).flatten()
-        assert cand is not None and bool(torch.all(cand[1:] > cand[:-1]))
-        assert bool(torch.isin(need, cand).all())
-        assert cand.numel() < exp_pos.shape[0]
+        assert bool(torch.isin(need, index).all())
+        assert index.numel() < exp_pos.shape[0]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 8])
+def test_domain_graph_edges_equal_whole_system_search(world, monkeypatch):
+    """A rank's edges from the slab keys equal, edge for edge and in order (query, neighbour position,
+    distance bit for bit), those of a radius search of its owned atoms over the whole system's PBC
+    expansion."""
+    from ubio_molfm_b200 import domain
+    from ubio_molfm_b200.graph import expand_pbc, radius_graph
+    from ubio_molfm_b200.synthetic import blob_in_water
+
+    pos_np, _, cell = blob_in_water(box=40.0, n_blob=1000, seed=5)
+    pos = torch.tensor(pos_np, dtype=torch.float32, device="cuda")
+    monkeypatch.setattr(domain, "HaloPlan", _LocalPlan)
+    for rank in (0, world - 1):
+        plan, own_gid, local_gid, geom = domain.domain_graph(pos, cell, (True,) * 3, 6.0, 32, world, rank)
+        pos_local = pos[local_gid]
+        key_pos = pos_local[geom["outcell"]] + geom["offsets"]
+        exp_pos, _, _ = expand_pbc(pos, torch.tensor(cell, dtype=torch.float32), [True] * 3, 6.0)
+        ref = radius_graph(pos[own_gid], exp_pos, torch.tensor([0, own_gid.numel()]),
+                           torch.tensor([0, exp_pos.shape[0]]), 6.0, 1e-4, 32, with_key_csr=False)
+        assert torch.equal(geom["query_idx"], ref["query_idx"])
+        assert torch.equal(key_pos[geom["neighbor_idx"]], exp_pos[ref["neighbor_idx"]])
+        assert torch.equal(geom["dist"], ref["f_dist"].detach())
 
 
 @pytest.mark.gpu

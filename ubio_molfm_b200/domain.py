@@ -19,7 +19,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, ops
-from .graph import _DistFn, expand_pbc, morton_row_order, pbc_image_offsets, radius_graph
+from .graph import _DistFn, morton_row_order, pbc_image_cells, radius_graph
 from .nn import polynomial
 
 
@@ -130,19 +130,29 @@ class _HaloFn(torch.autograd.Function):
         return g_own, None
 
 
-def slab_candidates(exp_pos, cell, cutoff, world, rank):
-    """Indices (ascending) of the expanded nodes whose fractional coordinate along the first lattice
-    vector lies, modulo 1, within ``cutoff`` (as a perpendicular distance, plus a small margin) of rank
-    ``rank``'s slab [rank / world, (rank + 1) / world): every node that can be within ``cutoff`` of an
-    atom of the slab, whatever image the atom's stored position is in."""
-    inv = torch.linalg.inv(torch.as_tensor(cell, dtype=torch.float64, device=exp_pos.device))
-    f = torch.remainder(exp_pos.detach().to(torch.float64) @ inv[:, 0], 1.0)
-    delta = float(cutoff) * float(torch.linalg.norm(inv[:, 0])) + 1e-6
-    lo, hi = rank / world - delta, (rank + 1) / world + delta
-    if hi - lo >= 1.0:
-        return None
-    keep = ((f >= lo) & (f < hi)) | ((f + 1.0 >= lo) & (f + 1.0 < hi)) | ((f - 1.0 >= lo) & (f - 1.0 < hi))
-    return torch.nonzero(keep).flatten()
+def slab_keys(pos_all, own_gid, cell, pbc, cutoff):
+    """Candidate keys of this rank's radius search without expanding the whole system: the periodic
+    images (cell shift k, atom a) whose fractional coordinates lie inside the owned atoms' fractional
+    bounding box widened by the cutoff (as a perpendicular distance per lattice direction, plus a small
+    margin).  Every image within the cutoff of an owned atom is among them.
+
+    Returns ``(index [K'] int64, cell_shift [K'] int64, atom [K'] int64, offsets [K,3] fp32)`` with
+    ``index = k * N + a`` ascending: the order of :func:`~ubio_molfm_b200.graph.expand_pbc`'s images (its
+    compaction keeps this order), so a search over these keys finds the same neighbours in the same
+    order as one over the whole expansion."""
+    dev = pos_all.device
+    n = pos_all.shape[0]
+    cells, offsets = pbc_image_cells(torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff)
+    cell64 = torch.as_tensor(cell, dtype=torch.float64).cpu()
+    inv = torch.linalg.inv(cell64)
+    delta = (float(cutoff) * torch.linalg.norm(inv, dim=0) + 1e-6).to(dev)          # per lattice direction
+    frac = pos_all.detach().to(torch.float64) @ inv.to(dev)                             # [N, 3]
+    own = frac[own_gid]
+    lo, hi = own.min(dim=0).values - delta, own.max(dim=0).values + delta
+    f_img = frac.unsqueeze(0) + cells.to(dev, torch.float64).unsqueeze(1)              # [K, N, 3]
+    inside = ((f_img >= lo) & (f_img <= hi)).all(dim=-1)
+    index = torch.nonzero(inside.reshape(-1)).flatten()
+    return index, index // n, index % n, offsets.to(dev)
 
 
 def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=None):
@@ -156,16 +166,13 @@ def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=N
     own_gid = torch.nonzero(owner == rank).flatten()
     n_own = own_gid.numel()
     p = pos_all.detach().to(torch.float32)
-    exp_pos, outcell_g, image_g = expand_pbc(p, torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff)
-    # candidate keys: the expanded nodes within the cutoff of this slab (periodically), a superset of every
-    # owned atom's neighbours kept in ascending order, so the search sees the same keys in the same order
-    cand = slab_candidates(exp_pos, cell, cutoff, world, rank) if world > 1 else None
-    keys = exp_pos if cand is None else exp_pos[cand]
+    # keys: the images near the owned atoms only (the same neighbours, in the same order, as a search
+    # over the whole system's expansion)
+    _, image_g, outcell_g, offsets = slab_keys(p, own_gid, cell, pbc, cutoff)
+    keys = p[outcell_g] + offsets[image_g]
     g = radius_graph(p[own_gid], keys, torch.tensor([0, n_own]), torch.tensor([0, keys.shape[0]]), cutoff,
                      1e-4, max_neighbors, with_key_csr=False)
-    if cand is not None:
-        g["neighbor_idx"] = cand[g["neighbor_idx"]]
-    used = torch.unique(g["neighbor_idx"])                                   # global expanded nodes (sorted)
+    used = torch.unique(g["neighbor_idx"])                                   # candidate keys used (sorted)
     atoms_needed = torch.unique(outcell_g[used])
     is_own = torch.zeros(pos_all.shape[0], dtype=torch.bool, device=dev)
     is_own[own_gid] = True
@@ -174,9 +181,8 @@ def domain_graph(pos_all, cell, pbc, cutoff, max_neighbors, world, rank, group=N
     local_gid = torch.cat([own_gid, plan.ghost_gid])
     g2l = torch.full((pos_all.shape[0],), -1, dtype=torch.int64, device=dev)
     g2l[local_gid] = torch.arange(local_gid.numel(), device=dev)
-    e2l = torch.full((exp_pos.shape[0],), -1, dtype=torch.int64, device=dev)
+    e2l = torch.full((keys.shape[0],), -1, dtype=torch.int64, device=dev)
     e2l[used] = torch.arange(used.numel(), device=dev)
-    offsets = pbc_image_offsets(torch.as_tensor(cell, dtype=torch.float32), list(pbc), cutoff).to(dev)
     geometry = {
         "outcell": g2l[outcell_g[used]],
         "offsets": offsets[image_g[used]],

@@ -46,6 +46,12 @@ def pbc_image_offsets(cell, pbc, cutoff, num_cell_per_direction=4):
     ``ceil(cutoff / |n_d . a_d|)`` and the fp32 ``offset = n @ cell`` follow module_utils.py:956-999 and
     1092-1104; cells with a non-zero shift along a non-periodic direction are dropped as in 1151-1157.
     """
+    return pbc_image_cells(cell, pbc, cutoff, num_cell_per_direction)[1]
+
+
+def pbc_image_cells(cell, pbc, cutoff, num_cell_per_direction=4):
+    """``(cells [K,3] int64, offsets [K,3] fp32)``: the integer cell shifts n of
+    :func:`pbc_image_offsets` (same order) with their translations ``n @ cell``."""
     cell = torch.as_tensor(cell, dtype=torch.float32).reshape(1, 3, 3).cpu()
     pbc = torch.as_tensor(pbc, dtype=torch.bool).reshape(3).cpu()
     cells = _candidate_cells(num_cell_per_direction)
@@ -66,7 +72,7 @@ def pbc_image_offsets(cell, pbc, cutoff, num_cell_per_direction=4):
     allowed = torch.all(pbc.unsqueeze(0) >= (sel != 0), dim=-1)
     sel = sel[allowed]
     offsets = torch.bmm(sel.to(torch.float32).unsqueeze(0), cell)[0]
-    return offsets.contiguous()
+    return sel.to(torch.int64), offsets.contiguous()
 
 
 def expand_pbc(pos, cell, pbc, cutoff, num_cell_per_direction=4):
