@@ -27,11 +27,20 @@ k_ln_silu_fwd(const float* __restrict__ h, const float* __restrict__ T, const in
   const int lane = threadIdx.x & 31;
   int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // the next row's input is loaded before this row's reductions (one more row of loads in flight)
+  float4 nxt[V];
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) nxt[i] = ldg4(h + r * W + 4 * (lane + 32 * i));
+  }
   for (; r < rows; r += nw) {
     float4 v[V];
-    const float* hr = h + r * W;
 #pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = ldg4(hr + 4 * (lane + 32 * i));
+    for (int i = 0; i < V; ++i) v[i] = nxt[i];
+    if (r + nw < rows) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) nxt[i] = ldg4(h + (r + nw) * W + 4 * (lane + 32 * i));
+    }
     if (T) {
       const float* tr = T + zt[r] * W;
       const float* sr = S + zs[r] * W;
@@ -82,14 +91,38 @@ k_ln_silu_bwd(const float* __restrict__ x, const float* __restrict__ dy, const f
   const int lane = threadIdx.x & 31;
   int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // the next row's operands are loaded before this row's reductions (one more row of loads in flight)
+  float4 nx[V], nd[V];
+  float nmean = 0.f, nrstd = 0.f;
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      nx[i] = ldg4(x + r * W + 4 * (lane + 32 * i));
+      nd[i] = ldg4(dy + r * W + 4 * (lane + 32 * i));
+    }
+    nmean = mean_in[r];
+    nrstd = rstd_in[r];
+  }
   for (; r < rows; r += nw) {
-    const float mean = mean_in[r], rstd = rstd_in[r];
+    const float mean = nmean, rstd = nrstd;
+    float4 cx[V], cd[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) { cx[i] = nx[i]; cd[i] = nd[i]; }
+    if (r + nw < rows) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        nx[i] = ldg4(x + (r + nw) * W + 4 * (lane + 32 * i));
+        nd[i] = ldg4(dy + (r + nw) * W + 4 * (lane + 32 * i));
+      }
+      nmean = mean_in[r + nw];
+      nrstd = rstd_in[r + nw];
+    }
     float4 xh[V], g[V];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const int c = 4 * (lane + 32 * i);
-      const float4 xv = ldg4(x + r * W + c), d = ldg4(dy + r * W + c);
+      const float4 xv = cx[i], d = cd[i];
       const float4 ga = ldg4(gamma + c), be = ldg4(beta + c);
       const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, ds[4] = {d.x, d.y, d.z, d.w};
       const float gs[4] = {ga.x, ga.y, ga.z, ga.w}, bs[4] = {be.x, be.y, be.z, be.w};
