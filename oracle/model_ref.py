@@ -135,7 +135,9 @@ def wigner(pos, jd, l3_sequential, eps=1e-5):
         for _ in range(cnt):
             Wi[:, s:s + 2 * l + 1, s:s + 2 * l + 1] = blocks[l]
             s += 2 * l + 1
-    return W.float(), Wi.transpose(1, 2).contiguous().float()
+    # the reference casts to fp32 for its fp32 model; a float64 caller (second-order checks) keeps float64
+    out = torch.float64 if pos.dtype == torch.float64 else torch.float32
+    return W.to(out), Wi.transpose(1, 2).contiguous().to(out)
 
 
 def gaussian_rbf(dist, nb, cutoff):

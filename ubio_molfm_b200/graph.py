@@ -158,6 +158,9 @@ class _DistFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         vec, dist = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            # create_graph=True: |v| formed again from v so that v/|v| is differentiable in v
+            dist = torch.linalg.vector_norm(vec, dim=-1)
         safe = torch.where(dist > 0, dist, torch.ones_like(dist))
         gv = torch.where((dist > 0).unsqueeze(-1), vec * (g / safe).unsqueeze(-1), torch.zeros_like(vec))
         return gv, None

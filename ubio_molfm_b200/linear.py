@@ -17,6 +17,14 @@ PASSES = 3
 PRESPLIT_WEIGHTS = True
 
 
+def first_order_only(name):
+    """Raise for a second-order (``create_graph=True``) backward through an inference-only fused op: these
+    treat their parameters as constants and have no differentiable backward.  Force-loss training runs the
+    model in training mode, whose ops all have one."""
+    raise RuntimeError(f"{name}: double backward (create_graph=True) is not supported by this eval-mode fused op; "
+                       "put the model in training mode (model.train()) for force-loss training")
+
+
 def split_tf32(b):
     """``b`` (fp32, rows of K) -> (hi, lo) contiguous with hi = tf32(b), lo = tf32(b - hi): the
     pre-split weight operand of the GEMM (one small launch, reused by every product with ``b`` or a
@@ -138,16 +146,27 @@ class _LinearFn(torch.autograd.Function):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
         y = gemm(x2, w, b)
-        ctx.save_for_backward(x2 if w.requires_grad else None, w)
+        ctx.save_for_backward(x if w.requires_grad else None, w)
         ctx.shape = shape
         ctx.has_b = b is not None
         return y.reshape(*shape[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, gy):
-        x2, w = ctx.saved_tensors
+        x, w = ctx.saved_tensors
+        x2 = None if x is None else x.reshape(-1, x.shape[-1])
         g2 = gy.reshape(-1, gy.shape[-1]).contiguous()
         dx = dw = db = None
+        if torch.is_grad_enabled():
+            # create_graph=True: dx through this same tensor-core op (differentiable in g and w), dw / db
+            # as PyTorch products, so the gradients carry their own graph for force-loss training
+            if ctx.needs_input_grad[0]:
+                dx = _LinearFn.apply(g2, w.t(), None).reshape(ctx.shape)
+            if ctx.needs_input_grad[1]:
+                dw = g2.t() @ x2
+            if ctx.has_b and ctx.needs_input_grad[2]:
+                db = g2.sum(0)
+            return dx, dw, db
         if ctx.needs_input_grad[0]:
             dx = gemm(g2, w.t().contiguous()).reshape(ctx.shape)
         if ctx.needs_input_grad[1]:
@@ -174,13 +193,14 @@ class _SO3LinearFn(torch.autograd.Function):
     def forward(ctx, x, w, bias, lidx):
         N, R, C = x.shape
         Co = w.shape[1]
+        x_in = x
         x = x.contiguous()
         out = torch.empty((N, R, Co), device=x.device, dtype=torch.float32)
         whi, wlo = _maybe_split(w)
         for m in range(R):
             gemm(x[:, m, :], w[lidx[m]], bias if (m == 0 and bias is not None) else None, out=out[:, m, :],
                  b_split=(whi[lidx[m]], wlo[lidx[m]]))
-        ctx.save_for_backward(x if w.requires_grad else None, w)
+        ctx.save_for_backward(x_in if w.requires_grad else None, w)
         ctx.lidx = lidx
         ctx.has_bias = bias is not None
         return out
@@ -192,6 +212,17 @@ class _SO3LinearFn(torch.autograd.Function):
         N, R, Co = g.shape
         C = w.shape[2]
         dx = dw = db = None
+        if torch.is_grad_enabled():
+            # create_graph=True: the same strided op with W^T for dx, PyTorch products for dW
+            if ctx.needs_input_grad[0]:
+                dx = _SO3LinearFn.apply(g, w.transpose(1, 2).contiguous(), None, ctx.lidx)
+            if ctx.needs_input_grad[1]:
+                x = x.float()
+                dw = torch.stack([sum(g[:, m, :].t() @ x[:, m, :] for m in range(R) if ctx.lidx[m] == l)
+                                  if l in ctx.lidx else torch.zeros_like(w[l]) for l in range(w.shape[0])])
+            if ctx.has_bias and ctx.needs_input_grad[2]:
+                db = g[:, 0, :].sum(0)
+            return dx, dw, db, None
         if ctx.needs_input_grad[0]:
             wt = w.transpose(1, 2).contiguous()  # [L, C, Co]
             thi, tlo = _maybe_split(wt)
@@ -234,6 +265,8 @@ class _LnSiluFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
+        if torch.is_grad_enabled():
+            first_order_only("ln_silu")
         lib = _lib.load()
         x, gamma, beta, mean, rstd = ctx.saved_tensors
         dy = dy.contiguous()
@@ -308,6 +341,8 @@ class _SO3PairProdFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, G):
+        if torch.is_grad_enabled():
+            first_order_only("so3_pair_product")
         lib = _lib.load()
         t0, w12, b12 = ctx.saved_tensors
         if ctx.recompute:
@@ -371,6 +406,7 @@ class _NodeApplyFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, A, h, mode):
         lib = _lib.load()
+        A_in, h_in = A, h
         A = A.contiguous()
         n, KO, KI = A.shape
         C = h.shape[2]
@@ -388,7 +424,8 @@ class _NodeApplyFn(torch.autograd.Function):
             out = torch.empty((n, rows, C), device=dev, dtype=torch.float32)
             check(lib.e2a_node_apply_fwd(ptr(A), ptr(h), h.stride(0), None, 0, n, KO, KI, C, ptr(out), out.stride(0),
                                          1 if mode == "merge" else 0, stream_of(dev)), "e2a_node_apply_fwd")
-        ctx.save_for_backward(A, h)
+            h = h_in
+        ctx.save_for_backward(A_in, h)
         ctx.mode = mode
         return out
 
@@ -396,6 +433,22 @@ class _NodeApplyFn(torch.autograd.Function):
     def backward(ctx, g):
         lib = _lib.load()
         A, h = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            # create_graph=True: the bilinear map's gradients as batched products that carry their own graph
+            if ctx.mode == "sub":
+                first_order_only("node_apply(mode='sub')")
+            KO = A.shape[1]
+            gp = g[:, :KO]
+            dA = torch.bmm(gp, h.transpose(1, 2)) if ctx.needs_input_grad[0] else None
+            dh = None
+            if ctx.needs_input_grad[1]:
+                dh = torch.bmm(A.transpose(1, 2), gp)
+                if ctx.mode == "merge":
+                    dh = dh + g[:, KO:]
+            return dA, dh, None
+        A = A.contiguous()
+        if h.stride(2) != 1 or h.stride(1) != h.shape[2]:
+            h = h.contiguous()
         g = g.contiguous()
         n, KO, KI = A.shape
         C = h.shape[2]
@@ -445,6 +498,8 @@ class _RowBlockLinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            first_order_only("rowblock_linear")
         lib = _lib.load()
         g = g.contiguous()
         n, R, C, out_rows, Co = ctx.shape
@@ -491,6 +546,8 @@ class _RmsNormFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            first_order_only("rms_norm")
         lib = _lib.load()
         x, w, stats = ctx.saved_tensors
         g = g.contiguous()
@@ -525,6 +582,8 @@ class _GateFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            first_order_only("gate")
         lib = _lib.load()
         s, h = ctx.saved_tensors
         g = g.contiguous()
@@ -579,6 +638,8 @@ class _RbfLinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            first_order_only("rbf_linear")
         lib = _lib.load()
         d, mu, w = ctx.saved_tensors
         g = g.contiguous()
@@ -654,6 +715,8 @@ class _NodeMapFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            first_order_only("node_map_from_pos")
         lib = _lib.load()
         (p,) = ctx.saved_tensors
         g = g.contiguous()

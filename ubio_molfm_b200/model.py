@@ -516,11 +516,20 @@ class E2FormerPotential(nn.Module):
         return g, pbc_any
 
     def forward(self, pos, atomic_numbers, cell=None, pbc=(False, False, False), batch=None, need_forces=True,
-                charge=None, multiplicity=None):
+                charge=None, multiplicity=None, create_graph=None):
         """``charge`` / ``multiplicity``: per-system integers ([B] or None).  Given (as the reference's
         interface always does, interface/data_utils.py:53-65), their system embedding is added to the
         normed l=0 row of every block; None evaluates the decoder without it (e2former_wrapper.py:249-250
-        with no ``charge`` key).  ``multiplicity`` defaults to 1 when only ``charge`` is given."""
+        with no ``charge`` key).  ``multiplicity`` defaults to 1 when only ``charge`` is given.
+
+        ``create_graph`` (default: ``self.training``, as pipeline/head.py:318-325 takes the force gradient):
+        the forces keep their graph and the energy is not detached, so a loss on both can be
+        back-propagated to the parameters (force-loss training; training mode only)."""
+        if create_graph is None:
+            create_graph = self.training and need_forces
+        if create_graph and not self.training:
+            raise RuntimeError("create_graph=True needs training mode (model.train()): the eval-mode fused "
+                               "ops are first-order only")
         pos = pos.detach().to(torch.float32).requires_grad_(need_forces)
         with torch.enable_grad() if need_forces else torch.no_grad():
             g, pbc_any = self.build_graph(pos, cell, pbc, batch)
@@ -541,8 +550,8 @@ class E2FormerPotential(nn.Module):
                 energy = energy.index_add(0, batch, e_atom)
             forces = None
             if need_forces:
-                (grad,) = torch.autograd.grad(energy.sum(), pos)
+                (grad,) = torch.autograd.grad(energy.sum(), pos, create_graph=create_graph)
                 forces = -grad
         if pos.is_cuda and self.check_device_status:
             _lib.raise_on_device_status(pos.device)
-        return energy.detach(), forces
+        return (energy if create_graph else energy.detach()), forces

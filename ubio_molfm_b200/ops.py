@@ -112,13 +112,19 @@ class SparseQKEdgeIndexFn(torch.autograd.Function):
         q, k = _f32(query), _f32(key)
         E = md[1].numel()
         out = _qk_forward(q, k, md, E)
-        ctx.save_for_backward(q, k, *md)
+        ctx.save_for_backward(query, key, *md)
         ctx.dtypes = (query.dtype, key.dtype)
         return out.to(query.dtype)
 
     @staticmethod
     def backward(ctx, g):
         q, k, *md = ctx.saved_tensors
+        q, k = _f32(q), _f32(k)
+        if torch.is_grad_enabled():
+            # create_graph=True: the backward is itself a differentiable op
+            # (SparseQKEdgeIndex_Fn.backward -> SparseQKEdgeBackward_Fn, triton_sparse_qk_autograd.py:725-740).
+            dq, dk = SparseQKEdgeBackwardFn.apply(g, q, k, tuple(md))
+            return dq.to(ctx.dtypes[0]), dk.to(ctx.dtypes[1]), None
         g = _f32(g)
         dq = dk = None
         if ctx.needs_input_grad[0]:
@@ -126,6 +132,42 @@ class SparseQKEdgeIndexFn(torch.autograd.Function):
         if ctx.needs_input_grad[1]:
             dk = _grouped_reduce(g, q, md[3], md[4], md[5], k.shape[0]).to(ctx.dtypes[1])
         return dq, dk, None
+
+
+class SparseQKEdgeBackwardFn(torch.autograd.Function):
+    """``(dq, dk) = backward of sparse_qk(q, k)`` at upstream gradient ``g`` as an op of its own, so that
+    force-loss training can differentiate it (triton_sparse_qk_autograd.py:754-836).
+
+    Both outputs are bilinear: ``dq = G_q(g, k)`` and ``dk = G_k(g, q)``, grouped reductions over the
+    query- and key-CSR.  Their gradients therefore reuse the same two kernels:
+    ``d g = qk(gg_dq, k) + qk(q, gg_dk)``, ``d q = G_q(g, gg_dk)``, ``d k = G_k(g, gg_dq)``."""
+
+    @staticmethod
+    def forward(ctx, g, q, k, md):
+        g = _f32(g)
+        dq = _grouped_reduce(g, k, md[0], md[1], md[2], q.shape[0])
+        dk = _grouped_reduce(g, q, md[3], md[4], md[5], k.shape[0])
+        ctx.save_for_backward(g, q, k, *md)
+        return dq, dk
+
+    @staticmethod
+    def backward(ctx, gg_dq, gg_dk):
+        g, q, k, *md = ctx.saved_tensors
+        E = g.shape[0]
+        d_g = d_q = d_k = None
+        gg_dq = None if gg_dq is None else _f32(gg_dq)
+        gg_dk = None if gg_dk is None else _f32(gg_dk)
+        if ctx.needs_input_grad[0]:
+            d_g = torch.zeros_like(g)
+            if gg_dq is not None:
+                d_g += _qk_forward(gg_dq, k, md, E)
+            if gg_dk is not None:
+                d_g += _qk_forward(q, gg_dk, md, E)
+        if ctx.needs_input_grad[1] and gg_dk is not None:
+            d_q = _grouped_reduce(g, gg_dk, md[0], md[1], md[2], q.shape[0])
+        if ctx.needs_input_grad[2] and gg_dq is not None:
+            d_k = _grouped_reduce(g, gg_dq, md[3], md[4], md[5], k.shape[0])
+        return d_g, d_q, d_k, None
 
 
 def sparse_qk_edge_index(query, key, query_index, neighbor_index, metadata=None):
@@ -150,26 +192,56 @@ def prepare_sparse_alpha_sum_edge_index_metadata(query_index, num_queries):
 class SparseAlphaSumFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, alpha, query_index, row_ptr, perm, num_queries):
-        lib = _lib.load()
         a = _f32(alpha)
-        H = a.shape[1]
-        out = torch.empty((num_queries, H), device=a.device, dtype=torch.float32)
-        check(lib.e2a_alpha_sum_fwd(ptr(a), ptr(row_ptr), ptr(perm), num_queries, H, ptr(out), stream_of(a.device)),
-              "e2a_alpha_sum_fwd")
-        ctx.save_for_backward(_i32(query_index))
+        out = _alpha_sum(a, row_ptr, perm, num_queries)
+        ctx.save_for_backward(_i32(query_index), row_ptr, perm)
         ctx.shape = a.shape
         ctx.dtype = alpha.dtype
         return out.to(alpha.dtype)
 
     @staticmethod
     def backward(ctx, g):
-        (qi,) = ctx.saved_tensors
-        lib = _lib.load()
-        g = _f32(g)
-        E, H = ctx.shape
-        ga = torch.empty((E, H), device=g.device, dtype=torch.float32)
-        check(lib.e2a_alpha_sum_bwd(ptr(g), ptr(qi), E, H, ptr(ga), stream_of(g.device)), "e2a_alpha_sum_bwd")
+        qi, row_ptr, perm = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            # sparse_alpha_sum_edge_index_autograd.py:145-155 (SparseAlphaSumEdgeIndexBackwardFn)
+            ga = SparseAlphaSumBackwardFn.apply(g, qi, row_ptr, perm, ctx.shape)
+        else:
+            ga = _alpha_gather(_f32(g), qi, ctx.shape)
         return ga.to(ctx.dtype), None, None, None, None
+
+
+def _alpha_gather(g, qi, shape):
+    lib = _lib.load()
+    E, H = shape
+    ga = torch.empty((E, H), device=g.device, dtype=torch.float32)
+    check(lib.e2a_alpha_sum_bwd(ptr(g), ptr(qi), E, H, ptr(ga), stream_of(g.device)), "e2a_alpha_sum_bwd")
+    return ga
+
+
+def _alpha_sum(a, row_ptr, perm, num_queries):
+    lib = _lib.load()
+    H = a.shape[1]
+    out = torch.empty((num_queries, H), device=a.device, dtype=torch.float32)
+    check(lib.e2a_alpha_sum_fwd(ptr(a), ptr(row_ptr), ptr(perm), num_queries, H, ptr(out), stream_of(a.device)),
+          "e2a_alpha_sum_fwd")
+    return out
+
+
+class SparseAlphaSumBackwardFn(torch.autograd.Function):
+    """The alpha-sum backward (``ga[e] = g[query_index[e]]``, a gather) as a differentiable op; its
+    gradient is the segmented sum again (sparse_alpha_sum_edge_index_autograd.py:173-208)."""
+
+    @staticmethod
+    def forward(ctx, g, qi, row_ptr, perm, shape):
+        ctx.save_for_backward(row_ptr, perm)
+        ctx.rows = g.shape[0]
+        return _alpha_gather(_f32(g), qi, shape)
+
+    @staticmethod
+    def backward(ctx, gg):
+        row_ptr, perm = ctx.saved_tensors
+        d_g = _alpha_sum(_f32(gg), row_ptr, perm, ctx.rows) if ctx.needs_input_grad[0] else None
+        return d_g, None, None, None, None
 
 
 def sparse_alpha_sum_edge_index(alpha, query_index, num_queries, metadata=None):
@@ -184,38 +256,92 @@ def sparse_alpha_sum_edge_index(alpha, query_index, num_queries, metadata=None):
 # ------------------------------------------------------------------------------------------------
 # sparse_v_agg_edge_index_cblocked  (sparse_v_agg_edge_index_cblocked_bench.py:428-449)
 # ------------------------------------------------------------------------------------------------
+def _v_agg(v, a, md, num_queries):
+    """``out[n, c, h] = sum_{e in row n} a[e, h] * v[key_e, c, h]`` over the query-CSR."""
+    lib = _lib.load()
+    M, C, H = v.shape
+    out = torch.empty((num_queries, C, H), device=v.device, dtype=torch.float32)
+    check(lib.e2a_v_agg_fwd(ptr(v), ptr(a), ptr(md[0]), ptr(md[1]), ptr(md[2]), num_queries, C, H, ptr(out),
+                            stream_of(v.device)), "e2a_v_agg_fwd")
+    return out
+
+
+def _v_agg_dvalue(a, g, md, M):
+    """``dv[m, c, h] = sum_{e with key m} a[e, h] * g[query_e, c, h]`` over the key-CSR."""
+    lib = _lib.load()
+    _, C, H = g.shape
+    dv = torch.empty((M, C, H), device=g.device, dtype=torch.float32)
+    check(lib.e2a_v_agg_bwd_value(ptr(a), ptr(g), ptr(md[3]), ptr(md[4]), ptr(md[5]), M, C, H, ptr(dv),
+                                  stream_of(g.device)), "e2a_v_agg_bwd_value")
+    return dv
+
+
+def _v_agg_dalpha(g, v, md):
+    """``da[e, h] = sum_c g[query_e, c, h] * v[key_e, c, h]``."""
+    lib = _lib.load()
+    N, C, H = g.shape
+    da = torch.empty((md[1].numel(), H), device=g.device, dtype=torch.float32)
+    check(lib.e2a_v_agg_bwd_alpha(ptr(g), ptr(v), ptr(md[0]), ptr(md[1]), ptr(md[2]), N, C, H, ptr(da),
+                                  stream_of(g.device)), "e2a_v_agg_bwd_alpha")
+    return da
+
+
 class SparseVAggFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, value, alpha, md, num_queries):
-        lib = _lib.load()
-        v, a = _f32(value), _f32(alpha)
-        M, C, H = v.shape
-        out = torch.empty((num_queries, C, H), device=v.device, dtype=torch.float32)
-        check(lib.e2a_v_agg_fwd(ptr(v), ptr(a), ptr(md[0]), ptr(md[1]), ptr(md[2]), num_queries, C, H, ptr(out),
-                                stream_of(v.device)), "e2a_v_agg_fwd")
-        ctx.save_for_backward(v, a, *md)
+        out = _v_agg(_f32(value), _f32(alpha), md, num_queries)
+        ctx.save_for_backward(value, alpha, *md)
         ctx.dtypes = (value.dtype, alpha.dtype)
         return out.to(value.dtype)
 
     @staticmethod
     def backward(ctx, g):
         v, a, *md = ctx.saved_tensors
-        lib = _lib.load()
+        v, a = _f32(v), _f32(a)
+        if torch.is_grad_enabled():
+            # sparse_v_agg_edge_index_cblocked_bench.py:334-347 (SparseVAggEdgeIndexCBlocked_Backward_Fn)
+            dv, da = SparseVAggBackwardFn.apply(g, v, a, tuple(md))
+            return dv.to(ctx.dtypes[0]), da.to(ctx.dtypes[1]), None, None
         g = _f32(g)
-        M, C, H = v.shape
-        N = g.shape[0]
         dv = da = None
         if ctx.needs_input_grad[0]:
-            dv = torch.empty_like(v)
-            check(lib.e2a_v_agg_bwd_value(ptr(a), ptr(g), ptr(md[3]), ptr(md[4]), ptr(md[5]), M, C, H, ptr(dv),
-                                          stream_of(g.device)), "e2a_v_agg_bwd_value")
-            dv = dv.to(ctx.dtypes[0])
+            dv = _v_agg_dvalue(a, g, md, v.shape[0]).to(ctx.dtypes[0])
         if ctx.needs_input_grad[1]:
-            da = torch.empty_like(a)
-            check(lib.e2a_v_agg_bwd_alpha(ptr(g), ptr(v), ptr(md[0]), ptr(md[1]), ptr(md[2]), N, C, H, ptr(da),
-                                          stream_of(g.device)), "e2a_v_agg_bwd_alpha")
-            da = da.to(ctx.dtypes[1])
+            da = _v_agg_dalpha(g, v, md).to(ctx.dtypes[1])
         return dv, da, None, None
+
+
+class SparseVAggBackwardFn(torch.autograd.Function):
+    """``(dv, da)`` of the value aggregation as a differentiable op
+    (sparse_v_agg_edge_index_cblocked_bench.py:361-420).  ``dv`` is bilinear in ``(a, g)`` and ``da`` in
+    ``(g, v)``, so the second-order terms are the same three kernels with other operands:
+    ``d g = agg(gg_dv, a) + agg(v, gg_da)``, ``d v = dvalue(gg_da, g)``, ``d a = dalpha(g, gg_dv)``."""
+
+    @staticmethod
+    def forward(ctx, g, v, a, md):
+        g = _f32(g)
+        dv = _v_agg_dvalue(a, g, md, v.shape[0])
+        da = _v_agg_dalpha(g, v, md)
+        ctx.save_for_backward(g, v, a, *md)
+        return dv, da
+
+    @staticmethod
+    def backward(ctx, gg_dv, gg_da):
+        g, v, a, *md = ctx.saved_tensors
+        gg_dv = None if gg_dv is None else _f32(gg_dv)
+        gg_da = None if gg_da is None else _f32(gg_da)
+        d_g = d_v = d_a = None
+        if ctx.needs_input_grad[0]:
+            d_g = torch.zeros_like(g)
+            if gg_dv is not None:
+                d_g += _v_agg(gg_dv, a, md, g.shape[0])
+            if gg_da is not None:
+                d_g += _v_agg(v, gg_da, md, g.shape[0])
+        if ctx.needs_input_grad[1] and gg_da is not None:
+            d_v = _v_agg_dvalue(gg_da, g, md, v.shape[0])
+        if ctx.needs_input_grad[2] and gg_dv is not None:
+            d_a = _v_agg_dalpha(g, gg_dv, md)
+        return d_g, d_v, d_a, None
 
 
 def sparse_v_agg_edge_index_cblocked(value, alpha, query_index, value_index, num_queries, metadata=None):
@@ -234,34 +360,80 @@ def sparse_v_agg_edge_index_cblocked(value, alpha, query_index, value_index, num
 # ------------------------------------------------------------------------------------------------
 # edge_degree_outer  (edge_degree_outer_autograd.py:348-375)
 # ------------------------------------------------------------------------------------------------
+def _edge_outer(sh, fea, row_ptr, perm, num_queries):
+    lib = _lib.load()
+    E, L = sh.shape
+    F = fea.shape[1]
+    out = torch.empty((num_queries, L, F), device=sh.device, dtype=torch.float32)
+    check(lib.e2a_edge_outer_fwd(ptr(sh), ptr(fea), ptr(row_ptr), ptr(perm), num_queries, L, F, ptr(out),
+                                 stream_of(sh.device)), "e2a_edge_outer_fwd")
+    return out
+
+
+def _edge_outer_bwd(g, sh, fea, qi, want_sh, want_fea):
+    """``d_sh[e, l] = sum_f g[q_e, l, f] fea[e, f]`` and ``d_fea[e, f] = sum_l g[q_e, l, f] sh[e, l]``
+    (either may be skipped; a skipped one's other operand is not read)."""
+    lib = _lib.load()
+    E, L = sh.shape
+    F = g.shape[2]
+    dsh = torch.empty((E, L), device=g.device, dtype=torch.float32) if want_sh else None
+    dfea = torch.empty((E, F), device=g.device, dtype=torch.float32) if want_fea else None
+    if dsh is not None or dfea is not None:
+        check(lib.e2a_edge_outer_bwd(ptr(g), ptr(sh), ptr(fea), ptr(qi), E, L, F, ptr(dsh), ptr(dfea),
+                                     stream_of(g.device)), "e2a_edge_outer_bwd")
+    return dsh, dfea
+
+
 class EdgeDegreeOuterFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, edge_sh, edge_fea, query_index, row_ptr, perm, num_queries):
-        lib = _lib.load()
-        sh, fea = _f32(edge_sh), _f32(edge_fea)
-        E, L = sh.shape
-        F = fea.shape[1]
-        out = torch.empty((num_queries, L, F), device=sh.device, dtype=torch.float32)
-        check(lib.e2a_edge_outer_fwd(ptr(sh), ptr(fea), ptr(row_ptr), ptr(perm), num_queries, L, F, ptr(out),
-                                     stream_of(sh.device)), "e2a_edge_outer_fwd")
-        ctx.save_for_backward(sh, fea, _i32(query_index))
+        out = _edge_outer(_f32(edge_sh), _f32(edge_fea), row_ptr, perm, num_queries)
+        ctx.save_for_backward(edge_sh, edge_fea, _i32(query_index), row_ptr, perm)
         ctx.dtypes = (edge_sh.dtype, edge_fea.dtype)
         return out.to(edge_fea.dtype)
 
     @staticmethod
     def backward(ctx, g):
-        sh, fea, qi = ctx.saved_tensors
-        lib = _lib.load()
-        g = _f32(g)
-        E, L = sh.shape
-        F = fea.shape[1]
-        dsh = torch.empty_like(sh) if ctx.needs_input_grad[0] else None
-        dfea = torch.empty_like(fea) if ctx.needs_input_grad[1] else None
-        if dsh is not None or dfea is not None:
-            check(lib.e2a_edge_outer_bwd(ptr(g), ptr(sh), ptr(fea), ptr(qi), E, L, F, ptr(dsh), ptr(dfea),
-                                         stream_of(g.device)), "e2a_edge_outer_bwd")
+        sh, fea, qi, row_ptr, perm = ctx.saved_tensors
+        sh, fea = _f32(sh), _f32(fea)
+        if torch.is_grad_enabled():
+            # edge_degree_outer_autograd.py:316-325 (EdgeDegreeOuterBackward_Fn)
+            dsh, dfea = EdgeDegreeOuterBackwardFn.apply(g, sh, fea, qi, row_ptr, perm)
+        else:
+            dsh, dfea = _edge_outer_bwd(_f32(g), sh, fea, qi, ctx.needs_input_grad[0], ctx.needs_input_grad[1])
         return (None if dsh is None else dsh.to(ctx.dtypes[0]), None if dfea is None else dfea.to(ctx.dtypes[1]),
                 None, None, None, None)
+
+
+class EdgeDegreeOuterBackwardFn(torch.autograd.Function):
+    """``(d_sh, d_fea)`` of the edge-degree outer product as a differentiable op
+    (edge_degree_outer_autograd.py:259-296): ``d g = outer(gg_dsh, fea) + outer(sh, gg_dfea)``,
+    ``d sh = d_sh-kernel(g, gg_dfea)``, ``d fea = d_fea-kernel(g, gg_dsh)``."""
+
+    @staticmethod
+    def forward(ctx, g, sh, fea, qi, row_ptr, perm):
+        g = _f32(g)
+        dsh, dfea = _edge_outer_bwd(g, sh, fea, qi, True, True)
+        ctx.save_for_backward(g, sh, fea, qi, row_ptr, perm)
+        return dsh, dfea
+
+    @staticmethod
+    def backward(ctx, gg_dsh, gg_dfea):
+        g, sh, fea, qi, row_ptr, perm = ctx.saved_tensors
+        gg_dsh = None if gg_dsh is None else _f32(gg_dsh)
+        gg_dfea = None if gg_dfea is None else _f32(gg_dfea)
+        d_g = d_sh = d_fea = None
+        if ctx.needs_input_grad[0]:
+            d_g = torch.zeros_like(g)
+            if gg_dsh is not None:
+                d_g += _edge_outer(gg_dsh, fea, row_ptr, perm, g.shape[0])
+            if gg_dfea is not None:
+                d_g += _edge_outer(sh, gg_dfea, row_ptr, perm, g.shape[0])
+        if ctx.needs_input_grad[1] and gg_dfea is not None:
+            d_sh = _edge_outer_bwd(g, sh, gg_dfea, qi, True, False)[0]
+        if ctx.needs_input_grad[2] and gg_dsh is not None:
+            d_fea = _edge_outer_bwd(g, gg_dsh, fea, qi, False, True)[1]
+        return d_g, d_sh, d_fea, None, None, None
 
 
 def edge_degree_outer(edge_sh, edge_fea, query_index, num_queries, metadata=None):
@@ -300,6 +472,7 @@ class AttnSpanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, key, value, edge_gate, poly, dist, md, row_order, key_order, keep_logits=False):
         lib = _lib.load()
+        q_in, key_in, value_in, edge_gate_in, poly_in, dist_in = q, key, value, edge_gate, poly, dist
         q, key, value = _f32(q), _f32(key), _f32(value)
         edge_gate, poly, dist = _f32(edge_gate), _f32(poly), _f32(dist)
         N, H, D = q.shape
@@ -323,11 +496,14 @@ class AttnSpanFn(torch.autograd.Function):
         TIMER.stop(tok)
         ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order,
                               *md)
+        ctx.inputs = (q_in, key_in, value_in, edge_gate_in, poly_in, dist_in)
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order, *md = ctx.saved_tensors
+        if torch.is_grad_enabled():
+            return _span_double_backward(ctx, dout, md)
         lib = _lib.load()
         dout = _f32(dout)
         N, H, D = q.shape
@@ -384,6 +560,45 @@ class AttnSpanFn(torch.autograd.Function):
                                    ptr(key_order), N, M, E, H, D, C, ptr(d_k), ptr(d_v), st), "e2a_attn_bwd_key")
         TIMER.stop(tok)
         return d_q, d_k, d_v, d_gate, d_poly, d_dist, None, None, None, None
+
+
+def _span_composite(q, key, value, edge_gate, poly, dist, md, N):
+    """The span as a chain of differentiable ops -- the kernel-level q.k and value-aggregation ops (each with
+    its own double backward) around the gated segmented softmax in PyTorch elementwise / scatter ops,
+    written as the reference writes it (e2former.py:311-364, 422), including its ``amax`` reduction."""
+    H = q.shape[1]
+    rows = torch.repeat_interleave(torch.arange(N, device=q.device), (md[0][1:] - md[0][:-1]).long())
+    qi = torch.empty_like(rows)
+    qi[md[2].long()] = rows                                   # query row of each edge id
+    gate, inputhead = edge_gate[:, :H], edge_gate[:, H:]
+    alpha = gate * SparseQKEdgeIndexFn.apply(q, key, md)
+    idx = qi.unsqueeze(-1).expand(-1, H)
+    amax = torch.full((N, H), -torch.inf, device=q.device, dtype=alpha.dtype)
+    amax = amax.scatter_reduce(0, idx, alpha, reduce="amax", include_self=True)
+    alpha = torch.exp(alpha - amax[qi]) * poly.unsqueeze(-1)
+    asum = torch.zeros((N, H), device=q.device, dtype=alpha.dtype).scatter_add(0, idx, alpha)
+    alpha = alpha * inputhead / (asum[qi] + 1e-3)
+    alpha = alpha / dist.unsqueeze(-1).clamp_min(1e-6)
+    return SparseVAggFn.apply(value, alpha, md, N)
+
+
+def _span_double_backward(ctx, dout, md):
+    """Backward of :class:`AttnSpanFn` under ``create_graph=True`` (force-loss training): the span is formed
+    again from :func:`_span_composite` and differentiated with a graph, so the returned gradients are
+    themselves differentiable in the inputs and in ``dout``.  The first-order values equal the fused
+    kernels' up to fp32 rounding; the fused kernels keep serving every first-order backward."""
+    ins = ctx.inputs
+    need = [bool(n) for n in ctx.needs_input_grad[:6]]
+    with torch.enable_grad():
+        # one fresh view per input: the inputs may depend on one another (poly and the radial gate are
+        # functions of dist), and a gradient w.r.t. the tensors themselves would be the total derivative
+        f32 = [t.contiguous().to(torch.float32).view_as(t) for t in ins]
+        out = _span_composite(*f32, tuple(md), int(ctx.inputs[0].shape[0]))
+        wrt = [t for t, n in zip(f32, need) if n]
+        got = iter(torch.autograd.grad(out, wrt, dout, create_graph=True, allow_unused=True))
+    grads = [next(got) if n else None for n in need]
+    grads = [None if g is None else g.to(t.dtype) for g, t in zip(grads, ins)]
+    return (*grads, None, None, None, None)
 
 
 def span_keeps_logits(H, D):
