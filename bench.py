@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--molecules", type=int, default=4096, help="molecules workload: batch size")
     ap.add_argument("--atoms", type=int, default=100_000, help="layer workload: atoms")
     ap.add_argument("--k", type=int, default=32)
+    ap.add_argument("--edge-chunk", type=int, default=None,
+                    help="layer workload: run the edge side in checkpointed row blocks of about this many edges "
+                         "(the radial basis is then formed inside its GEMM, not a leaf)")
     ap.add_argument("--cpu-atoms", type=int, default=None,
                     help="CPU baseline sample size (default 500 for the model, 1500 for the layer)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -105,6 +108,8 @@ def config_dict(args, E=None, N2=None, extra=None):
          "atoms_per_rank": args.atoms, "k_avg": args.k, "irreps": f"{C_CH}x0e+{C_CH}x1e+{C_CH}x2e",
          "heads": HEADS, "attn_scalar_head": DHEAD, "irreps_head": HEAD_IRREPS, "rbf": NB, "cutoff": CUTOFF,
          "l2": "inputs larger than L2 (value rows alone are GBs)", "parallelism": f"replicas x{args.gpus}"}
+    if getattr(args, "edge_chunk", None):
+        d["edge_chunk"] = args.edge_chunk
     if E is not None:
         d["edges_per_rank"] = E
         d["expanded_nodes_per_rank"] = N2
@@ -125,7 +130,7 @@ def make_layer(dev, seed=0):
     return layer.to(dev).eval()
 
 
-def build_inputs(pos, Z, cell, dev, layer):
+def build_inputs(pos, Z, cell, dev, layer, materialize_rbf=True):
     """Graph + per-node geometry for one periodic system (all on ``dev``)."""
     from ubio_molfm_b200.graph import expand_pbc, radius_graph
     from ubio_molfm_b200.nn import GaussianSmearing
@@ -136,7 +141,8 @@ def build_inputs(pos, Z, cell, dev, layer):
     g = radius_graph(pos, exp_pos, torch.tensor([0, N]), torch.tensor([0, exp_pos.shape[0]]), CUTOFF, 1e-4, None)
     W, Wi = node_wigner(pos)
     We, Wie = node_wigner(exp_pos)
-    rbf = GaussianSmearing(NB, cutoff=CUTOFF).to(dev)(g["f_dist"])
+    smear = GaussianSmearing(NB, cutoff=CUTOFF).to(dev)
+    rbf = smear(g["f_dist"]) if materialize_rbf else smear
     bd = dict(g)
     bd.update({"f_outcell_index": outcell, "f_exp_node_pos": exp_pos, "wigner": W, "wigner_inv": Wi,
                "wigner_exp": We, "wigner_inv_exp": Wie})
@@ -365,23 +371,32 @@ def run_ours(args, ws, rank, local):
     pos_np, Z_np, cell = uniform_box(args.atoms, args.k, CUTOFF, seed=100 + rank)
     pos = torch.tensor(pos_np, dtype=torch.float32, device=dev)
     Z = torch.tensor(Z_np, device=dev)
-    bd, rbf = build_inputs(pos, Z, cell, dev, layer)
+    chunked = bool(args.edge_chunk)
+    bd, rbf = build_inputs(pos, Z, cell, dev, layer, materialize_rbf=not chunked)
     N, N2, E = args.atoms, bd["f_outcell_index"].shape[0], bd["query_idx"].numel()
     g = torch.Generator(device=dev).manual_seed(rank)
     x = torch.randn(N, 9, C_CH, device=dev, generator=g)
     dout = torch.randn(N, 9, C_CH, device=dev, generator=g)
     # leaves: everything the forces chain differentiates through
-    leaf = {k: v.detach().requires_grad_(True) for k, v in
-            {"x": x, "pos": pos, "f_dist": bd["f_dist"], "poly": bd["f_poly_dist"], "rbf": rbf,
-             "exp": bd["f_exp_node_pos"], "W": bd["wigner"], "Wi": bd["wigner_inv"], "We": bd["wigner_exp"],
-             "Wie": bd["wigner_inv_exp"]}.items()}
+    base = {"x": x, "pos": pos, "f_dist": bd["f_dist"], "poly": bd["f_poly_dist"], "exp": bd["f_exp_node_pos"],
+            "W": bd["wigner"], "Wi": bd["wigner_inv"], "We": bd["wigner_exp"], "Wie": bd["wigner_inv_exp"]}
+    if not chunked:
+        base["rbf"] = rbf
+    leaf = {k: v.detach().requires_grad_(True) for k, v in base.items()}
     bdl = dict(bd)
     bdl.update({"f_dist": leaf["f_dist"], "f_poly_dist": leaf["poly"], "f_exp_node_pos": leaf["exp"],
                 "wigner": leaf["W"], "wigner_inv": leaf["Wi"], "wigner_exp": leaf["We"], "wigner_inv_exp": leaf["Wie"]})
     leaves = list(leaf.values())
+    if chunked:
+        from ubio_molfm_b200.nn import RbfSpec
+        # the memory mode: edge side in checkpointed row blocks, Q / K projections formed again in the backward
+        layer.edge_chunk = args.edge_chunk
+        layer.query_linear.recompute_pair_product = True
+        layer.key_linear.recompute_pair_product = True
 
     def step():
-        return layer_step(layer, leaf["pos"], leaf["x"], Z, bdl, leaf["rbf"], dout, leaves)
+        aw = RbfSpec(leaf["f_dist"], rbf.offset, rbf.coeff) if chunked else leaf["rbf"]
+        return layer_step(layer, leaf["pos"], leaf["x"], Z, bdl, aw, dout, leaves)
 
     for _ in range(args.warmup):
         step()
@@ -413,15 +428,19 @@ def run_ours(args, ws, rank, local):
     alg = {"e2a_attn_fwd": fwd_algorithmic_bytes, "e2a_attn_bwd_query": bwdq_algorithmic_bytes,
            "e2a_attn_bwd_key": bwdk_algorithmic_bytes, "e2a_attn_bwd_value": bwdv_algorithmic_bytes,
            "e2a_attn_bwd_softmax": bwds_algorithmic_bytes, "e2a_attn_bwd_dk": bwddk_algorithmic_bytes}[name](N, N2, E)
+    # in row blocks each launch covers one block: its share of the graph's bytes (the key-table term split
+    # evenly, which undercounts the key rows a block reads)
+    blocks = len(layer._edge_chunks(dict(bdl), N) or [None]) if chunked else 1
+    alg = alg / blocks
     per_launch_ms = tot / nl
     peak, peak_kind = measured_peaks()
     achieved = alg / (per_launch_ms * 1e-3) / 1e9
     roof = {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_kind,
             "traffic": (MEASURED_TRAFFIC_DEFAULT.get(name)
-                        if (args.atoms, args.k) == (100_000, 32) else None),
-            "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4),
-            "kernels_ms_per_step": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
+                        if (args.atoms, args.k) == (100_000, 32) and not chunked else None),
+            "algorithmic_bytes_per_launch": alg, "launch_ms": round(per_launch_ms, 4), "edge_blocks": blocks,
+            "kernels_ms_per_launch": {k: round(v[1] / v[0], 4) for k, v in kern.items()},
             "step_share": {k: round(v[1] / args.steps / ms, 4) for k, v in kern.items()}}
     value = ws * N * 1e3 / ms
 
@@ -443,7 +462,9 @@ def run_ours(args, ws, rank, local):
             z = h_Z.to(dev, non_blocking=True)
             xx = h_x.to(dev, non_blocking=True).requires_grad_(True)
             do = h_dout.to(dev, non_blocking=True)
-            b, r = build_inputs(p, z, cell, dev, layer)
+            b, r = build_inputs(p, z, cell, dev, layer, materialize_rbf=not chunked)
+            if chunked:
+                r = RbfSpec(b["f_dist"], r.offset, r.coeff)
             out, (gx, gp) = layer_step(layer, p, xx, z, b, r, do, [xx, p])
             h_out.copy_(out.detach(), non_blocking=True)
             h_dx.copy_(gx, non_blocking=True)

@@ -67,6 +67,11 @@ class E2AttentionArbOrder_sparse(nn.Module):
         # keep the span's q.k scores ([E, heads] fp32) from the forward for the backward, which then
         # gathers no key rows for them (taken where the span kernels support it: 128 heads of 8)
         self.keep_logits = True
+        # edge_chunk (inference path): with a number of edges set, the edge side (radial MLP and attention
+        # span) runs over blocks of query rows of about that many edges, each block checkpointed: its
+        # [edges, .] tensors exist only while the block runs, forward and backward (the backward forms
+        # them again), so activation memory is linear in the nodes plus one block of edges
+        self.edge_chunk = None
 
     def _fused_rows(self):
         if getattr(self, "_fused_rows_cache", None) is None:
@@ -119,6 +124,72 @@ class E2AttentionArbOrder_sparse(nn.Module):
         h = run_mlp(list(net)[1:], h, cw, first_tables=(t_tab, z_q, s_tab, z_k))
         return h  # [E, 2H]: gate = [:, :H], inputhead = [:, H:]
 
+    def _edge_chunks(self, bd, n_rows):
+        """Blocks of query rows of about ``edge_chunk`` edges each, or None (the option is off, the graph
+        fits one block, or its edges are not in query order).  Blocks are consecutive runs of the graph's
+        spatial row order (``row_order``, else the row index), so a block's keys are a compact region.
+        Per block: ``(rows, edges, md)`` = its rows in that order, its edge ids, and the CSR metadata of its
+        edges with the block's rows renumbered 0..n-1.  Formed once per graph (kept in ``bd``)."""
+        if not self.edge_chunk:
+            return None
+        rp0 = bd["metadata"][0]
+        key = (self.edge_chunk, n_rows, id(rp0), rp0.data_ptr(), rp0._version)
+        cached = bd.get("_edge_blocks")
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        from .ops import prepare_sparse_qk_edge_index_metadata
+
+        row_ptr = bd["metadata"][0][: n_rows + 1].to(torch.int64)
+        E = int(row_ptr[-1])
+        if E <= self.edge_chunk:
+            return None
+        if bd.get("query_sorted", None) is None:
+            qi = bd["query_idx"]
+            bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
+        if not bd["query_sorted"]:
+            return None
+        dev = row_ptr.device
+        order = bd.get("row_order")
+        order = (torch.arange(n_rows, device=dev) if order is None or order.numel() != n_rows
+                 else order.to(torch.int64))
+        deg = (row_ptr[1:] - row_ptr[:-1])[order]
+        csum = torch.cumsum(deg, 0)
+        targets = torch.arange(1, (E + self.edge_chunk - 1) // self.edge_chunk, device=dev) * self.edge_chunk
+        cuts = [0] + sorted(set(int(c) for c in torch.searchsorted(csum, targets).tolist() if 0 < int(c) < n_rows))
+        cuts.append(n_rows)
+        key_sorted = bd["neighbor_idx"]
+        blocks = []
+        for a, b in zip(cuts[:-1], cuts[1:]):
+            rows = order[a:b]
+            d = deg[a:b]
+            n_e = int(d.sum())
+            local = torch.repeat_interleave(torch.arange(b - a, device=dev), d, output_size=n_e)
+            starts = torch.repeat_interleave(row_ptr[rows] - (torch.cumsum(d, 0) - d), d, output_size=n_e)
+            edges = starts + torch.arange(n_e, device=dev)
+            md = prepare_sparse_qk_edge_index_metadata(local, key_sorted[edges], b - a, bd["f_outcell_index"].shape[0])
+            blocks.append((rows, edges, md))
+        bd["_edge_blocks"] = (key, blocks)
+        return blocks
+
+    def _chunk_span(self, q_scaled, key, merged, attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx, poly,
+                    edge_dis, rows, edges, md, key_order):
+        """Radial MLP and attention span for one block of query rows (checkpointed): [rows, C', H]."""
+        from torch.utils.checkpoint import checkpoint
+
+        if isinstance(attn_weight, RbfSpec):
+            aw_in, aw = attn_weight.dist[edges], attn_weight
+        else:
+            aw_in, aw = attn_weight[edges], None
+        qi, ni = query_idx[edges], neighbor_idx[edges]
+
+        def block(q, k, v, awd, pl, dd):
+            w = RbfSpec(awd, aw.offset, aw.coeff) if aw is not None else awd
+            gate = self.edge_gate(w, atomic_numbers, outcell, qi, ni)
+            return attention_span(q, k, v, gate, pl, dd, md, None, key_order, keep_logits=False)
+
+        return checkpoint(block, q_scaled[rows], key, merged, aw_in, poly[edges], edge_dis[edges],
+                          use_reentrant=False)
+
     def forward(self, node_pos, node_irreps_input, edge_dis, edge_vec, attn_weight, atomic_numbers,
                 poly_dist=None, attn_mask=None, batch=None, batched_data=None, **kwargs):
         if self.training and self.alpha_drop > 0:
@@ -136,6 +207,8 @@ class E2AttentionArbOrder_sparse(nn.Module):
         metadata = bd["metadata"]
         x = node_irreps_input
 
+        fused = x.is_cuda and not self.training
+        chunks = self._edge_chunks(bd, N1) if fused else None
         query = self.query_linear(x if N1 == n_all else x[:N1]).reshape(N1, H, -1)
         # kv_halo (domain decomposition): the rows of x are this rank's atoms only; the other atoms'
         # key / value projections come from their owners, appended after the own rows
@@ -145,14 +218,14 @@ class E2AttentionArbOrder_sparse(nn.Module):
             key = kv_halo(key, "key")
         key = key[outcell].reshape(N2, H, -1)
         q_scaled = query / math.sqrt(query.shape[-1])
-        gate = self.edge_gate(attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx)
+        if chunks is None:
+            gate = self.edge_gate(attn_weight, atomic_numbers, outcell, query_idx, neighbor_idx)
 
         value = self.proj_value(x)
         if kv_halo is not None:
             value = kv_halo(value, "value")
         value = value[outcell]                                                       # [N2, 9, C]
         tp = self.first_order_tp
-        fused = x.is_cuda and not self.training
         if fused:
             # rows of both halves in the (m, c) order of the output linear; [A_b v ; v] in one kernel
             row_perm, tasks = self._fused_rows()
@@ -170,10 +243,18 @@ class E2AttentionArbOrder_sparse(nn.Module):
         merged = merged.reshape(N2, -1, H)                                              # [N2, 29*C/H, H]
 
         poly = poly_dist if poly_dist is not None else torch.ones_like(edge_dis)
-        if bd.get("query_sorted", None) is None:
+        if chunks is not None:
+            parts = [self._chunk_span(q_scaled, key, merged, attn_weight, atomic_numbers, outcell, query_idx,
+                                      neighbor_idx, poly, edge_dis, rows, edges, md, bd.get("key_order"))
+                     for rows, edges, md in chunks]
+            rows_all = torch.cat([rows for rows, _, _ in chunks])
+            agg = torch.cat(parts, dim=0)[torch.argsort(rows_all)]
+        elif bd.get("query_sorted", None) is None:
             qi = bd["query_idx"]
             bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
-        if bd["query_sorted"]:
+        if chunks is not None:
+            pass
+        elif bd["query_sorted"]:
             agg = attention_span(q_scaled, key, merged, gate, poly, edge_dis, metadata, bd.get("row_order"),
                                  bd.get("key_order"), keep_logits=self.keep_logits)
         else:

@@ -412,7 +412,7 @@ class E2FormerPotential(nn.Module):
     ``(energy [B], forces [N,3])``.  Periodic systems are one per call; non-periodic molecules may be
     batched (``batch`` sorted, systems do not see each other)."""
 
-    def __init__(self, memory_saving="auto", use_faiss=False, **backbone_kwargs):
+    def __init__(self, memory_saving="auto", use_faiss=False, edge_chunk=None, **backbone_kwargs):
         super().__init__()
         # use_faiss: expanded nodes in the order of the reference's FAISS neighbour path
         # (distributed_cell_expand, one image cell per direction) instead of CellExpander's; the edges
@@ -428,22 +428,29 @@ class E2FormerPotential(nn.Module):
         # full-size model; ~10% of the step's tensor-core work) and the attention span's q.k scores are
         # not kept (heads floats per edge and layer, ~6.4 GB at 1e5 atoms); False = both kept; "auto" =
         # both kept unless the evaluation's estimated peak passes 85% of the device's memory, then the
-        # scores are dropped first and the projections second
+        # scores are dropped first, the projections second, and last the edge side runs in checkpointed
+        # blocks of rows (``edge_chunk``, below)
+        # edge_chunk: a number of edges; every attention layer then runs its radial MLP and span over
+        # blocks of query rows of about that many edges, each checkpointed, so no [edges, .] tensor of
+        # the whole graph is kept (eval mode; the backward forms each block's again)
         self.memory_saving = memory_saving
-        self._set_memory_mode(memory_saving is True, memory_saving is not True)
+        self.edge_chunk = edge_chunk
+        self._set_memory_mode(memory_saving is True, memory_saving is not True, edge_chunk)
 
-    def _set_memory_mode(self, recompute, keep_logits):
+    def _set_memory_mode(self, recompute, keep_logits, edge_chunk=None):
         for blk in self.decoder.blocks:
             blk.ga.query_linear.recompute_pair_product = recompute
             blk.ga.key_linear.recompute_pair_product = recompute
             blk.ga.keep_logits = keep_logits
+            blk.ga.edge_chunk = edge_chunk
 
     # peak bytes of an evaluation per edge, projections recomputed and scores not kept (measured:
     # 112.6 GB at 3.13 M edges)
     _PEAK_BYTES_PER_EDGE = 36.0e3
 
     def _auto_memory_mode(self, n_rows, n_edges, device):
-        """(recompute projections, keep scores) for a graph of this size (``memory_saving="auto"``)."""
+        """(recompute projections, keep scores, edge block) for a graph of this size
+        (``memory_saving="auto"``)."""
         dec = self.decoder
         blk = dec.blocks[0].ga
         layers = len(dec.blocks)
@@ -451,11 +458,17 @@ class E2FormerPotential(nn.Module):
         logits = layers * n_edges * blk.num_attn_heads * 4
         base = self._PEAK_BYTES_PER_EDGE * n_edges
         cap = 0.85 * torch.cuda.get_device_properties(device).total_memory
+        chunk = self.edge_chunk
         if base + proj + logits <= cap:
-            return False, True
+            return False, True, chunk
         if base + proj <= cap:
-            return False, False
-        return True, False
+            return False, False, chunk
+        if base <= cap:
+            return True, False, chunk
+        return True, False, chunk or self._AUTO_EDGE_CHUNK
+
+    # edges per block when "auto" has to run the edge side in blocks
+    _AUTO_EDGE_CHUNK = 4_000_000
 
     @property
     def decoder(self):
