@@ -978,11 +978,16 @@ def compare_kernel_functions(mods, ins, q_idx, n_idx, md_ref, md_ours, N, N2, ti
             lambda f, md, a: f(a[0], a[1], qi32, ni32, N, metadata=md), [ins[2], alpha]),
         "edge_degree_outer_triton": (
             lambda f, md, a: f(a[0], a[1], qi32, N, metadata=md), [sh, fea]),
+        # bf16 value rows and weights (this package gathers the bf16 rows and sums in fp32)
+        "sparse_v_agg_edge_index_triton_cblocked[bf16]": (
+            lambda f, md, a: f(a[0], a[1], qi32, ni32, N, metadata=md),
+            [ins[2].to(torch.bfloat16), alpha.to(torch.bfloat16)]),
     }
     impls = {"sparse_qk_edge_index_triton": (ref_qk, ops.sparse_qk_edge_index_triton),
              "sparse_alpha_sum_edge_index_triton": (ref_as, ops.sparse_alpha_sum_edge_index_triton),
              "sparse_v_agg_edge_index_triton_cblocked": (ref_va, ops.sparse_v_agg_edge_index_triton_cblocked),
-             "edge_degree_outer_triton": (ref_eo, ops.edge_degree_outer_triton)}
+             "edge_degree_outer_triton": (ref_eo, ops.edge_degree_outer_triton),
+             "sparse_v_agg_edge_index_triton_cblocked[bf16]": (ref_va, ops.sparse_v_agg_edge_index_triton_cblocked)}
     out = {}
     for name, (call, args) in cases.items():
         row = {}
@@ -999,7 +1004,7 @@ def compare_kernel_functions(mods, ins, q_idx, n_idx, md_ref, md_ours, N, N2, ti
                 return torch.autograd.grad(call(fn, md, leaves), leaves, w)
 
             row[who] = {"fwd_ms": timed(fwd), "fwd_bwd_ms": timed(fb), "y": y.detach()}
-        d = (row["reference"]["y"] - row["ours"]["y"]).abs().max().item()
+        d = (row["reference"]["y"].float() - row["ours"]["y"].float()).abs().max().item()
         out[name] = {"reference_fwd_ms": row["reference"]["fwd_ms"], "ours_fwd_ms": row["ours"]["fwd_ms"],
                      "reference_fwd_bwd_ms": row["reference"]["fwd_bwd_ms"], "ours_fwd_bwd_ms": row["ours"]["fwd_bwd_ms"],
                      "max_rel_diff": d / max(1.0, row["ours"]["y"].abs().max().item())}

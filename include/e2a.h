@@ -120,6 +120,13 @@ int e2a_alpha_sum_bwd(const float* grad_out, const int32_t* query_idx, int64_t n
 /* out[i,c,h] = sum_{p in row i} alpha[perm[p],h] * value[col[p],c,h].  value:[M,C,H] out:[N,C,H] */
 int e2a_v_agg_fwd(const float* value, const float* alpha, const int32_t* row_ptr, const int32_t* col,
                   const int32_t* perm, int64_t n_rows, int C, int H, float* out, void* stream);
+/* The same aggregation of bf16 value rows (value: [M,C,H] bfloat16, 8-byte aligned), widened to fp32  */
+/* as they are gathered; fp32 alpha, sums and out.  E2A_ERR_UNSUPPORTED unless H divides 1024, H % 4 == 0 */
+/* and C*H <= 16384 (the caller then widens value itself and calls e2a_v_agg_fwd).                       */
+/* Replaces: sparse_v_agg_edge_index_triton_cblocked on bf16 values                                      */
+/*           (e2f/triton_dr/sparse_v_agg_edge_index_cblocked_bench.py:428-449, 197-240).                 */
+int e2a_v_agg_fwd_bf16(const void* value, const float* alpha, const int32_t* row_ptr, const int32_t* col,
+                       const int32_t* perm, int64_t n_rows, int C, int H, float* out, void* stream);
 /* d_alpha[perm[p],h] = sum_c dout[i,c,h] * value[col[p],c,h]  (query-CSR) */
 int e2a_v_agg_bwd_alpha(const float* dout, const float* value, const int32_t* row_ptr, const int32_t* col,
                         const int32_t* perm, int64_t n_rows, int C, int H, float* d_alpha, void* stream);

@@ -40,6 +40,7 @@ SIGNATURES = {
     "e2a_alpha_sum_fwd": (I32, [P, P, P, I64, I32, P, P]),
     "e2a_alpha_sum_bwd": (I32, [P, P, I64, I32, P, P]),
     "e2a_v_agg_fwd": (I32, [P, P, P, P, P, I64, I32, I32, P, P]),
+    "e2a_v_agg_fwd_bf16": (I32, [P, P, P, P, P, I64, I32, I32, P, P]),
     "e2a_v_agg_bwd_alpha": (I32, [P, P, P, P, P, I64, I32, I32, P, P]),
     "e2a_v_agg_bwd_value": (I32, [P, P, P, P, P, I64, I32, I32, P, P]),
     "e2a_edge_outer_fwd": (I32, [P, P, P, P, I64, I32, I32, P, P]),

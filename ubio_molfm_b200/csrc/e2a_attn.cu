@@ -82,9 +82,9 @@ __device__ __forceinline__ void combine_stripes(float* red, float* out_s, int H,
 //   HEAD_INNER = false: rows are [H, D] (head = f / D, one head per float4, D % 4 == 0)
 // e_p = perm[p] (or p).  One CTA per output row, launched over the rows in `order`.
 // ------------------------------------------------------------------------------------------------
-template <int KS, bool HEAD_INNER, int MINB = 3>
+template <int KS, bool HEAD_INNER, int MINB = 3, typename T = float>
 __global__ void __launch_bounds__(kThreads, MINB)
-k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D, int row_f4,
+k_row_agg(const T* __restrict__ X, const float* __restrict__ w, int H, int D, int row_f4,
           const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const int32_t* __restrict__ perm,
           const int32_t* __restrict__ order, int64_t n_rows, float* __restrict__ out) {
   for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
@@ -107,7 +107,7 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int64_t e = perm ? perm[p + u] : p + u;
-            x[u] = ldg4(X + (int64_t)col[p + u] * row_f4 * 4 + 4 * f);
+            x[u] = ld4v(X, (int64_t)col[p + u] * row_f4 * 4 + 4 * f);
             wv[u] = __ldg(w + e * H + hcol);
           }
 #pragma unroll
@@ -117,19 +117,19 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
     }
     for (; p < re; ++p) {
       const int64_t e = perm ? perm[p] : p;
-      const float* xr = X + (int64_t)col[p] * row_f4 * 4;
+      const int64_t xr = (int64_t)col[p] * row_f4 * 4;   // row start, in values
       if (HEAD_INNER) {
         const float4 b = ldg4(w + e * H + h0);
 #pragma unroll
         for (int s = 0; s < KS; ++s) {
           const int f = threadIdx.x + s * kThreads;
-          if (f < row_f4) acc[s] = f4_fma4(b, ldg4(xr + 4 * f), acc[s]);
+          if (f < row_f4) acc[s] = f4_fma4(b, ld4v(X, xr + 4 * f), acc[s]);
         }
       } else {
 #pragma unroll
         for (int s = 0; s < KS; ++s) {
           const int f = threadIdx.x + s * kThreads;
-          if (f < row_f4) acc[s] = f4_fma(__ldg(w + e * H + (4 * f) / D), ldg4(xr + 4 * f), acc[s]);
+          if (f < row_f4) acc[s] = f4_fma(__ldg(w + e * H + (4 * f) / D), ld4v(X, xr + 4 * f), acc[s]);
         }
       }
     }
@@ -138,6 +138,81 @@ k_row_agg(const float* __restrict__ X, const float* __restrict__ w, int H, int D
     for (int s = 0; s < KS; ++s) {
       const int f = threadIdx.x + s * kThreads;
       if (f < row_f4) reinterpret_cast<float4*>(orow)[f] = acc[s];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// CSR row aggregation of bf16 [C, H] rows: out[r, :] = sum_{p in row r} w[e_p, f % H] * X[col[p], f], one
+// CTA per output row.  Each thread owns KS groups of eight consecutive values (one 16-byte load of eight
+// bf16, widened to fp32 exactly; eight consecutive heads, H % 8 == 0), fp32 sums and output.  Edges are
+// gathered two at a time (more loads in flight) and accumulated in CSR order.
+// ------------------------------------------------------------------------------------------------
+template <int KS>
+__global__ void __launch_bounds__(kThreads, 3)
+k_row_agg_bf16(const uint4* __restrict__ X, const float* __restrict__ w, int H, int row_f8,
+               const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col, const int32_t* __restrict__ perm,
+               int64_t n_rows, float* __restrict__ out) {
+  for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const int rs = row_ptr[r], re = row_ptr[r + 1];
+    float4 acc[2 * KS];
+#pragma unroll
+    for (int s = 0; s < 2 * KS; ++s) acc[s] = f4_zero();
+    const int h0 = (8 * threadIdx.x) % H;   // the same heads for every slot (kThreads * 8 is a multiple of H)
+    int p = rs;
+    for (; p + 2 <= re; p += 2) {
+      uint4 x[2][KS];
+      float4 b[2][2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t e = perm ? perm[p + u] : p + u;
+        const uint4* xr = X + (int64_t)col[p + u] * row_f8;
+        b[u][0] = ldg4(w + e * H + h0);
+        b[u][1] = ldg4(w + e * H + h0 + 4);
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const int f = threadIdx.x + s * kThreads;
+          x[u][s] = f < row_f8 ? __ldg(xr + f) : make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int s = 0; s < KS; ++s) {
+          const uint4 v = x[u][s];
+          acc[2 * s] = f4_fma4(b[u][0], make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                                    __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u)),
+                               acc[2 * s]);
+          acc[2 * s + 1] = f4_fma4(b[u][1], make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                                        __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u)),
+                                   acc[2 * s + 1]);
+        }
+    }
+    for (; p < re; ++p) {
+      const int64_t e = perm ? perm[p] : p;
+      const uint4* xr = X + (int64_t)col[p] * row_f8;
+      const float4 b0 = ldg4(w + e * H + h0), b1 = ldg4(w + e * H + h0 + 4);
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const int f = threadIdx.x + s * kThreads;
+        if (f < row_f8) {
+          const uint4 v = __ldg(xr + f);
+          acc[2 * s] = f4_fma4(b0, make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                                               __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u)), acc[2 * s]);
+          acc[2 * s + 1] = f4_fma4(b1, make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u),
+                                                   __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u)),
+                                   acc[2 * s + 1]);
+        }
+      }
+    }
+    float4* orow = reinterpret_cast<float4*>(out + r * (int64_t)row_f8 * 8);
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int f = threadIdx.x + s * kThreads;
+      if (f < row_f8) {
+        orow[2 * f] = acc[2 * s];
+        orow[2 * f + 1] = acc[2 * s + 1];
+      }
     }
   }
 }
@@ -779,11 +854,26 @@ cudaError_t prep_smem(Kern kern, size_t smem) {
     default: { auto kf = KERN<16>; __VA_ARGS__; break; }             \
   }
 
-template <int KS>
-void agg_ch(const float* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
+template <int KS, typename T = float>
+void agg_ch(const T* X, const float* w, const Dims& dm, const int32_t* row_ptr, const int32_t* col,
             const int32_t* perm, const int32_t* order, int64_t n_rows, float* out, cudaStream_t st) {
-  k_row_agg<KS, true, (KS >= 16 ? 2 : 4)><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr, col, perm, order,
-                                                             n_rows, out);
+  k_row_agg<KS, true, (KS >= 16 ? 2 : 4), T><<<grid_for(n_rows), kThreads, 0, st>>>(X, w, dm.H, dm.D, dm.CH4, row_ptr,
+                                                                                  col, perm, order, n_rows, out);
+}
+
+// the same aggregation of bf16 [C,H] rows (widened to fp32 as they are loaded; fp32 sums and output)
+int launch_agg_ch_bf16(const e2a_bf16x4* X, const float* w, const Dims& dm, int ks, const int32_t* row_ptr,
+                       const int32_t* col, const int32_t* perm, const int32_t* order, int64_t n_rows, float* out,
+                       cudaStream_t st) {
+  switch (ks) {
+    case 1: agg_ch<1>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 2: agg_ch<2>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 4: agg_ch<4>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    case 8: agg_ch<8>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+    default: agg_ch<16>(X, w, dm, row_ptr, col, perm, order, n_rows, out, st); break;
+  }
+  E2A_CHECK_LAUNCH();
+  return E2A_OK;
 }
 
 // out rows = CSR aggregation of [C,H] rows (value / cotangent), weights w[E,H]
@@ -1190,6 +1280,30 @@ int agg_ch(const float* X, const float* w, int H, int C, const int32_t* row_ptr,
   const int need = (dm.CH4 + kThreads - 1) / kThreads;
   const int ks = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 16;
   return launch_agg_ch(X, w, dm, ks, row_ptr, col, perm, nullptr, n_rows, out, st);
+}
+
+int agg_ch_bf16(const void* X, const float* w, int H, int C, const int32_t* row_ptr, const int32_t* col,
+                const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st) {
+  if (H <= 0 || C <= 0 || H % 4 || 1024 % H || (C * H) % 4 || (C * H) / 4 > 16 * kThreads) return E2A_ERR_UNSUPPORTED;
+  if (((uintptr_t)X & 7u) || !al16(w) || !al16(out)) return E2A_ERR_UNSUPPORTED;
+  if (H % 8 == 0 && (C * H) % 8 == 0 && al16(X) && (C * H) / 8 <= 4 * kThreads) {
+    // 16-byte loads of eight values
+    const int f8 = C * H / 8;
+    const int need = (f8 + kThreads - 1) / kThreads;
+    const uint4* x8 = reinterpret_cast<const uint4*>(X);
+    const int g = grid_for(n_rows);
+    if (need <= 1) k_row_agg_bf16<1><<<g, kThreads, 0, st>>>(x8, w, H, f8, row_ptr, col, perm, n_rows, out);
+    else if (need <= 2) k_row_agg_bf16<2><<<g, kThreads, 0, st>>>(x8, w, H, f8, row_ptr, col, perm, n_rows, out);
+    else k_row_agg_bf16<4><<<g, kThreads, 0, st>>>(x8, w, H, f8, row_ptr, col, perm, n_rows, out);
+    E2A_CHECK_LAUNCH();
+    return E2A_OK;
+  }
+  Dims dm{};
+  dm.H = H; dm.C = C; dm.D = 4; dm.CH4 = C * H / 4; dm.HD4 = H; dm.g = 1;
+  const int need = (dm.CH4 + kThreads - 1) / kThreads;
+  const int ks = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 16;
+  return launch_agg_ch_bf16(reinterpret_cast<const e2a_bf16x4*>(X), w, dm, ks, row_ptr, col, perm, nullptr, n_rows,
+                            out, st);
 }
 
 int agg_hd(const float* X, const float* w, int H, int D, const int32_t* row_ptr, const int32_t* col,

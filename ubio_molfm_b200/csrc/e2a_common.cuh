@@ -69,6 +69,18 @@ __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
+// Four consecutive bf16 values (one 8-byte load) widened to fp32; bf16 -> fp32 is exact (the bf16 bits
+// are the high half of the fp32 word).
+struct e2a_bf16x4 { uint16_t v[4]; };
+__device__ __forceinline__ float4 ldg4(const e2a_bf16x4* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xFFFF0000u));
+}
+// Row element offsets counted in values: float rows are addressed per value, bf16 rows per group of four.
+__device__ __forceinline__ float4 ld4v(const float* base, int64_t off) { return ldg4(base + off); }
+__device__ __forceinline__ float4 ld4v(const e2a_bf16x4* base, int64_t off) { return ldg4(base + (off >> 2)); }
+
 // Euclidean norm of a 3-vector, evaluated as fma(z,z,fma(y,y,x*x)) then a correctly rounded
 // sqrt: the exact fp32 operation sequence of PyTorch's CPU vector-norm kernel for a length-3
 // reduction (torch.linalg.norm / torch.norm, p=2), which the reference uses for every distance

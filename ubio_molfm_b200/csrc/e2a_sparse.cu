@@ -7,6 +7,8 @@
 namespace e2a_fast {
 int agg_ch(const float* X, const float* w, int H, int C, const int32_t* row_ptr, const int32_t* col,
            const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
+int agg_ch_bf16(const void* X, const float* w, int H, int C, const int32_t* row_ptr, const int32_t* col,
+                const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
 int agg_hd(const float* X, const float* w, int H, int D, const int32_t* row_ptr, const int32_t* col,
            const int32_t* perm, int64_t n_rows, float* out, cudaStream_t st);
 int dbeta(const float* value, const float* dout, int H, int C, const int32_t* row_ptr, const int32_t* col,
@@ -339,6 +341,14 @@ int e2a_v_agg_fwd(const float* value, const float* alpha, const int32_t* row_ptr
                                                                      out);
   E2A_CHECK_LAUNCH();
   return E2A_OK;
+}
+
+int e2a_v_agg_fwd_bf16(const void* value, const float* alpha, const int32_t* row_ptr, const int32_t* col,
+                       const int32_t* perm, int64_t n_rows, int C, int H, float* out, void* stream) {
+  if (n_rows < 0 || C <= 0 || H <= 0) return E2A_ERR_ARG;
+  if (n_rows == 0) return E2A_OK;
+  if (!row_ptr || !out || !value || !alpha || !col) return E2A_ERR_ARG;
+  return e2a_fast::agg_ch_bf16(value, alpha, H, C, row_ptr, col, perm, n_rows, out, (cudaStream_t)stream);
 }
 
 int e2a_v_agg_bwd_alpha(const float* dout, const float* value, const int32_t* row_ptr, const int32_t* col,

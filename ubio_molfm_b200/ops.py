@@ -286,10 +286,28 @@ def _v_agg_dalpha(g, v, md):
     return da
 
 
+def _v_agg_bf16(v, a, md, num_queries):
+    """:func:`_v_agg` reading bf16 value rows directly (widened in the gather); None where the entry point
+    does not take the layout."""
+    lib = _lib.load()
+    M, C, H = v.shape
+    out = torch.empty((num_queries, C, H), device=v.device, dtype=torch.float32)
+    rc = lib.e2a_v_agg_fwd_bf16(ptr(v), ptr(a), ptr(md[0]), ptr(md[1]), ptr(md[2]), num_queries, C, H, ptr(out),
+                                stream_of(v.device))
+    if rc == _lib.E2A_ERR_UNSUPPORTED:
+        return None
+    check(rc, "e2a_v_agg_fwd_bf16")
+    return out
+
+
 class SparseVAggFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, value, alpha, md, num_queries):
-        out = _v_agg(_f32(value), _f32(alpha), md, num_queries)
+        out = None
+        if value.dtype == torch.bfloat16:
+            out = _v_agg_bf16(value.contiguous(), _f32(alpha), md, num_queries)
+        if out is None:
+            out = _v_agg(_f32(value), _f32(alpha), md, num_queries)
         ctx.save_for_backward(value, alpha, *md)
         ctx.dtypes = (value.dtype, alpha.dtype)
         return out.to(value.dtype)
