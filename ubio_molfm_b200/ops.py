@@ -512,16 +512,19 @@ class AttnSpanFn(torch.autograd.Function):
                                       C, ptr(out), ptr(beta), ptr(rmax), ptr(rsum), ptr(logits), stream_of(dev)),
               "e2a_attn_fwd")
         TIMER.stop(tok)
+        # the caller's own tensors too (the same objects, no copies, where they are already fp32 and
+        # contiguous): a create_graph backward differentiates through them
         ctx.save_for_backward(q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order,
-                              *md)
-        ctx.inputs = (q_in, key_in, value_in, edge_gate_in, poly_in, dist_in)
+                              q_in, key_in, value_in, edge_gate_in, poly_in, dist_in, *md)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order, *md = ctx.saved_tensors
+        (q, key, value, edge_gate, poly, dist, beta, rmax, rsum, logits, row_order, key_order,
+         *rest) = ctx.saved_tensors
+        inputs, md = tuple(rest[:6]), rest[6:]
         if torch.is_grad_enabled():
-            return _span_double_backward(ctx, dout, md)
+            return _span_double_backward(ctx, inputs, dout, md)
         lib = _lib.load()
         dout = _f32(dout)
         N, H, D = q.shape
@@ -600,18 +603,17 @@ def _span_composite(q, key, value, edge_gate, poly, dist, md, N):
     return SparseVAggFn.apply(value, alpha, md, N)
 
 
-def _span_double_backward(ctx, dout, md):
+def _span_double_backward(ctx, ins, dout, md):
     """Backward of :class:`AttnSpanFn` under ``create_graph=True`` (force-loss training): the span is formed
     again from :func:`_span_composite` and differentiated with a graph, so the returned gradients are
     themselves differentiable in the inputs and in ``dout``.  The first-order values equal the fused
     kernels' up to fp32 rounding; the fused kernels keep serving every first-order backward."""
-    ins = ctx.inputs
     need = [bool(n) for n in ctx.needs_input_grad[:6]]
     with torch.enable_grad():
         # one fresh view per input: the inputs may depend on one another (poly and the radial gate are
         # functions of dist), and a gradient w.r.t. the tensors themselves would be the total derivative
         f32 = [t.contiguous().to(torch.float32).view_as(t) for t in ins]
-        out = _span_composite(*f32, tuple(md), int(ctx.inputs[0].shape[0]))
+        out = _span_composite(*f32, tuple(md), int(ins[0].shape[0]))
         wrt = [t for t, n in zip(f32, need) if n]
         got = iter(torch.autograd.grad(out, wrt, dout, create_graph=True, allow_unused=True))
     grads = [next(got) if n else None for n in need]
