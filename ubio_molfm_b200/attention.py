@@ -25,6 +25,34 @@ from . import linear as tc
 from .ops import attention_span
 
 
+def edge_blocks(row_ptr, row_order, edge_chunk):
+    """Split the query rows of a query-sorted CSR (``row_ptr`` [n+1]) into blocks of about ``edge_chunk``
+    edges: consecutive runs of ``row_order`` (all rows once; None = index order).  Per block
+    ``(rows, local, edges)``: its rows in that order, each of its edges' row position within the block
+    (ascending), and the edges' ids, row by row in CSR order.  Device tensors; a few host reads."""
+    row_ptr = row_ptr.to(torch.int64)
+    n_rows = row_ptr.numel() - 1
+    dev = row_ptr.device
+    order = (torch.arange(n_rows, device=dev) if row_order is None or row_order.numel() != n_rows
+             else row_order.to(torch.int64))
+    E = int(row_ptr[-1])
+    deg = (row_ptr[1:] - row_ptr[:-1])[order]
+    csum = torch.cumsum(deg, 0)
+    targets = torch.arange(1, max((E + edge_chunk - 1) // edge_chunk, 1), device=dev) * edge_chunk
+    cuts = [0] + sorted(set(int(c) for c in torch.searchsorted(csum, targets).tolist() if 0 < int(c) < n_rows))
+    cuts.append(n_rows)
+    out = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        rows = order[a:b]
+        d = deg[a:b]
+        n_e = int(d.sum())
+        local = torch.repeat_interleave(torch.arange(b - a, device=dev), d, output_size=n_e)
+        # edge j of the block, in row slot i: row_ptr[rows[i]] + (j - first slot of row i in the block)
+        starts = torch.repeat_interleave(row_ptr[rows] - (torch.cumsum(d, 0) - d), d, output_size=n_e)
+        out.append((rows, local, starts + torch.arange(n_e, device=dev)))
+    return out
+
+
 class E2AttentionArbOrder_sparse(nn.Module):
     def __init__(self, irreps_node_input="256x0e+256x1e+256x2e", attn_weight_input_dim: int = 32,
                  num_attn_heads: int = 8, attn_scalar_head: int = 32, irreps_head="32x0e+32x1e+32x2e",
@@ -148,25 +176,11 @@ class E2AttentionArbOrder_sparse(nn.Module):
             bd["query_sorted"] = bool(qi.numel() < 2 or not bool((qi[1:] < qi[:-1]).any()))
         if not bd["query_sorted"]:
             return None
-        dev = row_ptr.device
-        order = bd.get("row_order")
-        order = (torch.arange(n_rows, device=dev) if order is None or order.numel() != n_rows
-                 else order.to(torch.int64))
-        deg = (row_ptr[1:] - row_ptr[:-1])[order]
-        csum = torch.cumsum(deg, 0)
-        targets = torch.arange(1, (E + self.edge_chunk - 1) // self.edge_chunk, device=dev) * self.edge_chunk
-        cuts = [0] + sorted(set(int(c) for c in torch.searchsorted(csum, targets).tolist() if 0 < int(c) < n_rows))
-        cuts.append(n_rows)
         key_sorted = bd["neighbor_idx"]
         blocks = []
-        for a, b in zip(cuts[:-1], cuts[1:]):
-            rows = order[a:b]
-            d = deg[a:b]
-            n_e = int(d.sum())
-            local = torch.repeat_interleave(torch.arange(b - a, device=dev), d, output_size=n_e)
-            starts = torch.repeat_interleave(row_ptr[rows] - (torch.cumsum(d, 0) - d), d, output_size=n_e)
-            edges = starts + torch.arange(n_e, device=dev)
-            md = prepare_sparse_qk_edge_index_metadata(local, key_sorted[edges], b - a, bd["f_outcell_index"].shape[0])
+        for rows, local, edges in edge_blocks(row_ptr, bd.get("row_order"), self.edge_chunk):
+            md = prepare_sparse_qk_edge_index_metadata(local, key_sorted[edges], rows.numel(),
+                                                       bd["f_outcell_index"].shape[0])
             blocks.append((rows, edges, md))
         bd["_edge_blocks"] = (key, blocks)
         return blocks
